@@ -1,0 +1,309 @@
+"""Benchmark: Lloyd rows x iterations / s on the KMeans metric workload.
+
+Default workload (BASELINE.json ``configs[1]``): X 500,000 x 100 fp32 from a
+50-component Gaussian mixture (seed 1), k = 50, explicit init = 50 seeded rows,
+n_init = 1, max_iter = 100, tol = 0. One *step* is one full fit (all its Lloyd
+iterations, the final E-step and the inertia).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+
+* ``value``: whole-job rows x iterations / s with X already resident in HBM
+  (device time of the fit, CUDA events on the library's stream; max over ranks).
+* ``e2e``: the same metric through the public C-ABI call with host buffers
+  (pinned X in, labels/centres out, host<->device copies inside the timed region).
+* ``roofline``: the E-step kernel (dominant) against the measured HBM copy
+  bandwidth; algorithmic bytes = 4 n d per launch (X read once).
+* ``cpu_baseline`` (rank 0, N = 1): scikit-learn's Lloyd (the reference's CPU
+  path) on a bounded sample of the same workload.
+
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): rows are split
+into N contiguous shards (strong scaling of the same dataset); the per-iteration
+k x d sums and k counts are all-reduced with NCCL inside the library.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Lloyd rows x iters/s (500k x 100, k=50)"
+UNIT = "rows*iters/s"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _traffic_for(config: str, launches_rows: int):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    e = d.get(config)
+    if not e:
+        return None
+    # bytes per row measured by ncu on a smaller case, scaled to this launch
+    return float(e["dram_bytes_per_row"]) * launches_rows
+
+
+def cpu_baseline(X, init, k, sample_iters: int):
+    """scikit-learn's Lloyd (the reference's CPU path) on a bounded sample."""
+    from sklearn.cluster import KMeans
+    from threadpoolctl import threadpool_info
+    from sklearn.utils._openmp_helpers import _openmp_effective_n_threads
+
+    times, iters = [], []
+    for _ in range(2):
+        t0 = time.perf_counter()
+        km = KMeans(k, init=init, n_init=1, max_iter=sample_iters, tol=0, algorithm="lloyd").fit(X)
+        times.append(time.perf_counter() - t0)
+        iters.append(km.n_iter_)
+    t = statistics.median(times)
+    cores = _openmp_effective_n_threads()
+    blas = [f"{i.get('internal_api')}:{i.get('num_threads')}" for i in threadpool_info()]
+    return {"value": X.shape[0] * iters[0] / t, "unit": UNIT, "cores": int(cores), "kind": "reference",
+            "sample": (f"sklearn {__import__('sklearn').__version__} KMeans(lloyd, n_init=1, tol=0) on the full "
+                       f"{X.shape[0]}x{X.shape[1]} k={k} workload, max_iter={sample_iters} "
+                       f"(median of 2 fits, {t:.2f}s each); threads {blas}")}
+
+
+def run_reference(args, w, X, init):
+    """--impl reference: the reference's own CPU implementation of the path."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from sklearn.cluster import KMeans
+    from sklearn.utils._openmp_helpers import _openmp_effective_n_threads
+
+    sample_iters = 20
+    for _ in range(args.warmup):
+        KMeans(w.k, init=init, n_init=1, max_iter=sample_iters, tol=0, algorithm="lloyd").fit(X)
+    rows_iters, t_total = 0, 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        km = KMeans(w.k, init=init, n_init=1, max_iter=sample_iters, tol=0, algorithm="lloyd").fit(X)
+        t_total += time.perf_counter() - t0
+        rows_iters += X.shape[0] * km.n_iter_
+    v = rows_iters / t_total
+    cores = _openmp_effective_n_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture, BASELINE configs[1])",
+        "config": {"workload": w.name, "n": w.n, "d": w.d, "k": w.k, "max_iter": sample_iters, "tol": 0,
+                   "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": int(cores), "kind": "reference",
+                         "sample": f"scikit-learn {__import__('sklearn').__version__} Lloyd, max_iter={sample_iters} "
+                                   f"per step on the full {w.n}x{w.d} k={w.k} workload"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--rows", type=int, default=0, help="override n (testing)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    from skmetal_b200._synthetic import WORKLOADS, make_workload, scaled
+
+    w = WORKLOADS[args.config] if not args.rows else scaled(args.config, args.rows)
+    X, init = make_workload(w)
+    if args.impl == "reference":
+        run_reference(args, w, X, init)
+        return
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from skmetal_b200 import _bridge
+
+    _bridge.set_device(local)
+    _bridge.ensure_warmed_up()
+    if world > 1:
+        uid = [_bridge.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        _bridge.comm_init(uid[0], world, rank)
+
+    n = X.shape[0]
+    lo, hi = (n * rank) // world, (n * (rank + 1)) // world
+    Xs = np.ascontiguousarray(X[lo:hi])
+    shard = (lo, n) if world > 1 else None
+    ds = _bridge.Dataset(Xs)
+    labels = np.empty(Xs.shape[0], dtype=np.int32)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        ds.fit(init, w.max_iter, 0.0, shard=shard)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = _bridge.launch_count()
+    ms_total, ms_loop, est_ms, est_n, iters = 0.0, 0.0, 0.0, 0, 0
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, _, n_iter = ds.fit(init, w.max_iter, 0.0, profile=True, shard=shard)
+        st = _bridge.last_fit_stats()
+        ms_total += st["ms_total"]
+        ms_loop += st["ms_loop"]
+        est_ms += st["estep_ms_sum"]
+        est_n += st["estep_launches"]
+        iters += n_iter
+    wall = time.perf_counter() - t0
+    launches = _bridge.launch_count() - l0
+    barrier()
+    clk = clocks.stop()
+    t_dev = ms_total / 1e3
+    if dist is not None:
+        tt = torch.tensor([t_dev, wall], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_dev, wall = float(tt[0]), float(tt[1])
+    rows_iters = n * iters  # every rank ran the same iterations over its shard of n rows
+    value = rows_iters / t_dev
+
+    # end to end through the host-buffer C-ABI call (pinned X in, labels + centres out)
+    Xp = torch.empty(Xs.shape, dtype=torch.float32, pin_memory=True).numpy()
+    Xp[...] = Xs
+    lab_p = torch.empty(Xs.shape[0], dtype=torch.int32, pin_memory=True).numpy()
+    e2e_steps = max(1, min(args.steps, 3))
+    barrier()
+    t0 = time.perf_counter()
+    e2e_iters = 0
+    for _ in range(e2e_steps):
+        if world > 1:
+            c, lab, inertia, n_iter = _bridge.kmeans_fit_shard(Xp, init, w.max_iter, 0.0, lo, n)
+        else:
+            c, lab, inertia, n_iter = _bridge.kmeans_fit(Xp, init, w.max_iter, 0.0)
+        e2e_iters += n_iter
+    e2e_t = time.perf_counter() - t0
+    if dist is not None:
+        tt = torch.tensor([e2e_t], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_t = float(tt[0])
+    e2e_value = n * e2e_iters / e2e_t
+
+    hbm, bf16, src = _peaks()
+    est_avg_s = est_ms / max(1, est_n) / 1e3
+    alg_bytes = 4.0 * Xs.shape[0] * w.d
+    achieved = alg_bytes / est_avg_s / 1e9 if est_avg_s > 0 else None
+    traffic = _traffic_for(w.name, Xs.shape[0])
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture, BASELINE configs[1]); X resident in HBM",
+        "config": {"workload": w.name, "n": n, "d": w.d, "k": w.k, "max_iter": w.max_iter, "tol": 0,
+                   "iters_per_step": iters / args.steps, "parallelism": f"rows sharded x{world}",
+                   "l2": "X (%.0f MB per GPU) > L2 (126 MB) between iterations" % (alg_bytes / 1e6)},
+        "e2e": {"value": e2e_value, "unit": UNIT,
+                "h2d_bytes_per_step": int(Xs.nbytes + init.nbytes),
+                "d2h_bytes_per_step": int(Xs.shape[0] * 4 + init.nbytes + 12)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
+                     "kernel": "E-step (estep_tc_kernel)", "peak_source": src,
+                     "loop_frac": (alg_bytes * iters / (ms_loop / 1e3)) / 1e9 / hbm if ms_loop > 0 else None},
+        "clocks": clk,
+        "wall_s": wall,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(X, init, w.k, sample_iters=20)
+    if world > 1:
+        _bridge.comm_destroy()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

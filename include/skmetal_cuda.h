@@ -1,0 +1,171 @@
+/*
+ * skmetal_cuda.h -- C ABI of libskmetal_cuda.so, the B200 (sm_100a) KMeans
+ * Lloyd library that replaces the reference's libSkMetalBridge.dylib for the
+ * KMeans path.
+ *
+ * Conventions (kept from the reference bridge, skmetal/_bridge.py:78-103):
+ *   - every entry point is synchronous and returns an int status, 0 = success
+ *     (skmetal_kmeans_inertia returns the value itself, -1.0f on error, as the
+ *     reference does);
+ *   - matrices are host pointers to C-contiguous row-major float32 arrays;
+ *     sizes are size_t; labels are 4-byte integers;
+ *   - a failing call returns a nonzero code; skmetal_last_error() gives the
+ *     message of the calling thread's last failure.
+ * Status codes: 1 invalid argument, 2 CUDA error, 3 out of device memory,
+ * 4 NCCL error, 5 timeout, 6 unsupported, 7 device-side check failed,
+ * 8 injected failure (tests).
+ *
+ * All arithmetic runs on the GPU; there is no CPU fallback.
+ */
+#ifndef SKMETAL_CUDA_H
+#define SKMETAL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- flags for the fit entry points ------------------------------------ */
+#define SKMETAL_FIT_CENTER      0x1u  /* centre X and init by the column mean (KMeans.fit semantics) */
+#define SKMETAL_FIT_SIMT        0x2u  /* force the SIMT E-step instead of the tensor-core one */
+#define SKMETAL_FIT_PROFILE     0x4u  /* time every E-step launch with CUDA events (see fit stats) */
+#define SKMETAL_FIT_DISTRIBUTED 0x8u  /* X is this rank's shard; sums are all-reduced over the communicator */
+#define SKMETAL_FIT_TOL_ABS     0x10u /* tol is the absolute threshold on the sum of squared centre shifts */
+
+/* ---- device / library management --------------------------------------- */
+
+/* Replaces skmetal_init (skmetal_bridge/Sources/SkMetalBridge/Bridge.swift:19-23). */
+int skmetal_init(void);
+
+/* Replaces skmetal_warmup (Bridge.swift:52-144): loads the kernels once. */
+int skmetal_warmup(void);
+
+/* Replaces skmetal_device_info (Bridge.swift:25-48). `has_unified_memory` is 0
+ * on a discrete GPU; `recommended_working_set_size` is the device memory size. */
+int skmetal_device_info(char* name, int name_capacity, size_t* max_threads, uint8_t* has_unified_memory,
+                        uint64_t* recommended_working_set_size);
+
+/* No reference counterpart (the reference drives one implicit device). */
+int skmetal_device_count(int* count);
+int skmetal_set_device(int device);
+
+/* Message of the calling thread's last failure; returns its status code. */
+int skmetal_last_error(char* buf, size_t capacity);
+
+/* Number of kernel launches issued by this library since load. */
+unsigned long long skmetal_launch_count(void);
+
+/* Host-side fault injection (tests): the `after_calls`-th guarded entry
+ * point from now fails with `code` before doing any GPU work. */
+int skmetal_debug_inject_failure(int code, int after_calls);
+
+/* ---- KMeans path: reference entry points -------------------------------- */
+
+/* Replaces skmetal_kmeans_assign (KMeansBridge.swift:138-181; bound at
+ * skmetal/_bridge.py:111-119,576-578). labels[i] = argmin_j ||x_i - c_j||^2,
+ * strict '<', first index wins. */
+int skmetal_kmeans_assign(const float* X, const float* centroids, uint32_t* labels, size_t n, size_t d, size_t k);
+
+/* Replaces skmetal_kmeans_batch_fused (KMeansBridge.swift:187-320; bound at
+ * skmetal/_bridge.py:120-132,591-617) with scikit-learn's single Lloyd run
+ * (sklearn/cluster/_kmeans.py:628-758) on X as given (no centring):
+ * `centroids` holds the initial centres on entry and the final ones on exit,
+ * `labels` the final labels; `tol` is the absolute threshold on the sum of
+ * squared centre shifts; iterations stop on strict convergence, on the
+ * tolerance or at max_iter; *n_iter_out follows scikit-learn's i+1 count.
+ * `num_groups` is accepted for ABI compatibility and ignored. */
+int skmetal_kmeans_batch_fused(const float* X, float* centroids, uint32_t* labels, size_t n, size_t d, size_t k,
+                               size_t num_groups, size_t max_iter, float tol, int32_t* n_iter_out);
+
+/* Replaces skmetal_compute_mindists (KMeansBridge.swift:89-134; bound at
+ * skmetal/_bridge.py:133-142,620-624): dists[i] = ||x_i - c_{labels[i]}||^2. */
+int skmetal_compute_mindists(const float* X, const float* centroids, const uint32_t* labels, float* dists, size_t n,
+                             size_t d, size_t k);
+
+/* Replaces skmetal_kmeans_inertia (KMeansBridge.swift:324-373; bound at
+ * skmetal/_bridge.py:627-639): sum_i ||x_i - c_{labels[i]}||^2 accumulated in
+ * float64 in a fixed order; returns -1.0f on error. */
+float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint32_t* labels, size_t n, size_t d,
+                             size_t k);
+
+/* Declared by the reference header (skmetal_bridge/Sources/SkMetalBridgeC/
+ * include/bridge.h:25), kernel row_norm_sq (DistanceKernels.metal:6-28). */
+int skmetal_row_norm_sq(const float* X, float* norms, size_t n, size_t d);
+
+/* ---- KMeans path: extended entry points ---------------------------------- */
+
+/* Full KMeans.fit for one explicit initialisation (sklearn/cluster/
+ * _kmeans.py:1436-1562 with n_init=1, algorithm="lloyd"), replacing the
+ * MetalKMeans.fit orchestration (skmetal/estimators/cluster.py:20-65).
+ * `tol` is scikit-learn's relative tolerance unless SKMETAL_FIT_TOL_ABS.
+ * Outputs may be NULL. centers_out is k x d (mean added back). */
+int skmetal_kmeans_fit(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter, double tol,
+                       uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
+                       int32_t* n_iter_out);
+
+/* One E+M step of sklearn's lloyd_iter_chunked_dense
+ * (sklearn/cluster/_k_means_lloyd.pyx:23-165, update_centers=True) on X as
+ * given: labels_out gets the E-step labels against centers_old, centers_new
+ * the M-step centres, weight_out the per-cluster weights after relocation,
+ * center_shift_out the per-centre Euclidean shift. Outputs may be NULL. */
+int skmetal_kmeans_lloyd_iter(const float* X, const float* centers_old, float* centers_new, int32_t* labels_out,
+                              float* weight_out, float* center_shift_out, size_t n, size_t d, size_t k);
+
+/* Distances of every row to every centre, D[i*k + j] = ||x_i - c_j||
+ * (replaces the MetalKMeans.transform gemm route, skmetal/estimators/
+ * cluster.py:135-146 and skmetal/_bridge.py:499-563). */
+int skmetal_kmeans_transform(const float* X, const float* centroids, float* D, size_t n, size_t d, size_t k);
+
+/* ---- device-resident datasets -------------------------------------------- */
+
+/* Copy X (n x d, host) to the current device once; fits on the handle then
+ * start from HBM-resident data. */
+int skmetal_dataset_create(const float* X, size_t n, size_t d, void** handle);
+int skmetal_dataset_free(void* handle);
+
+/* skmetal_kmeans_fit on a resident dataset (X is not modified). */
+int skmetal_kmeans_fit_dataset(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
+                               uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
+                               int32_t* n_iter_out);
+
+/* Predict on a resident dataset: labels_out (host, may be NULL to keep the
+ * labels on the device). */
+int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t k, int32_t* labels_out);
+
+/* Statistics of the calling thread's last fit / predict: device times in
+ * milliseconds measured with CUDA events on the library's stream
+ * (total, preparation, Lloyd loop, final E-step + inertia), the number of
+ * E-step launches timed individually (SKMETAL_FIT_PROFILE) and their summed
+ * duration, the kernel launches issued, and the iterations run. */
+int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,
+                           int32_t* estep_launches, double* estep_ms_sum, uint64_t* launches, int32_t* iterations);
+
+/* ---- multi-GPU (one process per GPU) -------------------------------------- */
+
+/* 128-byte NCCL unique id, produced on one rank and broadcast by the caller. */
+int skmetal_comm_unique_id(uint8_t* id128);
+
+/* Create this process's communicator on the current device. */
+int skmetal_comm_init(const uint8_t* id128, int nranks, int rank);
+
+int skmetal_comm_destroy(void);
+
+/* Distributed fit: X is this rank's shard (rows [row_base, row_base + n) of a
+ * dataset of n_total rows); all ranks pass the same init and parameters and
+ * obtain the same centres, inertia and n_iter; labels_out gets the shard's
+ * labels. */
+int skmetal_kmeans_fit_shard(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter,
+                             double tol, uint32_t flags, uint64_t row_base, uint64_t n_total, float* centers_out,
+                             int32_t* labels_out, double* inertia_out, int32_t* n_iter_out);
+
+int skmetal_dataset_fit_shard(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
+                              uint32_t flags, uint64_t row_base, uint64_t n_total, float* centers_out,
+                              int32_t* labels_out, double* inertia_out, int32_t* n_iter_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SKMETAL_CUDA_H */

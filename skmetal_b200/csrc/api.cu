@@ -1,0 +1,254 @@
+// Host driver and C ABI of libskmetal_cuda.so.
+//
+// The exported names and argument conventions are those of the reference's
+// Swift/Metal bridge (skmetal_bridge/Sources/SkMetalBridge/*.swift, bound by
+// skmetal/_bridge.py): host pointers, size_t sizes, int status (0 = ok),
+// synchronous calls. Each calling host thread gets its own CUDA stream per
+// device (the reference keeps one Metal command queue per thread,
+// MetalContext.swift:20-34). Nothing here falls back to the CPU: every result
+// is computed by the kernels of this library.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "driver.h"
+#include "kernels.cuh"
+#include "../../include/skmetal_cuda.h"
+
+namespace skm {
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+
+static thread_local std::string t_last_error;
+static thread_local int t_last_code = 0;
+std::atomic<unsigned long long> g_launches{0};
+static std::atomic<int> g_inject_code{0};
+static std::atomic<int> g_inject_countdown{-1};
+
+void set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  t_last_code = code;
+}
+
+// Host-side fault injection for tests: the N-th guarded call after arming
+// fails with the armed code before touching the GPU.
+int check_injected(const char* where) {
+  int cd = g_inject_countdown.load();
+  if (cd < 0) return OK;
+  if (g_inject_countdown.fetch_sub(1) == 0) {
+    const int code = g_inject_code.load();
+    g_inject_countdown.store(-1);
+    set_error(code, "injected failure at %s", where);
+    return code;
+  }
+  return OK;
+}
+
+// ---------------------------------------------------------------------------
+// per-thread, per-device stream
+// ---------------------------------------------------------------------------
+
+struct ThreadDev {
+  cudaStream_t stream = nullptr;
+  double* pinned = nullptr;  // small pinned scratch for flags / scalars
+};
+
+static thread_local std::map<int, ThreadDev> t_devs;
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) {
+    set_error(ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    return ERR_CUDA;
+  }
+  return OK;
+}
+
+int thread_stream(cudaStream_t* s, double** pinned) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  ThreadDev& td = t_devs[dev];
+  if (!td.stream) {
+    SKM_CUDA(cudaStreamCreateWithFlags(&td.stream, cudaStreamNonBlocking));
+    SKM_CUDA(cudaMallocHost(&td.pinned, 4096));
+  }
+  *s = td.stream;
+  if (pinned) *pinned = td.pinned;
+  return OK;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int v = 148;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = v;
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// stream-ordered allocations released at scope exit
+// ---------------------------------------------------------------------------
+
+DevBuffers::~DevBuffers() {
+  for (void* p : ptrs) cudaFreeAsync(p, stream);
+}
+
+int DevBuffers::alloc(void** p, size_t bytes) {
+  *p = nullptr;
+  if (bytes == 0) bytes = 16;
+  cudaError_t e = cudaMallocAsync(p, bytes, stream);
+  if (e != cudaSuccess) {
+    set_error(e == cudaErrorMemoryAllocation ? ERR_OOM : ERR_CUDA, "cudaMallocAsync(%zu): %s", bytes,
+              cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? ERR_OOM : ERR_CUDA;
+  }
+  ptrs.push_back(*p);
+  return OK;
+}
+
+static void configure_mempool_once() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return;
+    for (int d = 0; d < n; ++d) {
+      cudaMemPool_t pool;
+      if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
+        unsigned long long thr = ~0ull;  // keep freed blocks pooled between calls
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+      }
+    }
+  });
+}
+
+int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
+    return ERR_CUDA;
+  }
+  return OK;
+}
+
+// ---------------------------------------------------------------------------
+// host <-> device staging of row-major matrices into the padded layout
+// ---------------------------------------------------------------------------
+
+int upload_rows(float* dst, int ld, const float* src, long long n, int d, cudaStream_t s) {
+  if (n == 0) return OK;
+  if (ld == d) {
+    SKM_CUDA(cudaMemcpyAsync(dst, src, sizeof(float) * (size_t)n * d, cudaMemcpyDefault, s));
+  } else {
+    SKM_CUDA(cudaMemcpy2DAsync(dst, sizeof(float) * ld, src, sizeof(float) * d, sizeof(float) * d, n,
+                               cudaMemcpyDefault, s));
+    SKM_CUDA(cudaMemset2DAsync(dst + d, sizeof(float) * ld, 0, sizeof(float) * (ld - d), n, s));
+  }
+  return OK;
+}
+
+}  // namespace skm
+
+using namespace skm;
+
+// ===========================================================================
+// exported C ABI
+// ===========================================================================
+
+extern "C" {
+
+int skmetal_last_error(char* buf, size_t cap) {
+  if (buf && cap) {
+    size_t m = std::min(cap - 1, t_last_error.size());
+    memcpy(buf, t_last_error.data(), m);
+    buf[m] = 0;
+  }
+  return t_last_code;
+}
+
+int skmetal_init(void) {
+  configure_mempool_once();
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    set_error(ERR_CUDA, "no CUDA device: %s", e == cudaSuccess ? "device count 0" : cudaGetErrorString(e));
+    return ERR_CUDA;
+  }
+  cudaStream_t s;
+  return thread_stream(&s, nullptr);
+}
+
+int skmetal_warmup(void) {
+  int rc = skmetal_init();
+  if (rc) return rc;
+  cudaStream_t s;
+  rc = thread_stream(&s, nullptr);
+  if (rc) return rc;
+  // touch the kernels once so that module loading is off the timed path
+  const float X[8] = {0, 0, 1, 1, 10, 10, 9, 9};
+  const float C[4] = {0, 0, 10, 10};
+  uint32_t lab[4];
+  return skmetal_kmeans_assign(X, C, lab, 4, 2, 2);
+}
+
+int skmetal_device_info(char* name, int name_capacity, size_t* max_threads, uint8_t* has_unified_memory,
+                        uint64_t* recommended_working_set_size) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc) return rc;
+  cudaDeviceProp p;
+  SKM_CUDA(cudaGetDeviceProperties(&p, dev));
+  if (name && name_capacity > 0) {
+    size_t m = std::min((size_t)name_capacity - 1, strlen(p.name));
+    memcpy(name, p.name, m);
+    name[m] = 0;
+  }
+  if (max_threads) *max_threads = (size_t)p.maxThreadsPerBlock;
+  if (has_unified_memory) *has_unified_memory = p.integrated ? 1 : 0;
+  if (recommended_working_set_size) {
+    size_t fr = 0, tot = 0;
+    cudaMemGetInfo(&fr, &tot);
+    *recommended_working_set_size = (uint64_t)tot;
+  }
+  return OK;
+}
+
+int skmetal_device_count(int* count) {
+  SKM_CUDA(cudaGetDeviceCount(count));
+  return OK;
+}
+
+int skmetal_set_device(int device) {
+  SKM_CUDA(cudaSetDevice(device));
+  return OK;
+}
+
+unsigned long long skmetal_launch_count(void) { return g_launches.load(); }
+
+int skmetal_debug_inject_failure(int code, int after_calls) {
+  g_inject_code.store(code);
+  g_inject_countdown.store(after_calls);
+  return OK;
+}
+
+}  // extern "C"

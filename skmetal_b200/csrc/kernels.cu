@@ -1,0 +1,735 @@
+// SIMT kernels of the KMeans Lloyd path: data preparation (mean, centring,
+// scales), the direct-difference assignment used for predict and for small
+// shapes, the bulk fixed-point centroid sums, the M-step (relocation, average,
+// shift, convergence) and the inertia / distance outputs.
+//
+// Semantics follow scikit-learn 1.9.0's Lloyd, which is what the reference's
+// accelerate(KMeans) runs off Apple hardware:
+//   argmin with strict '<', first index wins  (_k_means_lloyd.pyx:205-213)
+//   relocation of empty clusters              (_k_means_common.pyx:167-211)
+//   averaging, empty -> heaviest cluster      (_k_means_common.pyx:274-295)
+//   centre shift                              (_k_means_common.pyx:298-311)
+//   strict convergence / tol / max_iter       (_kmeans.py:705-758)
+#include "kernels.cuh"
+
+#include <cfloat>
+#include <cmath>
+
+namespace skm {
+
+// ---------------------------------------------------------------------------
+// helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ long long to_fixed(float v, double scale) {
+  return __double2ll_rn(static_cast<double>(v) * scale);
+}
+
+__device__ __forceinline__ void red_add_s64(long long* p, long long v) {
+  atomicAdd(reinterpret_cast<unsigned long long*>(p), static_cast<unsigned long long>(v));
+}
+
+// Bounded software grid barrier for cooperative launches. Returns false (and
+// records an error in the fit state) if the other blocks do not arrive within
+// the spin limit, so that a broken launch ends instead of hanging the GPU.
+__device__ bool grid_barrier(FitState* st, unsigned int nblocks) {
+  __shared__ int ok_s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    volatile unsigned int* genp = &st->barrier_gen;
+    unsigned int gen = *genp;
+    __threadfence();
+    unsigned int arrived = atomicAdd(&st->barrier_count, 1u) + 1u;
+    if (arrived == nblocks) {
+      atomicExch(&st->barrier_count, 0u);
+      __threadfence();
+      atomicAdd(&st->barrier_gen, 1u);
+    } else {
+      long long spins = 0;
+      while (*genp == gen) {
+        if (++spins > (1LL << 25)) {
+          atomicExch(&st->error, 1001);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    ok_s = ok;
+  }
+  __syncthreads();
+  return ok_s != 0;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Deterministic block sum (fixed tree); result valid in thread 0.
+__device__ double block_sum_f64(double v, double* scratch /* >= 32 */) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  double r = 0.0;
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    r = lane < nw ? scratch[lane] : 0.0;
+    r = warp_sum(r);
+  }
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// data preparation
+// ---------------------------------------------------------------------------
+
+// max |x| over the first d columns (float bits; |x| >= 0 so uint order = float order)
+__global__ void maxabs_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                              unsigned int* __restrict__ out_bits) {
+  unsigned int m = 0;
+  const long long total = n * (long long)ld;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % ld);
+    if (c < d) {
+      unsigned int b = __float_as_uint(X[i]) & 0x7fffffffu;
+      if (b > 0x7f800000u) b = 0x7f800000u;  // NaN treated as +inf (rejected on host)
+      m = max(m, b);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out_bits, m);
+}
+
+// Column sums of X in fixed point (exact): colsum[j] = sum_r round(x_rj * scale).
+// Block b handles a contiguous row range; one thread per column.
+__global__ void colsum_fixed_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                    const double* __restrict__ scale_ptr, long long* __restrict__ colsum) {
+  const double scale = *scale_ptr;
+  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
+  const long long r0 = blockIdx.x * rows_per;
+  const long long r1 = min(n, r0 + rows_per);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    long long acc = 0;
+    for (long long r = r0; r < r1; ++r) acc += to_fixed(X[r * ld + j], scale);
+    if (acc != 0) red_add_s64(&colsum[j], acc);
+  }
+}
+
+// mean[j] = colsum[j] * inv_scale / n   (float32 result)
+__global__ void mean_from_colsum_kernel(const long long* __restrict__ colsum, int d, const double* __restrict__ scale_ptr,
+                                        double n_total, float* __restrict__ mean) {
+  const double inv_scale = 1.0 / *scale_ptr;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < d; j += gridDim.x * blockDim.x)
+    mean[j] = (float)((double)colsum[j] * inv_scale / n_total);
+}
+
+// X[:, :d] -= mean (float32, in place) and track max |x - mean|
+__global__ void center_kernel(float* __restrict__ X, int ld, long long n, int d,
+                              const float* __restrict__ mean, unsigned int* __restrict__ maxabs_bits) {
+  unsigned int m = 0;
+  const long long total = n * (long long)ld;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % ld);
+    if (c < d) {
+      const float v = X[i] - mean[c];
+      X[i] = v;
+      m = max(m, __float_as_uint(v) & 0x7fffffffu);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && maxabs_bits) atomicMax(maxabs_bits, m);
+}
+
+// Per-block float64 partial of sum_r sum_j x_rj^2 over a fixed row range
+// (for the scaled tolerance); combined by ordered_sum_kernel.
+__global__ void sumsq_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                     double* __restrict__ partial) {
+  __shared__ double scratch[32];
+  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
+  const long long r0 = blockIdx.x * rows_per;
+  const long long r1 = min(n, r0 + rows_per);
+  double acc = 0.0;
+  for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x)
+    for (int j = 0; j < d; ++j) {
+      const double v = X[r * ld + j];
+      acc += v * v;
+    }
+  acc = block_sum_f64(acc, scratch);
+  if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+// Fixed-point scale 2^F for sums of up to n_total values bounded by the max |x|
+// recorded in maxabs_bits: F = 62 - E - L with max < 2^E and n_total <= 2^L,
+// so no partial or total sum can reach 2^62.
+__device__ double fixed_scale(unsigned int maxabs_bits, double n_total) {
+  const float mx = __uint_as_float(maxabs_bits);
+  int E = -60;
+  if (mx > 0.0f) frexp((double)mx, &E);
+  int L = 0;
+  frexp(fmax(n_total, 1.0), &L);  // n_total < 2^L
+  int F = 62 - E - L;
+  F = max(-1000, min(1000, F));
+  return ldexp(1.0, F);
+}
+
+__global__ void scale_kernel(const unsigned int* __restrict__ maxabs_bits, double n_total, double* __restrict__ out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *out = fixed_scale(*maxabs_bits, n_total);
+}
+
+// Initialise the fit state. tol_mode 0: `tol` is already absolute; 1: `tol` is
+// relative and is scaled by the mean column variance sumsq / (n_total * d).
+__global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
+                                  double n_total, int d, const unsigned int* maxabs_bits) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  st->iter = 0;
+  st->done = max_iter <= 0;
+  st->strict = 0;
+  st->max_iter = max_iter;
+  st->n_empty = 0;
+  st->relocated = 0;
+  st->error = 0;
+  st->full_update = 1;
+  st->changed = 0;
+  st->sel_count = 0;
+  st->barrier_count = 0;
+  st->barrier_gen = 0;
+  st->shift_tot = 0.0;
+  st->inertia = 0.0;
+  double t = tol;
+  if (tol_mode == 1) t = (tol == 0.0 || sumsq == nullptr) ? 0.0 : (*sumsq / (n_total * (double)d)) * tol;
+  st->tol = t;
+  st->maxabs_bits = *maxabs_bits;
+  st->scale = fixed_scale(*maxabs_bits, n_total);
+  st->inv_scale = 1.0 / st->scale;
+}
+
+// centres: C[c][j] = init[c][j] - mean[j] for j < d, 0 in the padding
+__global__ void center_init_kernel(const float* __restrict__ init, int d, int k, const float* __restrict__ mean,
+                                   float* __restrict__ C, int ld) {
+  const int total = k * ld;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c = i / ld, j = i % ld;
+    C[i] = j < d ? (mean ? init[c * d + j] - mean[j] : init[c * d + j]) : 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// assignment (direct differences, float32): labels, min distance, change count
+// ---------------------------------------------------------------------------
+
+// Generic kernel: one thread per row, centres staged through shared memory.
+__global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                   const float* __restrict__ C, int k,
+                                   int32_t* __restrict__ labels, float* __restrict__ mind,
+                                   const FitState* __restrict__ st, unsigned long long* __restrict__ changed,
+                                   int skip_if_strict) {
+  extern __shared__ float csh[];
+  if (st) {
+    if (skip_if_strict ? (st->strict != 0) : (st->done != 0)) return;
+  }
+  const int chunk = max(1, min(k, (int)(kAssignSmemFloats / ld)));
+  const long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const bool active = r < n;
+  const float* xr = X + (active ? r : 0) * ld;
+  float best = FLT_MAX;
+  int bl = 0;
+  for (int c0 = 0; c0 < k; c0 += chunk) {
+    const int cn = min(chunk, k - c0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < cn * ld; i += blockDim.x) csh[i] = C[(long long)c0 * ld + i];
+    __syncthreads();
+    if (active) {
+      for (int c = 0; c < cn; ++c) {
+        const float* cr = csh + c * ld;
+        float acc = 0.0f;
+        int j = 0;
+        for (; j + 4 <= d; j += 4) {
+          const float4 xv = *reinterpret_cast<const float4*>(xr + j);
+          const float d0 = xv.x - cr[j], d1 = xv.y - cr[j + 1], d2 = xv.z - cr[j + 2], d3 = xv.w - cr[j + 3];
+          acc = fmaf(d0, d0, acc);
+          acc = fmaf(d1, d1, acc);
+          acc = fmaf(d2, d2, acc);
+          acc = fmaf(d3, d3, acc);
+        }
+        for (; j < d; ++j) {
+          const float t = xr[j] - cr[j];
+          acc = fmaf(t, t, acc);
+        }
+        if (acc < best) {
+          best = acc;
+          bl = c0 + c;
+        }
+      }
+    }
+  }
+  bool ch = false;
+  if (active) {
+    if (changed) ch = labels[r] != bl;
+    labels[r] = bl;
+    if (mind) mind[r] = best;
+  }
+  if (changed) {
+    const unsigned int b = __ballot_sync(0xffffffffu, ch);
+    if ((threadIdx.x & 31) == 0 && b) atomicAdd(changed, (unsigned long long)__popc(b));
+  }
+}
+
+// Small-d specialisation: the row lives in registers, all centres in shared memory.
+template <int D>
+__global__ void assign_small_kernel(const float* __restrict__ X, int ld, long long n,
+                                    const float* __restrict__ C, int k,
+                                    int32_t* __restrict__ labels, float* __restrict__ mind) {
+  extern __shared__ float csh[];
+  for (int i = threadIdx.x; i < k * D; i += blockDim.x) csh[i] = C[(i / D) * ld + (i % D)];
+  __syncthreads();
+  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n;
+       r += (long long)gridDim.x * blockDim.x) {
+    float x[D];
+#pragma unroll
+    for (int j = 0; j < D; j += 4) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(X + r * ld + j));
+      x[j] = v.x; x[j + 1] = v.y; x[j + 2] = v.z; x[j + 3] = v.w;
+    }
+    float best = FLT_MAX;
+    int bl = 0;
+    for (int c = 0; c < k; ++c) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < D; ++j) {
+        const float t = x[j] - csh[c * D + j];
+        acc = fmaf(t, t, acc);
+      }
+      if (acc < best) { best = acc; bl = c; }
+    }
+    __stcs(labels + r, bl);
+    if (mind) mind[r] = best;
+  }
+}
+
+bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
+                         long long n, const float* C, int k, int32_t* labels, float* mind) {
+  switch (d) {
+    case 4: assign_small_kernel<4><<<blocks, threads, smem, s>>>(X, ld, n, C, k, labels, mind); return true;
+    case 8: assign_small_kernel<8><<<blocks, threads, smem, s>>>(X, ld, n, C, k, labels, mind); return true;
+    case 16: assign_small_kernel<16><<<blocks, threads, smem, s>>>(X, ld, n, C, k, labels, mind); return true;
+    case 32: assign_small_kernel<32><<<blocks, threads, smem, s>>>(X, ld, n, C, k, labels, mind); return true;
+    default: return false;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// bulk fixed-point sums from the labels (S and counts must be zero on entry)
+// ---------------------------------------------------------------------------
+
+// Each warp walks rows; lanes cover 32 columns at a time. With `use_smem` the
+// block accumulates k x ld int64 in shared memory and flushes nonzero entries
+// with one global atomic each; otherwise it adds straight into global memory.
+// Integer addition is exact, so the result does not depend on the order.
+__global__ void bulk_sums_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                 const int32_t* __restrict__ labels, int k,
+                                 long long* __restrict__ S, long long* __restrict__ counts,
+                                 FitState* __restrict__ st, int use_smem) {
+  extern __shared__ long long ssum[];
+  if (st->done) return;
+  const double scale = st->scale;
+  long long* scnt = ssum + (size_t)k * ld;
+  if (use_smem) {
+    for (int i = threadIdx.x; i < k * ld + k; i += blockDim.x) ssum[i] = 0;
+    __syncthreads();
+  }
+  long long* Sd = use_smem ? ssum : S;
+  long long* Cd = use_smem ? scnt : counts;
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const long long gw = blockIdx.x * (long long)warps + (threadIdx.x >> 5);
+  const long long tw = (long long)gridDim.x * warps;
+  for (long long r = gw; r < n; r += tw) {
+    const int l = labels[r];
+    if (lane == 0) {
+      if (use_smem) atomicAdd(reinterpret_cast<unsigned long long*>(&Cd[l]), 1ull);
+      else red_add_s64(&Cd[l], 1);
+    }
+    for (int j = lane; j < d; j += 32) {
+      const long long v = to_fixed(X[r * ld + j], scale);
+      if (v != 0) red_add_s64(&Sd[(long long)l * ld + j], v);
+    }
+  }
+  if (use_smem) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < k * ld; i += blockDim.x)
+      if (ssum[i] != 0) red_add_s64(&S[i], ssum[i]);
+    for (int i = threadIdx.x; i < k; i += blockDim.x)
+      if (scnt[i] != 0) red_add_s64(&counts[i], scnt[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// M-step (cooperative): empty clusters, relocation, averaging, shift, flags
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned long long reloc_key(float dist, long long row) {
+  unsigned int b = __float_as_uint(dist);
+  if (b & 0x80000000u) b = 0;  // -0.0 and (impossible) negatives sort as zero
+  return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - (unsigned int)row);
+}
+
+// Selection of the m rows farthest from their assigned centre (largest
+// (distance, -row) keys) by an exact 8-pass radix select over 64-bit keys.
+// Keys are unique, so exactly m rows are collected. Runs inside the
+// cooperative M-step; `hist` holds 2 x 256 counters.
+__device__ bool select_farthest(const float* __restrict__ mind, long long n, long long row_base, int m,
+                                FitState* st, unsigned int* hist, long long* sel, unsigned int nblocks) {
+  __shared__ unsigned int h[256];
+  __shared__ unsigned long long prefix_s, mask_s;
+  __shared__ int remaining_s;
+  unsigned long long prefix = 0, mask = 0;
+  int remaining = m;
+  for (int pass = 0; pass < 8; ++pass) {
+    const int shift = 56 - 8 * pass;
+    unsigned int* gh = hist + (pass & 1) * 256;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)nblocks * blockDim.x) {
+      const unsigned long long key = reloc_key(mind[r], row_base + r);
+      if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 256; i += blockDim.x)
+      if (h[i]) atomicAdd(&gh[i], h[i]);
+    if (!grid_barrier(st, nblocks)) return false;
+    if (threadIdx.x == 0) {
+      // every block computes the same choice from the same global histogram
+      int cum = 0, digit = 0;
+      for (int dgt = 255; dgt >= 0; --dgt) {
+        const int c = (int)gh[dgt];
+        if (cum + c >= remaining) { digit = dgt; break; }
+        cum += c;
+      }
+      prefix_s = prefix | ((unsigned long long)digit << shift);
+      mask_s = mask | (255ull << shift);
+      remaining_s = remaining - cum;
+    }
+    __syncthreads();
+    prefix = prefix_s;
+    mask = mask_s;
+    remaining = remaining_s;
+    // clear the other histogram for the next pass (nobody reads it until the
+    // next barrier)
+    if (blockIdx.x == 0) {
+      unsigned int* oh = hist + ((pass + 1) & 1) * 256;
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) oh[i] = 0;
+    }
+    if (!grid_barrier(st, nblocks)) return false;
+  }
+  // prefix is now the m-th largest key: collect keys >= prefix (exactly m)
+  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)nblocks * blockDim.x) {
+    const unsigned long long key = reloc_key(mind[r], row_base + r);
+    if (key >= prefix) {
+      const int slot = atomicAdd(&st->sel_count, 1);
+      if (slot < m) sel[slot] = r;
+    }
+  }
+  return grid_barrier(st, nblocks);
+}
+
+// Averaged centre value of a non-empty cluster c (after relocation), column j.
+__device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, int n_reloc) {
+  for (int i = 0; i < n_reloc; ++i)
+    if (a.empty_ids[i] == c) return a.reloc_x[(long long)i * a.ld + j];  // exactly the far row
+  long long s = a.S[(long long)c * a.ld + j];
+  for (int i = 0; i < n_reloc; ++i)
+    if (a.reloc_label[i] == c) s -= to_fixed(a.reloc_x[(long long)i * a.ld + j], a.st->scale);
+  return (float)((double)s * a.st->inv_scale / (double)a.cnt_adj[c]);
+}
+
+__global__ void mstep_kernel(MStepArgs a) {
+  FitState* st = a.st;
+  if (st->done) return;  // uniform: `done` is only written after the last barrier
+  const unsigned long long changed_now = *a.changed;  // read before step 6 clears it
+  const unsigned int nb = gridDim.x;
+  __shared__ int n_empty_s;
+  __shared__ int wcount[32];
+  __shared__ double scratch[32];
+
+  // 1. empty clusters in ascending id order (every block; block 0 stores them)
+  if (threadIdx.x == 0) n_empty_s = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
+    const int c = c0 + threadIdx.x;
+    const bool e = c < a.k && a.counts[c] == 0;
+    const unsigned int b = __ballot_sync(0xffffffffu, e);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) wcount[warp] = __popc(b);
+    __syncthreads();
+    int base = n_empty_s;
+    for (int w = 0; w < warp; ++w) base += wcount[w];
+    const int pos = base + __popc(b & ((1u << lane) - 1u));
+    if (e && blockIdx.x == 0 && pos < kMaxEmptyCap) a.empty_ids[pos] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int t = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += wcount[w];
+      n_empty_s += t;
+    }
+    __syncthreads();
+  }
+  const int n_empty = n_empty_s;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st->n_empty = n_empty;
+    st->sel_count = 0;
+    if (n_empty > kMaxEmptyCap) atomicExch(&st->error, 1002);
+  }
+  if (n_empty > kMaxEmptyCap) return;  // uniform
+  if (!grid_barrier(st, nb)) return;
+
+  // 2. relocation: the n_empty rows farthest from their centre, paired in
+  //    decreasing (distance, -row) order with the ascending empty ids
+  int n_reloc = 0;
+  if (n_empty > 0) {
+    int m_cand = n_empty;
+    if (a.cand_row == nullptr) {
+      if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
+    } else {
+      m_cand = a.n_cand;
+      if (a.n_cand < n_empty) {  // exchanged candidates cannot cover this many empties
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&st->error, 1003);
+        return;
+      }
+    }
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i < m_cand; i += blockDim.x) {
+        float di;
+        long long gi;
+        if (a.cand_row) { di = a.cand_dist[i]; gi = a.cand_row[i]; }
+        else { di = a.mind[a.sel[i]]; gi = a.row_base + a.sel[i]; }
+        const unsigned long long ki = reloc_key(di, gi);
+        int rank = 0;
+        for (int j = 0; j < m_cand; ++j) {
+          float dj;
+          long long gj;
+          if (a.cand_row) { dj = a.cand_dist[j]; gj = a.cand_row[j]; }
+          else { dj = a.mind[a.sel[j]]; gj = a.row_base + a.sel[j]; }
+          if (reloc_key(dj, gj) > ki) ++rank;
+        }
+        if (rank < n_empty) {
+          a.reloc_dist[rank] = di;
+          if (a.cand_row) {
+            a.reloc_label[rank] = a.cand_label[i];
+            for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.cand_x[(long long)i * a.ld + j];
+          } else {
+            const long long r = a.sel[i];
+            a.reloc_label[rank] = a.labels[r];
+            for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[r * a.ld + j];
+          }
+        }
+      }
+    }
+    if (!grid_barrier(st, nb)) return;
+    // reference: no relocation when every distance is zero (_k_means_common.pyx:192-194)
+    n_reloc = a.reloc_dist[0] > 0.0f ? n_empty : 0;
+  }
+
+  // 3. counts after relocation (block 0), then the heaviest cluster (first max)
+  if (blockIdx.x == 0) {
+    for (int c = threadIdx.x; c < a.k; c += blockDim.x) a.cnt_adj[c] = a.counts[c];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < n_reloc; ++i) {
+        a.cnt_adj[a.reloc_label[i]] -= 1;
+        a.cnt_adj[a.empty_ids[i]] += 1;
+      }
+      st->relocated = n_reloc;
+    }
+  }
+  if (!grid_barrier(st, nb)) return;
+  __shared__ long long hv_cnt[32];
+  __shared__ int hv_idx[32];
+  long long bc = -1;
+  int bi = 0;
+  for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
+    const long long v = a.cnt_adj[c];
+    if (v > bc) { bc = v; bi = c; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long ov = __shfl_xor_sync(0xffffffffu, bc, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bc || (ov == bc && oi < bi)) { bc = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { hv_cnt[threadIdx.x >> 5] = bc; hv_idx[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (hv_cnt[w] > hv_cnt[0] || (hv_cnt[w] == hv_cnt[0] && hv_idx[w] < hv_idx[0])) {
+        hv_cnt[0] = hv_cnt[w];
+        hv_idx[0] = hv_idx[w];
+      }
+  }
+  __syncthreads();
+  const int heavy = hv_idx[0];
+
+  // 4. new centres and per-block partial sums of squared shifts
+  double shift_part = 0.0;
+  for (int c = blockIdx.x; c < a.k; c += nb) {
+    const int src = a.cnt_adj[c] > 0 ? c : heavy;
+    double dsq = 0.0;
+    for (int j = threadIdx.x; j < a.ld; j += blockDim.x) {
+      float v = 0.0f;
+      if (j < a.d) {
+        v = centre_value(a, src, j, n_reloc);
+        const double df = (double)v - (double)a.C_old[(long long)c * a.ld + j];
+        dsq += df * df;
+      }
+      a.C_new[(long long)c * a.ld + j] = v;
+    }
+    dsq = block_sum_f64(dsq, scratch);
+    if (threadIdx.x == 0) {
+      shift_part += dsq;
+      if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
+    }
+  }
+  if (threadIdx.x == 0) a.shift_partial[blockIdx.x] = shift_part;
+  if (!grid_barrier(st, nb)) return;
+
+  // 6. the next iteration recomputes its sums from zero (bulk mode)
+  if (a.zero_sums) {
+    // payload = S | counts | changed, contiguous
+    long long* P = const_cast<long long*>(a.S);
+    const long long len = (long long)a.k * a.ld + a.k + 1;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < len; i += (long long)nb * blockDim.x)
+      P[i] = 0;
+  }
+
+  // 5. convergence bookkeeping (_kmeans.py:723-741), fixed summation order
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    double tot = 0.0;
+    for (unsigned int b = 0; b < nb; ++b) tot += a.shift_partial[b];
+    st->shift_tot = tot;
+    st->iter += 1;
+    if (changed_now == 0) {
+      st->strict = 1;
+      st->done = 1;
+    } else if (tot <= st->tol) {
+      st->done = 1;
+    }
+    if (st->iter >= st->max_iter) st->done = 1;
+  }
+}
+
+__global__ void counts_to_float_kernel(const long long* __restrict__ c, int k, float* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) out[i] = (float)c[i];
+}
+
+// bias[c] = ||c||^2 (float64 sum, rounded) and the tf32 split of the centres
+// for the tensor-core E-step: Chi = C with the low 13 mantissa bits cleared,
+// Clo = C - Chi (exact in float32).
+__global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, int d, float* __restrict__ bias,
+                                   float* __restrict__ Chi, float* __restrict__ Clo, const FitState* st) {
+  if (st && st->done) return;
+  __shared__ double scratch[32];
+  for (int c = blockIdx.x; c < k; c += gridDim.x) {
+    double acc = 0.0;
+    for (int j = threadIdx.x; j < ld; j += blockDim.x) {
+      const float v = j < d ? C[(long long)c * ld + j] : 0.0f;
+      acc += (double)v * v;
+      const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+      if (Chi) Chi[(long long)c * ld + j] = hi;
+      if (Clo) Clo[(long long)c * ld + j] = v - hi;
+    }
+    acc = block_sum_f64(acc, scratch);
+    if (threadIdx.x == 0 && bias) bias[c] = (float)acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// outputs: inertia, per-row distance to the assigned centre, transform
+// ---------------------------------------------------------------------------
+
+// Per-block float64 partial of sum_r ||x_r - c_{l_r}||^2 over a fixed row range.
+__global__ void inertia_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                       const float* __restrict__ C, const int32_t* __restrict__ labels,
+                                       double* __restrict__ partial) {
+  __shared__ double scratch[32];
+  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
+  const long long r0 = blockIdx.x * rows_per;
+  const long long r1 = min(n, r0 + rows_per);
+  double acc = 0.0;
+  for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    const float* xr = X + r * ld;
+    const float* cr = C + (long long)labels[r] * ld;
+    double s = 0.0;
+    for (int j = 0; j < d; ++j) {
+      const double t = (double)xr[j] - (double)cr[j];
+      s += t * t;
+    }
+    acc += s;
+  }
+  acc = block_sum_f64(acc, scratch);
+  if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+__global__ void ordered_sum_kernel(const double* __restrict__ partial, int m, double* __restrict__ out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < m; ++i) t += partial[i];
+    *out = t;
+  }
+}
+
+__global__ void mindist_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                               const float* __restrict__ C, const int32_t* __restrict__ labels,
+                               float* __restrict__ out) {
+  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n;
+       r += (long long)gridDim.x * blockDim.x) {
+    const float* xr = X + r * ld;
+    const float* cr = C + (long long)labels[r] * ld;
+    float s = 0.0f;
+    for (int j = 0; j < d; ++j) {
+      const float t = xr[j] - cr[j];
+      s = fmaf(t, t, s);
+    }
+    out[r] = s;
+  }
+}
+
+// D[r][c] = sqrt(sum_j (x_rj - c_cj)^2), accumulated in float64
+__global__ void transform_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                 const float* __restrict__ C, int k, float* __restrict__ D) {
+  const long long total = n * (long long)k;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / k;
+    const int c = (int)(i % k);
+    const float* xr = X + r * ld;
+    const float* cr = C + (long long)c * ld;
+    double s = 0.0;
+    for (int j = 0; j < d; ++j) {
+      const double t = (double)xr[j] - (double)cr[j];
+      s += t * t;
+    }
+    D[i] = (float)sqrt(s);
+  }
+}
+
+__global__ void add_mean_kernel(const float* __restrict__ C, int k, int ld, int d, const float* __restrict__ mean,
+                                float* __restrict__ out) {
+  const int total = k * d;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c = i / d, j = i % d;
+    const float v = C[(long long)c * ld + j];
+    out[i] = mean ? v + mean[j] : v;
+  }
+}
+
+}  // namespace skm

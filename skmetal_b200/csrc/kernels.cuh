@@ -1,0 +1,74 @@
+// Kernel declarations shared by the host driver and the kernel files.
+#pragma once
+
+#include "skm.cuh"
+
+namespace skm {
+
+constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
+
+struct MStepArgs {
+  FitState* st;
+  const float* X;
+  int ld;
+  int d;
+  long long n;          // local rows
+  long long row_base;   // global index of local row 0
+  const int32_t* labels;
+  const float* mind;    // per-row distance to the assigned centre
+  const long long* S;   // k x ld fixed-point sums (global over ranks)
+  const long long* counts;
+  const unsigned long long* changed;  // rows whose label changed (global)
+  int k;
+  const float* C_old;
+  float* C_new;
+  int zero_sums;        // zero S and counts after use (next iteration is bulk)
+  // scratch
+  int* empty_ids;       // kMaxEmptyCap
+  unsigned int* hist;   // 512
+  long long* sel;       // kMaxEmptyCap
+  long long* cnt_adj;   // k
+  int* reloc_label;     // kMaxEmptyCap
+  float* reloc_dist;    // kMaxEmptyCap
+  float* reloc_x;       // min(k, kMaxEmptyCap) x ld
+  double* shift_partial;  // gridDim.x
+  float* shift_out;       // per-centre shift (nullable)
+  // exchanged relocation candidates (multi-GPU); null on one GPU
+  int n_cand;
+  const float* cand_dist;
+  const long long* cand_row;
+  const int* cand_label;
+  const float* cand_x;
+};
+
+__global__ void maxabs_kernel(const float* X, int ld, long long n, int d, unsigned int* out_bits);
+__global__ void colsum_fixed_kernel(const float* X, int ld, long long n, int d, const double* scale, long long* colsum);
+__global__ void mean_from_colsum_kernel(const long long* colsum, int d, const double* scale, double n_total, float* mean);
+__global__ void scale_kernel(const unsigned int* maxabs_bits, double n_total, double* out);
+__global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
+                                  double n_total, int d, const unsigned int* maxabs_bits);
+__global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits);
+__global__ void sumsq_partial_kernel(const float* X, int ld, long long n, int d, double* partial);
+__global__ void center_init_kernel(const float* init, int d, int k, const float* mean, float* C, int ld);
+__global__ void assign_simt_kernel(const float* X, int ld, long long n, int d, const float* C, int k,
+                                   int32_t* labels, float* mind, const FitState* st, unsigned long long* changed,
+                                   int skip_if_strict);
+__global__ void counts_to_float_kernel(const long long* c, int k, float* out);
+// Small-d assignment (d in {4, 8, 16, 32}, all centres in shared memory);
+// returns false when d has no specialisation.
+bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
+                         long long n, const float* C, int k, int32_t* labels, float* mind);
+__global__ void bulk_sums_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
+                                 long long* S, long long* counts, FitState* st, int use_smem);
+__global__ void mstep_kernel(MStepArgs a);
+__global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, float* Chi, float* Clo,
+                                   const FitState* st);
+__global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
+                                       const int32_t* labels, double* partial);
+__global__ void ordered_sum_kernel(const double* partial, int m, double* out);
+__global__ void mindist_kernel(const float* X, int ld, long long n, int d, const float* C, const int32_t* labels,
+                               float* out);
+__global__ void transform_kernel(const float* X, int ld, long long n, int d, const float* C, int k, float* D);
+__global__ void add_mean_kernel(const float* C, int k, int ld, int d, const float* mean, float* out);
+
+}  // namespace skm

@@ -1,0 +1,844 @@
+// KMeans fit / predict engine and the KMeans entry points of the C ABI.
+//
+// A fit runs entirely on the device and follows scikit-learn's
+// KMeans(algorithm="lloyd", n_init=1, init=array).fit
+// (sklearn/cluster/_kmeans.py:1436-1562, loop at :705-758):
+//   prep   : mean (exact fixed-point column sums), centring of X and of the
+//            init centres, fixed-point scale, scaled tolerance
+//   loop   : per iteration one E-step launch (labels, change count, sums),
+//            [all-reduce of the sums over ranks], one cooperative M-step launch
+//            (relocation, averaging, shift, convergence flags)
+//   final  : E-step again when the loop did not converge strictly, inertia,
+//            centres + mean.
+// The host enqueues iterations in chunks and only reads the `done` flag of the
+// previous chunk, so the GPU never waits for the host inside the loop.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "comm.h"
+#include "driver.h"
+#include "estep_tc.h"
+#include "kernels.cuh"
+#include "../../include/skmetal_cuda.h"
+
+namespace skm {
+
+struct FitStats {
+  double ms_total = 0, ms_prep = 0, ms_loop = 0, ms_final = 0;
+  int estep_launches = 0;
+  double estep_ms_sum = 0;
+  unsigned long long launches = 0;
+  int iterations = 0;
+};
+static thread_local FitStats t_stats;
+
+struct Dataset {
+  int device = 0;
+  float* X = nullptr;  // n x ld, raw (not centred)
+  long long n = 0;
+  int d = 0;
+  int ld = 0;
+};
+
+struct FitParams {
+  const float* X_host = nullptr;  // n x d host rows, or
+  const float* X_dev = nullptr;   // n x ld device rows (raw)
+  long long n = 0;
+  int d = 0;
+  int k = 0;
+  const float* init_host = nullptr;  // k x d
+  int max_iter = 300;
+  double tol = 0.0;
+  bool tol_abs = false;
+  bool center = true;
+  bool simt = false;
+  bool profile = false;
+  bool distributed = false;
+  long long row_base = 0;
+  long long n_total = 0;
+  // outputs (host, nullable)
+  float* centers_out = nullptr;
+  int32_t* labels_out = nullptr;
+  uint32_t* labels_out_u32 = nullptr;
+  double* inertia_out = nullptr;
+  int32_t* n_iter_out = nullptr;
+  // single Lloyd step (skmetal_kmeans_lloyd_iter)
+  bool single_step = false;
+  float* weight_out = nullptr;
+  float* shift_out = nullptr;
+};
+
+static int validate(long long n, long long d, long long k) {
+  if (n <= 0 || d <= 0 || k <= 0) {
+    set_error(ERR_INVALID, "invalid shape n=%lld d=%lld k=%lld", n, d, k);
+    return ERR_INVALID;
+  }
+  if (n >= (1LL << 31) || d > (1 << 20) || k > (1 << 20)) {
+    set_error(ERR_INVALID, "shape too large n=%lld d=%lld k=%lld", n, d, k);
+    return ERR_INVALID;
+  }
+  return OK;
+}
+
+static inline int ld_of(int d) { return (int)round_up((size_t)d, 4); }
+
+static int blocks_for(long long work, int threads, int cap_per_sm = 8) {
+  long long b = (work + threads - 1) / threads;
+  long long cap = (long long)sm_count() * cap_per_sm;
+  return (int)std::max(1LL, std::min(b, cap));
+}
+
+// ---------------------------------------------------------------------------
+// E-step dispatch: tensor-core kernel when the shape is supported, else SIMT
+// ---------------------------------------------------------------------------
+
+struct EStepPlan {
+  bool tc = false;
+  TcPlan tcp;
+};
+
+static int launch_assign_simt(const float* X, int ld, long long n, int d, const float* C, int k, int32_t* labels,
+                              float* mind, const FitState* st, unsigned long long* changed, int skip_if_strict,
+                              cudaStream_t s) {
+  const int chunk = std::max(1, std::min(k, kAssignSmemFloats / ld));
+  const size_t smem = sizeof(float) * (size_t)chunk * ld;
+  const int threads = 256;
+  const int blocks = (int)((n + threads - 1) / threads);
+  assign_simt_kernel<<<blocks, threads, smem, s>>>(X, ld, n, d, C, k, labels, mind, st, changed, skip_if_strict);
+  return check_launch("assign_simt_kernel");
+}
+
+static int launch_bulk_sums(const float* X, int ld, long long n, int d, const int32_t* labels, int k, long long* S,
+                            long long* counts, FitState* st, cudaStream_t s) {
+  const size_t need = sizeof(long long) * ((size_t)k * ld + k);
+  const bool smem = need <= 96 * 1024;
+  const int threads = 256;
+  int blocks = smem ? sm_count() : blocks_for(n * 32, threads, 4);
+  if (smem) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(bulk_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      attr_set = true;
+    }
+  }
+  bulk_sums_kernel<<<blocks, threads, smem ? need : 0, s>>>(X, ld, n, d, labels, k, S, counts, st, smem ? 1 : 0);
+  return check_launch("bulk_sums_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// the fit
+// ---------------------------------------------------------------------------
+
+static int run_fit(const FitParams& p) {
+  SKM_TRY(check_injected("fit"));
+  SKM_TRY(validate(p.n, p.d, p.k));
+  const long long n_total = p.distributed ? p.n_total : p.n;
+  if (!p.distributed && p.k > p.n) {
+    set_error(ERR_INVALID, "n_samples=%lld should be >= n_clusters=%d", p.n, p.k);
+    return ERR_INVALID;
+  }
+  if (n_total >= (1LL << 32) - 1) {
+    set_error(ERR_INVALID, "too many rows (%lld)", n_total);
+    return ERR_INVALID;
+  }
+  Comm* comm = nullptr;
+  if (p.distributed) {
+    comm = comm_get();
+    if (!comm) {
+      set_error(ERR_INVALID, "distributed fit without a communicator (call skmetal_comm_init)");
+      return ERR_INVALID;
+    }
+  }
+  cudaStream_t s;
+  double* pinned;
+  SKM_TRY(thread_stream(&s, &pinned));
+  const unsigned long long launches0 = g_launches.load();
+  const long long n = p.n;
+  const int d = p.d, k = p.k, ld = ld_of(d);
+  const int nsm = sm_count();
+
+  cudaEvent_t ev0, ev1, ev2, ev3;
+  SKM_CUDA(cudaEventCreate(&ev0));
+  SKM_CUDA(cudaEventCreate(&ev1));
+  SKM_CUDA(cudaEventCreate(&ev2));
+  SKM_CUDA(cudaEventCreate(&ev3));
+  struct EvGuard {
+    cudaEvent_t e[4];
+    ~EvGuard() {
+      for (auto x : e) cudaEventDestroy(x);
+    }
+  } evg{{ev0, ev1, ev2, ev3}};
+
+  DevBuffers buf(s);
+  float *X = nullptr, *Cb0 = nullptr, *Cb1 = nullptr, *mean = nullptr, *mind = nullptr, *init_d = nullptr;
+  int32_t* labels = nullptr;
+  long long *S = nullptr, *colsum = nullptr;
+  FitState* st = nullptr;
+  unsigned int* u32s = nullptr;  // [0] raw maxabs, [1] centred maxabs, [2..513] hist
+  double* dscr = nullptr;        // scale(1) sumsq(1) partials(...)
+  int* empty_ids = nullptr;
+  long long *sel = nullptr, *cnt_adj = nullptr;
+  int* reloc_label = nullptr;
+  float *reloc_dist = nullptr, *reloc_x = nullptr;
+  const int n_part = nsm * 4;
+  const int reloc_rows = std::min(k, kMaxEmptyCap);
+
+  SKM_TRY(buf.alloc_n(&X, (size_t)n * ld));
+  SKM_TRY(buf.alloc_n(&Cb0, (size_t)k * ld));
+  SKM_TRY(buf.alloc_n(&Cb1, (size_t)k * ld));
+  SKM_TRY(buf.alloc_n(&mean, (size_t)ld));
+  SKM_TRY(buf.alloc_n(&mind, (size_t)n));
+  SKM_TRY(buf.alloc_n(&init_d, (size_t)k * d));
+  SKM_TRY(buf.alloc_n(&labels, (size_t)n));
+  // payload: S (k*ld) | counts (k) | changed (1)
+  const size_t payload_len = (size_t)k * ld + k + 1;
+  SKM_TRY(buf.alloc_n(&S, payload_len));
+  long long* counts = S + (size_t)k * ld;
+  unsigned long long* changed = reinterpret_cast<unsigned long long*>(counts + k);
+  SKM_TRY(buf.alloc_n(&colsum, (size_t)ld));
+  SKM_TRY(buf.alloc_n(&st, 1));
+  SKM_TRY(buf.alloc_n(&u32s, 2 + 512));
+  SKM_TRY(buf.alloc_n(&dscr, 2 + n_part + nsm));
+  SKM_TRY(buf.alloc_n(&empty_ids, kMaxEmptyCap));
+  SKM_TRY(buf.alloc_n(&sel, kMaxEmptyCap));
+  SKM_TRY(buf.alloc_n(&cnt_adj, (size_t)k));
+  SKM_TRY(buf.alloc_n(&reloc_label, kMaxEmptyCap));
+  SKM_TRY(buf.alloc_n(&reloc_dist, kMaxEmptyCap));
+  SKM_TRY(buf.alloc_n(&reloc_x, (size_t)reloc_rows * ld));
+  double* scale_mean = dscr;
+  double* sumsq = dscr + 1;
+  double* partials = dscr + 2;
+  double* shift_partial = dscr + 2 + n_part;
+
+  SKM_CUDA(cudaEventRecord(ev0, s));
+  // ---- data in ------------------------------------------------------------
+  if (p.X_host) {
+    SKM_TRY(upload_rows(X, ld, p.X_host, n, d, s));
+  } else {
+    SKM_CUDA(cudaMemcpyAsync(X, p.X_dev, sizeof(float) * (size_t)n * ld, cudaMemcpyDeviceToDevice, s));
+  }
+  SKM_CUDA(cudaMemcpyAsync(init_d, p.init_host, sizeof(float) * (size_t)k * d, cudaMemcpyHostToDevice, s));
+  SKM_CUDA(cudaMemsetAsync(u32s, 0, sizeof(unsigned int) * (2 + 512), s));
+  SKM_CUDA(cudaMemsetAsync(colsum, 0, sizeof(long long) * ld, s));
+
+  // ---- centring (exact mean) ----------------------------------------------
+  const int ew_blocks = blocks_for(n * ld, 256, 8);
+  if (p.center) {
+    maxabs_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, &u32s[0]);
+    SKM_TRY(check_launch("maxabs_kernel"));
+    if (comm) SKM_TRY(comm_allreduce_max_u32(comm, &u32s[0], 1, s));
+    scale_kernel<<<1, 32, 0, s>>>(&u32s[0], (double)n_total, scale_mean);
+    SKM_TRY(check_launch("scale_kernel"));
+    colsum_fixed_kernel<<<nsm, std::min(1024, (int)round_up(d, 32)), 0, s>>>(X, ld, n, d, scale_mean, colsum);
+    SKM_TRY(check_launch("colsum_fixed_kernel"));
+    if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, colsum, ld, s));
+    mean_from_colsum_kernel<<<1, 256, 0, s>>>(colsum, d, scale_mean, (double)n_total, mean);
+    SKM_TRY(check_launch("mean_from_colsum_kernel"));
+    center_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, mean, &u32s[1]);
+    SKM_TRY(check_launch("center_kernel"));
+  } else {
+    maxabs_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, &u32s[1]);
+    SKM_TRY(check_launch("maxabs_kernel"));
+  }
+  if (comm) SKM_TRY(comm_allreduce_max_u32(comm, &u32s[1], 1, s));
+  center_init_kernel<<<std::max(1, std::min(1024, (k * ld + 255) / 256)), 256, 0, s>>>(
+      init_d, d, k, p.center ? mean : nullptr, Cb0, ld);
+  SKM_TRY(check_launch("center_init_kernel"));
+  const bool tol_rel = !p.tol_abs && p.tol != 0.0;
+  if (tol_rel) {
+    sumsq_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, partials);
+    SKM_TRY(check_launch("sumsq_partial_kernel"));
+    ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, sumsq);
+    SKM_TRY(check_launch("ordered_sum_kernel"));
+    if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, sumsq, 1, s));
+  }
+  init_state_kernel<<<1, 32, 0, s>>>(st, p.max_iter, p.tol, tol_rel ? 1 : 0, tol_rel ? sumsq : nullptr,
+                                     (double)n_total, d, &u32s[1]);
+  SKM_TRY(check_launch("init_state_kernel"));
+  SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n, s));  // label -1: every row changes in iteration 1
+  SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * payload_len, s));
+
+  // ---- E-step plan ---------------------------------------------------------
+  EStepPlan plan;
+  if (!p.simt) {
+    int rc = tc_plan(X, ld, n, d, k, &plan.tcp);
+    plan.tc = (rc == OK) && plan.tcp.supported;
+  }
+  float *bias = nullptr, *chi = nullptr, *clo = nullptr;
+  if (plan.tc) {
+    SKM_TRY(buf.alloc_n(&bias, (size_t)plan.tcp.k_pad));
+    SKM_TRY(buf.alloc_n(&chi, (size_t)k * ld));
+    SKM_TRY(buf.alloc_n(&clo, (size_t)k * ld));
+  }
+  int* dev_err = &st->error;
+  SKM_CUDA(cudaEventRecord(ev1, s));
+
+  // ---- Lloyd loop -----------------------------------------------------------
+  MStepArgs ma{};
+  ma.st = st;
+  ma.X = X;
+  ma.ld = ld;
+  ma.d = d;
+  ma.n = n;
+  ma.row_base = p.row_base;
+  ma.labels = labels;
+  ma.mind = mind;
+  ma.S = S;
+  ma.counts = counts;
+  ma.changed = changed;
+  float* shift_dev = nullptr;
+  if (p.single_step) {
+    SKM_TRY(buf.alloc_n(&shift_dev, (size_t)k));
+    ma.shift_out = shift_dev;
+  }
+  ma.k = k;
+  ma.zero_sums = 1;
+  ma.empty_ids = empty_ids;
+  ma.hist = &u32s[2];
+  ma.sel = sel;
+  ma.cnt_adj = cnt_adj;
+  ma.reloc_label = reloc_label;
+  ma.reloc_dist = reloc_dist;
+  ma.reloc_x = reloc_x;
+  ma.shift_partial = shift_partial;
+  const int mstep_blocks = nsm;
+  const int mstep_threads = 512;
+
+  std::vector<cudaEvent_t> prof_ev;
+  if (p.profile) {
+    prof_ev.resize(2 * (size_t)p.max_iter);
+    for (auto& e : prof_ev) SKM_CUDA(cudaEventCreate(&e));
+  }
+  struct ProfGuard {
+    std::vector<cudaEvent_t>* v;
+    ~ProfGuard() {
+      for (auto e : *v) cudaEventDestroy(e);
+    }
+  } pg{&prof_ev};
+
+  int32_t* flags = reinterpret_cast<int32_t*>(pinned);  // done snapshot per chunk (slots 0..63)
+  const int chunk = 8;
+  int it = 0, chunk_idx = 0, pending = -1;
+  bool done_seen = false;
+  cudaEvent_t chunk_ev[2];
+  SKM_CUDA(cudaEventCreateWithFlags(&chunk_ev[0], cudaEventDisableTiming));
+  SKM_CUDA(cudaEventCreateWithFlags(&chunk_ev[1], cudaEventDisableTiming));
+  struct ChunkGuard {
+    cudaEvent_t* e;
+    ~ChunkGuard() {
+      cudaEventDestroy(e[0]);
+      cudaEventDestroy(e[1]);
+    }
+  } cg{chunk_ev};
+
+  auto wait_event = [&](cudaEvent_t e) -> int {
+    if (!comm) {
+      SKM_CUDA(cudaEventSynchronize(e));
+      return OK;
+    }
+    return comm_wait_event(comm, e);
+  };
+
+  while (it < p.max_iter && !done_seen) {
+    const int end = std::min(p.max_iter, it + chunk);
+    for (; it < end; ++it) {
+      const float* Cin = (it & 1) ? Cb1 : Cb0;
+      float* Cout = (it & 1) ? Cb0 : Cb1;
+      if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
+      if (plan.tc) {
+        centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cin, k, ld, d, bias, chi, clo, st);
+        SKM_TRY(check_launch("centre_prep_kernel"));
+        SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, changed, st, dev_err, s));
+      } else {
+        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, mind, st, changed, 0, s));
+      }
+      if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
+      SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, S, counts, st, s));
+      if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, S, payload_len, s));
+      ma.C_old = Cin;
+      ma.C_new = Cout;
+      void* args[] = {&ma};
+      SKM_CUDA(cudaLaunchCooperativeKernel((void*)mstep_kernel, dim3(mstep_blocks), dim3(mstep_threads), args, 0, s));
+      SKM_TRY(check_launch("mstep_kernel"));
+    }
+    const int slot = chunk_idx & 63;
+    SKM_CUDA(cudaMemcpyAsync(&flags[slot], &st->done, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    SKM_CUDA(cudaEventRecord(chunk_ev[chunk_idx & 1], s));
+    if (pending >= 0) {
+      SKM_TRY(wait_event(chunk_ev[pending & 1]));
+      if (flags[pending & 63]) done_seen = true;
+    }
+    pending = chunk_idx++;
+  }
+  if (pending >= 0) SKM_TRY(wait_event(chunk_ev[pending & 1]));
+  SKM_CUDA(cudaEventRecord(ev2, s));
+
+  FitState hs;
+  SKM_CUDA(cudaMemcpyAsync(&hs, st, sizeof(FitState), cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  if (hs.error) {
+    set_error(ERR_DEVICE, "device-side check failed in the Lloyd loop (code %d)", hs.error);
+    return ERR_DEVICE;
+  }
+  if ((hs.maxabs_bits & 0x7fffffffu) >= 0x7f800000u) {
+    set_error(ERR_INVALID, "X contains NaN or infinity");
+    return ERR_INVALID;
+  }
+  const int iters = hs.iter;
+  float* Cfin = (iters & 1) ? Cb1 : Cb0;
+
+  if (p.single_step) {
+    // outputs of one lloyd_iter: E-step labels, M-step centres, weights after
+    // relocation, per-centre shifts
+    float* wf = reinterpret_cast<float*>(sel);  // k floats fit in the selection scratch when k <= cap
+    float* wbuf = nullptr;
+    if (k > kMaxEmptyCap * 2) SKM_TRY(buf.alloc_n(&wbuf, (size_t)k));
+    if (wbuf) wf = wbuf;
+    counts_to_float_kernel<<<std::max(1, std::min(1024, (k + 255) / 256)), 256, 0, s>>>(cnt_adj, k, wf);
+    SKM_TRY(check_launch("counts_to_float_kernel"));
+    add_mean_kernel<<<std::max(1, std::min(1024, (k * d + 255) / 256)), 256, 0, s>>>(Cfin, k, ld, d, nullptr,
+                                                                                    init_d);
+    SKM_TRY(check_launch("add_mean_kernel"));
+    if (p.centers_out)
+      SKM_CUDA(cudaMemcpyAsync(p.centers_out, init_d, sizeof(float) * (size_t)k * d, cudaMemcpyDeviceToHost, s));
+    if (p.labels_out)
+      SKM_CUDA(cudaMemcpyAsync(p.labels_out, labels, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
+    if (p.weight_out) SKM_CUDA(cudaMemcpyAsync(p.weight_out, wf, sizeof(float) * k, cudaMemcpyDeviceToHost, s));
+    if (p.shift_out)
+      SKM_CUDA(cudaMemcpyAsync(p.shift_out, shift_dev, sizeof(float) * k, cudaMemcpyDeviceToHost, s));
+    SKM_CUDA(cudaStreamSynchronize(s));
+    return OK;
+  }
+
+  // ---- final E-step, inertia, outputs ----------------------------------------
+  if (!hs.strict) {
+    if (plan.tc) {
+      centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cfin, k, ld, d, bias, chi, clo, nullptr);
+      SKM_TRY(check_launch("centre_prep_kernel"));
+      SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, nullptr, nullptr, dev_err, s));
+    } else {
+      SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, 0, s));
+    }
+  }
+  inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials);
+  SKM_TRY(check_launch("inertia_partial_kernel"));
+  ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, &dscr[1]);
+  SKM_TRY(check_launch("ordered_sum_kernel"));
+  if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, &dscr[1], 1, s));
+  float* cout_d = init_d;  // reuse: k x d
+  add_mean_kernel<<<std::max(1, std::min(1024, (k * d + 255) / 256)), 256, 0, s>>>(Cfin, k, ld, d,
+                                                                                  p.center ? mean : nullptr, cout_d);
+  SKM_TRY(check_launch("add_mean_kernel"));
+  SKM_CUDA(cudaEventRecord(ev3, s));
+  double inertia = 0.0;
+  SKM_CUDA(cudaMemcpyAsync(&inertia, &dscr[1], sizeof(double), cudaMemcpyDeviceToHost, s));
+  if (p.centers_out)
+    SKM_CUDA(cudaMemcpyAsync(p.centers_out, cout_d, sizeof(float) * (size_t)k * d, cudaMemcpyDeviceToHost, s));
+  if (p.labels_out)
+    SKM_CUDA(cudaMemcpyAsync(p.labels_out, labels, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
+  if (p.labels_out_u32)
+    SKM_CUDA(cudaMemcpyAsync(p.labels_out_u32, labels, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  if (p.inertia_out) *p.inertia_out = inertia;
+  if (p.n_iter_out) *p.n_iter_out = iters;
+
+  FitStats fs;
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0, ev3);
+  fs.ms_total = ms;
+  cudaEventElapsedTime(&ms, ev0, ev1);
+  fs.ms_prep = ms;
+  cudaEventElapsedTime(&ms, ev1, ev2);
+  fs.ms_loop = ms;
+  cudaEventElapsedTime(&ms, ev2, ev3);
+  fs.ms_final = ms;
+  if (p.profile) {
+    for (int i = 0; i < iters; ++i) {
+      float m = 0;
+      if (cudaEventElapsedTime(&m, prof_ev[2 * i], prof_ev[2 * i + 1]) == cudaSuccess) {
+        fs.estep_ms_sum += m;
+        fs.estep_launches += 1;
+      }
+    }
+  }
+  fs.launches = g_launches.load() - launches0;
+  fs.iterations = iters;
+  t_stats = fs;
+  return OK;
+}
+
+// ---------------------------------------------------------------------------
+// predict-style helpers (no centring)
+// ---------------------------------------------------------------------------
+
+static int launch_assign_any(const float* X, int ld, long long n, int d, const float* C, int k, int32_t* labels,
+                             float* mind, cudaStream_t s) {
+  const bool small = k * std::max(d, 4) <= 12288 && ld == d && (d == 4 || d == 8 || d == 16 || d == 32);
+  if (small) {
+    const int threads = 256;
+    const int blocks = blocks_for(n, threads, 16);
+    const size_t smem = sizeof(float) * (size_t)k * d;
+    launch_assign_small(d, blocks, threads, smem, s, X, ld, n, C, k, labels, mind);
+    return check_launch("assign_small_kernel");
+  }
+  return launch_assign_simt(X, ld, n, d, C, k, labels, mind, nullptr, nullptr, 0, s);
+}
+
+struct Staged {
+  float* X = nullptr;
+  float* C = nullptr;
+  int32_t* labels = nullptr;
+  int ld = 0;
+};
+
+static int stage_xc(DevBuffers& buf, const float* X, const float* C, long long n, int d, int k, bool want_labels,
+                    const uint32_t* labels_in, Staged* out, cudaStream_t s) {
+  out->ld = ld_of(d);
+  SKM_TRY(buf.alloc_n(&out->X, (size_t)n * out->ld));
+  SKM_TRY(buf.alloc_n(&out->C, (size_t)k * out->ld));
+  SKM_TRY(upload_rows(out->X, out->ld, X, n, d, s));
+  SKM_TRY(upload_rows(out->C, out->ld, C, k, d, s));
+  if (want_labels || labels_in) {
+    SKM_TRY(buf.alloc_n(&out->labels, (size_t)n));
+    if (labels_in)
+      SKM_CUDA(cudaMemcpyAsync(out->labels, labels_in, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s));
+  }
+  return OK;
+}
+
+}  // namespace skm
+
+using namespace skm;
+
+extern "C" {
+
+int skmetal_kmeans_assign(const float* X, const float* centroids, uint32_t* labels, size_t n, size_t d, size_t k) {
+  SKM_TRY(check_injected("kmeans_assign"));
+  SKM_TRY(validate((long long)n, (long long)d, (long long)k));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  DevBuffers buf(s);
+  Staged g;
+  SKM_TRY(stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, true, nullptr, &g, s));
+  SKM_TRY(launch_assign_any(g.X, g.ld, (long long)n, (int)d, g.C, (int)k, g.labels, nullptr, s));
+  SKM_CUDA(cudaMemcpyAsync(labels, g.labels, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  return OK;
+}
+
+int skmetal_compute_mindists(const float* X, const float* centroids, const uint32_t* labels, float* dists, size_t n,
+                             size_t d, size_t k) {
+  SKM_TRY(check_injected("compute_mindists"));
+  SKM_TRY(validate((long long)n, (long long)d, (long long)k));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  DevBuffers buf(s);
+  Staged g;
+  SKM_TRY(stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, false, labels, &g, s));
+  float* out = nullptr;
+  SKM_TRY(buf.alloc_n(&out, n));
+  mindist_kernel<<<blocks_for((long long)n, 256), 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, out);
+  SKM_TRY(check_launch("mindist_kernel"));
+  SKM_CUDA(cudaMemcpyAsync(dists, out, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  return OK;
+}
+
+float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint32_t* labels, size_t n, size_t d,
+                             size_t k) {
+  if (check_injected("kmeans_inertia")) return -1.0f;
+  if (validate((long long)n, (long long)d, (long long)k)) return -1.0f;
+  cudaStream_t s;
+  if (thread_stream(&s, nullptr)) return -1.0f;
+  DevBuffers buf(s);
+  Staged g;
+  if (stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, false, labels, &g, s)) return -1.0f;
+  const int n_part = sm_count() * 4;
+  double* part = nullptr;
+  if (buf.alloc_n(&part, (size_t)n_part + 1)) return -1.0f;
+  inertia_partial_kernel<<<n_part, 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, part);
+  if (check_launch("inertia_partial_kernel")) return -1.0f;
+  ordered_sum_kernel<<<1, 32, 0, s>>>(part, n_part, part + n_part);
+  if (check_launch("ordered_sum_kernel")) return -1.0f;
+  double v = 0;
+  if (cudaMemcpyAsync(&v, part + n_part, sizeof(double), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
+  if (cudaStreamSynchronize(s) != cudaSuccess) {
+    set_error(ERR_CUDA, "kmeans_inertia: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1.0f;
+  }
+  return (float)v;
+}
+
+int skmetal_row_norm_sq(const float* X, float* norms, size_t n, size_t d) {
+  SKM_TRY(check_injected("row_norm_sq"));
+  SKM_TRY(validate((long long)n, (long long)d, 1));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  DevBuffers buf(s);
+  const int ld = ld_of((int)d);
+  float *Xd = nullptr, *zero = nullptr, *out = nullptr;
+  int32_t* lab = nullptr;
+  SKM_TRY(buf.alloc_n(&Xd, n * ld));
+  SKM_TRY(buf.alloc_n(&zero, (size_t)ld));
+  SKM_TRY(buf.alloc_n(&out, n));
+  SKM_TRY(buf.alloc_n(&lab, n));
+  SKM_TRY(upload_rows(Xd, ld, X, (long long)n, (int)d, s));
+  SKM_CUDA(cudaMemsetAsync(zero, 0, sizeof(float) * ld, s));
+  SKM_CUDA(cudaMemsetAsync(lab, 0, sizeof(int32_t) * n, s));
+  mindist_kernel<<<blocks_for((long long)n, 256), 256, 0, s>>>(Xd, ld, (long long)n, (int)d, zero, lab, out);
+  SKM_TRY(check_launch("mindist_kernel"));
+  SKM_CUDA(cudaMemcpyAsync(norms, out, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  return OK;
+}
+
+int skmetal_kmeans_transform(const float* X, const float* centroids, float* D, size_t n, size_t d, size_t k) {
+  SKM_TRY(check_injected("kmeans_transform"));
+  SKM_TRY(validate((long long)n, (long long)d, (long long)k));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  DevBuffers buf(s);
+  Staged g;
+  SKM_TRY(stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, false, nullptr, &g, s));
+  float* out = nullptr;
+  SKM_TRY(buf.alloc_n(&out, n * k));
+  transform_kernel<<<blocks_for((long long)n * k, 256), 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, (int)k,
+                                                                   out);
+  SKM_TRY(check_launch("transform_kernel"));
+  SKM_CUDA(cudaMemcpyAsync(D, out, sizeof(float) * n * k, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  return OK;
+}
+
+int skmetal_kmeans_batch_fused(const float* X, float* centroids, uint32_t* labels, size_t n, size_t d, size_t k,
+                               size_t num_groups, size_t max_iter, float tol, int32_t* n_iter_out) {
+  (void)num_groups;
+  FitParams p;
+  p.X_host = X;
+  p.n = (long long)n;
+  p.d = (int)d;
+  p.k = (int)k;
+  p.init_host = centroids;
+  p.max_iter = (int)std::min<size_t>(max_iter, 1 << 30);
+  p.tol = tol;
+  p.tol_abs = true;
+  p.center = false;
+  p.centers_out = centroids;
+  p.labels_out_u32 = labels;
+  p.n_iter_out = n_iter_out;
+  return run_fit(p);
+}
+
+int skmetal_kmeans_fit(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter, double tol,
+                       uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
+                       int32_t* n_iter_out) {
+  if (flags & SKMETAL_FIT_DISTRIBUTED) {
+    set_error(ERR_INVALID, "use skmetal_kmeans_fit_shard for distributed fits");
+    return ERR_INVALID;
+  }
+  FitParams p;
+  p.X_host = X;
+  p.n = (long long)n;
+  p.d = (int)d;
+  p.k = (int)k;
+  p.init_host = init;
+  p.max_iter = max_iter;
+  p.tol = tol;
+  p.tol_abs = (flags & SKMETAL_FIT_TOL_ABS) != 0;
+  p.center = (flags & SKMETAL_FIT_CENTER) != 0;
+  p.simt = (flags & SKMETAL_FIT_SIMT) != 0;
+  p.profile = (flags & SKMETAL_FIT_PROFILE) != 0;
+  p.centers_out = centers_out;
+  p.labels_out = labels_out;
+  p.inertia_out = inertia_out;
+  p.n_iter_out = n_iter_out;
+  return run_fit(p);
+}
+
+int skmetal_kmeans_fit_shard(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter,
+                             double tol, uint32_t flags, uint64_t row_base, uint64_t n_total, float* centers_out,
+                             int32_t* labels_out, double* inertia_out, int32_t* n_iter_out) {
+  FitParams p;
+  p.X_host = X;
+  p.n = (long long)n;
+  p.d = (int)d;
+  p.k = (int)k;
+  p.init_host = init;
+  p.max_iter = max_iter;
+  p.tol = tol;
+  p.tol_abs = (flags & SKMETAL_FIT_TOL_ABS) != 0;
+  p.center = (flags & SKMETAL_FIT_CENTER) != 0;
+  p.simt = (flags & SKMETAL_FIT_SIMT) != 0;
+  p.profile = (flags & SKMETAL_FIT_PROFILE) != 0;
+  p.distributed = true;
+  p.row_base = (long long)row_base;
+  p.n_total = (long long)n_total;
+  p.centers_out = centers_out;
+  p.labels_out = labels_out;
+  p.inertia_out = inertia_out;
+  p.n_iter_out = n_iter_out;
+  return run_fit(p);
+}
+
+int skmetal_kmeans_lloyd_iter(const float* X, const float* centers_old, float* centers_new, int32_t* labels_out,
+                              float* weight_out, float* center_shift_out, size_t n, size_t d, size_t k) {
+  SKM_TRY(check_injected("lloyd_iter"));
+  SKM_TRY(validate((long long)n, (long long)d, (long long)k));
+  // one Lloyd iteration = the fit engine with max_iter = 1, no centring, whose
+  // M-step results are read back instead of running the final E-step
+  FitParams p;
+  p.X_host = X;
+  p.n = (long long)n;
+  p.d = (int)d;
+  p.k = (int)k;
+  p.init_host = centers_old;
+  p.max_iter = 1;
+  p.tol = 0.0;
+  p.tol_abs = true;
+  p.center = false;
+  p.single_step = true;
+  p.centers_out = centers_new;
+  p.labels_out = labels_out;
+  p.weight_out = weight_out;
+  p.shift_out = center_shift_out;
+  return run_fit(p);
+}
+
+int skmetal_dataset_create(const float* X, size_t n, size_t d, void** handle) {
+  SKM_TRY(check_injected("dataset_create"));
+  SKM_TRY(validate((long long)n, (long long)d, 1));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  Dataset* ds = new Dataset();
+  ds->n = (long long)n;
+  ds->d = (int)d;
+  ds->ld = ld_of((int)d);
+  current_device(&ds->device);
+  cudaError_t e = cudaMalloc(&ds->X, sizeof(float) * n * ds->ld);
+  if (e != cudaSuccess) {
+    delete ds;
+    set_error(e == cudaErrorMemoryAllocation ? ERR_OOM : ERR_CUDA, "dataset allocation: %s", cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? ERR_OOM : ERR_CUDA;
+  }
+  int rc = upload_rows(ds->X, ds->ld, X, (long long)n, (int)d, s);
+  if (rc == OK && cudaStreamSynchronize(s) != cudaSuccess) rc = ERR_CUDA;
+  if (rc != OK) {
+    cudaFree(ds->X);
+    delete ds;
+    return rc;
+  }
+  *handle = ds;
+  return OK;
+}
+
+int skmetal_dataset_free(void* handle) {
+  Dataset* ds = static_cast<Dataset*>(handle);
+  if (!ds) return OK;
+  cudaFree(ds->X);
+  delete ds;
+  return OK;
+}
+
+static int fit_dataset_common(void* handle, const float* init, size_t k, int32_t max_iter, double tol, uint32_t flags,
+                              bool distributed, uint64_t row_base, uint64_t n_total, float* centers_out,
+                              int32_t* labels_out, double* inertia_out, int32_t* n_iter_out) {
+  Dataset* ds = static_cast<Dataset*>(handle);
+  if (!ds) {
+    set_error(ERR_INVALID, "null dataset handle");
+    return ERR_INVALID;
+  }
+  FitParams p;
+  p.X_dev = ds->X;
+  p.n = ds->n;
+  p.d = ds->d;
+  p.k = (int)k;
+  p.init_host = init;
+  p.max_iter = max_iter;
+  p.tol = tol;
+  p.tol_abs = (flags & SKMETAL_FIT_TOL_ABS) != 0;
+  p.center = (flags & SKMETAL_FIT_CENTER) != 0;
+  p.simt = (flags & SKMETAL_FIT_SIMT) != 0;
+  p.profile = (flags & SKMETAL_FIT_PROFILE) != 0;
+  p.distributed = distributed;
+  p.row_base = (long long)row_base;
+  p.n_total = (long long)n_total;
+  p.centers_out = centers_out;
+  p.labels_out = labels_out;
+  p.inertia_out = inertia_out;
+  p.n_iter_out = n_iter_out;
+  return run_fit(p);
+}
+
+int skmetal_kmeans_fit_dataset(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
+                               uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
+                               int32_t* n_iter_out) {
+  return fit_dataset_common(handle, init, k, max_iter, tol, flags, false, 0, 0, centers_out, labels_out, inertia_out,
+                            n_iter_out);
+}
+
+int skmetal_dataset_fit_shard(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
+                              uint32_t flags, uint64_t row_base, uint64_t n_total, float* centers_out,
+                              int32_t* labels_out, double* inertia_out, int32_t* n_iter_out) {
+  return fit_dataset_common(handle, init, k, max_iter, tol, flags, true, row_base, n_total, centers_out, labels_out,
+                            inertia_out, n_iter_out);
+}
+
+int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t k, int32_t* labels_out) {
+  SKM_TRY(check_injected("predict_dataset"));
+  Dataset* ds = static_cast<Dataset*>(handle);
+  if (!ds) {
+    set_error(ERR_INVALID, "null dataset handle");
+    return ERR_INVALID;
+  }
+  SKM_TRY(validate(ds->n, ds->d, (long long)k));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  const unsigned long long l0 = g_launches.load();
+  cudaEvent_t e0, e1;
+  SKM_CUDA(cudaEventCreate(&e0));
+  SKM_CUDA(cudaEventCreate(&e1));
+  DevBuffers buf(s);
+  float* C = nullptr;
+  int32_t* lab = nullptr;
+  SKM_TRY(buf.alloc_n(&C, k * ds->ld));
+  SKM_TRY(buf.alloc_n(&lab, (size_t)ds->n));
+  SKM_TRY(upload_rows(C, ds->ld, centroids, (long long)k, ds->d, s));
+  SKM_CUDA(cudaEventRecord(e0, s));
+  SKM_TRY(launch_assign_any(ds->X, ds->ld, ds->n, ds->d, C, (int)k, lab, nullptr, s));
+  SKM_CUDA(cudaEventRecord(e1, s));
+  if (labels_out) SKM_CUDA(cudaMemcpyAsync(labels_out, lab, sizeof(int32_t) * ds->n, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  FitStats fs;
+  float ms = 0;
+  cudaEventElapsedTime(&ms, e0, e1);
+  fs.ms_total = fs.ms_loop = ms;
+  fs.estep_launches = 1;
+  fs.estep_ms_sum = ms;
+  fs.launches = g_launches.load() - l0;
+  t_stats = fs;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return OK;
+}
+
+int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,
+                           int32_t* estep_launches, double* estep_ms_sum, uint64_t* launches, int32_t* iterations) {
+  const FitStats& f = t_stats;
+  if (ms_total) *ms_total = f.ms_total;
+  if (ms_prep) *ms_prep = f.ms_prep;
+  if (ms_loop) *ms_loop = f.ms_loop;
+  if (ms_final) *ms_final = f.ms_final;
+  if (estep_launches) *estep_launches = f.estep_launches;
+  if (estep_ms_sum) *estep_ms_sum = f.estep_ms_sum;
+  if (launches) *launches = f.launches;
+  if (iterations) *iterations = f.iterations;
+  return OK;
+}
+
+}  // extern "C"

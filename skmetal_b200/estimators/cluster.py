@@ -1,0 +1,183 @@
+"""GPU KMeans (the estimator the Lloyd hot path lives behind).
+
+Replaces ``MetalKMeans`` of the reference (``skmetal/estimators/cluster.py:18-146``)
+with scikit-learn's ``KMeans.fit`` semantics (``sklearn/cluster/_kmeans.py:1436-1562``)
+run on the CUDA library:
+
+* the init is honoured: an explicit array is used as given; ``"k-means++"``,
+  ``"random"`` and callables are drawn with scikit-learn's own initialisation
+  routine and random stream, so a fixed ``random_state`` yields the same
+  initial centres as scikit-learn;
+* ``n_init`` restarts keep scikit-learn's best-run rule (lower inertia and
+  not the same clustering up to a permutation);
+* the Lloyd loop, the final E-step, the inertia, ``predict``, ``transform``,
+  ``fit_predict``, ``fit_transform`` and ``score`` run on the GPU;
+* there is no CPU fallback: without a GPU, or under ``set_device("cpu")``,
+  the estimator raises.
+"""
+
+from __future__ import annotations
+
+import time
+import warnings
+
+import numpy as np
+from sklearn.exceptions import ConvergenceWarning
+from sklearn.utils import check_random_state
+from sklearn.utils.validation import check_array, check_is_fitted
+
+from .. import _bridge
+from .._config import _get_device, get_config
+from ._base import BaseGPUEstimator
+
+try:  # scikit-learn's helper for the n_init best-run rule
+    from sklearn.cluster._k_means_common import _is_same_clustering
+except Exception:  # noqa: BLE001
+    _is_same_clustering = None
+
+
+def _same_clustering(a: np.ndarray, b: np.ndarray, k: int) -> bool:
+    if _is_same_clustering is not None:
+        return bool(_is_same_clustering(a.astype(np.int32), b.astype(np.int32), k))
+    mapping = np.full(k, -1)
+    for x, y in zip(a, b):
+        if mapping[x] == -1:
+            mapping[x] = y
+        elif mapping[x] != y:
+            return False
+    return True
+
+
+class MetalKMeans(BaseGPUEstimator):
+    """KMeans whose Lloyd iterations, assignment and distances run on the GPU."""
+
+    # ------------------------------------------------------------------ helpers
+    def _require_gpu(self, X):
+        if not self._should_use_gpu(X):
+            raise RuntimeError(
+                "skmetal_b200 KMeans has no CPU path: device is set to 'cpu' (set_device / "
+                "accelerate_context). Use sklearn.cluster.KMeans directly for CPU execution.")
+        if not _bridge.GPU_AVAILABLE:
+            raise RuntimeError("skmetal_b200 KMeans requires a CUDA GPU (none visible; no CPU fallback)")
+        _bridge.set_device(get_config().gpu_index)
+
+    def _check_weights(self, sample_weight, n):
+        if sample_weight is None:
+            return
+        w = np.asarray(sample_weight, dtype=np.float64)
+        if w.ndim == 0:
+            w = np.full(n, float(w))
+        if w.shape != (n,) or not np.all(w == 1.0):
+            raise NotImplementedError("skmetal_b200 KMeans supports unit sample weights only")
+
+    # ---------------------------------------------------------------------- fit
+    def fit(self, X, y=None, sample_weight=None):
+        est = self._estimator
+        est._validate_params()
+        X = self._validate_data(X)[0]
+        self._require_gpu(X)
+        n, d = X.shape
+        k = int(est.n_clusters)
+        if n < k:
+            raise ValueError(f"n_samples={n} should be >= n_clusters={k}.")
+        self._check_weights(sample_weight, n)
+
+        init = est.init
+        init_is_array = hasattr(init, "__array__") or isinstance(init, (list, tuple))
+        if est.n_init == "auto":
+            n_init = 1 if (init_is_array or (isinstance(init, str) and init == "k-means++")) else 10
+        else:
+            n_init = int(est.n_init)
+        if init_is_array:
+            init = check_array(init, dtype=np.float32, order="C", copy=True)
+            if init.shape != (k, d):
+                raise ValueError(f"The shape of the initial centers {init.shape} does not match "
+                                 f"the number of clusters {k} and features {d}.")
+            if n_init != 1:
+                warnings.warn("Explicit initial center position passed: performing only one init in "
+                              f"KMeans instead of n_init={n_init}.", RuntimeWarning, stacklevel=2)
+                n_init = 1
+        random_state = check_random_state(est.random_state)
+
+        # scikit-learn draws non-array inits on the centred data
+        Xc = x_sq = mean = None
+        if not init_is_array:
+            mean = X.mean(axis=0)
+            Xc = X - mean
+            x_sq = np.einsum("ij,ij->i", Xc, Xc)
+        ones = np.ones(n, dtype=np.float32)
+
+        t0 = time.perf_counter()
+        best = None
+        for _ in range(n_init):
+            if init_is_array:
+                centers_init = init
+            else:
+                centers_init = est._init_centroids(Xc, x_squared_norms=x_sq, init=init,
+                                                   random_state=random_state, sample_weight=ones)
+                centers_init = np.ascontiguousarray((centers_init + mean).astype(np.float32))
+            centers, labels, inertia, n_iter = _bridge.kmeans_fit(
+                X, centers_init, int(est.max_iter), float(est.tol), center=True)
+            if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
+                best = (centers, labels, inertia, n_iter)
+        centers, labels, inertia, n_iter = best
+
+        if len(np.unique(labels)) < k:
+            warnings.warn(f"Number of distinct clusters ({len(np.unique(labels))}) found smaller than "
+                          f"n_clusters ({k}). Possibly due to duplicate points in X.", ConvergenceWarning,
+                          stacklevel=2)
+        est.cluster_centers_ = centers
+        est._n_features_out = k
+        est.labels_ = labels
+        est.inertia_ = float(inertia)
+        est.n_iter_ = int(n_iter)
+        est.n_features_in_ = d
+        est._n_threads = 1
+        est._tol = float(est.tol)
+        est._n_init = n_init
+        est._algorithm = "lloyd"
+        self._fitted = True
+        if get_config().verbose:
+            st = _bridge.last_fit_stats()
+            print(f"[skmetal] KMeans: {n}x{d} k={k} n_init={n_init} n_iter={n_iter} "
+                  f"wall={time.perf_counter() - t0:.4f}s gpu_loop={st['ms_loop']:.3f}ms "
+                  f"({st['ms_loop'] / max(1, st['iterations']):.4f} ms/iter)")
+        return self
+
+    # ------------------------------------------------------------------ inference
+    def _centers(self):
+        check_is_fitted(self._estimator, "cluster_centers_")
+        return np.ascontiguousarray(self._estimator.cluster_centers_, dtype=np.float32)
+
+    def _check_test(self, X):
+        X = check_array(X, dtype=np.float32, order="C")
+        if X.shape[1] != self._estimator.n_features_in_:
+            raise ValueError(f"X has {X.shape[1]} features, but KMeans is expecting "
+                             f"{self._estimator.n_features_in_} features as input.")
+        self._require_gpu(X)
+        return X
+
+    def predict(self, X):
+        C = self._centers()
+        X = self._check_test(X)
+        labels = np.empty(X.shape[0], dtype=np.int32)
+        _bridge.kmeans_assign(X, C, labels, X.shape[0], X.shape[1], C.shape[0])
+        return labels
+
+    def transform(self, X):
+        C = self._centers()
+        X = self._check_test(X)
+        return _bridge.kmeans_transform(X, C)
+
+    def fit_predict(self, X, y=None, sample_weight=None):
+        return self.fit(X, sample_weight=sample_weight)._estimator.labels_
+
+    def fit_transform(self, X, y=None, sample_weight=None):
+        return self.fit(X, sample_weight=sample_weight).transform(X)
+
+    def score(self, X, y=None, sample_weight=None):
+        C = self._centers()
+        X = self._check_test(X)
+        self._check_weights(sample_weight, X.shape[0])
+        labels = self.predict(X)
+        return -_bridge.kmeans_inertia(X, C, labels, X.shape[0], X.shape[1], C.shape[0])

@@ -1,0 +1,75 @@
+"""Parity criteria shared by the GPU tests.
+
+The bar (from the project's acceptance criteria) for one Lloyd step or one
+assignment against the scikit-learn-semantics oracle on the same inputs:
+
+* label agreement >= 99.99 %;
+* every disagreement is a near-tie: the float64 squared distances of the row
+  to the two competing centres differ by less than REL_GAP = 1e-5 relative,
+  or by less than the float32 rounding bound of the reference's own distance
+  formula ||c||^2 - 2 x.c (scikit-learn evaluates it in float32, so rows
+  closer to a tie than that bound are decided by its rounding, not by the
+  data); the second kind is counted and reported separately;
+* per-cluster counts identical wherever labels agree (i.e. the count
+  difference is exactly the one implied by the disagreeing rows);
+* centres within rtol 1e-4, inertia within rtol 1e-5.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+REL_GAP = 1e-5
+MIN_AGREEMENT = 0.9999
+CENTER_RTOL = 1e-4
+INERTIA_RTOL = 1e-5
+EPS32 = np.finfo(np.float32).eps
+
+
+def fp32_expansion_bound(X, C, la, lb, d):
+    """Float32 rounding bound of ||c_a||^2 - 2x.c_a versus the same for c_b."""
+    Xa = np.abs(X.astype(np.float64))
+    Ca = np.abs(C.astype(np.float64))
+    dot_a = (Xa * Ca[la]).sum(axis=1)
+    dot_b = (Xa * Ca[lb]).sum(axis=1)
+    na = (Ca[la] ** 2).sum(axis=1)
+    nb = (Ca[lb] ** 2).sum(axis=1)
+    # gemm accumulation over d terms + the bias add, for both candidates
+    return (d + 2) * EPS32 * (2 * (dot_a + dot_b) + na + nb)
+
+
+def check_labels(X, C, got, want, what="labels"):
+    """Assert the label criteria; returns a small report dict."""
+    from oracle.lloyd import near_tie_gap
+
+    got = np.asarray(got)
+    want = np.asarray(want)
+    mism = np.nonzero(got != want)[0]
+    agree = 1.0 - mism.size / max(1, got.size)
+    rep = {"n": int(got.size), "mismatches": int(mism.size), "agreement": agree, "beyond_rel_gap": 0}
+    assert agree >= MIN_AGREEMENT, f"{what}: agreement {agree:.6f} < {MIN_AGREEMENT} ({mism.size} rows)"
+    if mism.size:
+        Xm = X[mism]
+        gap = near_tie_gap(Xm, C, got[mism], want[mism])
+        dist_a = ((Xm.astype(np.float64) - C.astype(np.float64)[got[mism]]) ** 2).sum(axis=1)
+        dist_b = ((Xm.astype(np.float64) - C.astype(np.float64)[want[mism]]) ** 2).sum(axis=1)
+        bound = fp32_expansion_bound(Xm, C, got[mism], want[mism], X.shape[1])
+        abs_gap = np.abs(dist_a - dist_b)
+        beyond = gap >= REL_GAP
+        rep["beyond_rel_gap"] = int(beyond.sum())
+        rep["max_rel_gap"] = float(gap.max())
+        bad = beyond & (abs_gap > bound)
+        assert not bad.any(), (f"{what}: {int(bad.sum())} disagreements are not near-ties "
+                               f"(rel gaps {gap[bad][:5]}, abs {abs_gap[bad][:5]}, bound {bound[bad][:5]})")
+    return rep
+
+
+def check_counts(got_counts, want_counts, got_labels, want_labels, k):
+    """Counts equal up to the rows whose labels disagree."""
+    got_counts = np.asarray(got_counts, dtype=np.int64)
+    want_counts = np.asarray(want_counts, dtype=np.int64)
+    mism = got_labels != want_labels
+    adj = want_counts.copy()
+    np.subtract.at(adj, want_labels[mism], 1)
+    np.add.at(adj, got_labels[mism], 1)
+    np.testing.assert_array_equal(got_counts, adj)

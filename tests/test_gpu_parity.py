@@ -1,0 +1,266 @@
+"""GPU parity tests: the CUDA path through the C ABI against the oracle.
+
+Protocol (scikit-learn's Lloyd is chaotic in float32, so end-to-end label
+agreement between two correct implementations with different summation
+orders drifts; parity is therefore judged in lockstep):
+
+* lockstep: each GPU Lloyd step starts from the oracle's centres of that
+  iteration and is compared with the oracle's step (labels, counts, centres,
+  shift);
+* end to end: full fits compared with scikit-learn on well-separated data
+  where both converge to the same clustering.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import lloyd as ora
+from skmetal_b200 import _bridge
+from skmetal_b200._synthetic import gaussian_mixture, make_workload, scaled
+
+from parity import CENTER_RTOL, INERTIA_RTOL, check_counts, check_labels
+
+pytestmark = pytest.mark.gpu
+
+
+def _fp64_centres(X, labels, k, init):
+    C = np.zeros((k, X.shape[1]))
+    cnt = np.bincount(labels, minlength=k)
+    np.add.at(C, labels, X.astype(np.float64))
+    nz = cnt > 0
+    C[nz] /= cnt[nz, None]
+    return C, cnt
+
+
+# ---------------------------------------------------------------------------
+# reference golden vector (skmetal tests/test_kernels.py:94-98)
+# ---------------------------------------------------------------------------
+
+def test_kmeans_assign_golden():
+    X = np.array([[0.0, 0.0], [1.0, 1.0], [10.0, 10.0], [9.0, 9.0]], dtype=np.float32)
+    centroids = np.array([[0.0, 0.0], [10.0, 10.0]], dtype=np.float32)
+    assignments = np.empty(4, dtype=np.int32)
+    _bridge.kmeans_assign(X, centroids, assignments, 4, 2, 2)
+    np.testing.assert_array_equal(assignments, [0, 0, 1, 1])
+
+
+def test_compute_mindists_and_inertia_golden():
+    X = np.array([[0.0, 0.0], [1.0, 1.0], [10.0, 10.0], [9.0, 9.0]], dtype=np.float32)
+    C = np.array([[0.0, 0.0], [10.0, 10.0]], dtype=np.float32)
+    lab = np.array([0, 0, 1, 1], dtype=np.uint32)
+    dists = np.empty(4, dtype=np.float32)
+    _bridge.compute_mindists(X, C, lab, dists, 4, 2, 2)
+    np.testing.assert_allclose(dists, [0.0, 2.0, 0.0, 2.0], rtol=1e-6)
+    assert _bridge.kmeans_inertia(X, C, lab, 4, 2, 2) == pytest.approx(4.0, rel=1e-6)
+    np.testing.assert_allclose(_bridge.row_norm_sq(X), [0, 2, 200, 162], rtol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# assignment
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("n,d,k", [(5000, 32, 8), (3000, 8, 16), (2000, 100, 50), (1000, 7, 3), (777, 1, 5)])
+def test_assign_matches_fp64_argmin(n, d, k):
+    rng = np.random.default_rng(n + d + k)
+    X = rng.standard_normal((n, d)).astype(np.float32) * 3
+    C = rng.standard_normal((k, d)).astype(np.float32) * 3
+    lab = np.empty(n, dtype=np.int32)
+    _bridge.kmeans_assign(X, C, lab, n, d, k)
+    want, _ = ora.assign(X, C, "fp64")
+    check_labels(X, C, lab, want, "assign")
+
+
+def test_transform_matches_fp64():
+    rng = np.random.default_rng(7)
+    X = rng.standard_normal((1500, 13)).astype(np.float32)
+    C = rng.standard_normal((9, 13)).astype(np.float32)
+    D = _bridge.kmeans_transform(X, C)
+    ref = np.sqrt(((X[:, None, :].astype(np.float64) - C[None].astype(np.float64)) ** 2).sum(-1))
+    np.testing.assert_allclose(D, ref, rtol=1e-5, atol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# lockstep Lloyd steps
+# ---------------------------------------------------------------------------
+
+def _lockstep(X, init, iters):
+    mean, Xc, C = ora.center_data(X, init)
+    reports = []
+    for _ in range(iters):
+        step = ora.lloyd_iter(Xc, C, "fp32", relocation_order="sorted")
+        lab, cnew, weight, shift = _bridge.kmeans_lloyd_iter(Xc, C)
+        rep = check_labels(Xc, C, lab, step.labels, "lloyd step labels")
+        check_counts(weight, step.weight, lab, step.labels, C.shape[0])
+        # centres: exact float64 means of the GPU's own assignment (+ relocation)
+        ref, cnt = _fp64_centres(Xc, lab, C.shape[0], C)
+        same = np.ones(C.shape[0], bool)
+        mism = lab != step.labels
+        same[np.unique(np.concatenate([lab[mism], step.labels[mism]]))] = False
+        moved = np.zeros(C.shape[0], bool)
+        if step.far.size:
+            moved[step.empty] = True
+            moved[step.labels[step.far]] = True
+        keep = (cnt > 0) & ~moved
+        scale = float(np.abs(Xc).max())
+        np.testing.assert_allclose(cnew[keep], ref[keep], rtol=CENTER_RTOL, atol=1e-6 * scale)
+        # against the oracle's own centres where nothing differs
+        ok = keep & same
+        np.testing.assert_allclose(cnew[ok], step.centers_new[ok], rtol=CENTER_RTOL, atol=1e-6 * scale)
+        if not mism.any():
+            np.testing.assert_allclose(cnew, step.centers_new, rtol=CENTER_RTOL, atol=1e-6 * scale)
+            np.testing.assert_allclose(shift, step.center_shift, rtol=1e-3, atol=1e-5 * scale)
+        reports.append(rep)
+        C = step.centers_new
+    return reports
+
+
+@pytest.mark.parametrize("name,n", [("c1", 20000), ("c2", 25000)])
+def test_lloyd_step_lockstep(name, n):
+    w = scaled(name, n)
+    X, init = make_workload(w)
+    reps = _lockstep(X, init, 8)
+    assert sum(r["mismatches"] for r in reps) <= 8 * max(1, n // 10000)
+
+
+def test_lloyd_step_relocation_lockstep():
+    # k=20 on 5 blobs with duplicate-heavy init: empty clusters every step
+    X, _ = gaussian_mixture(4000, 10, 5, seed=11)
+    init = np.ascontiguousarray(np.repeat(X[:4], 5, axis=0))
+    init[::5] += 0  # duplicates on purpose
+    _lockstep(X, init, 5)
+
+
+# ---------------------------------------------------------------------------
+# tensor-core vs SIMT E-step, full fits
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("name,n", [("c1", 30000), ("c2", 30000)])
+def test_tc_fit_matches_simt_fit(name, n):
+    w = scaled(name, n)
+    X, init = make_workload(w)
+    c_tc, l_tc, i_tc, n_tc = _bridge.kmeans_fit(X, init, 5, 0.0)
+    c_si, l_si, i_si, n_si = _bridge.kmeans_fit(X, init, 5, 0.0, simt=True)
+    mean, Xc, _ = ora.center_data(X)
+    check_labels(Xc, c_si - mean, l_tc, l_si, "tc vs simt")
+    assert i_tc == pytest.approx(i_si, rel=1e-5)
+
+
+@pytest.mark.parametrize("name,n,max_iter", [("c1", 20000, 50), ("c2", 20000, 30)])
+def test_fit_end_to_end_vs_sklearn(name, n, max_iter):
+    from sklearn.cluster import KMeans
+
+    w = scaled(name, n)
+    X, init = make_workload(w)
+    km = KMeans(w.k, init=init, n_init=1, max_iter=max_iter, tol=0, algorithm="lloyd").fit(X)
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, max_iter, 0.0)
+    res = ora.kmeans_lloyd(X, init, max_iter, 0.0)
+    # label agreement with scikit-learn is bounded by the float32 noise floor
+    # between two implementations (the oracle vs scikit-learn here)
+    floor = np.mean(res.labels == km.labels_)
+    agree = np.mean(lab == km.labels_)
+    assert agree >= min(floor, 0.9999) - 1e-3, (agree, floor)
+    assert inertia == pytest.approx(km.inertia_, rel=max(INERTIA_RTOL, abs(res.inertia / km.inertia_ - 1) * 2))
+    if agree == 1.0:
+        np.testing.assert_allclose(c, km.cluster_centers_, rtol=CENTER_RTOL, atol=1e-4)
+
+
+def test_fit_with_tolerance_matches_sklearn_iterations():
+    from sklearn.cluster import KMeans
+
+    X, init = gaussian_mixture(20000, 16, 6, seed=5)
+    km = KMeans(6, init=init, n_init=1, max_iter=300, tol=1e-4, algorithm="lloyd").fit(X)
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 300, 1e-4)
+    assert n_iter == km.n_iter_
+    assert np.mean(lab == km.labels_) >= 0.9999
+    assert inertia == pytest.approx(km.inertia_, rel=INERTIA_RTOL)
+
+
+def test_batch_fused_reference_abi():
+    X, init = gaussian_mixture(5000, 12, 4, seed=2)
+    C = init.copy()
+    lab = np.empty(X.shape[0], dtype=np.uint32)
+    n_iter = _bridge.kmeans_batch_fused(X, C, lab, X.shape[0], 12, 4, (X.shape[0] + 255) // 256, 100, 0.0)
+    res = ora.kmeans_lloyd(X, init, 100, 0.0)  # same loop, but centred
+    assert 1 <= n_iter <= 100
+    assert np.mean(lab.astype(np.int32) == res.labels) >= 0.999
+
+
+# ---------------------------------------------------------------------------
+# edge cases
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("n,d,k", [(5, 3, 2), (130, 1, 1), (257, 9, 7), (1000, 33, 32), (64, 4, 64),
+                                   (300, 129, 5), (2000, 16, 257)])
+def test_fit_odd_shapes(n, d, k):
+    rng = np.random.default_rng(n * 7 + d + k)
+    X = (rng.standard_normal((n, d)) * 2 + 5).astype(np.float32)
+    init = np.ascontiguousarray(X[rng.choice(n, k, replace=False)])
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 20, 0.0)
+    res = ora.kmeans_lloyd(X, init, 20, 0.0, relocation_order="sorted")
+    assert c.shape == (k, d) and lab.shape == (n,)
+    assert lab.min() >= 0 and lab.max() < k
+    # inertia is consistent with the returned labels and centres
+    ref_in = ora.inertia(X, c, lab)
+    assert inertia == pytest.approx(ref_in, rel=1e-5, abs=1e-6)
+    assert inertia <= res.inertia * (1 + 1e-3) + 1e-6 or np.mean(lab == res.labels) < 1.0
+
+
+def test_fit_all_rows_identical():
+    X = np.ones((500, 6), dtype=np.float32) * 3.5
+    init = np.ascontiguousarray(X[:4])
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 10, 0.0)
+    from sklearn.cluster import KMeans
+    import warnings
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        km = KMeans(4, init=init, n_init=1, max_iter=10, tol=0).fit(X)
+    np.testing.assert_array_equal(lab, km.labels_)
+    np.testing.assert_allclose(c, km.cluster_centers_)
+    assert n_iter == km.n_iter_
+    assert inertia == pytest.approx(0.0, abs=1e-6)
+
+
+def test_fit_rejects_bad_input():
+    X = np.ones((10, 3), dtype=np.float32)
+    with pytest.raises(RuntimeError):
+        _bridge.kmeans_fit(X, np.ones((11, 3), dtype=np.float32), 5, 0.0)  # k > n
+    Xn = X.copy()
+    Xn[3, 1] = np.nan
+    with pytest.raises(RuntimeError):
+        _bridge.kmeans_fit(Xn, Xn[:2].copy(), 5, 0.0)
+
+
+def test_fit_is_deterministic():
+    X, init = make_workload(scaled("c2", 20000))
+    a = _bridge.kmeans_fit(X, init, 10, 0.0)
+    b = _bridge.kmeans_fit(X, init, 10, 0.0)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+    assert a[2] == b[2] and a[3] == b[3]
+
+
+def test_dataset_fit_matches_host_fit():
+    X, init = make_workload(scaled("c1", 10000))
+    a = _bridge.kmeans_fit(X, init, 15, 0.0)
+    ds = _bridge.Dataset(X)
+    lab = np.empty(X.shape[0], dtype=np.int32)
+    c, inertia, n_iter = ds.fit(init, 15, 0.0, labels_out=lab)
+    np.testing.assert_array_equal(c, a[0])
+    np.testing.assert_array_equal(lab, a[1])
+    assert inertia == a[2] and n_iter == a[3]
+    p = np.empty(X.shape[0], dtype=np.int32)
+    ds.predict(c, p)
+    q = np.empty(X.shape[0], dtype=np.int32)
+    _bridge.kmeans_assign(X, c, q, X.shape[0], X.shape[1], c.shape[0])
+    np.testing.assert_array_equal(p, q)
+    ds.close()
+
+
+def test_injected_failure_raises():
+    X = np.ones((10, 3), dtype=np.float32)
+    _bridge.debug_inject_failure(8, 0)
+    with pytest.raises(RuntimeError, match="injected"):
+        _bridge.kmeans_fit(X, X[:2].copy(), 5, 0.0)
+    # the next call works again
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, X[:2].copy(), 5, 0.0)
+    assert c.shape == (2, 3)

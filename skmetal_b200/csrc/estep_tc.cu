@@ -29,6 +29,7 @@
 #include <cstdio>
 #include <cstring>
 
+#include "device_util.cuh"
 #include "driver.h"
 #include "estep_tc.h"
 
@@ -58,6 +59,10 @@ struct Params {
   int32_t* labels;
   float* mind;    // ||x||^2 + min_j (||c_j||^2 - 2 x.c_j)
   unsigned long long* changed;
+  long long* D;        // nullable: incremental deltas of rows that changed label
+  const float* X;      // rows (global) for the deltas
+  int ld;
+  int d;
   const FitState* st;  // nullable: skip when st->done
   int* err;
 };
@@ -364,14 +369,19 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           mbar_arrive(bar(ACC_EMPTY0 + b));
           const long long grow = (long long)((int)blockIdx.x + t * (int)gridDim.x) * BM + row;
           bool ch = false;
+          int old = -1;
           if (grow < p.n) {
-            if (p.changed) ch = p.labels[grow] != bl;
+            if (p.changed) {
+              old = p.labels[grow];
+              ch = old != bl;
+            }
             p.labels[grow] = bl;
             if (p.mind) p.mind[grow] = best + nx_s[b * BM + row];
           }
           if (p.changed) {
             const unsigned int m = __ballot_sync(0xffffffffu, ch);
             if (lane == 0 && m) atomicAdd(p.changed, (unsigned long long)__popc(m));
+            if (p.D) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, p.D, p.st->scale);
           }
         }
       }
@@ -467,7 +477,7 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
 }
 
 int tc_estep(const TcPlan& plan, const float* Chi, const float* Clo, const float* bias, int32_t* labels, float* mind,
-             unsigned long long* changed, const FitState* st, int* err, cudaStream_t s) {
+             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s) {
   CUtensorMap mhi, mlo;
   SKM_TRY(make_map(&mhi, Chi, plan.ld, plan.k, plan.k_pad));
   SKM_TRY(make_map(&mlo, Clo, plan.ld, plan.k, plan.k_pad));
@@ -481,6 +491,10 @@ int tc_estep(const TcPlan& plan, const float* Chi, const float* Clo, const float
   p.labels = labels;
   p.mind = mind;
   p.changed = changed;
+  p.D = D;
+  p.X = plan.X;
+  p.ld = plan.ld;
+  p.d = plan.d;
   p.st = st;
   p.err = err;
   tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(plan.tmap_x, mhi, mlo, p);

@@ -28,9 +28,10 @@ struct TcPlan {
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan);
 // Chi / Clo: tf32 split of the centres (k x ld); bias: ||c||^2 (k floats).
 // `changed` (nullable) counts rows whose label differs from labels[] on entry;
+// `D` (nullable, needs `st`) receives the fixed-point deltas of those rows;
 // `st` (nullable) makes the launch a no-op once st->done is set; `err`
 // receives a nonzero code if a pipeline wait times out.
 int tc_estep(const TcPlan& plan, const float* Chi, const float* Clo, const float* bias, int32_t* labels, float* mind,
-             unsigned long long* changed, const FitState* st, int* err, cudaStream_t s);
+             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s);
 
 }  // namespace skm

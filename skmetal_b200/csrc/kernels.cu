@@ -11,6 +11,7 @@
 //   centre shift                              (_k_means_common.pyx:298-311)
 //   strict convergence / tol / max_iter       (_kmeans.py:705-758)
 #include "kernels.cuh"
+#include "device_util.cuh"
 
 #include <cfloat>
 #include <cmath>
@@ -20,14 +21,6 @@ namespace skm {
 // ---------------------------------------------------------------------------
 // helpers
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ long long to_fixed(float v, double scale) {
-  return __double2ll_rn(static_cast<double>(v) * scale);
-}
-
-__device__ __forceinline__ void red_add_s64(long long* p, long long v) {
-  atomicAdd(reinterpret_cast<unsigned long long*>(p), static_cast<unsigned long long>(v));
-}
 
 // Bounded software grid barrier for cooperative launches. Returns false (and
 // records an error in the fit state) if the other blocks do not arrive within
@@ -233,7 +226,7 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
                                    const float* __restrict__ C, int k,
                                    int32_t* __restrict__ labels, float* __restrict__ mind,
                                    const FitState* __restrict__ st, unsigned long long* __restrict__ changed,
-                                   int skip_if_strict) {
+                                   long long* __restrict__ D, int skip_if_strict) {
   extern __shared__ float csh[];
   if (st) {
     if (skip_if_strict ? (st->strict != 0) : (st->done != 0)) return;
@@ -274,14 +267,19 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
     }
   }
   bool ch = false;
+  int old = -1;
   if (active) {
-    if (changed) ch = labels[r] != bl;
+    if (changed) {
+      old = labels[r];
+      ch = old != bl;
+    }
     labels[r] = bl;
     if (mind) mind[r] = best;
   }
   if (changed) {
     const unsigned int b = __ballot_sync(0xffffffffu, ch);
     if ((threadIdx.x & 31) == 0 && b) atomicAdd(changed, (unsigned long long)__popc(b));
+    if (D) warp_apply_changed(X, ld, d, k, r, old, bl, ch, D, st->scale);
   }
 }
 
@@ -329,48 +327,74 @@ bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream
 }
 
 // ---------------------------------------------------------------------------
-// bulk fixed-point sums from the labels (S and counts must be zero on entry)
+// bulk fixed-point sums from the labels into the delta buffer D (zero on entry)
 // ---------------------------------------------------------------------------
 
-// Each warp walks rows; lanes cover 32 columns at a time. With `use_smem` the
-// block accumulates k x ld int64 in shared memory and flushes nonzero entries
-// with one global atomic each; otherwise it adds straight into global memory.
-// Integer addition is exact, so the result does not depend on the order.
+// Block b owns a contiguous row range. With `groups` > 0 the block is split
+// into `groups` groups of `gsize` threads (gsize >= d, a multiple of 32);
+// thread j of group g owns column j of a private k x ld int64 accumulator in
+// shared memory and adds the rows r = r0 + g, r0 + g + groups, ... in order,
+// so the hot loop has no atomics. The groups are summed and flushed with one
+// global reduction per nonzero entry. With `groups` == 0 (accumulators do not
+// fit in shared memory) every warp adds rows straight into D. Integer sums
+// are exact, so the result does not depend on the order or the grid.
 __global__ void bulk_sums_kernel(const float* __restrict__ X, int ld, long long n, int d,
-                                 const int32_t* __restrict__ labels, int k,
-                                 long long* __restrict__ S, long long* __restrict__ counts,
-                                 FitState* __restrict__ st, int use_smem) {
-  extern __shared__ long long ssum[];
+                                 const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
+                                 const FitState* __restrict__ st, int groups, int gsize) {
+  extern __shared__ long long acc[];
   if (st->done) return;
   const double scale = st->scale;
-  long long* scnt = ssum + (size_t)k * ld;
-  if (use_smem) {
-    for (int i = threadIdx.x; i < k * ld + k; i += blockDim.x) ssum[i] = 0;
-    __syncthreads();
-  }
-  long long* Sd = use_smem ? ssum : S;
-  long long* Cd = use_smem ? scnt : counts;
-  const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
-  const long long gw = blockIdx.x * (long long)warps + (threadIdx.x >> 5);
-  const long long tw = (long long)gridDim.x * warps;
-  for (long long r = gw; r < n; r += tw) {
-    const int l = labels[r];
-    if (lane == 0) {
-      if (use_smem) atomicAdd(reinterpret_cast<unsigned long long*>(&Cd[l]), 1ull);
-      else red_add_s64(&Cd[l], 1);
+  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
+  const long long r0 = blockIdx.x * rows_per;
+  const long long r1 = min(n, r0 + rows_per);
+  long long* cntD = D + (long long)k * ld;
+  if (groups == 0) {
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    for (long long r = r0 + (threadIdx.x >> 5); r < r1; r += warps) {
+      const int l = labels[r];
+      if (lane == 0) red_add_s64(&cntD[l], 1);
+      for (int j = lane; j < d; j += 32) {
+        const long long v = to_fixed(X[r * ld + j], scale);
+        if (v != 0) red_add_s64(&D[(long long)l * ld + j], v);
+      }
     }
-    for (int j = lane; j < d; j += 32) {
-      const long long v = to_fixed(X[r * ld + j], scale);
-      if (v != 0) red_add_s64(&Sd[(long long)l * ld + j], v);
+    return;
+  }
+  const long long per = (long long)k * ld + k;  // one group's accumulators (sums, counts)
+  for (long long i = threadIdx.x; i < per * groups; i += blockDim.x) acc[i] = 0;
+  __syncthreads();
+  const int g = threadIdx.x / gsize, j = threadIdx.x % gsize;
+  if (g < groups) {
+    long long* a = acc + per * g;
+    long long* ac = a + (long long)k * ld;
+    if (j < d) {
+      long long r = r0 + g;
+      for (; r + 3 * groups < r1; r += 4 * groups) {
+        float xv[4];
+        int lv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          lv[u] = labels[r + u * groups];
+          xv[u] = X[(r + u * groups) * ld + j];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          a[(long long)lv[u] * ld + j] += to_fixed(xv[u], scale);
+          if (j == 0) ac[lv[u]] += 1;
+        }
+      }
+      for (; r < r1; r += groups) {
+        const int l = labels[r];
+        a[(long long)l * ld + j] += to_fixed(X[r * ld + j], scale);
+        if (j == 0) ac[l] += 1;
+      }
     }
   }
-  if (use_smem) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < k * ld; i += blockDim.x)
-      if (ssum[i] != 0) red_add_s64(&S[i], ssum[i]);
-    for (int i = threadIdx.x; i < k; i += blockDim.x)
-      if (scnt[i] != 0) red_add_s64(&counts[i], scnt[i]);
+  __syncthreads();
+  for (long long i = threadIdx.x; i < per; i += blockDim.x) {
+    long long s = 0;
+    for (int gg = 0; gg < groups; ++gg) s += acc[per * gg + i];
+    if (s != 0) red_add_s64(i < (long long)k * ld ? &D[i] : &cntD[i - (long long)k * ld], s);
   }
 }
 
@@ -456,11 +480,28 @@ __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, 
 __global__ void mstep_kernel(MStepArgs a) {
   FitState* st = a.st;
   if (st->done) return;  // uniform: `done` is only written after the last barrier
-  const unsigned long long changed_now = *a.changed;  // read before step 6 clears it
+  const unsigned long long changed_now = *a.changed;  // cleared by block 0 at the end
   const unsigned int nb = gridDim.x;
   __shared__ int n_empty_s;
   __shared__ int wcount[32];
   __shared__ double scratch[32];
+
+  // 0. S += dS, counts += dcount; clear the deltas (all but `changed`)
+  {
+    long long* S = const_cast<long long*>(a.S);
+    long long* cnt = const_cast<long long*>(a.counts);
+    const long long ks = (long long)a.k * a.ld;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + a.k;
+         i += (long long)nb * blockDim.x) {
+      const long long v = a.D[i];
+      if (v != 0) {
+        if (i < ks) S[i] += v;
+        else cnt[i - ks] += v;
+        a.D[i] = 0;
+      }
+    }
+  }
+  if (!grid_barrier(st, nb)) return;
 
   // 1. empty clusters in ascending id order (every block; block 0 stores them)
   if (threadIdx.x == 0) n_empty_s = 0;
@@ -602,15 +643,6 @@ __global__ void mstep_kernel(MStepArgs a) {
   if (threadIdx.x == 0) a.shift_partial[blockIdx.x] = shift_part;
   if (!grid_barrier(st, nb)) return;
 
-  // 6. the next iteration recomputes its sums from zero (bulk mode)
-  if (a.zero_sums) {
-    // payload = S | counts | changed, contiguous
-    long long* P = const_cast<long long*>(a.S);
-    const long long len = (long long)a.k * a.ld + a.k + 1;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < len; i += (long long)nb * blockDim.x)
-      P[i] = 0;
-  }
-
   // 5. convergence bookkeeping (_kmeans.py:723-741), fixed summation order
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     double tot = 0.0;
@@ -624,6 +656,7 @@ __global__ void mstep_kernel(MStepArgs a) {
       st->done = 1;
     }
     if (st->iter >= st->max_iter) st->done = 1;
+    *const_cast<unsigned long long*>(a.changed) = 0;
   }
 }
 

@@ -16,13 +16,13 @@ struct MStepArgs {
   long long row_base;   // global index of local row 0
   const int32_t* labels;
   const float* mind;    // per-row distance to the assigned centre
-  const long long* S;   // k x ld fixed-point sums (global over ranks)
+  const long long* S;   // k x ld fixed-point sums of the current labels (global over ranks)
   const long long* counts;
-  const unsigned long long* changed;  // rows whose label changed (global)
+  long long* D;         // deltas of this iteration: dS (k x ld) | dcount (k) | changed
+  const unsigned long long* changed;  // = D + k*ld + k
   int k;
   const float* C_old;
   float* C_new;
-  int zero_sums;        // zero S and counts after use (next iteration is bulk)
   // scratch
   int* empty_ids;       // kMaxEmptyCap
   unsigned int* hist;   // 512
@@ -52,14 +52,15 @@ __global__ void sumsq_partial_kernel(const float* X, int ld, long long n, int d,
 __global__ void center_init_kernel(const float* init, int d, int k, const float* mean, float* C, int ld);
 __global__ void assign_simt_kernel(const float* X, int ld, long long n, int d, const float* C, int k,
                                    int32_t* labels, float* mind, const FitState* st, unsigned long long* changed,
-                                   int skip_if_strict);
+                                   long long* D, int skip_if_strict);
 __global__ void counts_to_float_kernel(const long long* c, int k, float* out);
 // Small-d assignment (d in {4, 8, 16, 32}, all centres in shared memory);
 // returns false when d has no specialisation.
 bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
                          long long n, const float* C, int k, int32_t* labels, float* mind);
 __global__ void bulk_sums_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
-                                 long long* S, long long* counts, FitState* st, int use_smem);
+                                 long long* D, const FitState* st, int groups, int gsize);
+
 __global__ void mstep_kernel(MStepArgs a);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, float* Chi, float* Clo,
                                    const FitState* st);

@@ -104,30 +104,36 @@ struct EStepPlan {
 };
 
 static int launch_assign_simt(const float* X, int ld, long long n, int d, const float* C, int k, int32_t* labels,
-                              float* mind, const FitState* st, unsigned long long* changed, int skip_if_strict,
-                              cudaStream_t s) {
+                              float* mind, const FitState* st, unsigned long long* changed, long long* D,
+                              int skip_if_strict, cudaStream_t s) {
   const int chunk = std::max(1, std::min(k, kAssignSmemFloats / ld));
   const size_t smem = sizeof(float) * (size_t)chunk * ld;
   const int threads = 256;
   const int blocks = (int)((n + threads - 1) / threads);
-  assign_simt_kernel<<<blocks, threads, smem, s>>>(X, ld, n, d, C, k, labels, mind, st, changed, skip_if_strict);
+  assign_simt_kernel<<<blocks, threads, smem, s>>>(X, ld, n, d, C, k, labels, mind, st, changed, D,
+                                                   skip_if_strict);
   return check_launch("assign_simt_kernel");
 }
 
-static int launch_bulk_sums(const float* X, int ld, long long n, int d, const int32_t* labels, int k, long long* S,
-                            long long* counts, FitState* st, cudaStream_t s) {
-  const size_t need = sizeof(long long) * ((size_t)k * ld + k);
-  const bool smem = need <= 96 * 1024;
-  const int threads = 256;
-  int blocks = smem ? sm_count() : blocks_for(n * 32, threads, 4);
-  if (smem) {
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(bulk_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      attr_set = true;
-    }
+static int launch_bulk_sums(const float* X, int ld, long long n, int d, const int32_t* labels, int k, long long* D,
+                            const FitState* st, cudaStream_t s) {
+  static int optin = 0;
+  if (!optin) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncSetAttribute(bulk_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
   }
-  bulk_sums_kernel<<<blocks, threads, smem ? need : 0, s>>>(X, ld, n, d, labels, k, S, counts, st, smem ? 1 : 0);
+  const int gsize = (int)round_up((size_t)d, 32);
+  const size_t per = sizeof(long long) * ((size_t)k * ld + k);
+  int groups = 0;
+  if (gsize <= 1024) groups = (int)std::min<size_t>(1024 / gsize, (size_t)(optin - 1024) / per);
+  groups = std::min(groups, 8);
+  if (groups >= 1) {
+    bulk_sums_kernel<<<sm_count(), groups * gsize, per * groups, s>>>(X, ld, n, d, labels, k, D, st, groups, gsize);
+  } else {
+    bulk_sums_kernel<<<blocks_for(n * 32, 256, 4), 256, 0, s>>>(X, ld, n, d, labels, k, D, st, 0, 0);
+  }
   return check_launch("bulk_sums_kernel");
 }
 
@@ -196,11 +202,14 @@ static int run_fit(const FitParams& p) {
   SKM_TRY(buf.alloc_n(&mind, (size_t)n));
   SKM_TRY(buf.alloc_n(&init_d, (size_t)k * d));
   SKM_TRY(buf.alloc_n(&labels, (size_t)n));
-  // payload: S (k*ld) | counts (k) | changed (1)
-  const size_t payload_len = (size_t)k * ld + k + 1;
-  SKM_TRY(buf.alloc_n(&S, payload_len));
+  // persistent sums of the current labels: S (k*ld) | counts (k)
+  SKM_TRY(buf.alloc_n(&S, (size_t)k * ld + k));
   long long* counts = S + (size_t)k * ld;
-  unsigned long long* changed = reinterpret_cast<unsigned long long*>(counts + k);
+  // per-iteration deltas (the all-reduced payload): dS (k*ld) | dcount (k) | changed (1)
+  const size_t payload_len = (size_t)k * ld + k + 1;
+  long long* D = nullptr;
+  SKM_TRY(buf.alloc_n(&D, payload_len));
+  unsigned long long* changed = reinterpret_cast<unsigned long long*>(D + (size_t)k * ld + k);
   SKM_TRY(buf.alloc_n(&colsum, (size_t)ld));
   SKM_TRY(buf.alloc_n(&st, 1));
   SKM_TRY(buf.alloc_n(&u32s, 2 + 512));
@@ -262,7 +271,8 @@ static int run_fit(const FitParams& p) {
                                      (double)n_total, d, &u32s[1]);
   SKM_TRY(check_launch("init_state_kernel"));
   SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n, s));  // label -1: every row changes in iteration 1
-  SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * payload_len, s));
+  SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
+  SKM_CUDA(cudaMemsetAsync(D, 0, sizeof(long long) * payload_len, s));
 
   // ---- E-step plan ---------------------------------------------------------
   EStepPlan plan;
@@ -291,6 +301,7 @@ static int run_fit(const FitParams& p) {
   ma.mind = mind;
   ma.S = S;
   ma.counts = counts;
+  ma.D = D;
   ma.changed = changed;
   float* shift_dev = nullptr;
   if (p.single_step) {
@@ -298,7 +309,6 @@ static int run_fit(const FitParams& p) {
     ma.shift_out = shift_dev;
   }
   ma.k = k;
-  ma.zero_sums = 1;
   ma.empty_ids = empty_ids;
   ma.hist = &u32s[2];
   ma.sel = sel;
@@ -351,16 +361,19 @@ static int run_fit(const FitParams& p) {
       const float* Cin = (it & 1) ? Cb1 : Cb0;
       float* Cout = (it & 1) ? Cb0 : Cb1;
       if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
+      // iteration 0 has no previous labels: sums are built in bulk afterwards;
+      // later iterations add the deltas of the rows that changed label
+      long long* Dinc = it == 0 ? nullptr : D;
       if (plan.tc) {
         centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cin, k, ld, d, bias, chi, clo, st);
         SKM_TRY(check_launch("centre_prep_kernel"));
-        SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, changed, st, dev_err, s));
+        SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, changed, Dinc, st, dev_err, s));
       } else {
-        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, mind, st, changed, 0, s));
+        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, mind, st, changed, Dinc, 0, s));
       }
       if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
-      SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, S, counts, st, s));
-      if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, S, payload_len, s));
+      if (it == 0) SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, D, st, s));
+      if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
       ma.C_old = Cin;
       ma.C_new = Cout;
       void* args[] = {&ma};
@@ -421,9 +434,9 @@ static int run_fit(const FitParams& p) {
     if (plan.tc) {
       centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cfin, k, ld, d, bias, chi, clo, nullptr);
       SKM_TRY(check_launch("centre_prep_kernel"));
-      SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, nullptr, nullptr, dev_err, s));
+      SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, nullptr, nullptr, nullptr, dev_err, s));
     } else {
-      SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, 0, s));
+      SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, nullptr, 0, s));
     }
   }
   inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials);
@@ -487,7 +500,7 @@ static int launch_assign_any(const float* X, int ld, long long n, int d, const f
     launch_assign_small(d, blocks, threads, smem, s, X, ld, n, C, k, labels, mind);
     return check_launch("assign_small_kernel");
   }
-  return launch_assign_simt(X, ld, n, d, C, k, labels, mind, nullptr, nullptr, 0, s);
+  return launch_assign_simt(X, ld, n, d, C, k, labels, mind, nullptr, nullptr, nullptr, 0, s);
 }
 
 struct Staged {

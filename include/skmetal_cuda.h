@@ -33,6 +33,7 @@ extern "C" {
 #define SKMETAL_FIT_PROFILE     0x4u  /* time every E-step launch with CUDA events (see fit stats) */
 #define SKMETAL_FIT_DISTRIBUTED 0x8u  /* X is this rank's shard; sums are all-reduced over the communicator */
 #define SKMETAL_FIT_TOL_ABS     0x10u /* tol is the absolute threshold on the sum of squared centre shifts */
+#define SKMETAL_FIT_BULK_SUMS   0x20u /* recompute the centroid sums from all rows every iteration (diagnostic) */
 
 /* ---- device / library management --------------------------------------- */
 
@@ -60,6 +61,14 @@ unsigned long long skmetal_launch_count(void);
 /* Host-side fault injection (tests): the `after_calls`-th guarded entry
  * point from now fails with `code` before doing any GPU work. */
 int skmetal_debug_inject_failure(int code, int after_calls);
+
+/* Tensor-core self-check (no reference counterpart): runs a 128 x 8 tf32 MMA
+ * probe on the current device. *mode = 0 when the tensor core truncates fp32
+ * operands to tf32, 1 when it rounds to nearest even, -1 when the result
+ * matches neither (the library then uses its SIMT E-step). raw3072, if not
+ * NULL, receives the probe's raw output (copied operand, products with the
+ * operand read from tensor memory, products with it read from shared memory). */
+int skmetal_debug_tc_probe(int* mode, uint32_t* raw3072);
 
 /* ---- KMeans path: reference entry points -------------------------------- */
 

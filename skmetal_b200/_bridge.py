@@ -34,6 +34,7 @@ FIT_SIMT = 0x2
 FIT_PROFILE = 0x4
 FIT_DISTRIBUTED = 0x8
 FIT_TOL_ABS = 0x10
+FIT_BULK_SUMS = 0x20
 
 _c_void_p, _c_size_t, _c_int, _c_float, _c_double = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
                                                       ctypes.c_float, ctypes.c_double)
@@ -50,6 +51,7 @@ _SIGNATURES = [
     ("skmetal_last_error", _c_int, [ctypes.c_char_p, _c_size_t]),
     ("skmetal_launch_count", ctypes.c_ulonglong, []),
     ("skmetal_debug_inject_failure", _c_int, [_c_int, _c_int]),
+    ("skmetal_debug_tc_probe", _c_int, [ctypes.POINTER(_c_int), _c_void_p]),
     ("skmetal_kmeans_assign", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t]),
     ("skmetal_kmeans_batch_fused", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t,
                                             _c_size_t, _c_size_t, _c_float, ctypes.POINTER(_c_i32)]),
@@ -265,7 +267,7 @@ def row_norm_sq(X) -> np.ndarray:
 # ----------------------------------------------------------------------------
 
 def kmeans_fit(X, init, max_iter: int, tol: float, *, center: bool = True, tol_abs: bool = False,
-               simt: bool = False, profile: bool = False, want_labels: bool = True):
+               simt: bool = False, profile: bool = False, want_labels: bool = True, bulk_sums: bool = False):
     """One Lloyd run from ``init`` (KMeans.fit semantics with n_init=1).
 
     Returns ``(centers, labels, inertia, n_iter)``; ``labels`` is None when
@@ -282,7 +284,7 @@ def kmeans_fit(X, init, max_iter: int, tol: float, *, center: bool = True, tol_a
     inertia = _c_double(0.0)
     n_iter = _c_i32(0)
     flags = (FIT_CENTER if center else 0) | (FIT_TOL_ABS if tol_abs else 0) | (FIT_SIMT if simt else 0) \
-        | (FIT_PROFILE if profile else 0)
+        | (FIT_PROFILE if profile else 0) | (FIT_BULK_SUMS if bulk_sums else 0)
     _bridge_call("skmetal_kmeans_fit", X, int(n), int(d), int(k), init, _c_i32(int(max_iter)), _c_double(tol),
                  _c_u32(flags), centers, labels if labels is not None else None, ctypes.byref(inertia),
                  ctypes.byref(n_iter))
@@ -390,6 +392,16 @@ def device_info() -> dict:
         raise RuntimeError(f"skmetal: device_info() failed: {_last_error()}")
     return {"name": name.value.decode("utf-8", "replace"), "max_threads_per_threadgroup": mt.value,
             "has_unified_memory": bool(un.value), "recommended_working_set_size_bytes": ws.value}
+
+
+def debug_tc_probe(raw: bool = False):
+    """Tensor-core self-check: (mode, raw) with mode 0 truncation, 1 rounding, -1 unusable."""
+    mode = _c_int(-3)
+    out = np.zeros(3072, dtype=np.uint32) if raw else None
+    rc = _fn("skmetal_debug_tc_probe")(ctypes.byref(mode), out.ctypes.data if raw else None)
+    if rc != 0:
+        raise RuntimeError(f"skmetal_debug_tc_probe failed with code {rc}: {_last_error()}")
+    return int(mode.value), out
 
 
 def debug_inject_failure(code: int, after_calls: int = 0) -> None:

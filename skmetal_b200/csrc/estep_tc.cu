@@ -1,33 +1,45 @@
 // Tensor-core E-step for sm_100a: labels[i] = argmin_j (||c_j||^2 - 2 x_i . c_j)
-// for 128-row tiles of X, with the dot products computed by tcgen05.mma in
-// 3xTF32 (x = x_hi + x_lo, c = c_hi + c_lo; x_hi.c_hi + x_hi.c_lo + x_lo.c_hi,
-// accumulated in fp32 in tensor memory). The n x k distance matrix never
-// leaves the SM: the epilogue reads each row's k accumulators from TMEM and
-// keeps a running argmin in registers (strict '<', lowest index first, as
-// sklearn/cluster/_k_means_lloyd.pyx:205-213).
+// over 128-row tiles of X, with the dot products computed by tcgen05.mma in
+// 3xTF32 split precision and accumulated in fp32 in tensor memory (TMEM):
+//     x . c  ~=  T(x).T(c) + T(x).c_lo + x_lo.T(c)
+// where T is the tensor core's own fp32 -> tf32 conversion (measured once per
+// device by tc_probe), x_lo = x - T(x) and c_lo = c - T(c). The n x k
+// distance matrix never leaves the SM: the epilogue reads each row's k
+// accumulators from TMEM and keeps a running argmin in registers (strict '<',
+// lowest index first, as sklearn/cluster/_k_means_lloyd.pyx:205-213). Rows
+// whose label changed add their exact fixed-point deltas to the centroid sums
+// (the incremental M-step input).
 //
-// CTA = 6 warps, persistent over row tiles (tile t handled by CTA t % grid):
-//   warp 0      TMA producer: X tiles (2-stage ring), centre tiles once
-//   warp 1      TMEM owner + MMA issuer (one elected lane)
-//   warps 2..5  per tile: split X into tf32 hi (in place) / lo and compute
-//               ||x||^2 (converter), then read the accumulators of the
-//               previous tile and take the argmin (epilogue); thread r of the
-//               group owns TMEM lane / tile row r.
-// Shared-memory layout of a tile: K is cut into 8-column chunks (32 bytes
-// per row); chunk c of a 128-row tile occupies 4 KB in the canonical
-// K-major SWIZZLE_32B layout that TMA writes and UMMA reads (8-row atoms of
-// 256 bytes). Columns past d are zero (TMA out-of-bounds fill).
+// Data path of one tile (all asynchronous, one CTA per SM, persistent):
+//   HBM --TMA--> smem stage --tcgen05.cp--> TMEM x (A operand, 2 buffers)
+//   converter warps: TMEM x --tcgen05.ld--> regs --> x_lo --tcgen05.st--> TMEM
+//   MMA thread: acc  = x.C_lo + x.C_hi        (A = x from TMEM, B = smem)
+//               acc += x_lo.C_hi              (A = x_lo from TMEM)
+//   epilogue warps: TMEM acc --tcgen05.ld--> argmin --> labels, deltas
+// so shared memory only carries the TMA write, one read by tcgen05.cp and the
+// small centre operands: X is read from HBM exactly once.
+//
+// Warp roles (320 threads): 0 TMA producer, 1 TMEM owner + MMA/cp issuer,
+// 2-5 converter, 6-9 epilogue; warp w of the converter / epilogue groups owns
+// TMEM lanes 32*(w%4) .. +31 (= tile rows).
+//
+// Shared-memory tiles: K is cut into 8-column chunks (32 bytes per row);
+// chunk c of a 128-row tile is 4 KB in the canonical K-major SWIZZLE_32B
+// layout (8-row atoms of 256 bytes) that TMA writes and tcgen05 reads.
+// Columns past d are zero (TMA out-of-bounds fill).
 //
 // Every mbarrier wait is bounded in time; on timeout the CTA records an error
-// code, stops issuing work, waits for its own in-flight copies and MMAs,
-// frees its tensor memory and returns.
+// code, stops issuing work, waits (bounded) for its own in-flight copies and
+// tensor-core operations, frees its tensor memory and returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <vector>
 
 #include "device_util.cuh"
 #include "driver.h"
@@ -37,30 +49,32 @@ namespace skm {
 
 namespace tc {
 
-constexpr int BM = 128;          // rows per tile (UMMA M)
-constexpr int KC = 8;            // fp32 columns per K chunk (UMMA K for tf32)
+constexpr int BM = 128;                   // rows per tile (UMMA M)
+constexpr int KC = 8;                     // fp32 columns per K chunk (UMMA K for tf32)
 constexpr int CHUNK_BYTES = BM * KC * 4;  // 4096
-constexpr int MAX_NK = 16;       // d <= 128
-constexpr int MAX_KPAD = 256;    // k <= 256 (one UMMA N)
-constexpr int THREADS = 192;
-constexpr int NUM_BARS = 12;
+constexpr int MAX_NK = 16;                // d <= 128
+constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
+constexpr int THREADS = 320;
+constexpr int MAX_STAGES = 4;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
-
-enum Bar { FULL0 = 0, FULL1, EMPTY0, EMPTY1, LO_FULL, LO_EMPTY, ACC_FULL0, ACC_FULL1, ACC_EMPTY0, ACC_EMPTY1,
-           C_FULL, MMA_DONE };
 
 struct Params {
   int n_tiles;
   long long n;
   int k;
   int k_pad;
-  int nk;         // K chunks
-  const float* bias;   // ||c||^2, k entries
+  int nk;      // K chunks of 8 columns
+  int stages;  // X stages in shared memory
+  int nbx;     // x buffers in TMEM (1 or 2)
+  int nba;     // accumulator buffers in TMEM (1 or 2)
+  int xcols;   // TMEM columns of one x buffer (>= 8 nk, multiple of 32)
+  int tmem_cols;
+  int round_mode;  // fp32->tf32 conversion of the tensor core: 0 truncate, 1 nearest-even
+  const float* bias;  // ||c||^2, k entries
   int32_t* labels;
-  float* mind;    // ||x||^2 + min_j (||c_j||^2 - 2 x.c_j)
   unsigned long long* changed;
-  long long* D;        // nullable: incremental deltas of rows that changed label
-  const float* X;      // rows (global) for the deltas
+  long long* D;  // nullable: incremental deltas of rows that changed label
+  const float* X;
   int ld;
   int d;
   const FitState* st;  // nullable: skip when st->done
@@ -101,7 +115,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false on timeout or when another thread aborted.
+// Bounded wait: false on timeout (after recording `code`) or when another
+// thread of the CTA aborted.
 __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
@@ -125,16 +140,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// K-major SWIZZLE_32B UMMA shared-memory descriptor: rows of 32 bytes, 8-row
-// atoms of 256 bytes (stride byte offset), leading byte offset unused (1),
-// descriptor version 1 (sm_100), layout type 6 (SWIZZLE_32B).
+// K-major SWIZZLE_32B shared-memory matrix descriptor: rows of 32 bytes,
+// 8-row atoms of 256 bytes (stride byte offset), leading byte offset unused
+// (1), descriptor version 1 (sm_100), layout type 6 (SWIZZLE_32B).
 __device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;                 // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(256u >> 4) << 32;        // SBO = 256 B
-  d |= (uint64_t)1u << 46;                 // version
-  d |= (uint64_t)6u << 61;                 // SWIZZLE_32B
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(256u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)6u << 61;
   return d;
 }
 
@@ -143,8 +158,9 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D[tmem] (+)= A[smem] . B[smem]^T
+__device__ __forceinline__ void mma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -153,53 +169,96 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
+// D[tmem] (+)= A[tmem] . B[smem]^T
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 128 rows x 8 fp32 (one chunk) from shared memory into TMEM lanes 0..127
+__device__ __forceinline__ void tmem_cp_chunk(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void named_bar(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+
+// The tensor core's fp32 -> tf32 conversion: 0 = truncate the low 13 mantissa
+// bits, 1 = round to nearest even at bit 13 (finite inputs).
+__host__ __device__ __forceinline__ uint32_t to_tf32_bits(uint32_t u, int mode) {
+  if (mode == 0) return u & 0xffffe000u;
+  const uint32_t lsb = (u >> 13) & 1u;
+  return (u + 0x0fffu + lsb) & 0xffffe000u;
 }
 
-__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
-
 struct Smem {
-  // byte offsets from the 1024-aligned dynamic smem base
-  uint32_t x[2], xlo, chi, clo, bias, nx, bars, misc;
-  uint32_t total;
+  uint32_t x[MAX_STAGES], chi, clo, bias, bars, misc, total;
 };
 
-__host__ __device__ inline Smem smem_layout(int nk, int k_pad) {
+// barrier indices
+__host__ __device__ constexpr int B_FULL(int s) { return s; }
+__host__ __device__ constexpr int B_EMPTY(int s) { return MAX_STAGES + s; }
+__host__ __device__ constexpr int B_XT(int b) { return 2 * MAX_STAGES + b; }  // x tile in TMEM
+__host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + 2 + a; }
+__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + 4 + a; }
+constexpr int B_XLO_FULL = 2 * MAX_STAGES + 6;
+constexpr int B_XLO_FREE = 2 * MAX_STAGES + 7;
+constexpr int B_C_FULL = 2 * MAX_STAGES + 8;
+constexpr int B_DONE = 2 * MAX_STAGES + 9;
+constexpr int NUM_BARS = 2 * MAX_STAGES + 10;
+
+__host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
   Smem s;
   uint32_t off = 0;
   const uint32_t stage = (uint32_t)nk * CHUNK_BYTES;
-  s.x[0] = off; off += stage;
-  s.x[1] = off; off += stage;
-  s.xlo = off; off += stage;
-  s.chi = off; off += (uint32_t)nk * k_pad * 32;
-  s.clo = off; off += (uint32_t)nk * k_pad * 32;
-  s.bias = off; off += (uint32_t)k_pad * 4;
-  s.nx = off; off += 2 * BM * 4;
+  for (int i = 0; i < MAX_STAGES; ++i) {
+    s.x[i] = off;
+    if (i < stages) off += stage;
+  }
+  s.chi = off;
+  off += (uint32_t)nk * k_pad * 32;
+  s.clo = off;
+  off += (uint32_t)nk * k_pad * 32;
+  s.bias = off;
+  off += (uint32_t)k_pad * 4;
   off = (off + 15) & ~15u;
-  s.bars = off; off += NUM_BARS * 8;
-  s.misc = off; off += 16;  // [0] tmem base, [1] abort flag
-  s.total = off + 1024;     // slack for aligning the base to 1024
+  s.bars = off;
+  off += NUM_BARS * 8;
+  s.misc = off;
+  off += 16;             // [0] tmem base, [1] abort flag
+  s.total = off + 1024;  // slack for aligning the base to 1024
   return s;
 }
 
@@ -208,41 +267,40 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
                 const __grid_constant__ CUtensorMap tmap_clo, Params p) {
   if (p.st && p.st->done) return;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Smem L = smem_layout(p.nk, p.k_pad);
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Smem L = smem_layout(p.nk, p.k_pad, p.stages);
   const uint32_t sbase = smem_u32(base);
   const uint32_t bar0 = sbase + L.bars;
   auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   uint32_t* misc = reinterpret_cast<uint32_t*>(base + L.misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
   float* bias_s = reinterpret_cast<float*>(base + L.bias);
-  float* nx_s = reinterpret_cast<float*>(base + L.nx);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int my_tiles = (p.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const uint32_t stage_bytes = (uint32_t)p.nk * CHUNK_BYTES;
   const uint32_t cbytes = (uint32_t)p.nk * p.k_pad * 32;
-  const int tmem_cols_alloc = (2 * p.k_pad <= 32) ? 32 : (2 * p.k_pad <= 64) ? 64 : (2 * p.k_pad <= 128) ? 128
-                              : (2 * p.k_pad <= 256) ? 256 : 512;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(FULL0), 1);
-    mbar_init(bar(FULL1), 1);
-    mbar_init(bar(EMPTY0), 1);
-    mbar_init(bar(EMPTY1), 1);
-    mbar_init(bar(LO_FULL), 128);
-    mbar_init(bar(LO_EMPTY), 1);
-    mbar_init(bar(ACC_FULL0), 1);
-    mbar_init(bar(ACC_FULL1), 1);
-    mbar_init(bar(ACC_EMPTY0), 128);
-    mbar_init(bar(ACC_EMPTY1), 128);
-    mbar_init(bar(C_FULL), 1);
-    mbar_init(bar(MMA_DONE), 1);
+    for (int s = 0; s < MAX_STAGES; ++s) {
+      mbar_init(bar(B_FULL(s)), 1);
+      mbar_init(bar(B_EMPTY(s)), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(B_XT(b)), 1);
+      mbar_init(bar(B_ACC_FULL(b)), 1);
+      mbar_init(bar(B_ACC_EMPTY(b)), 128);
+    }
+    mbar_init(bar(B_XLO_FULL), 128);
+    mbar_init(bar(B_XLO_FREE), 1);
+    mbar_init(bar(B_C_FULL), 1);
+    mbar_init(bar(B_DONE), 1);
     misc[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + L.misc),
-                 "r"(tmem_cols_alloc));
+                 "r"(p.tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   for (int j = threadIdx.x; j < p.k_pad; j += blockDim.x) bias_s[j] = j < p.k ? p.bias[j] : INFINITY;
@@ -250,142 +308,158 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = misc[0];
+  // TMEM column map: x[0..nbx) | x_lo | acc[0..nba)
+  const uint32_t col_xlo = (uint32_t)(p.nbx * p.xcols);
+  const uint32_t col_acc = col_xlo + (uint32_t)p.xcols;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      mbar_expect_tx(bar(C_FULL), 2 * cbytes);
+      mbar_expect_tx(bar(B_C_FULL), 2 * cbytes);
       for (int c = 0; c < p.nk; ++c) {
-        tma_load_2d(sbase + L.chi + (uint32_t)c * p.k_pad * 32, &tmap_chi, c * KC, 0, bar(C_FULL));
-        tma_load_2d(sbase + L.clo + (uint32_t)c * p.k_pad * 32, &tmap_clo, c * KC, 0, bar(C_FULL));
+        tma_load_2d(sbase + L.chi + (uint32_t)c * p.k_pad * 32, &tmap_chi, c * KC, 0, bar(B_C_FULL));
+        tma_load_2d(sbase + L.clo + (uint32_t)c * p.k_pad * 32, &tmap_clo, c * KC, 0, bar(B_C_FULL));
       }
       int armed = 0;
       for (int i = 0; i < my_tiles; ++i) {
-        const int s = i & 1;
-        if (!mbar_wait(bar(EMPTY0 + s), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2101)) break;
+        const int s = i % p.stages;
+        if (!mbar_wait(bar(B_EMPTY(s)), ((i / p.stages) & 1) ^ 1, abort_flag, p.err, 2101)) break;
         const int tile = (int)blockIdx.x + i * (int)gridDim.x;
-        mbar_expect_tx(bar(FULL0 + s), stage_bytes);
+        mbar_expect_tx(bar(B_FULL(s)), stage_bytes);
         for (int c = 0; c < p.nk; ++c)
-          tma_load_2d(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES, &tmap_x, c * KC, tile * BM, bar(FULL0 + s));
+          tma_load_2d(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES, &tmap_x, c * KC, tile * BM, bar(B_FULL(s)));
         armed = i + 1;
       }
-      // drain: wait for our own copies before the CTA can exit
+      // our own copies must land before the CTA may exit
       volatile int no_abort = 0;
-      mbar_wait(bar(C_FULL), 0, &no_abort, p.err, 2102);
-      for (int i = (armed > 2 ? armed - 2 : 0); i < armed; ++i)
-        mbar_wait(bar(FULL0 + (i & 1)), (i >> 1) & 1, &no_abort, p.err, 2103);
+      mbar_wait(bar(B_C_FULL), 0, &no_abort, p.err, 2102);
+      for (int i = (armed > p.stages ? armed - p.stages : 0); i < armed; ++i)
+        mbar_wait(bar(B_FULL(i % p.stages)), (i / p.stages) & 1, &no_abort, p.err, 2103);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // -------------------------------------------------- cp + MMA issuer (1 lane)
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(p.k_pad);
-      bool ok = mbar_wait(bar(C_FULL), 0, abort_flag, p.err, 2201);
-      for (int i = 0; ok && i < my_tiles; ++i) {
-        const int s = i & 1, b = i & 1;
-        if (!mbar_wait(bar(FULL0 + s), (i >> 1) & 1, abort_flag, p.err, 2202)) break;
-        if (!mbar_wait(bar(LO_FULL), i & 1, abort_flag, p.err, 2203)) break;
-        if (!mbar_wait(bar(ACC_EMPTY0 + b), ((i >> 1) & 1) ^ 1, abort_flag, p.err, 2204)) break;
+      bool ok = mbar_wait(bar(B_C_FULL), 0, abort_flag, p.err, 2201);
+      tc_fence_after();
+      // tile i: smem stage -> TMEM x[i % nbx]; tcgen05 operations issued by
+      // this thread execute in issue order, so the MMAs that follow read the
+      // copied values
+      auto issue_cp = [&](int i) -> bool {
+        const int s = i % p.stages;
+        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) return false;
         tc_fence_after();
-        const uint32_t tacc = tmem_base + (uint32_t)(b * p.k_pad);
+        const uint32_t tx = tmem_base + (uint32_t)((i % p.nbx) * p.xcols);
+        for (int c = 0; c < p.nk; ++c)
+          tmem_cp_chunk(tx + (uint32_t)(c * KC), sw32_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES));
+        tc_commit(bar(B_XT(i % p.nbx)));
+        tc_commit(bar(B_EMPTY(s)));
+        return true;
+      };
+      if (ok && my_tiles > 0) ok = issue_cp(0);
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int a = i % p.nba;
+        if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nba) & 1) ^ 1, abort_flag, p.err, 2203)) break;
+        tc_fence_after();
+        const uint32_t tacc = tmem_base + col_acc + (uint32_t)(a * p.k_pad);
+        const uint32_t tx = tmem_base + (uint32_t)((i % p.nbx) * p.xcols);
         for (int c = 0; c < p.nk; ++c) {
-          const uint64_t a_hi = sw32_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES);
-          const uint64_t a_lo = sw32_desc(sbase + L.xlo + (uint32_t)c * CHUNK_BYTES);
           const uint64_t b_hi = sw32_desc(sbase + L.chi + (uint32_t)c * p.k_pad * 32);
           const uint64_t b_lo = sw32_desc(sbase + L.clo + (uint32_t)c * p.k_pad * 32);
-          mma_tf32(tacc, a_lo, b_hi, idesc, c > 0 ? 1u : 0u);
-          mma_tf32(tacc, a_hi, b_lo, idesc, 1u);
-          mma_tf32(tacc, a_hi, b_hi, idesc, 1u);
+          mma_ts(tacc, tx + (uint32_t)(c * KC), b_lo, idesc, c > 0 ? 1u : 0u);
+          mma_ts(tacc, tx + (uint32_t)(c * KC), b_hi, idesc, 1u);
         }
-        mma_commit(bar(ACC_FULL0 + b));
-        mma_commit(bar(EMPTY0 + s));
-        mma_commit(bar(LO_EMPTY));
+        // x_lo of this tile; its converter waited for the previous tile's
+        // MMAs, so every MMA of tile i-1 is complete past this point
+        if (!mbar_wait(bar(B_XLO_FULL), i & 1, abort_flag, p.err, 2204)) break;
+        tc_fence_after();
+        for (int c = 0; c < p.nk; ++c) {
+          const uint64_t b_hi = sw32_desc(sbase + L.chi + (uint32_t)c * p.k_pad * 32);
+          mma_ts(tacc, tmem_base + col_xlo + (uint32_t)(c * KC), b_hi, idesc, 1u);
+        }
+        tc_commit(bar(B_ACC_FULL(a)));
+        tc_commit(bar(B_XLO_FREE));
+        if (i + 1 < my_tiles) {
+          if (p.nbx == 1) {
+            // single x buffer: tile i's MMAs must be done before it is refilled
+            if (!mbar_wait(bar(B_XLO_FREE), i & 1, abort_flag, p.err, 2205)) break;
+          }
+          if (!issue_cp(i + 1)) break;
+        }
       }
-      // all MMAs issued by this thread are complete once MMA_DONE fires
-      mma_commit(bar(MMA_DONE));
+      // every tcgen05 operation issued by this thread is complete once DONE fires
+      tc_commit(bar(B_DONE));
       volatile int no_abort = 0;
-      mbar_wait(bar(MMA_DONE), 0, &no_abort, p.err, 2205);
+      mbar_wait(bar(B_DONE), 0, &no_abort, p.err, 2206);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- converter
+    const int q = warp & 3;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i % p.nbx;
+      if (!mbar_wait(bar(B_XT(b)), (i / p.nbx) & 1, abort_flag, p.err, 2301)) break;
+      if (!mbar_wait(bar(B_XLO_FREE), (i & 1) ^ 1, abort_flag, p.err, 2302)) break;
+      tc_fence_after();
+      const uint32_t tx = tmem_base + lane_off + (uint32_t)(b * p.xcols);
+      const uint32_t tl = tmem_base + lane_off + col_xlo;
+      for (int c = 0; c < p.nk; ++c) {
+        uint32_t r[8];
+        tmem_ld8(tx + (uint32_t)(c * KC), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float v = __uint_as_float(r[e]);
+          r[e] = __float_as_uint(v - __uint_as_float(to_tf32_bits(r[e], p.round_mode)));
+        }
+        tmem_st8(tl + (uint32_t)(c * KC), r);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar(B_XLO_FULL));
     }
   } else {
-    // ------------------------------------------------ converter + epilogue
-    const int q = warp & 3;            // TMEM lane quarter of this warp
-    const int row = q * 32 + lane;     // tile row owned in the epilogue
-    const int ct = threadIdx.x - 64;   // 0..127 within the group
-    bool ok = true;
-    for (int i = 0; i <= my_tiles; ++i) {
-      // ---- converter for tile i
-      if (ok && i < my_tiles) {
-        const int s = i & 1;
-        ok = mbar_wait(bar(FULL0 + s), (i >> 1) & 1, abort_flag, p.err, 2301) &&
-             mbar_wait(bar(LO_EMPTY), (i & 1) ^ 1, abort_flag, p.err, 2302);
-        if (ok) {
-          // flat pass over the tile: float4 index f = ct + 128*j covers rows
-          // (ct>>1) and (ct>>1)+64 of every chunk, half (ct&1) of each row
-          float4* xs = reinterpret_cast<float4*>(base + L.x[s]);
-          float4* xl = reinterpret_cast<float4*>(base + L.xlo);
-          float na = 0.f, nb = 0.f;
-          const int nf4 = p.nk * (CHUNK_BYTES / 16);
-          for (int f = ct, j = 0; f < nf4; f += 128, ++j) {
-            float4 v = xs[f];
-            float4 h = make_float4(tf32_trunc(v.x), tf32_trunc(v.y), tf32_trunc(v.z), tf32_trunc(v.w));
-            xs[f] = h;
-            xl[f] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-            const float sq = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            if (j & 1) nb += sq; else na += sq;
-          }
-          na += __shfl_xor_sync(0xffffffffu, na, 1);
-          nb += __shfl_xor_sync(0xffffffffu, nb, 1);
-          if ((ct & 1) == 0) {
-            nx_s[(i & 1) * BM + (ct >> 1)] = na;
-            nx_s[(i & 1) * BM + (ct >> 1) + 64] = nb;
-          }
-          fence_async_smem();
-          mbar_arrive(bar(LO_FULL));
-        }
-      }
-      named_bar(1, 128);  // nx of tile i visible; epilogue of tile i-1 may read nx[(i-1)&1]
-      // ---- epilogue for tile i-1
-      if (ok && i > 0) {
-        const int t = i - 1, b = t & 1;
-        ok = mbar_wait(bar(ACC_FULL0 + b), (t >> 1) & 1, abort_flag, p.err, 2303);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * p.k_pad);
-          float best = INFINITY;
-          int bl = 0;
-          for (int j0 = 0; j0 < p.k_pad; j0 += 16) {
-            float v[16];
-            tmem_ld16(taddr + (uint32_t)j0, v);
-            tmem_ld_wait();
+    // ----------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int a = i % p.nba;
+      if (!mbar_wait(bar(B_ACC_FULL(a)), (i / p.nba) & 1, abort_flag, p.err, 2401)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + lane_off + col_acc + (uint32_t)(a * p.k_pad);
+      float best = INFINITY;
+      int bl = 0;
+      for (int j0 = 0; j0 < p.k_pad; j0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(taddr + (uint32_t)j0, v);
+        tmem_ld_wait();
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const float dist = fmaf(-2.0f, v[jj], bias_s[j0 + jj]);
-              if (dist < best) {
-                best = dist;
-                bl = j0 + jj;
-              }
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(bar(ACC_EMPTY0 + b));
-          const long long grow = (long long)((int)blockIdx.x + t * (int)gridDim.x) * BM + row;
-          bool ch = false;
-          int old = -1;
-          if (grow < p.n) {
-            if (p.changed) {
-              old = p.labels[grow];
-              ch = old != bl;
-            }
-            p.labels[grow] = bl;
-            if (p.mind) p.mind[grow] = best + nx_s[b * BM + row];
-          }
-          if (p.changed) {
-            const unsigned int m = __ballot_sync(0xffffffffu, ch);
-            if (lane == 0 && m) atomicAdd(p.changed, (unsigned long long)__popc(m));
-            if (p.D) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, p.D, p.st->scale);
+        for (int jj = 0; jj < 16; ++jj) {
+          const float dist = fmaf(-2.0f, __uint_as_float(v[jj]), bias_s[j0 + jj]);
+          if (dist < best) {
+            best = dist;
+            bl = j0 + jj;
           }
         }
       }
-      named_bar(1, 128);  // nx[(i-1)&1] consumed before tile i+1 overwrites it
+      tc_fence_before();
+      mbar_arrive(bar(B_ACC_EMPTY(a)));
+      const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
+      bool ch = false;
+      int old = -1;
+      if (grow < p.n) {
+        if (p.changed) {
+          old = p.labels[grow];
+          ch = old != bl;
+        }
+        p.labels[grow] = bl;
+      }
+      if (p.changed) {
+        const unsigned int m = __ballot_sync(0xffffffffu, ch);
+        if (lane == 0 && m) atomicAdd(p.changed, (unsigned long long)__popc(m));
+        if (p.D) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, p.D, p.st->scale);
+      }
     }
   }
 
@@ -393,7 +467,89 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols_alloc));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// probe: tcgen05.cp layout and the tensor core's fp32 -> tf32 conversion
+// ---------------------------------------------------------------------------
+// A (128 x 8) holds fp32 values whose dropped mantissa bits distinguish
+// truncation from rounding (rows 64..127 negative); B (16 x 8) is the identity
+// on its first 8 rows, so D[m][n] = tf32(A[m][n]) for n < 8. out: [0,1024) the
+// TMEM copy of A made by tcgen05.cp, [1024,2048) D with A read from TMEM,
+// [2048,3072) D with A read from shared memory, [3072] error code.
+__host__ __device__ __forceinline__ uint32_t probe_bits(int m, int k) {
+  const uint32_t low = 0x1000u | ((uint32_t)(m * 8 + k) & 0x0fffu);
+  return 0x3f800000u | ((uint32_t)k << 13) | low | (m >= 64 ? 0x80000000u : 0u);
+}
+
+__global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
+  __shared__ __align__(1024) unsigned char sm[CHUNK_BYTES + 512 + 64];
+  const uint32_t sa = smem_u32(sm), sb = sa + CHUNK_BYTES, sbar = sb + 512;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + CHUNK_BYTES + 512 + 16);
+  const uint32_t smisc = smem_u32(misc);
+  int* err = reinterpret_cast<int*>(out + 3072);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  // SWIZZLE_32B: bit 4 of the byte offset is XORed with bit 7
+  auto sw32 = [](uint32_t off) { return off ^ (((off >> 7) & 1u) << 4); };
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<uint32_t*>(sm + sw32((uint32_t)(tid * 32 + k * 4))) = probe_bits(tid, k);
+  if (tid < 16)
+    for (int k = 0; k < 8; ++k)
+      *reinterpret_cast<float*>(sm + CHUNK_BYTES + sw32((uint32_t)(tid * 32 + k * 4))) = (tid == k) ? 1.0f : 0.0f;
+  if (tid == 0) {
+    mbar_init(sbar, 1);
+    misc[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smisc), "r"(32));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = misc[0];
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
+  // TMEM columns: [0,8) copy of A, [8,24) D (A from TMEM); then [16,32) D (A from smem)
+  if (tid == 0) {
+    const uint32_t idesc = idesc_tf32(16);
+    tmem_cp_chunk(tb, sw32_desc(sa));
+    mma_ts(tb + 8, tb, sw32_desc(sb), idesc, 0u);
+    tc_commit(sbar);
+  }
+  __syncwarp();
+  mbar_wait(sbar, 0, abort_flag, err, 2501);
+  tc_fence_after();
+  const uint32_t lo = (uint32_t)(warp * 32) << 16;
+  uint32_t r[8];
+  tmem_ld8(tb + lo, r);
+  tmem_ld_wait();
+  for (int e = 0; e < 8; ++e) out[tid * 8 + e] = r[e];
+  tmem_ld8(tb + lo + 8, r);
+  tmem_ld_wait();
+  for (int e = 0; e < 8; ++e) out[1024 + tid * 8 + e] = r[e];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+    const uint32_t idesc = idesc_tf32(16);
+    mma_ss(tb + 16, sw32_desc(sa), sw32_desc(sb), idesc, 0u);
+    tc_commit(sbar);
+  }
+  __syncwarp();
+  mbar_wait(sbar, 1, abort_flag, err, 2502);
+  tc_fence_after();
+  tmem_ld8(tb + lo + 16, r);
+  tmem_ld_wait();
+  for (int e = 0; e < 8; ++e) out[2048 + tid * 8 + e] = r[e];
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tb), "r"(32));
   }
 }
 
@@ -444,8 +600,66 @@ static int make_map(CUtensorMap* m, const float* ptr, int ld, long long rows, in
   return OK;
 }
 
+// Per-device probe result: -2 not run, -1 unusable, 0 truncation, 1 rounding.
+static int g_probe_mode[64];
+static bool g_probe_init = false;
+
+int tc_probe(int* mode_out, uint32_t* raw_out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!g_probe_init) {
+    for (int& m : g_probe_mode) m = -2;
+    g_probe_init = true;
+  }
+  if (dev < 64 && g_probe_mode[dev] != -2 && !raw_out) {
+    *mode_out = g_probe_mode[dev];
+    return OK;
+  }
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  uint32_t* d_out = nullptr;
+  SKM_CUDA(cudaMallocAsync(&d_out, 3073 * 4, s));
+  SKM_CUDA(cudaMemsetAsync(d_out, 0, 3073 * 4, s));
+  tc::tc_probe_kernel<<<1, 128, 0, s>>>(d_out);
+  int rc = check_launch("tc_probe_kernel");
+  std::vector<uint32_t> h(3073, 0);
+  if (rc == OK) {
+    cudaMemcpyAsync(h.data(), d_out, 3073 * 4, cudaMemcpyDeviceToHost, s);
+    if (cudaStreamSynchronize(s) != cudaSuccess) rc = ERR_CUDA;
+  }
+  cudaFreeAsync(d_out, s);
+  if (rc != OK) {
+    set_error(ERR_CUDA, "tensor-core probe failed to run");
+    return rc;
+  }
+  if (raw_out) memcpy(raw_out, h.data(), 3072 * 4);
+  int mode = -1;
+  bool copy_ok = h[3072] == 0;
+  for (int m = 0; m < 128 && copy_ok; ++m)
+    for (int k = 0; k < 8; ++k)
+      if (h[m * 8 + k] != tc::probe_bits(m, k)) copy_ok = false;
+  if (copy_ok) {
+    for (int cand = 0; cand < 2 && mode < 0; ++cand) {
+      bool ok = true;
+      for (int m = 0; m < 128 && ok; ++m)
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t want = tc::to_tf32_bits(h[m * 8 + k], cand);
+          if (h[1024 + m * 8 + k] != want || h[2048 + m * 8 + k] != want) {
+            ok = false;
+            break;
+          }
+        }
+      if (ok) mode = cand;
+    }
+  }
+  if (dev < 64) g_probe_mode[dev] = mode;
+  *mode_out = mode;
+  return OK;
+}
+
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->supported = false;
+  if (getenv("SKMETAL_DISABLE_TC")) return OK;
   if (!encode_fn()) return OK;
   if (d > tc::MAX_NK * tc::KC || k > tc::MAX_KPAD || n < 1) return OK;
   if ((reinterpret_cast<uintptr_t>(X) & 15) || ((ld * 4) & 15)) return OK;
@@ -454,6 +668,10 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   if (major != 10) return OK;
+  int mode = -1;
+  SKM_TRY(tc_probe(&mode, nullptr));
+  if (mode < 0) return OK;  // unexpected tensor-core behaviour: use the SIMT E-step
+  plan->round_mode = mode;
   plan->X = X;
   plan->ld = ld;
   plan->n = n;
@@ -461,9 +679,28 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->k = k;
   plan->k_pad = (int)round_up((size_t)k, 16);
   plan->k_steps = (ld + tc::KC - 1) / tc::KC;
-  const tc::Smem L = tc::smem_layout(plan->k_steps, plan->k_pad);
-  plan->smem = L.total;
-  if ((int)plan->smem > optin) return OK;
+  // TMEM: x buffers (32-column aligned), one x_lo buffer, accumulators
+  plan->xcols = (int)round_up((size_t)plan->k_steps * tc::KC, 32);
+  plan->nbx = 2;
+  plan->nba = 2;
+  auto cols = [&]() { return (plan->nbx + 1) * plan->xcols + plan->nba * plan->k_pad; };
+  if (cols() > 512) plan->nba = 1;
+  if (cols() > 512) plan->nbx = 1;
+  if (cols() > 512) return OK;
+  int tcols = 32;
+  while (tcols < cols()) tcols *= 2;
+  plan->tmem_cols = tcols;
+  // shared memory: as many X stages as fit (2..4)
+  plan->stages = 0;
+  for (int st = tc::MAX_STAGES; st >= 2; --st) {
+    const tc::Smem L = tc::smem_layout(plan->k_steps, plan->k_pad, st);
+    if ((int)L.total <= optin) {
+      plan->stages = st;
+      plan->smem = L.total;
+      break;
+    }
+  }
+  if (plan->stages == 0) return OK;
   const int n_tiles = (int)((n + tc::BM - 1) / tc::BM);
   plan->grid = std::min(n_tiles, sm_count());
   SKM_TRY(make_map(&plan->tmap_x, X, ld, n, tc::BM));
@@ -476,20 +713,28 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   return OK;
 }
 
-int tc_estep(const TcPlan& plan, const float* Chi, const float* Clo, const float* bias, int32_t* labels, float* mind,
-             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s) {
-  CUtensorMap mhi, mlo;
-  SKM_TRY(make_map(&mhi, Chi, plan.ld, plan.k, plan.k_pad));
-  SKM_TRY(make_map(&mlo, Clo, plan.ld, plan.k, plan.k_pad));
+int tc_set_centres(TcPlan* plan, const float* Chi, const float* Clo) {
+  SKM_TRY(make_map(&plan->tmap_chi, Chi, plan->ld, plan->k, plan->k_pad));
+  SKM_TRY(make_map(&plan->tmap_clo, Clo, plan->ld, plan->k, plan->k_pad));
+  return OK;
+}
+
+int tc_estep(const TcPlan& plan, const float* bias, int32_t* labels, unsigned long long* changed, long long* D,
+             const FitState* st, int* err, cudaStream_t s) {
   tc::Params p;
   p.n_tiles = (int)((plan.n + tc::BM - 1) / tc::BM);
   p.n = plan.n;
   p.k = plan.k;
   p.k_pad = plan.k_pad;
   p.nk = plan.k_steps;
+  p.stages = plan.stages;
+  p.nbx = plan.nbx;
+  p.nba = plan.nba;
+  p.xcols = plan.xcols;
+  p.tmem_cols = plan.tmem_cols;
+  p.round_mode = plan.round_mode;
   p.bias = bias;
   p.labels = labels;
-  p.mind = mind;
   p.changed = changed;
   p.D = D;
   p.X = plan.X;
@@ -497,8 +742,10 @@ int tc_estep(const TcPlan& plan, const float* Chi, const float* Clo, const float
   p.d = plan.d;
   p.st = st;
   p.err = err;
-  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(plan.tmap_x, mhi, mlo, p);
+  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(plan.tmap_x, plan.tmap_chi, plan.tmap_clo, p);
   return check_launch("estep_tc_kernel");
 }
 
 }  // namespace skm
+
+extern "C" int skmetal_debug_tc_probe(int* mode, uint32_t* raw3072) { return skm::tc_probe(mode, raw3072); }

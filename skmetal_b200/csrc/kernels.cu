@@ -540,6 +540,22 @@ __global__ void mstep_kernel(MStepArgs a) {
   if (n_empty > 0) {
     int m_cand = n_empty;
     if (a.cand_row == nullptr) {
+      // distances of every row to its (new) label's old centre, float32
+      // direct differences: ((X - centers_old[labels])**2).sum(axis=1)
+      // (_k_means_common.pyx:185)
+      float* mind = const_cast<float*>(a.mind);
+      for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < a.n;
+           r += (long long)nb * blockDim.x) {
+        const float* xr = a.X + r * a.ld;
+        const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
+        float s = 0.0f;
+        for (int j = 0; j < a.d; ++j) {
+          const float t = xr[j] - cr[j];
+          s = fmaf(t, t, s);
+        }
+        mind[r] = s;
+      }
+      if (!grid_barrier(st, nb)) return;
       if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
     } else {
       m_cand = a.n_cand;
@@ -624,7 +640,7 @@ __global__ void mstep_kernel(MStepArgs a) {
   double shift_part = 0.0;
   for (int c = blockIdx.x; c < a.k; c += nb) {
     const int src = a.cnt_adj[c] > 0 ? c : heavy;
-    double dsq = 0.0;
+    double dsq = 0.0, nrm = 0.0;
     for (int j = threadIdx.x; j < a.ld; j += blockDim.x) {
       float v = 0.0f;
       if (j < a.d) {
@@ -633,11 +649,19 @@ __global__ void mstep_kernel(MStepArgs a) {
         dsq += df * df;
       }
       a.C_new[(long long)c * a.ld + j] = v;
+      if (a.Chi) {
+        const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+        a.Chi[(long long)c * a.ld + j] = hi;
+        a.Clo[(long long)c * a.ld + j] = v - hi;
+      }
+      nrm += (double)v * v;
     }
     dsq = block_sum_f64(dsq, scratch);
+    if (a.bias) nrm = block_sum_f64(nrm, scratch);
     if (threadIdx.x == 0) {
       shift_part += dsq;
       if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
+      if (a.bias) a.bias[c] = (float)nrm;
     }
   }
   if (threadIdx.x == 0) a.shift_partial[blockIdx.x] = shift_part;

@@ -33,6 +33,11 @@ struct MStepArgs {
   float* reloc_x;       // min(k, kMaxEmptyCap) x ld
   double* shift_partial;  // gridDim.x
   float* shift_out;       // per-centre shift (nullable)
+  // operands of the next tensor-core E-step (nullable): C_new split into
+  // tf32-exact high parts and remainders, and ||C_new||^2
+  float* Chi;
+  float* Clo;
+  float* bias;
   // exchanged relocation candidates (multi-GPU); null on one GPU
   int n_cand;
   const float* cand_dist;

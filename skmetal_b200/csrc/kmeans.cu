@@ -60,6 +60,7 @@ struct FitParams {
   bool simt = false;
   bool profile = false;
   bool distributed = false;
+  bool bulk_sums = false;  // recompute sums from scratch every iteration
   long long row_base = 0;
   long long n_total = 0;
   // outputs (host, nullable)
@@ -285,6 +286,10 @@ static int run_fit(const FitParams& p) {
     SKM_TRY(buf.alloc_n(&bias, (size_t)plan.tcp.k_pad));
     SKM_TRY(buf.alloc_n(&chi, (size_t)k * ld));
     SKM_TRY(buf.alloc_n(&clo, (size_t)k * ld));
+    SKM_TRY(tc_set_centres(&plan.tcp, chi, clo));
+    // operands of the first E-step; later ones come out of the M-step
+    centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cb0, k, ld, d, bias, chi, clo, st);
+    SKM_TRY(check_launch("centre_prep_kernel"));
   }
   int* dev_err = &st->error;
   SKM_CUDA(cudaEventRecord(ev1, s));
@@ -317,6 +322,9 @@ static int run_fit(const FitParams& p) {
   ma.reloc_dist = reloc_dist;
   ma.reloc_x = reloc_x;
   ma.shift_partial = shift_partial;
+  ma.Chi = chi;
+  ma.Clo = clo;
+  ma.bias = bias;
   const int mstep_blocks = nsm;
   const int mstep_threads = 512;
 
@@ -363,16 +371,16 @@ static int run_fit(const FitParams& p) {
       if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
       // iteration 0 has no previous labels: sums are built in bulk afterwards;
       // later iterations add the deltas of the rows that changed label
-      long long* Dinc = it == 0 ? nullptr : D;
+      const bool bulk = it == 0 || p.bulk_sums;
+      long long* Dinc = bulk ? nullptr : D;
+      if (bulk && it > 0) SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
       if (plan.tc) {
-        centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cin, k, ld, d, bias, chi, clo, st);
-        SKM_TRY(check_launch("centre_prep_kernel"));
-        SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, changed, Dinc, st, dev_err, s));
+        SKM_TRY(tc_estep(plan.tcp, bias, labels, changed, Dinc, st, dev_err, s));
       } else {
-        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, mind, st, changed, Dinc, 0, s));
+        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, Dinc, 0, s));
       }
       if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
-      if (it == 0) SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, D, st, s));
+      if (bulk) SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, D, st, s));
       if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
       ma.C_old = Cin;
       ma.C_new = Cout;
@@ -432,9 +440,8 @@ static int run_fit(const FitParams& p) {
   // ---- final E-step, inertia, outputs ----------------------------------------
   if (!hs.strict) {
     if (plan.tc) {
-      centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cfin, k, ld, d, bias, chi, clo, nullptr);
-      SKM_TRY(check_launch("centre_prep_kernel"));
-      SKM_TRY(tc_estep(plan.tcp, chi, clo, bias, labels, mind, nullptr, nullptr, nullptr, dev_err, s));
+      // chi / clo / bias of the final centres were written by the last M-step
+      SKM_TRY(tc_estep(plan.tcp, bias, labels, nullptr, nullptr, nullptr, dev_err, s));
     } else {
       SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, nullptr, 0, s));
     }
@@ -667,6 +674,7 @@ int skmetal_kmeans_fit(const float* X, size_t n, size_t d, size_t k, const float
   p.center = (flags & SKMETAL_FIT_CENTER) != 0;
   p.simt = (flags & SKMETAL_FIT_SIMT) != 0;
   p.profile = (flags & SKMETAL_FIT_PROFILE) != 0;
+  p.bulk_sums = (flags & SKMETAL_FIT_BULK_SUMS) != 0;
   p.centers_out = centers_out;
   p.labels_out = labels_out;
   p.inertia_out = inertia_out;
@@ -689,6 +697,7 @@ int skmetal_kmeans_fit_shard(const float* X, size_t n, size_t d, size_t k, const
   p.center = (flags & SKMETAL_FIT_CENTER) != 0;
   p.simt = (flags & SKMETAL_FIT_SIMT) != 0;
   p.profile = (flags & SKMETAL_FIT_PROFILE) != 0;
+  p.bulk_sums = (flags & SKMETAL_FIT_BULK_SUMS) != 0;
   p.distributed = true;
   p.row_base = (long long)row_base;
   p.n_total = (long long)n_total;
@@ -778,6 +787,7 @@ static int fit_dataset_common(void* handle, const float* init, size_t k, int32_t
   p.center = (flags & SKMETAL_FIT_CENTER) != 0;
   p.simt = (flags & SKMETAL_FIT_SIMT) != 0;
   p.profile = (flags & SKMETAL_FIT_PROFILE) != 0;
+  p.bulk_sums = (flags & SKMETAL_FIT_BULK_SUMS) != 0;
   p.distributed = distributed;
   p.row_base = (long long)row_base;
   p.n_total = (long long)n_total;

@@ -369,8 +369,11 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           mma_ts(tacc, tx + (uint32_t)(c * KC), b_lo, idesc, c > 0 ? 1u : 0u);
           mma_ts(tacc, tx + (uint32_t)(c * KC), b_hi, idesc, 1u);
         }
-        // x_lo of this tile; its converter waited for the previous tile's
-        // MMAs, so every MMA of tile i-1 is complete past this point
+        // next tile into the other x buffer (its last readers, tile i-1's MMAs
+        // and converter, are ordered before this point: tcgen05 operations of
+        // this thread execute in issue order, and the converter of tile i-1
+        // arrived on XLO_FULL before MMA_c(i-1) was issued)
+        if (p.nbx == 2 && i + 1 < my_tiles && !issue_cp(i + 1)) break;
         if (!mbar_wait(bar(B_XLO_FULL), i & 1, abort_flag, p.err, 2204)) break;
         tc_fence_after();
         for (int c = 0; c < p.nk; ++c) {
@@ -379,11 +382,9 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         }
         tc_commit(bar(B_ACC_FULL(a)));
         tc_commit(bar(B_XLO_FREE));
-        if (i + 1 < my_tiles) {
-          if (p.nbx == 1) {
-            // single x buffer: tile i's MMAs must be done before it is refilled
-            if (!mbar_wait(bar(B_XLO_FREE), i & 1, abort_flag, p.err, 2205)) break;
-          }
+        if (p.nbx == 1 && i + 1 < my_tiles) {
+          // single x buffer: tile i's MMAs must be done before it is refilled
+          if (!mbar_wait(bar(B_XLO_FREE), i & 1, abort_flag, p.err, 2205)) break;
           if (!issue_cp(i + 1)) break;
         }
       }
@@ -403,16 +404,24 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       tc_fence_after();
       const uint32_t tx = tmem_base + lane_off + (uint32_t)(b * p.xcols);
       const uint32_t tl = tmem_base + lane_off + col_xlo;
-      for (int c = 0; c < p.nk; ++c) {
-        uint32_t r[8];
-        tmem_ld8(tx + (uint32_t)(c * KC), r);
+      for (int c0 = 0; c0 < p.nk; c0 += 4) {
+        uint32_t r[4][8];
+        const int nc = min(4, p.nk - c0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u < nc) tmem_ld8(tx + (uint32_t)((c0 + u) * KC), r[u]);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float v = __uint_as_float(r[e]);
-          r[e] = __float_as_uint(v - __uint_as_float(to_tf32_bits(r[e], p.round_mode)));
+        for (int u = 0; u < 4; ++u) {
+          if (u < nc) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float v = __uint_as_float(r[u][e]);
+              r[u][e] = __float_as_uint(v - __uint_as_float(to_tf32_bits(r[u][e], p.round_mode)));
+            }
+            tmem_st8(tl + (uint32_t)((c0 + u) * KC), r[u]);
+          }
         }
-        tmem_st8(tl + (uint32_t)(c * KC), r);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -423,36 +432,51 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    int old_next = -1;
+    if (p.changed && my_tiles > 0) {
+      const long long g0 = (long long)blockIdx.x * BM + row;
+      old_next = g0 < p.n ? p.labels[g0] : -1;
+    }
     for (int i = 0; i < my_tiles; ++i) {
       const int a = i % p.nba;
+      const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
+      const int old = old_next;
+      if (p.changed && i + 1 < my_tiles) {  // prefetch the next tile's previous labels
+        const long long g1 = grow + (long long)gridDim.x * BM;
+        old_next = g1 < p.n ? p.labels[g1] : -1;
+      }
       if (!mbar_wait(bar(B_ACC_FULL(a)), (i / p.nba) & 1, abort_flag, p.err, 2401)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + lane_off + col_acc + (uint32_t)(a * p.k_pad);
       float best = INFINITY;
       int bl = 0;
-      for (int j0 = 0; j0 < p.k_pad; j0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + (uint32_t)j0, v);
+      for (int j0 = 0; j0 < p.k_pad; j0 += 64) {
+        uint32_t v[4][16];
+        const int nq = min(4, (p.k_pad - j0) >> 4);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u < nq) tmem_ld16(taddr + (uint32_t)(j0 + 16 * u), v[u]);
         tmem_ld_wait();
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const float dist = fmaf(-2.0f, __uint_as_float(v[jj]), bias_s[j0 + jj]);
-          if (dist < best) {
-            best = dist;
-            bl = j0 + jj;
+        for (int u = 0; u < 4; ++u) {
+          if (u < nq) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = j0 + 16 * u + jj;
+              const float dist = fmaf(-2.0f, __uint_as_float(v[u][jj]), bias_s[j]);
+              if (dist < best) {
+                best = dist;
+                bl = j;
+              }
+            }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(bar(B_ACC_EMPTY(a)));
-      const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
       bool ch = false;
-      int old = -1;
       if (grow < p.n) {
-        if (p.changed) {
-          old = p.labels[grow];
-          ch = old != bl;
-        }
+        ch = p.changed && old != bl;
         p.labels[grow] = bl;
       }
       if (p.changed) {

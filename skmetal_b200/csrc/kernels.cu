@@ -83,41 +83,88 @@ __device__ double block_sum_f64(double v, double* scratch /* >= 32 */) {
 // data preparation
 // ---------------------------------------------------------------------------
 
-// max |x| over the first d columns (float bits; |x| >= 0 so uint order = float order)
+// The padding columns [d, ld) of X are zero and the mean is zero there, so
+// the elementwise passes below run over the whole row-major buffer as float4
+// (ld is a multiple of 4) without masking. A thread that needs the column of
+// its float4 keeps c4 = i mod (ld/4) updated by addition instead of division.
+
+// max |x| (float bits; |x| >= 0 so unsigned order = float order)
 __global__ void maxabs_kernel(const float* __restrict__ X, int ld, long long n, int d,
                               unsigned int* __restrict__ out_bits) {
+  (void)d;
+  const float4* X4 = reinterpret_cast<const float4*>(X);
+  const long long total = n * (long long)(ld >> 2);
   unsigned int m = 0;
-  const long long total = n * (long long)ld;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % ld);
-    if (c < d) {
-      unsigned int b = __float_as_uint(X[i]) & 0x7fffffffu;
-      if (b > 0x7f800000u) b = 0x7f800000u;  // NaN treated as +inf (rejected on host)
-      m = max(m, b);
-    }
+    const float4 v = __ldcs(X4 + i);
+    m = max(m, __float_as_uint(v.x) & 0x7fffffffu);
+    m = max(m, __float_as_uint(v.y) & 0x7fffffffu);
+    m = max(m, __float_as_uint(v.z) & 0x7fffffffu);
+    m = max(m, __float_as_uint(v.w) & 0x7fffffffu);
   }
+  m = min(m, 0x7f800000u);  // NaN counts as +inf (rejected by the host)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) atomicMax(out_bits, m);
 }
 
 // Column sums of X in fixed point (exact): colsum[j] = sum_r round(x_rj * scale).
-// Block b handles a contiguous row range; one thread per column.
+// blockDim = q * g with q = ld / 4: thread t owns column group t % q and the
+// rows r = (block, t / q) strided, so its four int64 partials stay in
+// registers; partials meet in shared memory (integer atomics, exact).
 __global__ void colsum_fixed_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                     const double* __restrict__ scale_ptr, long long* __restrict__ colsum) {
+  extern __shared__ long long cs_acc[];
+  (void)d;
   const double scale = *scale_ptr;
-  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
-  const long long r0 = blockIdx.x * rows_per;
-  const long long r1 = min(n, r0 + rows_per);
-  for (int j = threadIdx.x; j < d; j += blockDim.x) {
-    long long acc = 0;
-    for (long long r = r0; r < r1; ++r) acc += to_fixed(X[r * ld + j], scale);
-    if (acc != 0) red_add_s64(&colsum[j], acc);
+  const int q = ld >> 2;
+  const int g = blockDim.x / q;
+  const int c4 = threadIdx.x % q, rg = threadIdx.x / q;
+  const float4* X4 = reinterpret_cast<const float4*>(X);
+  long long a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+  if (g == 0) {
+    // more column groups than threads: one thread per column group, straight
+    // to global memory
+    for (int cc = threadIdx.x; cc < q; cc += blockDim.x) {
+      long long b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+      for (long long r = blockIdx.x; r < n; r += gridDim.x) {
+        const float4 v = __ldcs(X4 + r * q + cc);
+        b0 += to_fixed(v.x, scale);
+        b1 += to_fixed(v.y, scale);
+        b2 += to_fixed(v.z, scale);
+        b3 += to_fixed(v.w, scale);
+      }
+      red_add_s64(&colsum[4 * cc + 0], b0);
+      red_add_s64(&colsum[4 * cc + 1], b1);
+      red_add_s64(&colsum[4 * cc + 2], b2);
+      red_add_s64(&colsum[4 * cc + 3], b3);
+    }
+    return;
   }
+  if (rg < g) {
+    for (long long r = (long long)blockIdx.x * g + rg; r < n; r += (long long)gridDim.x * g) {
+      const float4 v = __ldcs(X4 + r * q + c4);
+      a0 += to_fixed(v.x, scale);
+      a1 += to_fixed(v.y, scale);
+      a2 += to_fixed(v.z, scale);
+      a3 += to_fixed(v.w, scale);
+    }
+  }
+  for (int i = threadIdx.x; i < ld; i += blockDim.x) cs_acc[i] = 0;
+  __syncthreads();
+  if (rg < g) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 0]), (unsigned long long)a0);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 1]), (unsigned long long)a1);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 2]), (unsigned long long)a2);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 3]), (unsigned long long)a3);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ld; i += blockDim.x)
+    if (cs_acc[i] != 0) red_add_s64(&colsum[i], cs_acc[i]);
 }
 
-// mean[j] = colsum[j] * inv_scale / n   (float32 result)
+// mean[j] = colsum[j] * inv_scale / n (float32; zero in the padding)
 __global__ void mean_from_colsum_kernel(const long long* __restrict__ colsum, int d, const double* __restrict__ scale_ptr,
                                         double n_total, float* __restrict__ mean) {
   const double inv_scale = 1.0 / *scale_ptr;
@@ -125,41 +172,60 @@ __global__ void mean_from_colsum_kernel(const long long* __restrict__ colsum, in
     mean[j] = (float)((double)colsum[j] * inv_scale / n_total);
 }
 
-// X[:, :d] -= mean (float32, in place) and track max |x - mean|
-__global__ void center_kernel(float* __restrict__ X, int ld, long long n, int d,
-                              const float* __restrict__ mean, unsigned int* __restrict__ maxabs_bits) {
+// X -= mean (float32, in place), max |x - mean|, and per-block float64
+// partials of sum (x - mean)^2 (for the scaled tolerance) when `partial`.
+__global__ void center_kernel(float* __restrict__ X, int ld, long long n, int d, const float* __restrict__ mean,
+                              unsigned int* __restrict__ maxabs_bits, double* __restrict__ partial) {
+  __shared__ double scratch[32];
+  (void)d;
+  float4* X4 = reinterpret_cast<float4*>(X);
+  const int q = ld >> 2;
+  const long long total = n * (long long)q;
+  const long long start = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int sq = (int)(stride % q);
+  int c4 = (int)(start % q);
+  const float4* M4 = reinterpret_cast<const float4*>(mean);
   unsigned int m = 0;
-  const long long total = n * (long long)ld;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % ld);
-    if (c < d) {
-      const float v = X[i] - mean[c];
-      X[i] = v;
-      m = max(m, __float_as_uint(v) & 0x7fffffffu);
-    }
+  double ss = 0.0;
+  for (long long i = start; i < total; i += stride) {
+    float4 v = X4[i];
+    const float4 mu = M4[c4];
+    v.x -= mu.x;
+    v.y -= mu.y;
+    v.z -= mu.z;
+    v.w -= mu.w;
+    X4[i] = v;
+    m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                   max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+    ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    c4 += sq;
+    if (c4 >= q) c4 -= q;
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0 && maxabs_bits) atomicMax(maxabs_bits, m);
+  if (partial) {
+    ss = block_sum_f64(ss, scratch);
+    if (threadIdx.x == 0) partial[blockIdx.x] = ss;
+  }
 }
 
-// Per-block float64 partial of sum_r sum_j x_rj^2 over a fixed row range
-// (for the scaled tolerance); combined by ordered_sum_kernel.
+// Per-block float64 partials of sum x^2 (uncentred fits with a relative tolerance).
 __global__ void sumsq_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                      double* __restrict__ partial) {
   __shared__ double scratch[32];
-  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
-  const long long r0 = blockIdx.x * rows_per;
-  const long long r1 = min(n, r0 + rows_per);
-  double acc = 0.0;
-  for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x)
-    for (int j = 0; j < d; ++j) {
-      const double v = X[r * ld + j];
-      acc += v * v;
-    }
-  acc = block_sum_f64(acc, scratch);
-  if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+  (void)d;
+  const float4* X4 = reinterpret_cast<const float4*>(X);
+  const long long total = n * (long long)(ld >> 2);
+  double ss = 0.0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = X4[i];
+    ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  }
+  ss = block_sum_f64(ss, scratch);
+  if (threadIdx.x == 0) partial[blockIdx.x] = ss;
 }
 
 // Fixed-point scale 2^F for sums of up to n_total values bounded by the max |x|
@@ -330,71 +396,55 @@ bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream
 // bulk fixed-point sums from the labels into the delta buffer D (zero on entry)
 // ---------------------------------------------------------------------------
 
-// Block b owns a contiguous row range. With `groups` > 0 the block is split
-// into `groups` groups of `gsize` threads (gsize >= d, a multiple of 32);
-// thread j of group g owns column j of a private k x ld int64 accumulator in
-// shared memory and adds the rows r = r0 + g, r0 + g + groups, ... in order,
-// so the hot loop has no atomics. The groups are summed and flushed with one
-// global reduction per nonzero entry. With `groups` == 0 (accumulators do not
-// fit in shared memory) every warp adds rows straight into D. Integer sums
+// With `smem_acc` the block accumulates a private k x ld (+ k counts) int64
+// copy in shared memory: warps take rows (4 at a time for memory-level
+// parallelism), lanes take columns, and the adds are shared-memory integer
+// atomics; the copy is flushed with one global reduction per nonzero entry.
+// Otherwise every warp adds straight into D in global memory. Integer sums
 // are exact, so the result does not depend on the order or the grid.
 __global__ void bulk_sums_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                  const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                 const FitState* __restrict__ st, int groups, int gsize) {
+                                 const FitState* __restrict__ st, int smem_acc) {
   extern __shared__ long long acc[];
   if (st->done) return;
   const double scale = st->scale;
-  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
-  const long long r0 = blockIdx.x * rows_per;
-  const long long r1 = min(n, r0 + rows_per);
-  long long* cntD = D + (long long)k * ld;
-  if (groups == 0) {
-    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-    for (long long r = r0 + (threadIdx.x >> 5); r < r1; r += warps) {
-      const int l = labels[r];
-      if (lane == 0) red_add_s64(&cntD[l], 1);
-      for (int j = lane; j < d; j += 32) {
-        const long long v = to_fixed(X[r * ld + j], scale);
-        if (v != 0) red_add_s64(&D[(long long)l * ld + j], v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const long long ks = (long long)k * ld;
+  long long* A = smem_acc ? acc : D;
+  if (smem_acc) {
+    for (long long i = threadIdx.x; i < ks + k; i += blockDim.x) acc[i] = 0;
+    __syncthreads();
+  }
+  const long long step = (long long)gridDim.x * nw;
+  long long r = (long long)blockIdx.x * nw + warp;
+  for (; r + 3 * step < n; r += 4 * step) {
+    int l[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) l[u] = labels[r + u * step];
+    for (int j = lane; j < d; j += 32) {
+      float x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = __ldcs(X + (r + u * step) * ld + j);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long v = to_fixed(x[u], scale);
+        if (v != 0) red_add_s64(&A[(long long)l[u] * ld + j], v);
       }
     }
-    return;
+    if (lane < 4) red_add_s64(&A[ks + l[lane]], 1);
   }
-  const long long per = (long long)k * ld + k;  // one group's accumulators (sums, counts)
-  for (long long i = threadIdx.x; i < per * groups; i += blockDim.x) acc[i] = 0;
-  __syncthreads();
-  const int g = threadIdx.x / gsize, j = threadIdx.x % gsize;
-  if (g < groups) {
-    long long* a = acc + per * g;
-    long long* ac = a + (long long)k * ld;
-    if (j < d) {
-      long long r = r0 + g;
-      for (; r + 3 * groups < r1; r += 4 * groups) {
-        float xv[4];
-        int lv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          lv[u] = labels[r + u * groups];
-          xv[u] = X[(r + u * groups) * ld + j];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          a[(long long)lv[u] * ld + j] += to_fixed(xv[u], scale);
-          if (j == 0) ac[lv[u]] += 1;
-        }
-      }
-      for (; r < r1; r += groups) {
-        const int l = labels[r];
-        a[(long long)l * ld + j] += to_fixed(X[r * ld + j], scale);
-        if (j == 0) ac[l] += 1;
-      }
+  for (; r < n; r += step) {
+    const int lr = labels[r];
+    for (int j = lane; j < d; j += 32) {
+      const long long v = to_fixed(__ldcs(X + r * ld + j), scale);
+      if (v != 0) red_add_s64(&A[(long long)lr * ld + j], v);
     }
+    if (lane == 0) red_add_s64(&A[ks + lr], 1);
   }
-  __syncthreads();
-  for (long long i = threadIdx.x; i < per; i += blockDim.x) {
-    long long s = 0;
-    for (int gg = 0; gg < groups; ++gg) s += acc[per * gg + i];
-    if (s != 0) red_add_s64(i < (long long)k * ld ? &D[i] : &cntD[i - (long long)k * ld], s);
+  if (smem_acc) {
+    __syncthreads();
+    for (long long i = threadIdx.x; i < ks + k; i += blockDim.x)
+      if (acc[i] != 0) red_add_s64(&D[i], acc[i]);
   }
 }
 
@@ -477,20 +527,129 @@ __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, 
   return (float)((double)s * a.st->inv_scale / (double)a.cnt_adj[c]);
 }
 
+// One centre (cluster c, columns strided over the calling warp's lanes):
+// writes C_new, the tf32 split and returns (shift^2, ||c||^2) summed in a
+// fixed order (lane partials, then a fixed butterfly).
+__device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, int src, int n_reloc, double* dsq_out,
+                                            double* nrm_out) {
+  const int lane = threadIdx.x & 31;
+  double dsq = 0.0, nrm = 0.0;
+  for (int j = lane; j < a.ld; j += 32) {
+    float v = 0.0f;
+    if (j < a.d) {
+      v = centre_value(a, src, j, n_reloc);
+      const double df = (double)v - (double)a.C_old[(long long)c * a.ld + j];
+      dsq += df * df;
+      nrm += (double)v * v;
+    }
+    a.C_new[(long long)c * a.ld + j] = v;
+    if (a.Chi) {
+      const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+      a.Chi[(long long)c * a.ld + j] = hi;
+      a.Clo[(long long)c * a.ld + j] = v - hi;
+    }
+  }
+  *dsq_out = warp_sum(dsq);
+  *nrm_out = warp_sum(nrm);
+}
+
+// Convergence bookkeeping (_kmeans.py:723-741) from per-cluster squared
+// shifts summed in cluster order; one thread.
+__device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long long changed_now, double tot) {
+  st->shift_tot = tot;
+  st->iter += 1;
+  if (changed_now == 0) {
+    st->strict = 1;
+    st->done = 1;
+  } else if (tot <= st->tol) {
+    st->done = 1;
+  }
+  if (st->iter >= st->max_iter) st->done = 1;
+  *const_cast<unsigned long long*>(a.changed) = 0;
+}
+
 __global__ void mstep_kernel(MStepArgs a) {
   FitState* st = a.st;
-  if (st->done) return;  // uniform: `done` is only written after the last barrier
-  const unsigned long long changed_now = *a.changed;  // cleared by block 0 at the end
+  if (st->done) return;  // uniform: `done` is only written at the very end
+  const unsigned long long changed_now = *a.changed;  // cleared at the end
   const unsigned int nb = gridDim.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const long long ks = (long long)a.k * a.ld;
+  const long long* dcnt = a.D + ks;
   __shared__ int n_empty_s;
   __shared__ int wcount[32];
+  __shared__ long long hv_cnt[32];
+  __shared__ int hv_idx[32];
   __shared__ double scratch[32];
 
+  // 1. empty clusters of the new assignment (counts + this iteration's
+  //    deltas), ascending ids; every block computes the same answer
+  if (threadIdx.x == 0) n_empty_s = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
+    const int c = c0 + threadIdx.x;
+    const bool e = c < a.k && a.counts[c] + dcnt[c] == 0;
+    const unsigned int b = __ballot_sync(0xffffffffu, e);
+    if (lane == 0) wcount[warp] = __popc(b);
+    __syncthreads();
+    int base = n_empty_s;
+    for (int w = 0; w < warp; ++w) base += wcount[w];
+    const int pos = base + __popc(b & ((1u << lane) - 1u));
+    if (e && blockIdx.x == 0 && pos < kMaxEmptyCap) a.empty_ids[pos] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int t = 0;
+      for (int w = 0; w < nwarps; ++w) t += wcount[w];
+      n_empty_s += t;
+    }
+    __syncthreads();
+  }
+  const int n_empty = n_empty_s;
+
+  if (n_empty == 0) {
+    // ---------------- fast path: no relocation, one block does the update
+    if (blockIdx.x != 0) return;
+    long long* S = const_cast<long long*>(a.S);
+    long long* cnt = const_cast<long long*>(a.counts);
+    for (long long i = threadIdx.x; i < ks + a.k; i += blockDim.x) {
+      const long long v = a.D[i];
+      if (v != 0) {
+        if (i < ks) S[i] += v;
+        else cnt[i - ks] += v;
+        a.D[i] = 0;
+      }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < a.k; c += blockDim.x) a.cnt_adj[c] = cnt[c];
+    if (threadIdx.x == 0) {
+      st->n_empty = 0;
+      st->relocated = 0;
+    }
+    __syncthreads();
+    double* dsq_s = a.shift_partial;  // k entries (scratch sized for max(k, grid))
+    for (int c = warp; c < a.k; c += nwarps) {
+      double dsq, nrm;
+      warp_centre(a, c, c, 0, &dsq, &nrm);
+      if (lane == 0) {
+        dsq_s[c] = dsq;
+        if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
+        if (a.bias) a.bias[c] = (float)nrm;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double tot = 0.0;
+      for (int c = 0; c < a.k; ++c) tot += dsq_s[c];
+      finish_iteration(a, st, changed_now, tot);
+    }
+    return;
+  }
+
+  // ---------------- relocation path (cooperative, all blocks)
   // 0. S += dS, counts += dcount; clear the deltas (all but `changed`)
   {
     long long* S = const_cast<long long*>(a.S);
     long long* cnt = const_cast<long long*>(a.counts);
-    const long long ks = (long long)a.k * a.ld;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + a.k;
          i += (long long)nb * blockDim.x) {
       const long long v = a.D[i];
@@ -501,31 +660,6 @@ __global__ void mstep_kernel(MStepArgs a) {
       }
     }
   }
-  if (!grid_barrier(st, nb)) return;
-
-  // 1. empty clusters in ascending id order (every block; block 0 stores them)
-  if (threadIdx.x == 0) n_empty_s = 0;
-  __syncthreads();
-  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
-    const int c = c0 + threadIdx.x;
-    const bool e = c < a.k && a.counts[c] == 0;
-    const unsigned int b = __ballot_sync(0xffffffffu, e);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) wcount[warp] = __popc(b);
-    __syncthreads();
-    int base = n_empty_s;
-    for (int w = 0; w < warp; ++w) base += wcount[w];
-    const int pos = base + __popc(b & ((1u << lane) - 1u));
-    if (e && blockIdx.x == 0 && pos < kMaxEmptyCap) a.empty_ids[pos] = c;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int t = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += wcount[w];
-      n_empty_s += t;
-    }
-    __syncthreads();
-  }
-  const int n_empty = n_empty_s;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     st->n_empty = n_empty;
     st->sel_count = 0;
@@ -534,68 +668,64 @@ __global__ void mstep_kernel(MStepArgs a) {
   if (n_empty > kMaxEmptyCap) return;  // uniform
   if (!grid_barrier(st, nb)) return;
 
-  // 2. relocation: the n_empty rows farthest from their centre, paired in
-  //    decreasing (distance, -row) order with the ascending empty ids
-  int n_reloc = 0;
-  if (n_empty > 0) {
-    int m_cand = n_empty;
-    if (a.cand_row == nullptr) {
-      // distances of every row to its (new) label's old centre, float32
-      // direct differences: ((X - centers_old[labels])**2).sum(axis=1)
-      // (_k_means_common.pyx:185)
-      float* mind = const_cast<float*>(a.mind);
-      for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < a.n;
-           r += (long long)nb * blockDim.x) {
-        const float* xr = a.X + r * a.ld;
-        const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
-        float s = 0.0f;
-        for (int j = 0; j < a.d; ++j) {
-          const float t = xr[j] - cr[j];
-          s = fmaf(t, t, s);
-        }
-        mind[r] = s;
+  // 2. the n_empty rows farthest from their centre, paired in decreasing
+  //    (distance, -row) order with the ascending empty ids
+  int m_cand = n_empty;
+  if (a.cand_row == nullptr) {
+    // distances of every row to its (new) label's old centre, float32 direct
+    // differences: ((X - centers_old[labels])**2).sum(axis=1) (_k_means_common.pyx:185)
+    float* mind = const_cast<float*>(a.mind);
+    for (long long r = blockIdx.x * (long long)nwarps + warp; r < a.n; r += (long long)nb * nwarps) {
+      const float* xr = a.X + r * a.ld;
+      const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
+      float s = 0.0f;
+      for (int j = lane; j < a.d; j += 32) {
+        const float t = xr[j] - cr[j];
+        s = fmaf(t, t, s);
       }
-      if (!grid_barrier(st, nb)) return;
-      if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
-    } else {
-      m_cand = a.n_cand;
-      if (a.n_cand < n_empty) {  // exchanged candidates cannot cover this many empties
-        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&st->error, 1003);
-        return;
-      }
-    }
-    if (blockIdx.x == 0) {
-      for (int i = threadIdx.x; i < m_cand; i += blockDim.x) {
-        float di;
-        long long gi;
-        if (a.cand_row) { di = a.cand_dist[i]; gi = a.cand_row[i]; }
-        else { di = a.mind[a.sel[i]]; gi = a.row_base + a.sel[i]; }
-        const unsigned long long ki = reloc_key(di, gi);
-        int rank = 0;
-        for (int j = 0; j < m_cand; ++j) {
-          float dj;
-          long long gj;
-          if (a.cand_row) { dj = a.cand_dist[j]; gj = a.cand_row[j]; }
-          else { dj = a.mind[a.sel[j]]; gj = a.row_base + a.sel[j]; }
-          if (reloc_key(dj, gj) > ki) ++rank;
-        }
-        if (rank < n_empty) {
-          a.reloc_dist[rank] = di;
-          if (a.cand_row) {
-            a.reloc_label[rank] = a.cand_label[i];
-            for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.cand_x[(long long)i * a.ld + j];
-          } else {
-            const long long r = a.sel[i];
-            a.reloc_label[rank] = a.labels[r];
-            for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[r * a.ld + j];
-          }
-        }
-      }
+      s = warp_sum(s);
+      if (lane == 0) mind[r] = s;
     }
     if (!grid_barrier(st, nb)) return;
-    // reference: no relocation when every distance is zero (_k_means_common.pyx:192-194)
-    n_reloc = a.reloc_dist[0] > 0.0f ? n_empty : 0;
+    if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
+  } else {
+    m_cand = a.n_cand;
+    if (a.n_cand < n_empty) {  // exchanged candidates cannot cover this many empties
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&st->error, 1003);
+      return;
+    }
   }
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < m_cand; i += blockDim.x) {
+      float di;
+      long long gi;
+      if (a.cand_row) { di = a.cand_dist[i]; gi = a.cand_row[i]; }
+      else { di = a.mind[a.sel[i]]; gi = a.row_base + a.sel[i]; }
+      const unsigned long long ki = reloc_key(di, gi);
+      int rank = 0;
+      for (int j = 0; j < m_cand; ++j) {
+        float dj;
+        long long gj;
+        if (a.cand_row) { dj = a.cand_dist[j]; gj = a.cand_row[j]; }
+        else { dj = a.mind[a.sel[j]]; gj = a.row_base + a.sel[j]; }
+        if (reloc_key(dj, gj) > ki) ++rank;
+      }
+      if (rank < n_empty) {
+        a.reloc_dist[rank] = di;
+        if (a.cand_row) {
+          a.reloc_label[rank] = a.cand_label[i];
+          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.cand_x[(long long)i * a.ld + j];
+        } else {
+          const long long r = a.sel[i];
+          a.reloc_label[rank] = a.labels[r];
+          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[r * a.ld + j];
+        }
+      }
+    }
+  }
+  if (!grid_barrier(st, nb)) return;
+  // no relocation when every distance is zero (_k_means_common.pyx:192-194)
+  const int n_reloc = a.reloc_dist[0] > 0.0f ? n_empty : 0;
 
   // 3. counts after relocation (block 0), then the heaviest cluster (first max)
   if (blockIdx.x == 0) {
@@ -610,8 +740,6 @@ __global__ void mstep_kernel(MStepArgs a) {
     }
   }
   if (!grid_barrier(st, nb)) return;
-  __shared__ long long hv_cnt[32];
-  __shared__ int hv_idx[32];
   long long bc = -1;
   int bi = 0;
   for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
@@ -624,10 +752,10 @@ __global__ void mstep_kernel(MStepArgs a) {
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
     if (ov > bc || (ov == bc && oi < bi)) { bc = ov; bi = oi; }
   }
-  if ((threadIdx.x & 31) == 0) { hv_cnt[threadIdx.x >> 5] = bc; hv_idx[threadIdx.x >> 5] = bi; }
+  if (lane == 0) { hv_cnt[warp] = bc; hv_idx[warp] = bi; }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+    for (int w = 1; w < nwarps; ++w)
       if (hv_cnt[w] > hv_cnt[0] || (hv_cnt[w] == hv_cnt[0] && hv_idx[w] < hv_idx[0])) {
         hv_cnt[0] = hv_cnt[w];
         hv_idx[0] = hv_idx[w];
@@ -636,56 +764,26 @@ __global__ void mstep_kernel(MStepArgs a) {
   __syncthreads();
   const int heavy = hv_idx[0];
 
-  // 4. new centres and per-block partial sums of squared shifts
-  double shift_part = 0.0;
-  for (int c = blockIdx.x; c < a.k; c += nb) {
-    const int src = a.cnt_adj[c] > 0 ? c : heavy;
-    double dsq = 0.0, nrm = 0.0;
-    for (int j = threadIdx.x; j < a.ld; j += blockDim.x) {
-      float v = 0.0f;
-      if (j < a.d) {
-        v = centre_value(a, src, j, n_reloc);
-        const double df = (double)v - (double)a.C_old[(long long)c * a.ld + j];
-        dsq += df * df;
-      }
-      a.C_new[(long long)c * a.ld + j] = v;
-      if (a.Chi) {
-        const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
-        a.Chi[(long long)c * a.ld + j] = hi;
-        a.Clo[(long long)c * a.ld + j] = v - hi;
-      }
-      nrm += (double)v * v;
-    }
-    dsq = block_sum_f64(dsq, scratch);
-    if (a.bias) nrm = block_sum_f64(nrm, scratch);
-    if (threadIdx.x == 0) {
-      shift_part += dsq;
+  // 4. new centres (one warp per cluster) and their squared shifts
+  double* dsq_s = a.shift_partial;
+  for (int c = blockIdx.x * nwarps + warp; c < a.k; c += nb * nwarps) {
+    double dsq, nrm;
+    warp_centre(a, c, a.cnt_adj[c] > 0 ? c : heavy, n_reloc, &dsq, &nrm);
+    if (lane == 0) {
+      dsq_s[c] = dsq;
       if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
       if (a.bias) a.bias[c] = (float)nrm;
     }
   }
-  if (threadIdx.x == 0) a.shift_partial[blockIdx.x] = shift_part;
+  (void)scratch;
   if (!grid_barrier(st, nb)) return;
 
-  // 5. convergence bookkeeping (_kmeans.py:723-741), fixed summation order
+  // 5. convergence bookkeeping, cluster order
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     double tot = 0.0;
-    for (unsigned int b = 0; b < nb; ++b) tot += a.shift_partial[b];
-    st->shift_tot = tot;
-    st->iter += 1;
-    if (changed_now == 0) {
-      st->strict = 1;
-      st->done = 1;
-    } else if (tot <= st->tol) {
-      st->done = 1;
-    }
-    if (st->iter >= st->max_iter) st->done = 1;
-    *const_cast<unsigned long long*>(a.changed) = 0;
+    for (int c = 0; c < a.k; ++c) tot += dsq_s[c];
+    finish_iteration(a, st, changed_now, tot);
   }
-}
-
-__global__ void counts_to_float_kernel(const long long* __restrict__ c, int k, float* __restrict__ out) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) out[i] = (float)c[i];
 }
 
 // bias[c] = ||c||^2 (float64 sum, rounded) and the tf32 split of the centres
@@ -713,35 +811,36 @@ __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, i
 // outputs: inertia, per-row distance to the assigned centre, transform
 // ---------------------------------------------------------------------------
 
-// Per-block float64 partial of sum_r ||x_r - c_{l_r}||^2 over a fixed row range.
+// Per-block float64 partial of sum_r ||x_r - c_{l_r}||^2: warp w of block b
+// takes rows b*W + w, + gridDim*W, ... (W warps per block), lanes over the
+// columns; the per-block sum is a fixed tree, so the result is deterministic
+// for a given grid.
 __global__ void inertia_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                        const float* __restrict__ C, const int32_t* __restrict__ labels,
                                        double* __restrict__ partial) {
   __shared__ double scratch[32];
-  const long long rows_per = (n + gridDim.x - 1) / gridDim.x;
-  const long long r0 = blockIdx.x * rows_per;
-  const long long r1 = min(n, r0 + rows_per);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   double acc = 0.0;
-  for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+  for (long long r = (long long)blockIdx.x * nw + warp; r < n; r += (long long)gridDim.x * nw) {
     const float* xr = X + r * ld;
     const float* cr = C + (long long)labels[r] * ld;
-    double s = 0.0;
-    for (int j = 0; j < d; ++j) {
-      const double t = (double)xr[j] - (double)cr[j];
-      s += t * t;
+    for (int j = lane; j < d; j += 32) {
+      const double t = (double)__ldcs(xr + j) - (double)cr[j];
+      acc += t * t;
     }
-    acc += s;
   }
   acc = block_sum_f64(acc, scratch);
   if (threadIdx.x == 0) partial[blockIdx.x] = acc;
 }
 
+// out = sum of partial[0..m) in a fixed order (one warp: strided lane sums,
+// then a fixed butterfly)
 __global__ void ordered_sum_kernel(const double* __restrict__ partial, int m, double* __restrict__ out) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) {
-    double t = 0.0;
-    for (int i = 0; i < m; ++i) t += partial[i];
-    *out = t;
-  }
+  if (blockIdx.x != 0 || threadIdx.x >= 32) return;
+  double t = 0.0;
+  for (int i = threadIdx.x; i < m; i += 32) t += partial[i];
+  t = warp_sum(t);
+  if (threadIdx.x == 0) *out = t;
 }
 
 __global__ void mindist_kernel(const float* __restrict__ X, int ld, long long n, int d,

@@ -31,7 +31,7 @@ struct MStepArgs {
   int* reloc_label;     // kMaxEmptyCap
   float* reloc_dist;    // kMaxEmptyCap
   float* reloc_x;       // min(k, kMaxEmptyCap) x ld
-  double* shift_partial;  // gridDim.x
+  double* shift_partial;  // max(k, gridDim.x) entries
   float* shift_out;       // per-centre shift (nullable)
   // operands of the next tensor-core E-step (nullable): C_new split into
   // tf32-exact high parts and remainders, and ||C_new||^2
@@ -52,7 +52,8 @@ __global__ void mean_from_colsum_kernel(const long long* colsum, int d, const do
 __global__ void scale_kernel(const unsigned int* maxabs_bits, double n_total, double* out);
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
                                   double n_total, int d, const unsigned int* maxabs_bits);
-__global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits);
+__global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits,
+                              double* partial);
 __global__ void sumsq_partial_kernel(const float* X, int ld, long long n, int d, double* partial);
 __global__ void center_init_kernel(const float* init, int d, int k, const float* mean, float* C, int ld);
 __global__ void assign_simt_kernel(const float* X, int ld, long long n, int d, const float* C, int k,
@@ -64,7 +65,7 @@ __global__ void counts_to_float_kernel(const long long* c, int k, float* out);
 bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
                          long long n, const float* C, int k, int32_t* labels, float* mind);
 __global__ void bulk_sums_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
-                                 long long* D, const FitState* st, int groups, int gsize);
+                                 long long* D, const FitState* st, int smem_acc);
 
 __global__ void mstep_kernel(MStepArgs a);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, float* Chi, float* Clo,

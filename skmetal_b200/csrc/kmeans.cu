@@ -125,15 +125,11 @@ static int launch_bulk_sums(const float* X, int ld, long long n, int d, const in
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncSetAttribute(bulk_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
   }
-  const int gsize = (int)round_up((size_t)d, 32);
-  const size_t per = sizeof(long long) * ((size_t)k * ld + k);
-  int groups = 0;
-  if (gsize <= 1024) groups = (int)std::min<size_t>(1024 / gsize, (size_t)(optin - 1024) / per);
-  groups = std::min(groups, 8);
-  if (groups >= 1) {
-    bulk_sums_kernel<<<sm_count(), groups * gsize, per * groups, s>>>(X, ld, n, d, labels, k, D, st, groups, gsize);
+  const size_t need = sizeof(long long) * ((size_t)k * ld + k);
+  if (need + 2048 <= (size_t)optin) {
+    bulk_sums_kernel<<<sm_count(), 1024, need, s>>>(X, ld, n, d, labels, k, D, st, 1);
   } else {
-    bulk_sums_kernel<<<blocks_for(n * 32, 256, 4), 256, 0, s>>>(X, ld, n, d, labels, k, D, st, 0, 0);
+    bulk_sums_kernel<<<sm_count() * 4, 256, 0, s>>>(X, ld, n, d, labels, k, D, st, 0);
   }
   return check_launch("bulk_sums_kernel");
 }
@@ -214,7 +210,7 @@ static int run_fit(const FitParams& p) {
   SKM_TRY(buf.alloc_n(&colsum, (size_t)ld));
   SKM_TRY(buf.alloc_n(&st, 1));
   SKM_TRY(buf.alloc_n(&u32s, 2 + 512));
-  SKM_TRY(buf.alloc_n(&dscr, 2 + n_part + nsm));
+  SKM_TRY(buf.alloc_n(&dscr, 2 + n_part + std::max(nsm, k)));
   SKM_TRY(buf.alloc_n(&empty_ids, kMaxEmptyCap));
   SKM_TRY(buf.alloc_n(&sel, kMaxEmptyCap));
   SKM_TRY(buf.alloc_n(&cnt_adj, (size_t)k));
@@ -245,12 +241,17 @@ static int run_fit(const FitParams& p) {
     if (comm) SKM_TRY(comm_allreduce_max_u32(comm, &u32s[0], 1, s));
     scale_kernel<<<1, 32, 0, s>>>(&u32s[0], (double)n_total, scale_mean);
     SKM_TRY(check_launch("scale_kernel"));
-    colsum_fixed_kernel<<<nsm, std::min(1024, (int)round_up(d, 32)), 0, s>>>(X, ld, n, d, scale_mean, colsum);
+    {
+      const int q = ld / 4;
+      const int threads = q <= 1024 ? q * std::max(1, 256 / q) : 1024;
+      colsum_fixed_kernel<<<nsm * 2, threads, sizeof(long long) * ld, s>>>(X, ld, n, d, scale_mean, colsum);
+    }
     SKM_TRY(check_launch("colsum_fixed_kernel"));
     if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, colsum, ld, s));
     mean_from_colsum_kernel<<<1, 256, 0, s>>>(colsum, d, scale_mean, (double)n_total, mean);
     SKM_TRY(check_launch("mean_from_colsum_kernel"));
-    center_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, mean, &u32s[1]);
+    // the centring pass also yields the sum of squares for the relative tolerance
+    center_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, mean, &u32s[1], (!p.tol_abs && p.tol != 0.0) ? partials : nullptr);
     SKM_TRY(check_launch("center_kernel"));
   } else {
     maxabs_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, &u32s[1]);
@@ -262,8 +263,10 @@ static int run_fit(const FitParams& p) {
   SKM_TRY(check_launch("center_init_kernel"));
   const bool tol_rel = !p.tol_abs && p.tol != 0.0;
   if (tol_rel) {
-    sumsq_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, partials);
-    SKM_TRY(check_launch("sumsq_partial_kernel"));
+    if (!p.center) {
+      sumsq_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, partials);
+      SKM_TRY(check_launch("sumsq_partial_kernel"));
+    }
     ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, sumsq);
     SKM_TRY(check_launch("ordered_sum_kernel"));
     if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, sumsq, 1, s));
@@ -326,7 +329,7 @@ static int run_fit(const FitParams& p) {
   ma.Clo = clo;
   ma.bias = bias;
   const int mstep_blocks = nsm;
-  const int mstep_threads = 512;
+  const int mstep_threads = 1024;
 
   std::vector<cudaEvent_t> prof_ev;
   if (p.profile) {

@@ -59,6 +59,7 @@ def test_tensor_core_probe():
     """tcgen05.cp copies the SW32 tile unpermuted and the tensor core's
     fp32 -> tf32 conversion is one of the two the E-step can compensate."""
     mode, raw = _bridge.debug_tc_probe(raw=True)
+    print(f"tensor-core fp32->tf32 conversion: {['truncation', 'round-to-nearest-even'][mode] if mode >= 0 else mode}")
     assert mode in (0, 1), mode
     m = np.arange(128)[:, None]
     k = np.arange(8)[None, :]

@@ -580,7 +580,6 @@ __global__ void mstep_kernel(MStepArgs a) {
   __shared__ int wcount[32];
   __shared__ long long hv_cnt[32];
   __shared__ int hv_idx[32];
-  __shared__ double scratch[32];
 
   // 1. empty clusters of the new assignment (counts + this iteration's
   //    deltas), ascending ids; every block computes the same answer
@@ -775,7 +774,6 @@ __global__ void mstep_kernel(MStepArgs a) {
       if (a.bias) a.bias[c] = (float)nrm;
     }
   }
-  (void)scratch;
   if (!grid_barrier(st, nb)) return;
 
   // 5. convergence bookkeeping, cluster order
@@ -784,6 +782,10 @@ __global__ void mstep_kernel(MStepArgs a) {
     for (int c = 0; c < a.k; ++c) tot += dsq_s[c];
     finish_iteration(a, st, changed_now, tot);
   }
+}
+
+__global__ void counts_to_float_kernel(const long long* __restrict__ c, int k, float* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) out[i] = (float)c[i];
 }
 
 // bias[c] = ||c||^2 (float64 sum, rounded) and the tf32 split of the centres

@@ -7,6 +7,26 @@
 
 namespace skm {
 
+// ---------------------------------------------------------------------------
+// Blocked ("tile-major") layout of the fit's working copy of X.
+// Rows are grouped in tiles of 128; inside a tile, columns are grouped in
+// quads of 4 floats; quad q of tile t is a contiguous [128 rows][4 floats]
+// block (2 KB) and the quads of a tile follow each other. Element (r, j) is
+//   t * 128 * ld + (j / 4) * 512 + (r % 128) * 4 + j % 4      (floats)
+// with ld = round_up(d, 4). A tile is therefore one contiguous region of
+// 512 * ld bytes holding exactly the tile's data, and pairs of quads are the
+// canonical no-swizzle K-major layout of the tensor core (8-row core matrices
+// of 16-byte rows, 128 bytes apart; the two K halves of an 8-column chunk
+// 2048 bytes apart), so a tile moves HBM -> shared memory with one bulk copy
+// and shared memory -> tensor memory with tcgen05.cp. The buffer holds
+// round_up(n, 128) rows; padding rows and columns are zero.
+// ---------------------------------------------------------------------------
+constexpr int kTileRows = 128;
+
+__host__ __device__ __forceinline__ long long xblk_index(long long r, int j, int ld) {
+  return (r >> 7) * (128LL * ld) + (long long)(j >> 2) * 512 + (r & 127) * 4 + (j & 3);
+}
+
 // value * 2^F rounded to the nearest integer (2^F = scale, a power of two, so
 // the product is exact in float64)
 __device__ __forceinline__ long long to_fixed(float v, double scale) {
@@ -27,11 +47,11 @@ __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
 __device__ __forceinline__ void warp_apply_delta(const float* __restrict__ X, int ld, int d, int k, long long row, int old, int neu,
                                  long long* __restrict__ D, double scale) {
   const int lane = threadIdx.x & 31;
-  const float* xr = X + row * ld;
+  const float* xr = X + xblk_index(row, 0, ld);  // X is blocked: column j at xr[(j/4)*512 + j%4]
   long long* dn = D + (long long)neu * ld;
   long long* dold = old >= 0 ? D + (long long)old * ld : nullptr;
   for (int j = lane; j < d; j += 32) {
-    const long long v = to_fixed(__ldg(xr + j), scale);
+    const long long v = to_fixed(__ldg(xr + (j >> 2) * 512 + (j & 3)), scale);
     if (v != 0) {
       red_add_s64(dn + j, v);
       if (dold) red_add_s64(dold + j, -v);

@@ -11,22 +11,24 @@
 // (the incremental M-step input).
 //
 // Data path of one tile (all asynchronous, one CTA per SM, persistent):
-//   HBM --TMA--> smem stage --tcgen05.cp--> TMEM x (A operand, 2 buffers)
+//   HBM --bulk copy--> smem stage --tcgen05.cp--> TMEM x (A operand, 2 buffers)
 //   converter warps: TMEM x --tcgen05.ld--> regs --> x_lo --tcgen05.st--> TMEM
 //   MMA thread: acc  = x.C_lo + x.C_hi        (A = x from TMEM, B = smem)
 //               acc += x_lo.C_hi              (A = x_lo from TMEM)
 //   epilogue warps: TMEM acc --tcgen05.ld--> argmin --> labels, deltas
-// so shared memory only carries the TMA write, one read by tcgen05.cp and the
+// so shared memory only carries one bulk write, one read by tcgen05.cp and the
 // small centre operands: X is read from HBM exactly once.
 //
-// Warp roles (320 threads): 0 TMA producer, 1 TMEM owner + MMA/cp issuer,
-// 2-5 converter, 6-9 epilogue; warp w of the converter / epilogue groups owns
-// TMEM lanes 32*(w%4) .. +31 (= tile rows).
+// X is the fit's blocked working copy (xblk_index): a 128-row tile is one
+// contiguous region already in the tensor core's canonical no-swizzle K-major
+// layout (8-column chunk c = 4 KB at c * 4096: two 2 KB halves of 4 columns,
+// 8-row core matrices of 16-byte rows 128 bytes apart), so one bulk copy per
+// tile lands it ready for tcgen05.cp. The centres (B operand, k_pad rows) are
+// loaded once per CTA by TMA in the SWIZZLE_32B layout.
 //
-// Shared-memory tiles: K is cut into 8-column chunks (32 bytes per row);
-// chunk c of a 128-row tile is 4 KB in the canonical K-major SWIZZLE_32B
-// layout (8-row atoms of 256 bytes) that TMA writes and tcgen05 reads.
-// Columns past d are zero (TMA out-of-bounds fill).
+// Warp roles (352 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer,
+// 2-5 converter, 6-9 epilogue, 10 tcgen05.cp issuer; warp w of the converter
+// / epilogue groups owns TMEM lanes 32*(w%4) .. +31 (= tile rows).
 //
 // Every mbarrier wait is bounded in time; on timeout the CTA records an error
 // code, stops issuing work, waits (bounded) for its own in-flight copies and
@@ -54,7 +56,7 @@ constexpr int KC = 8;                     // fp32 columns per K chunk (UMMA K fo
 constexpr int CHUNK_BYTES = BM * KC * 4;  // 4096
 constexpr int MAX_NK = 16;                // d <= 128
 constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
-constexpr int THREADS = 320;
+constexpr int THREADS = 352;
 constexpr int MAX_STAGES = 4;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
 
@@ -74,9 +76,10 @@ struct Params {
   int32_t* labels;
   unsigned long long* changed;
   long long* D;  // nullable: incremental deltas of rows that changed label
-  const float* X;
+  const float* X;  // blocked layout
   int ld;
   int d;
+  uint32_t tile_bytes;  // 512 * ld: one tile of blocked X
   const FitState* st;  // nullable: skip when st->done
   int* err;
 };
@@ -138,6 +141,25 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// K-major no-swizzle shared-memory matrix descriptor for one 128 x 8 fp32
+// chunk of a blocked tile: core matrices of 8 rows x 16 bytes, 8-row groups
+// 128 bytes apart (stride byte offset), the two 4-column halves 2048 bytes
+// apart (leading byte offset), descriptor version 1, layout type 0.
+__device__ __forceinline__ uint64_t blk_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(2048u >> 4) << 16;
+  d |= (uint64_t)(128u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  return d;
 }
 
 // K-major SWIZZLE_32B shared-memory matrix descriptor: rows of 32 bytes,
@@ -237,7 +259,9 @@ constexpr int B_XLO_FULL = 2 * MAX_STAGES + 6;
 constexpr int B_XLO_FREE = 2 * MAX_STAGES + 7;
 constexpr int B_C_FULL = 2 * MAX_STAGES + 8;
 constexpr int B_DONE = 2 * MAX_STAGES + 9;
-constexpr int NUM_BARS = 2 * MAX_STAGES + 10;
+__host__ __device__ constexpr int B_XFREE(int b) { return 2 * MAX_STAGES + 10 + b; }  // x buffer reusable
+constexpr int B_CP_DONE = 2 * MAX_STAGES + 12;  // drain of the tcgen05.cp issuer
+constexpr int NUM_BARS = 2 * MAX_STAGES + 13;
 
 __host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
   Smem s;
@@ -263,8 +287,8 @@ __host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_chi,
-                const __grid_constant__ CUtensorMap tmap_clo, Params p) {
+estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_constant__ CUtensorMap tmap_clo,
+                Params p) {
   if (p.st && p.st->done) return;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base =
@@ -287,6 +311,7 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       mbar_init(bar(B_EMPTY(s)), 1);
     }
     for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(B_XFREE(b)), 1);
       mbar_init(bar(B_XT(b)), 1);
       mbar_init(bar(B_ACC_FULL(b)), 1);
       mbar_init(bar(B_ACC_EMPTY(b)), 128);
@@ -295,6 +320,7 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     mbar_init(bar(B_XLO_FREE), 1);
     mbar_init(bar(B_C_FULL), 1);
     mbar_init(bar(B_DONE), 1);
+    mbar_init(bar(B_CP_DONE), 1);
     misc[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -304,6 +330,13 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   for (int j = threadIdx.x; j < p.k_pad; j += blockDim.x) bias_s[j] = j < p.k ? p.bias[j] : INFINITY;
+  if (p.tile_bytes < stage_bytes) {
+    // 4-column tail of the last chunk (d % 8 in 1..4): never copied, must be zero
+    for (int s = 0; s < p.stages; ++s)
+      for (uint32_t o = p.tile_bytes + 16u * threadIdx.x; o < stage_bytes; o += 16u * blockDim.x)
+        *reinterpret_cast<uint4*>(base + L.x[s] + o) = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -325,9 +358,10 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         const int s = i % p.stages;
         if (!mbar_wait(bar(B_EMPTY(s)), ((i / p.stages) & 1) ^ 1, abort_flag, p.err, 2101)) break;
         const int tile = (int)blockIdx.x + i * (int)gridDim.x;
-        mbar_expect_tx(bar(B_FULL(s)), stage_bytes);
-        for (int c = 0; c < p.nk; ++c)
-          tma_load_2d(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES, &tmap_x, c * KC, tile * BM, bar(B_FULL(s)));
+        const char* src = reinterpret_cast<const char*>(p.X) + (size_t)tile * p.tile_bytes;
+        mbar_expect_tx(bar(B_FULL(s)), p.tile_bytes);
+        for (uint32_t o = 0; o < p.tile_bytes; o += 8192u)
+          bulk_load(sbase + L.x[s] + o, src + o, min(8192u, p.tile_bytes - o), bar(B_FULL(s)));
         armed = i + 1;
       }
       // our own copies must land before the CTA may exit
@@ -337,43 +371,25 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         mbar_wait(bar(B_FULL(i % p.stages)), (i / p.stages) & 1, &no_abort, p.err, 2103);
     }
   } else if (warp == 1) {
-    // -------------------------------------------------- cp + MMA issuer (1 lane)
+    // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(p.k_pad);
       bool ok = mbar_wait(bar(B_C_FULL), 0, abort_flag, p.err, 2201);
-      tc_fence_after();
-      // tile i: smem stage -> TMEM x[i % nbx]; tcgen05 operations issued by
-      // this thread execute in issue order, so the MMAs that follow read the
-      // copied values
-      auto issue_cp = [&](int i) -> bool {
-        const int s = i % p.stages;
-        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) return false;
-        tc_fence_after();
-        const uint32_t tx = tmem_base + (uint32_t)((i % p.nbx) * p.xcols);
-        for (int c = 0; c < p.nk; ++c)
-          tmem_cp_chunk(tx + (uint32_t)(c * KC), sw32_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES));
-        tc_commit(bar(B_XT(i % p.nbx)));
-        tc_commit(bar(B_EMPTY(s)));
-        return true;
-      };
-      if (ok && my_tiles > 0) ok = issue_cp(0);
       for (int i = 0; ok && i < my_tiles; ++i) {
-        const int a = i % p.nba;
+        const int a = i % p.nba, b = i % p.nbx;
         if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nba) & 1) ^ 1, abort_flag, p.err, 2203)) break;
+        if (!mbar_wait(bar(B_XT(b)), (i / p.nbx) & 1, abort_flag, p.err, 2202)) break;
         tc_fence_after();
         const uint32_t tacc = tmem_base + col_acc + (uint32_t)(a * p.k_pad);
-        const uint32_t tx = tmem_base + (uint32_t)((i % p.nbx) * p.xcols);
+        const uint32_t tx = tmem_base + (uint32_t)(b * p.xcols);
         for (int c = 0; c < p.nk; ++c) {
           const uint64_t b_hi = sw32_desc(sbase + L.chi + (uint32_t)c * p.k_pad * 32);
           const uint64_t b_lo = sw32_desc(sbase + L.clo + (uint32_t)c * p.k_pad * 32);
           mma_ts(tacc, tx + (uint32_t)(c * KC), b_lo, idesc, c > 0 ? 1u : 0u);
           mma_ts(tacc, tx + (uint32_t)(c * KC), b_hi, idesc, 1u);
         }
-        // next tile into the other x buffer (its last readers, tile i-1's MMAs
-        // and converter, are ordered before this point: tcgen05 operations of
-        // this thread execute in issue order, and the converter of tile i-1
-        // arrived on XLO_FULL before MMA_c(i-1) was issued)
-        if (p.nbx == 2 && i + 1 < my_tiles && !issue_cp(i + 1)) break;
+        // x_lo of this tile; its converter waited for the previous tile's
+        // MMAs (XLO_FREE), so x_lo is not overwritten while still read
         if (!mbar_wait(bar(B_XLO_FULL), i & 1, abort_flag, p.err, 2204)) break;
         tc_fence_after();
         for (int c = 0; c < p.nk; ++c) {
@@ -382,16 +398,31 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         }
         tc_commit(bar(B_ACC_FULL(a)));
         tc_commit(bar(B_XLO_FREE));
-        if (p.nbx == 1 && i + 1 < my_tiles) {
-          // single x buffer: tile i's MMAs must be done before it is refilled
-          if (!mbar_wait(bar(B_XLO_FREE), i & 1, abort_flag, p.err, 2205)) break;
-          if (!issue_cp(i + 1)) break;
-        }
+        tc_commit(bar(B_XFREE(b)));  // x[b]: all MMAs done; its converter finished before XLO_FULL
       }
       // every tcgen05 operation issued by this thread is complete once DONE fires
       tc_commit(bar(B_DONE));
       volatile int no_abort = 0;
       mbar_wait(bar(B_DONE), 0, &no_abort, p.err, 2206);
+    }
+  } else if (warp == 10) {
+    // --------------------------------------------- shared -> tensor memory copies
+    if (lane == 0) {
+      for (int i = 0; i < my_tiles; ++i) {
+        const int s = i % p.stages, b = i % p.nbx;
+        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2501)) break;
+        if (!mbar_wait(bar(B_XFREE(b)), ((i / p.nbx) & 1) ^ 1, abort_flag, p.err, 2502)) break;
+        tc_fence_after();
+        const uint32_t tx = tmem_base + (uint32_t)(b * p.xcols);
+        for (int c = 0; c < p.nk; ++c)
+          tmem_cp_chunk(tx + (uint32_t)(c * KC), blk_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES));
+        tc_commit(bar(B_XT(b)));
+        tc_commit(bar(B_EMPTY(s)));
+      }
+      // every copy issued by this thread is complete once CP_DONE fires
+      tc_commit(bar(B_CP_DONE));
+      volatile int no_abort = 0;
+      mbar_wait(bar(B_CP_DONE), 0, &no_abort, p.err, 2503);
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------------- converter
@@ -515,10 +546,11 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
   const uint32_t smisc = smem_u32(misc);
   int* err = reinterpret_cast<int*>(out + 3072);
   const int tid = threadIdx.x, warp = tid >> 5;
-  // SWIZZLE_32B: bit 4 of the byte offset is XORed with bit 7
+  // A in the blocked no-swizzle layout (column quad q at q * 2048, row m at
+  // m * 16); B in SWIZZLE_32B (bit 4 of the byte offset XORed with bit 7)
   auto sw32 = [](uint32_t off) { return off ^ (((off >> 7) & 1u) << 4); };
   for (int k = 0; k < 8; ++k)
-    *reinterpret_cast<uint32_t*>(sm + sw32((uint32_t)(tid * 32 + k * 4))) = probe_bits(tid, k);
+    *reinterpret_cast<uint32_t*>(sm + (uint32_t)((k >> 2) * 2048 + tid * 16 + (k & 3) * 4)) = probe_bits(tid, k);
   if (tid < 16)
     for (int k = 0; k < 8; ++k)
       *reinterpret_cast<float*>(sm + CHUNK_BYTES + sw32((uint32_t)(tid * 32 + k * 4))) = (tid == k) ? 1.0f : 0.0f;
@@ -540,7 +572,7 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
   // TMEM columns: [0,8) copy of A, [8,24) D (A from TMEM); then [16,32) D (A from smem)
   if (tid == 0) {
     const uint32_t idesc = idesc_tf32(16);
-    tmem_cp_chunk(tb, sw32_desc(sa));
+    tmem_cp_chunk(tb, blk_desc(sa));
     mma_ts(tb + 8, tb, sw32_desc(sb), idesc, 0u);
     tc_commit(sbar);
   }
@@ -560,7 +592,7 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
   tc_fence_after();
   if (tid == 0) {
     const uint32_t idesc = idesc_tf32(16);
-    mma_ss(tb + 16, sw32_desc(sa), sw32_desc(sb), idesc, 0u);
+    mma_ss(tb + 16, blk_desc(sa), sw32_desc(sb), idesc, 0u);
     tc_commit(sbar);
   }
   __syncwarp();
@@ -727,7 +759,6 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   if (plan->stages == 0) return OK;
   const int n_tiles = (int)((n + tc::BM - 1) / tc::BM);
   plan->grid = std::min(n_tiles, sm_count());
-  SKM_TRY(make_map(&plan->tmap_x, X, ld, n, tc::BM));
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(tc::estep_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
@@ -764,9 +795,10 @@ int tc_estep(const TcPlan& plan, const float* bias, int32_t* labels, unsigned lo
   p.X = plan.X;
   p.ld = plan.ld;
   p.d = plan.d;
+  p.tile_bytes = (uint32_t)(512 * plan.ld);
   p.st = st;
   p.err = err;
-  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(plan.tmap_x, plan.tmap_chi, plan.tmap_clo, p);
+  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(plan.tmap_chi, plan.tmap_clo, p);
   return check_launch("estep_tc_kernel");
 }
 

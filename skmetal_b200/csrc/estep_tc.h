@@ -29,7 +29,6 @@ struct TcPlan {
   int round_mode = 0;  // tensor-core fp32->tf32 conversion (probe result)
   int grid = 0;
   size_t smem = 0;
-  CUtensorMap tmap_x;
   CUtensorMap tmap_chi;
   CUtensorMap tmap_clo;
 };
@@ -40,6 +39,7 @@ struct TcPlan {
 // With raw3072 non-null the probe reruns and returns its raw output.
 int tc_probe(int* mode, uint32_t* raw3072);
 
+// X: the fit's blocked working copy (xblk_index), round_up(n, 128) rows.
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan);
 
 // Chi / Clo: tf32 split of the centres (k x ld), fixed for the plan's lifetime

@@ -211,6 +211,59 @@ __global__ void center_kernel(float* __restrict__ X, int ld, long long n, int d,
   }
 }
 
+// Blocked working copy of X (layout: see xblk_index): out = raw - mean (or
+// raw when mean is null), zero in padding rows; also max |out| and per-block
+// float64 partials of sum out^2 (when `partial`). Threads walk the blocked
+// output in order (consecutive threads write consecutive 16-byte rows of a
+// quad), so the writes are coalesced and each raw row is read as 16-byte
+// pieces that neighbouring warps share through L1/L2.
+__global__ void center_block_kernel(const float* __restrict__ raw, int ld, long long n, int d,
+                                    const float* __restrict__ mean, float* __restrict__ out,
+                                    unsigned int* __restrict__ maxabs_bits, double* __restrict__ partial) {
+  __shared__ double scratch[32];
+  (void)d;
+  const int q4 = ld >> 2;  // quads per row
+  const long long n_pad = (n + 127) / 128 * 128;
+  const long long total = n_pad * q4;  // float4 elements
+  const float4* R4 = reinterpret_cast<const float4*>(raw);
+  float4* O4 = reinterpret_cast<float4*>(out);
+  const float4* M4 = reinterpret_cast<const float4*>(mean);
+  unsigned int m = 0;
+  double ss = 0.0;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    // g = (tile * q4 + q) * 128 + rr
+    const long long tq = g >> 7;
+    const int rr = (int)(g & 127);
+    const long long t = tq / q4;
+    const int q = (int)(tq - t * q4);
+    const long long r = t * 128 + rr;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < n) {
+      v = __ldg(R4 + r * q4 + q);
+      if (mean) {
+        const float4 mu = M4[q];
+        v.x -= mu.x;
+        v.y -= mu.y;
+        v.z -= mu.z;
+        v.w -= mu.w;
+      }
+    }
+    O4[g] = v;
+    m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                   max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+    ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  }
+  m = min(m, 0x7f800000u);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && maxabs_bits) atomicMax(maxabs_bits, m);
+  if (partial) {
+    ss = block_sum_f64(ss, scratch);
+    if (threadIdx.x == 0) partial[blockIdx.x] = ss;
+  }
+}
+
 // Per-block float64 partials of sum x^2 (uncentred fits with a relative tolerance).
 __global__ void sumsq_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                      double* __restrict__ partial) {
@@ -292,7 +345,7 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
                                    const float* __restrict__ C, int k,
                                    int32_t* __restrict__ labels, float* __restrict__ mind,
                                    const FitState* __restrict__ st, unsigned long long* __restrict__ changed,
-                                   long long* __restrict__ D, int skip_if_strict) {
+                                   long long* __restrict__ D, int skip_if_strict, int blocked) {
   extern __shared__ float csh[];
   if (st) {
     if (skip_if_strict ? (st->strict != 0) : (st->done != 0)) return;
@@ -300,7 +353,9 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
   const int chunk = max(1, min(k, (int)(kAssignSmemFloats / ld)));
   const long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const bool active = r < n;
-  const float* xr = X + (active ? r : 0) * ld;
+  // blocked X: quad q of the row at xr + 512 q; row-major: at xr + 4 q
+  const float* xr = blocked ? X + xblk_index(active ? r : 0, 0, ld) : X + (active ? r : 0) * ld;
+  const int qstride = blocked ? 512 : 4;
   float best = FLT_MAX;
   int bl = 0;
   for (int c0 = 0; c0 < k; c0 += chunk) {
@@ -314,7 +369,7 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
         float acc = 0.0f;
         int j = 0;
         for (; j + 4 <= d; j += 4) {
-          const float4 xv = *reinterpret_cast<const float4*>(xr + j);
+          const float4 xv = *reinterpret_cast<const float4*>(xr + (j >> 2) * qstride);
           const float d0 = xv.x - cr[j], d1 = xv.y - cr[j + 1], d2 = xv.z - cr[j + 2], d3 = xv.w - cr[j + 3];
           acc = fmaf(d0, d0, acc);
           acc = fmaf(d1, d1, acc);
@@ -322,7 +377,7 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
           acc = fmaf(d3, d3, acc);
         }
         for (; j < d; ++j) {
-          const float t = xr[j] - cr[j];
+          const float t = xr[(j >> 2) * qstride + (j & 3)] - cr[j];
           acc = fmaf(t, t, acc);
         }
         if (acc < best) {
@@ -396,12 +451,13 @@ bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream
 // bulk fixed-point sums from the labels into the delta buffer D (zero on entry)
 // ---------------------------------------------------------------------------
 
-// With `smem_acc` the block accumulates a private k x ld (+ k counts) int64
-// copy in shared memory: warps take rows (4 at a time for memory-level
-// parallelism), lanes take columns, and the adds are shared-memory integer
-// atomics; the copy is flushed with one global reduction per nonzero entry.
-// Otherwise every warp adds straight into D in global memory. Integer sums
-// are exact, so the result does not depend on the order or the grid.
+// Bulk fixed-point sums of all rows by label, X blocked. A work item is a
+// group of 32 rows of one tile (lane = row) that walks the tile's quads, so
+// every warp load is 512 contiguous bytes. With `smem_acc` the block adds into
+// a private k x ld (+ k counts) int64 copy in shared memory (integer atomics)
+// and flushes it with one global reduction per nonzero entry; otherwise it
+// adds straight into D. Integer sums are exact, so the result does not depend
+// on the order or the grid.
 __global__ void bulk_sums_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                  const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
                                  const FitState* __restrict__ st, int smem_acc) {
@@ -415,32 +471,27 @@ __global__ void bulk_sums_kernel(const float* __restrict__ X, int ld, long long 
     for (long long i = threadIdx.x; i < ks + k; i += blockDim.x) acc[i] = 0;
     __syncthreads();
   }
-  const long long step = (long long)gridDim.x * nw;
-  long long r = (long long)blockIdx.x * nw + warp;
-  for (; r + 3 * step < n; r += 4 * step) {
-    int l[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) l[u] = labels[r + u * step];
-    for (int j = lane; j < d; j += 32) {
-      float x[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) x[u] = __ldcs(X + (r + u * step) * ld + j);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const long long v = to_fixed(x[u], scale);
-        if (v != 0) red_add_s64(&A[(long long)l[u] * ld + j], v);
-      }
+  const int q4 = ld >> 2;
+  const long long items = (n + 31) / 32;  // 32-row groups (4 per tile)
+  const float4* X4 = reinterpret_cast<const float4*>(X);
+  for (long long it = (long long)blockIdx.x * nw + warp; it < items; it += (long long)gridDim.x * nw) {
+    const long long r = it * 32 + lane;
+    if (r >= n) continue;
+    const int l = labels[r];
+    const float4* xp = X4 + (r >> 7) * (32LL * ld) + (r & 127);  // quad q at xp[q * 128]
+    long long* a = A + (long long)l * ld;
+    for (int q = 0; q < q4; ++q) {
+      const float4 v = __ldcs(xp + (long long)q * 128);
+      const long long v0 = to_fixed(v.x, scale), v1 = to_fixed(v.y, scale);
+      const long long v2 = to_fixed(v.z, scale), v3 = to_fixed(v.w, scale);
+      if (v0) red_add_s64(a + 4 * q + 0, v0);
+      if (v1) red_add_s64(a + 4 * q + 1, v1);
+      if (v2) red_add_s64(a + 4 * q + 2, v2);
+      if (v3) red_add_s64(a + 4 * q + 3, v3);
     }
-    if (lane < 4) red_add_s64(&A[ks + l[lane]], 1);
+    red_add_s64(&A[ks + l], 1);
   }
-  for (; r < n; r += step) {
-    const int lr = labels[r];
-    for (int j = lane; j < d; j += 32) {
-      const long long v = to_fixed(__ldcs(X + r * ld + j), scale);
-      if (v != 0) red_add_s64(&A[(long long)lr * ld + j], v);
-    }
-    if (lane == 0) red_add_s64(&A[ks + lr], 1);
-  }
+  (void)d;
   if (smem_acc) {
     __syncthreads();
     for (long long i = threadIdx.x; i < ks + k; i += blockDim.x)
@@ -673,17 +724,28 @@ __global__ void mstep_kernel(MStepArgs a) {
   if (a.cand_row == nullptr) {
     // distances of every row to its (new) label's old centre, float32 direct
     // differences: ((X - centers_old[labels])**2).sum(axis=1) (_k_means_common.pyx:185)
+    // (X blocked: lane per row of a 32-row group, columns in order)
     float* mind = const_cast<float*>(a.mind);
-    for (long long r = blockIdx.x * (long long)nwarps + warp; r < a.n; r += (long long)nb * nwarps) {
-      const float* xr = a.X + r * a.ld;
+    const long long items = (a.n + 31) / 32;
+    const float4* X4 = reinterpret_cast<const float4*>(a.X);
+    for (long long it = blockIdx.x * (long long)nwarps + warp; it < items; it += (long long)nb * nwarps) {
+      const long long r = it * 32 + lane;
+      if (r >= a.n) continue;
+      const float4* xp = X4 + (r >> 7) * (32LL * a.ld) + (r & 127);
       const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
       float s = 0.0f;
-      for (int j = lane; j < a.d; j += 32) {
-        const float t = xr[j] - cr[j];
+      for (int q = 0; q < (a.ld >> 2); ++q) {
+        const float4 v = xp[(long long)q * 128];
+        float t = v.x - cr[4 * q];
+        s = fmaf(t, t, s);
+        t = v.y - cr[4 * q + 1];
+        s = fmaf(t, t, s);
+        t = v.z - cr[4 * q + 2];
+        s = fmaf(t, t, s);
+        t = v.w - cr[4 * q + 3];
         s = fmaf(t, t, s);
       }
-      s = warp_sum(s);
-      if (lane == 0) mind[r] = s;
+      mind[r] = s;
     }
     if (!grid_barrier(st, nb)) return;
     if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
@@ -717,7 +779,7 @@ __global__ void mstep_kernel(MStepArgs a) {
         } else {
           const long long r = a.sel[i];
           a.reloc_label[rank] = a.labels[r];
-          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[r * a.ld + j];
+          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
         }
       }
     }
@@ -813,22 +875,39 @@ __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, i
 // outputs: inertia, per-row distance to the assigned centre, transform
 // ---------------------------------------------------------------------------
 
-// Per-block float64 partial of sum_r ||x_r - c_{l_r}||^2: warp w of block b
-// takes rows b*W + w, + gridDim*W, ... (W warps per block), lanes over the
-// columns; the per-block sum is a fixed tree, so the result is deterministic
-// for a given grid.
+// Per-block float64 partial of sum_r ||x_r - c_{l_r}||^2 over a fixed
+// assignment of rows to blocks (deterministic for a given grid).
+// Row-major X: warp per row, lanes over columns. Blocked X: lane per row of
+// a 32-row group, walking the quads (coalesced 512-byte warp loads).
 __global__ void inertia_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                        const float* __restrict__ C, const int32_t* __restrict__ labels,
-                                       double* __restrict__ partial) {
+                                       double* __restrict__ partial, int blocked) {
   __shared__ double scratch[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   double acc = 0.0;
-  for (long long r = (long long)blockIdx.x * nw + warp; r < n; r += (long long)gridDim.x * nw) {
-    const float* xr = X + r * ld;
-    const float* cr = C + (long long)labels[r] * ld;
-    for (int j = lane; j < d; j += 32) {
-      const double t = (double)__ldcs(xr + j) - (double)cr[j];
-      acc += t * t;
+  if (blocked) {
+    const long long items = (n + 31) / 32;
+    const float4* X4 = reinterpret_cast<const float4*>(X);
+    for (long long it = (long long)blockIdx.x * nw + warp; it < items; it += (long long)gridDim.x * nw) {
+      const long long r = it * 32 + lane;
+      if (r >= n) continue;
+      const float4* xp = X4 + (r >> 7) * (32LL * ld) + (r & 127);
+      const float* cr = C + (long long)labels[r] * ld;
+      for (int q = 0; q < (ld >> 2); ++q) {
+        const float4 v = __ldcs(xp + (long long)q * 128);
+        const double t0 = (double)v.x - cr[4 * q], t1 = (double)v.y - cr[4 * q + 1];
+        const double t2 = (double)v.z - cr[4 * q + 2], t3 = (double)v.w - cr[4 * q + 3];
+        acc += t0 * t0 + t1 * t1 + t2 * t2 + t3 * t3;  // padding columns are zero in X and C
+      }
+    }
+  } else {
+    for (long long r = (long long)blockIdx.x * nw + warp; r < n; r += (long long)gridDim.x * nw) {
+      const float* xr = X + r * ld;
+      const float* cr = C + (long long)labels[r] * ld;
+      for (int j = lane; j < d; j += 32) {
+        const double t = (double)__ldcs(xr + j) - (double)cr[j];
+        acc += t * t;
+      }
     }
   }
   acc = block_sum_f64(acc, scratch);

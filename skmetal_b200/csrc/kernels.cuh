@@ -9,7 +9,7 @@ constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
 
 struct MStepArgs {
   FitState* st;
-  const float* X;
+  const float* X;       // blocked layout (xblk_index)
   int ld;
   int d;
   long long n;          // local rows
@@ -55,10 +55,12 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
 __global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits,
                               double* partial);
 __global__ void sumsq_partial_kernel(const float* X, int ld, long long n, int d, double* partial);
+__global__ void center_block_kernel(const float* raw, int ld, long long n, int d, const float* mean, float* out,
+                                    unsigned int* maxabs_bits, double* partial);
 __global__ void center_init_kernel(const float* init, int d, int k, const float* mean, float* C, int ld);
 __global__ void assign_simt_kernel(const float* X, int ld, long long n, int d, const float* C, int k,
                                    int32_t* labels, float* mind, const FitState* st, unsigned long long* changed,
-                                   long long* D, int skip_if_strict);
+                                   long long* D, int skip_if_strict, int blocked);
 __global__ void counts_to_float_kernel(const long long* c, int k, float* out);
 // Small-d assignment (d in {4, 8, 16, 32}, all centres in shared memory);
 // returns false when d has no specialisation.
@@ -71,7 +73,7 @@ __global__ void mstep_kernel(MStepArgs a);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, float* Chi, float* Clo,
                                    const FitState* st);
 __global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
-                                       const int32_t* labels, double* partial);
+                                       const int32_t* labels, double* partial, int blocked);
 __global__ void ordered_sum_kernel(const double* partial, int m, double* out);
 __global__ void mindist_kernel(const float* X, int ld, long long n, int d, const float* C, const int32_t* labels,
                                float* out);

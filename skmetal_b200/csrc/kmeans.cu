@@ -106,13 +106,13 @@ struct EStepPlan {
 
 static int launch_assign_simt(const float* X, int ld, long long n, int d, const float* C, int k, int32_t* labels,
                               float* mind, const FitState* st, unsigned long long* changed, long long* D,
-                              int skip_if_strict, cudaStream_t s) {
+                              int skip_if_strict, int blocked, cudaStream_t s) {
   const int chunk = std::max(1, std::min(k, kAssignSmemFloats / ld));
   const size_t smem = sizeof(float) * (size_t)chunk * ld;
   const int threads = 256;
   const int blocks = (int)((n + threads - 1) / threads);
   assign_simt_kernel<<<blocks, threads, smem, s>>>(X, ld, n, d, C, k, labels, mind, st, changed, D,
-                                                   skip_if_strict);
+                                                   skip_if_strict, blocked);
   return check_launch("assign_simt_kernel");
 }
 
@@ -192,7 +192,9 @@ static int run_fit(const FitParams& p) {
   const int n_part = nsm * 4;
   const int reloc_rows = std::min(k, kMaxEmptyCap);
 
-  SKM_TRY(buf.alloc_n(&X, (size_t)n * ld));
+  // X: the blocked working copy (round_up(n, 128) rows, see xblk_index)
+  const long long n_pad = (n + 127) / 128 * 128;
+  SKM_TRY(buf.alloc_n(&X, (size_t)n_pad * ld));
   SKM_TRY(buf.alloc_n(&Cb0, (size_t)k * ld));
   SKM_TRY(buf.alloc_n(&Cb1, (size_t)k * ld));
   SKM_TRY(buf.alloc_n(&mean, (size_t)ld));
@@ -223,50 +225,60 @@ static int run_fit(const FitParams& p) {
   double* shift_partial = dscr + 2 + n_part;
 
   SKM_CUDA(cudaEventRecord(ev0, s));
-  // ---- data in ------------------------------------------------------------
+  // ---- data in: row-major X (host rows are staged, a dataset is used in place)
+  const float* raw = p.X_dev;
+  float* staged = nullptr;
   if (p.X_host) {
-    SKM_TRY(upload_rows(X, ld, p.X_host, n, d, s));
-  } else {
-    SKM_CUDA(cudaMemcpyAsync(X, p.X_dev, sizeof(float) * (size_t)n * ld, cudaMemcpyDeviceToDevice, s));
+    SKM_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&staged), sizeof(float) * (size_t)n * ld, s));
+    int rc = upload_rows(staged, ld, p.X_host, n, d, s);
+    if (rc) {
+      cudaFreeAsync(staged, s);
+      return rc;
+    }
+    raw = staged;
   }
   SKM_CUDA(cudaMemcpyAsync(init_d, p.init_host, sizeof(float) * (size_t)k * d, cudaMemcpyHostToDevice, s));
   SKM_CUDA(cudaMemsetAsync(u32s, 0, sizeof(unsigned int) * (2 + 512), s));
   SKM_CUDA(cudaMemsetAsync(colsum, 0, sizeof(long long) * ld, s));
+  SKM_CUDA(cudaMemsetAsync(mean, 0, sizeof(float) * ld, s));
 
-  // ---- centring (exact mean) ----------------------------------------------
-  const int ew_blocks = blocks_for(n * ld, 256, 8);
+  // ---- exact mean, then the blocked (centred) working copy -------------------
+  const int ew_blocks = blocks_for(n * ld / 4, 256, 8);
+  const bool tol_rel = !p.tol_abs && p.tol != 0.0;
+  int prep_rc = OK;
   if (p.center) {
-    maxabs_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, &u32s[0]);
-    SKM_TRY(check_launch("maxabs_kernel"));
-    if (comm) SKM_TRY(comm_allreduce_max_u32(comm, &u32s[0], 1, s));
-    scale_kernel<<<1, 32, 0, s>>>(&u32s[0], (double)n_total, scale_mean);
-    SKM_TRY(check_launch("scale_kernel"));
-    {
+    maxabs_kernel<<<ew_blocks, 256, 0, s>>>(raw, ld, n, d, &u32s[0]);
+    prep_rc = check_launch("maxabs_kernel");
+    if (!prep_rc && comm) prep_rc = comm_allreduce_max_u32(comm, &u32s[0], 1, s);
+    if (!prep_rc) {
+      scale_kernel<<<1, 32, 0, s>>>(&u32s[0], (double)n_total, scale_mean);
+      prep_rc = check_launch("scale_kernel");
+    }
+    if (!prep_rc) {
       const int q = ld / 4;
       const int threads = q <= 1024 ? q * std::max(1, 256 / q) : 1024;
-      colsum_fixed_kernel<<<nsm * 2, threads, sizeof(long long) * ld, s>>>(X, ld, n, d, scale_mean, colsum);
+      colsum_fixed_kernel<<<nsm * 2, threads, sizeof(long long) * ld, s>>>(raw, ld, n, d, scale_mean, colsum);
+      prep_rc = check_launch("colsum_fixed_kernel");
     }
-    SKM_TRY(check_launch("colsum_fixed_kernel"));
-    if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, colsum, ld, s));
-    mean_from_colsum_kernel<<<1, 256, 0, s>>>(colsum, d, scale_mean, (double)n_total, mean);
-    SKM_TRY(check_launch("mean_from_colsum_kernel"));
-    // the centring pass also yields the sum of squares for the relative tolerance
-    center_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, mean, &u32s[1], (!p.tol_abs && p.tol != 0.0) ? partials : nullptr);
-    SKM_TRY(check_launch("center_kernel"));
-  } else {
-    maxabs_kernel<<<ew_blocks, 256, 0, s>>>(X, ld, n, d, &u32s[1]);
-    SKM_TRY(check_launch("maxabs_kernel"));
+    if (!prep_rc && comm) prep_rc = comm_allreduce_sum_s64(comm, colsum, ld, s);
+    if (!prep_rc) {
+      mean_from_colsum_kernel<<<1, 256, 0, s>>>(colsum, d, scale_mean, (double)n_total, mean);
+      prep_rc = check_launch("mean_from_colsum_kernel");
+    }
   }
+  if (!prep_rc) {
+    // one pass: blocked copy (minus the mean), max |x|, sum of squares for the relative tolerance
+    center_block_kernel<<<n_part, 256, 0, s>>>(raw, ld, n, d, p.center ? mean : nullptr, X, &u32s[1],
+                                               tol_rel ? partials : nullptr);
+    prep_rc = check_launch("center_block_kernel");
+  }
+  if (staged) cudaFreeAsync(staged, s);
+  SKM_TRY(prep_rc);
   if (comm) SKM_TRY(comm_allreduce_max_u32(comm, &u32s[1], 1, s));
   center_init_kernel<<<std::max(1, std::min(1024, (k * ld + 255) / 256)), 256, 0, s>>>(
       init_d, d, k, p.center ? mean : nullptr, Cb0, ld);
   SKM_TRY(check_launch("center_init_kernel"));
-  const bool tol_rel = !p.tol_abs && p.tol != 0.0;
   if (tol_rel) {
-    if (!p.center) {
-      sumsq_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, partials);
-      SKM_TRY(check_launch("sumsq_partial_kernel"));
-    }
     ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, sumsq);
     SKM_TRY(check_launch("ordered_sum_kernel"));
     if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, sumsq, 1, s));
@@ -380,7 +392,7 @@ static int run_fit(const FitParams& p) {
       if (plan.tc) {
         SKM_TRY(tc_estep(plan.tcp, bias, labels, changed, Dinc, st, dev_err, s));
       } else {
-        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, Dinc, 0, s));
+        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, Dinc, 0, 1, s));
       }
       if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
       if (bulk) SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, D, st, s));
@@ -446,10 +458,10 @@ static int run_fit(const FitParams& p) {
       // chi / clo / bias of the final centres were written by the last M-step
       SKM_TRY(tc_estep(plan.tcp, bias, labels, nullptr, nullptr, nullptr, dev_err, s));
     } else {
-      SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, nullptr, 0, s));
+      SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, nullptr, 0, 1, s));
     }
   }
-  inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials);
+  inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials, 1);
   SKM_TRY(check_launch("inertia_partial_kernel"));
   ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, &dscr[1]);
   SKM_TRY(check_launch("ordered_sum_kernel"));
@@ -510,7 +522,7 @@ static int launch_assign_any(const float* X, int ld, long long n, int d, const f
     launch_assign_small(d, blocks, threads, smem, s, X, ld, n, C, k, labels, mind);
     return check_launch("assign_small_kernel");
   }
-  return launch_assign_simt(X, ld, n, d, C, k, labels, mind, nullptr, nullptr, nullptr, 0, s);
+  return launch_assign_simt(X, ld, n, d, C, k, labels, mind, nullptr, nullptr, nullptr, 0, 0, s);
 }
 
 struct Staged {
@@ -585,7 +597,7 @@ float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint3
   const int n_part = sm_count() * 4;
   double* part = nullptr;
   if (buf.alloc_n(&part, (size_t)n_part + 1)) return -1.0f;
-  inertia_partial_kernel<<<n_part, 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, part);
+  inertia_partial_kernel<<<n_part, 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, part, 0);
   if (check_launch("inertia_partial_kernel")) return -1.0f;
   ordered_sum_kernel<<<1, 32, 0, s>>>(part, n_part, part + n_part);
   if (check_launch("ordered_sum_kernel")) return -1.0f;

@@ -12,12 +12,12 @@
 //
 // Data path of one tile (all asynchronous, one CTA per SM, persistent):
 //   HBM --bulk copy--> smem stage --tcgen05.cp--> TMEM x (A operand, 2 buffers)
-//   converter warps: TMEM x --tcgen05.ld--> regs --> x_lo --tcgen05.st--> TMEM
+//   converter warps: smem stage --ld.shared--> regs --> x_lo --tcgen05.st--> TMEM
 //   MMA thread: acc  = x.C_lo + x.C_hi        (A = x from TMEM, B = smem)
 //               acc += x_lo.C_hi              (A = x_lo from TMEM)
 //   epilogue warps: TMEM acc --tcgen05.ld--> argmin --> labels, deltas
-// so shared memory only carries one bulk write, one read by tcgen05.cp and the
-// small centre operands: X is read from HBM exactly once.
+// so shared memory only carries one bulk write, one read by tcgen05.cp, one by
+// the converter and the small centre operands: X is read from HBM once.
 //
 // X is the fit's blocked working copy (xblk_index): a 128-row tile is one
 // contiguous region already in the tensor core's canonical no-swizzle K-major
@@ -308,7 +308,7 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < MAX_STAGES; ++s) {
       mbar_init(bar(B_FULL(s)), 1);
-      mbar_init(bar(B_EMPTY(s)), 1);
+      mbar_init(bar(B_EMPTY(s)), 1 + 4);  // tcgen05.cp done + the 4 converter warps
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(B_XFREE(b)), 1);
@@ -426,34 +426,36 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------------- converter
+    // thread = tile row: reads its row's 16-byte quads from the shared-memory
+    // stage (a warp reads 512 contiguous bytes per quad), writes x - T(x) to
+    // its TMEM lane
     const int q = warp & 3;
+    const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     for (int i = 0; i < my_tiles; ++i) {
-      const int b = i % p.nbx;
-      if (!mbar_wait(bar(B_XT(b)), (i / p.nbx) & 1, abort_flag, p.err, 2301)) break;
+      const int s = i % p.stages;
+      if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2301)) break;
       if (!mbar_wait(bar(B_XLO_FREE), (i & 1) ^ 1, abort_flag, p.err, 2302)) break;
       tc_fence_after();
-      const uint32_t tx = tmem_base + lane_off + (uint32_t)(b * p.xcols);
+      const float4* stg = reinterpret_cast<const float4*>(base + L.x[s]) + row;  // quad j at stg[128 j]
       const uint32_t tl = tmem_base + lane_off + col_xlo;
-      for (int c0 = 0; c0 < p.nk; c0 += 4) {
-        uint32_t r[4][8];
-        const int nc = min(4, p.nk - c0);
+#pragma unroll 4
+      for (int c = 0; c < p.nk; ++c) {
+        const float4 a0 = stg[(2 * c) * 128];
+        const float4 a1 = stg[(2 * c + 1) * 128];  // zero past the last column (stage tail is zero)
+        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        uint32_t r[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (u < nc) tmem_ld8(tx + (uint32_t)((c0 + u) * KC), r[u]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (u < nc) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float v = __uint_as_float(r[u][e]);
-              r[u][e] = __float_as_uint(v - __uint_as_float(to_tf32_bits(r[u][e], p.round_mode)));
-            }
-            tmem_st8(tl + (uint32_t)((c0 + u) * KC), r[u]);
-          }
+        for (int e2 = 0; e2 < 8; ++e2) {
+          const uint32_t u = __float_as_uint(v[e2]);
+          r[e2] = __float_as_uint(v[e2] - __uint_as_float(to_tf32_bits(u, p.round_mode)));
         }
+        tmem_st8(tl + (uint32_t)(c * KC), r);
       }
+      // the stage may be refilled once tcgen05.cp and all converter warps are done
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_EMPTY(s)));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(B_XLO_FULL));

@@ -11,24 +11,26 @@
 // (the incremental M-step input).
 //
 // Data path of one tile (all asynchronous, one CTA per SM, persistent):
-//   HBM --bulk copy--> smem stage --tcgen05.cp--> TMEM x (A operand, 2 buffers)
-//   converter warps: smem stage --ld.shared--> regs --> x_lo --tcgen05.st--> TMEM
-//   MMA thread: acc  = x.C_lo + x.C_hi        (A = x from TMEM, B = smem)
-//               acc += x_lo.C_hi              (A = x_lo from TMEM)
-//   epilogue warps: TMEM acc --tcgen05.ld--> argmin --> labels, deltas
-// so shared memory only carries one bulk write, one read by tcgen05.cp, one by
-// the converter and the small centre operands: X is read from HBM once.
+//   HBM --bulk copy--> smem stage (x, the A operand of the first MMAs)
+//   MMA thread : acc  = x.[C_hi | C_lo]     (A = smem stage, B = smem; one MMA
+//                                            per K chunk with N = 2k, or two)
+//   converter  : smem stage --> x_lo = x - T(x) --tcgen05.st--> TMEM (2 buffers)
+//   MMA thread : acc += x_lo.C_hi           (A = TMEM, B = smem)
+//   epilogue   : TMEM acc --tcgen05.ld--> argmin --> labels, deltas
+// X is read from HBM exactly once per iteration.
 //
 // X is the fit's blocked working copy (xblk_index): a 128-row tile is one
 // contiguous region already in the tensor core's canonical no-swizzle K-major
 // layout (8-column chunk c = 4 KB at c * 4096: two 2 KB halves of 4 columns,
 // 8-row core matrices of 16-byte rows 128 bytes apart), so one bulk copy per
-// tile lands it ready for tcgen05.cp. The centres (B operand, k_pad rows) are
-// loaded once per CTA by TMA in the SWIZZLE_32B layout.
+// tile lands it ready for the MMAs. The centres (B operand) are loaded once
+// per CTA by TMA in the SWIZZLE_32B layout, C_hi and C_lo of chunk c side by
+// side so that [C_hi | C_lo] is one 2k-row operand.
 //
-// Warp roles (352 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer,
-// 2-5 converter, 6-9 epilogue, 10 tcgen05.cp issuer; warp w of the converter
-// / epilogue groups owns TMEM lanes 32*(w%4) .. +31 (= tile rows).
+// Warp roles (576 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer,
+// 2-9 converter, 10-17 epilogue. Warp w owns TMEM lanes 32*(w%4) .. +31 (= tile
+// rows); the two converter (epilogue) warps of a lane quarter split the K
+// chunks (the clusters) between them.
 //
 // Every mbarrier wait is bounded in time; on timeout the CTA records an error
 // code, stops issuing work, waits (bounded) for its own in-flight copies and
@@ -56,7 +58,7 @@ constexpr int KC = 8;                     // fp32 columns per K chunk (UMMA K fo
 constexpr int CHUNK_BYTES = BM * KC * 4;  // 4096
 constexpr int MAX_NK = 16;                // d <= 128
 constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
-constexpr int THREADS = 352;
+constexpr int THREADS = 576;
 constexpr int MAX_STAGES = 4;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
 
@@ -67,9 +69,9 @@ struct Params {
   int k_pad;
   int nk;      // K chunks of 8 columns
   int stages;  // X stages in shared memory
-  int nbx;     // x buffers in TMEM (1 or 2)
+  int nbl;     // x_lo buffers in TMEM (1 or 2)
   int nba;     // accumulator buffers in TMEM (1 or 2)
-  int xcols;   // TMEM columns of one x buffer (>= 8 nk, multiple of 32)
+  int xcols;   // TMEM columns of one x_lo buffer (>= 8 nk, multiple of 32)
   int tmem_cols;
   int round_mode;  // fp32->tf32 conversion of the tensor core: 0 truncate, 1 nearest-even
   const float* bias;  // ||c||^2, k entries
@@ -236,6 +238,9 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 // The tensor core's fp32 -> tf32 conversion: 0 = truncate the low 13 mantissa
 // bits, 1 = round to nearest even at bit 13 (finite inputs).
@@ -246,22 +251,24 @@ __host__ __device__ __forceinline__ uint32_t to_tf32_bits(uint32_t u, int mode) 
 }
 
 struct Smem {
-  uint32_t x[MAX_STAGES], chi, clo, bias, bars, misc, total;
+  uint32_t x[MAX_STAGES], c, bias, ep, bars, misc, total;
 };
 
 // barrier indices
 __host__ __device__ constexpr int B_FULL(int s) { return s; }
 __host__ __device__ constexpr int B_EMPTY(int s) { return MAX_STAGES + s; }
-__host__ __device__ constexpr int B_XT(int b) { return 2 * MAX_STAGES + b; }  // x tile in TMEM
-__host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + 2 + a; }
-__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + 4 + a; }
-constexpr int B_XLO_FULL = 2 * MAX_STAGES + 6;
-constexpr int B_XLO_FREE = 2 * MAX_STAGES + 7;
+__host__ __device__ constexpr int B_XLO_FULL(int b) { return 2 * MAX_STAGES + b; }
+__host__ __device__ constexpr int B_XLO_FREE(int b) { return 2 * MAX_STAGES + 2 + b; }
+__host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + 4 + a; }
+__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + 6 + a; }
 constexpr int B_C_FULL = 2 * MAX_STAGES + 8;
 constexpr int B_DONE = 2 * MAX_STAGES + 9;
-__host__ __device__ constexpr int B_XFREE(int b) { return 2 * MAX_STAGES + 10 + b; }  // x buffer reusable
-constexpr int B_CP_DONE = 2 * MAX_STAGES + 12;  // drain of the tcgen05.cp issuer
-constexpr int NUM_BARS = 2 * MAX_STAGES + 13;
+constexpr int NUM_BARS = 2 * MAX_STAGES + 10;
+
+constexpr int CONV_WARPS = 8;
+constexpr int EPI_WARPS = 8;
+constexpr int CONV_W0 = 2;
+constexpr int EPI_W0 = CONV_W0 + CONV_WARPS;
 
 __host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
   Smem s;
@@ -271,12 +278,12 @@ __host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
     s.x[i] = off;
     if (i < stages) off += stage;
   }
-  s.chi = off;
-  off += (uint32_t)nk * k_pad * 32;
-  s.clo = off;
-  off += (uint32_t)nk * k_pad * 32;
+  s.c = off;  // chunk c: C_hi (k_pad rows) then C_lo (k_pad rows), 32 bytes each
+  off += (uint32_t)nk * 2 * k_pad * 32;
   s.bias = off;
   off += (uint32_t)k_pad * 4;
+  s.ep = off;  // epilogue pair exchange: [2 parities][128 rows] (float, int)
+  off += 2 * BM * 8;
   off = (off + 15) & ~15u;
   s.bars = off;
   off += NUM_BARS * 8;
@@ -285,6 +292,8 @@ __host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
   s.total = off + 1024;  // slack for aligning the base to 1024
   return s;
 }
+
+__device__ __forceinline__ bool better(float d, int i, float bd, int bi) { return d < bd || (d == bd && i < bi); }
 
 __global__ void __launch_bounds__(THREADS, 1)
 estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_constant__ CUtensorMap tmap_clo,
@@ -303,24 +312,23 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int my_tiles = (p.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const uint32_t stage_bytes = (uint32_t)p.nk * CHUNK_BYTES;
-  const uint32_t cbytes = (uint32_t)p.nk * p.k_pad * 32;
+  const uint32_t cstride = (uint32_t)(2 * p.k_pad * 32);  // bytes per K chunk of [C_hi | C_lo]
+  const bool stacked = 2 * p.k_pad <= 256;
+  const int acc_cols = stacked ? 2 * p.k_pad : p.k_pad;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < MAX_STAGES; ++s) {
       mbar_init(bar(B_FULL(s)), 1);
-      mbar_init(bar(B_EMPTY(s)), 1 + 4);  // tcgen05.cp done + the 4 converter warps
+      mbar_init(bar(B_EMPTY(s)), 1 + CONV_WARPS);  // first MMAs done + every converter warp
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(B_XFREE(b)), 1);
-      mbar_init(bar(B_XT(b)), 1);
+      mbar_init(bar(B_XLO_FULL(b)), 32 * CONV_WARPS);
+      mbar_init(bar(B_XLO_FREE(b)), 1);
       mbar_init(bar(B_ACC_FULL(b)), 1);
-      mbar_init(bar(B_ACC_EMPTY(b)), 128);
+      mbar_init(bar(B_ACC_EMPTY(b)), 32 * EPI_WARPS);
     }
-    mbar_init(bar(B_XLO_FULL), 128);
-    mbar_init(bar(B_XLO_FREE), 1);
     mbar_init(bar(B_C_FULL), 1);
     mbar_init(bar(B_DONE), 1);
-    mbar_init(bar(B_CP_DONE), 1);
     misc[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -341,17 +349,17 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = misc[0];
-  // TMEM column map: x[0..nbx) | x_lo | acc[0..nba)
-  const uint32_t col_xlo = (uint32_t)(p.nbx * p.xcols);
-  const uint32_t col_acc = col_xlo + (uint32_t)p.xcols;
+  // TMEM column map: acc[0..nba) | x_lo[0..nbl)
+  const uint32_t col_xlo = (uint32_t)(p.nba * acc_cols);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      mbar_expect_tx(bar(B_C_FULL), 2 * cbytes);
+      mbar_expect_tx(bar(B_C_FULL), 2u * (uint32_t)p.nk * p.k_pad * 32u);
       for (int c = 0; c < p.nk; ++c) {
-        tma_load_2d(sbase + L.chi + (uint32_t)c * p.k_pad * 32, &tmap_chi, c * KC, 0, bar(B_C_FULL));
-        tma_load_2d(sbase + L.clo + (uint32_t)c * p.k_pad * 32, &tmap_clo, c * KC, 0, bar(B_C_FULL));
+        tma_load_2d(sbase + L.c + (uint32_t)c * cstride, &tmap_chi, c * KC, 0, bar(B_C_FULL));
+        tma_load_2d(sbase + L.c + (uint32_t)c * cstride + (uint32_t)p.k_pad * 32, &tmap_clo, c * KC, 0,
+                    bar(B_C_FULL));
       }
       int armed = 0;
       for (int i = 0; i < my_tiles; ++i) {
@@ -373,100 +381,90 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_tf32(p.k_pad);
+      const uint32_t idesc_k = idesc_tf32(p.k_pad);
+      const uint32_t idesc_2k = idesc_tf32(stacked ? 2 * p.k_pad : p.k_pad);
       bool ok = mbar_wait(bar(B_C_FULL), 0, abort_flag, p.err, 2201);
       for (int i = 0; ok && i < my_tiles; ++i) {
-        const int a = i % p.nba, b = i % p.nbx;
+        const int s = i % p.stages, a = i % p.nba, b = i % p.nbl;
         if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nba) & 1) ^ 1, abort_flag, p.err, 2203)) break;
-        if (!mbar_wait(bar(B_XT(b)), (i / p.nbx) & 1, abort_flag, p.err, 2202)) break;
+        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) break;
         tc_fence_after();
-        const uint32_t tacc = tmem_base + col_acc + (uint32_t)(a * p.k_pad);
-        const uint32_t tx = tmem_base + (uint32_t)(b * p.xcols);
+        const uint32_t tacc = tmem_base + (uint32_t)(a * acc_cols);
         for (int c = 0; c < p.nk; ++c) {
-          const uint64_t b_hi = sw32_desc(sbase + L.chi + (uint32_t)c * p.k_pad * 32);
-          const uint64_t b_lo = sw32_desc(sbase + L.clo + (uint32_t)c * p.k_pad * 32);
-          mma_ts(tacc, tx + (uint32_t)(c * KC), b_lo, idesc, c > 0 ? 1u : 0u);
-          mma_ts(tacc, tx + (uint32_t)(c * KC), b_hi, idesc, 1u);
+          const uint64_t a_desc = blk_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES);
+          const uint32_t cb = sbase + L.c + (uint32_t)c * cstride;
+          if (stacked) {
+            mma_ss(tacc, a_desc, sw32_desc(cb), idesc_2k, c > 0 ? 1u : 0u);
+          } else {
+            mma_ss(tacc, a_desc, sw32_desc(cb + (uint32_t)p.k_pad * 32), idesc_k, c > 0 ? 1u : 0u);
+            mma_ss(tacc, a_desc, sw32_desc(cb), idesc_k, 1u);
+          }
         }
-        // x_lo of this tile; its converter waited for the previous tile's
-        // MMAs (XLO_FREE), so x_lo is not overwritten while still read
-        if (!mbar_wait(bar(B_XLO_FULL), i & 1, abort_flag, p.err, 2204)) break;
+        tc_commit(bar(B_EMPTY(s)));  // the stage is no longer read by the tensor core
+        if (!mbar_wait(bar(B_XLO_FULL(b)), (i / p.nbl) & 1, abort_flag, p.err, 2204)) break;
         tc_fence_after();
-        for (int c = 0; c < p.nk; ++c) {
-          const uint64_t b_hi = sw32_desc(sbase + L.chi + (uint32_t)c * p.k_pad * 32);
-          mma_ts(tacc, tmem_base + col_xlo + (uint32_t)(c * KC), b_hi, idesc, 1u);
-        }
+        const uint32_t txl = tmem_base + col_xlo + (uint32_t)(b * p.xcols);
+        for (int c = 0; c < p.nk; ++c)
+          mma_ts(tacc, txl + (uint32_t)(c * KC), sw32_desc(sbase + L.c + (uint32_t)c * cstride), idesc_k, 1u);
         tc_commit(bar(B_ACC_FULL(a)));
-        tc_commit(bar(B_XLO_FREE));
-        tc_commit(bar(B_XFREE(b)));  // x[b]: all MMAs done; its converter finished before XLO_FULL
+        tc_commit(bar(B_XLO_FREE(b)));
       }
       // every tcgen05 operation issued by this thread is complete once DONE fires
       tc_commit(bar(B_DONE));
       volatile int no_abort = 0;
       mbar_wait(bar(B_DONE), 0, &no_abort, p.err, 2206);
     }
-  } else if (warp == 10) {
-    // --------------------------------------------- shared -> tensor memory copies
-    if (lane == 0) {
-      for (int i = 0; i < my_tiles; ++i) {
-        const int s = i % p.stages, b = i % p.nbx;
-        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2501)) break;
-        if (!mbar_wait(bar(B_XFREE(b)), ((i / p.nbx) & 1) ^ 1, abort_flag, p.err, 2502)) break;
-        tc_fence_after();
-        const uint32_t tx = tmem_base + (uint32_t)(b * p.xcols);
-        for (int c = 0; c < p.nk; ++c)
-          tmem_cp_chunk(tx + (uint32_t)(c * KC), blk_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES));
-        tc_commit(bar(B_XT(b)));
-        tc_commit(bar(B_EMPTY(s)));
-      }
-      // every copy issued by this thread is complete once CP_DONE fires
-      tc_commit(bar(B_CP_DONE));
-      volatile int no_abort = 0;
-      mbar_wait(bar(B_CP_DONE), 0, &no_abort, p.err, 2503);
-    }
-  } else if (warp < 6) {
+  } else if (warp < EPI_W0) {
     // ---------------------------------------------------------------- converter
-    // thread = tile row: reads its row's 16-byte quads from the shared-memory
-    // stage (a warp reads 512 contiguous bytes per quad), writes x - T(x) to
-    // its TMEM lane
+    // thread = tile row: reads its row's 16-byte quads of its K chunks from the
+    // shared-memory stage (a warp reads 512 contiguous bytes per quad) and
+    // writes x - T(x) to its TMEM lane
     const int q = warp & 3;
+    const int h = (warp - CONV_W0) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int half = (p.nk + 1) >> 1;
+    const int c0 = h ? half : 0, c1 = h ? p.nk : half;
     for (int i = 0; i < my_tiles; ++i) {
-      const int s = i % p.stages;
+      const int s = i % p.stages, b = i % p.nbl;
       if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2301)) break;
-      if (!mbar_wait(bar(B_XLO_FREE), (i & 1) ^ 1, abort_flag, p.err, 2302)) break;
+      if (!mbar_wait(bar(B_XLO_FREE(b)), ((i / p.nbl) & 1) ^ 1, abort_flag, p.err, 2302)) break;
       tc_fence_after();
       const float4* stg = reinterpret_cast<const float4*>(base + L.x[s]) + row;  // quad j at stg[128 j]
-      const uint32_t tl = tmem_base + lane_off + col_xlo;
-#pragma unroll 4
-      for (int c = 0; c < p.nk; ++c) {
+      const uint32_t tl = tmem_base + lane_off + col_xlo + (uint32_t)(b * p.xcols);
+#pragma unroll 2
+      for (int c = c0; c < c1; ++c) {
         const float4 a0 = stg[(2 * c) * 128];
         const float4 a1 = stg[(2 * c + 1) * 128];  // zero past the last column (stage tail is zero)
         const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         uint32_t r[8];
 #pragma unroll
-        for (int e2 = 0; e2 < 8; ++e2) {
-          const uint32_t u = __float_as_uint(v[e2]);
-          r[e2] = __float_as_uint(v[e2] - __uint_as_float(to_tf32_bits(u, p.round_mode)));
-        }
+        for (int e2 = 0; e2 < 8; ++e2)
+          r[e2] = __float_as_uint(v[e2] - __uint_as_float(to_tf32_bits(__float_as_uint(v[e2]), p.round_mode)));
         tmem_st8(tl + (uint32_t)(c * KC), r);
       }
-      // the stage may be refilled once tcgen05.cp and all converter warps are done
+      // the stage may be refilled once the first MMAs and all converter warps are done
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_EMPTY(s)));
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar(B_XLO_FULL));
+      mbar_arrive(bar(B_XLO_FULL(b)));
     }
   } else {
     // ----------------------------------------------------------------- epilogue
+    // the two warps of a lane quarter take the clusters [0, k/2) and
+    // [k/2, k); the upper warp hands its (min, index) to the lower one
     const int q = warp & 3;
+    const int h = (warp - EPI_W0) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int kh = p.k_pad >> 1;  // multiple of 8
+    const int j0 = h * kh;
+    float* ep_best = reinterpret_cast<float*>(base + L.ep);
+    int* ep_idx = reinterpret_cast<int*>(base + L.ep + 2 * BM * 4);
     int old_next = -1;
-    if (p.changed && my_tiles > 0) {
+    if (h == 0 && p.changed && my_tiles > 0) {
       const long long g0 = (long long)blockIdx.x * BM + row;
       old_next = g0 < p.n ? p.labels[g0] : -1;
     }
@@ -474,39 +472,56 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
       const int a = i % p.nba;
       const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
       const int old = old_next;
-      if (p.changed && i + 1 < my_tiles) {  // prefetch the next tile's previous labels
+      if (h == 0 && p.changed && i + 1 < my_tiles) {  // prefetch the next tile's previous labels
         const long long g1 = grow + (long long)gridDim.x * BM;
         old_next = g1 < p.n ? p.labels[g1] : -1;
       }
       if (!mbar_wait(bar(B_ACC_FULL(a)), (i / p.nba) & 1, abort_flag, p.err, 2401)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + lane_off + col_acc + (uint32_t)(a * p.k_pad);
-      float best = INFINITY;
-      int bl = 0;
-      for (int j0 = 0; j0 < p.k_pad; j0 += 64) {
-        uint32_t v[4][16];
-        const int nq = min(4, (p.k_pad - j0) >> 4);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (u < nq) tmem_ld16(taddr + (uint32_t)(j0 + 16 * u), v[u]);
+      const uint32_t taddr = tmem_base + lane_off + (uint32_t)(a * acc_cols);
+      // four independent running minima (columns j = 4m + u), merged in index order
+      float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+      int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
+      for (int jb = 0; jb < kh; jb += 16) {
+        uint32_t v[16], w[16];
+        tmem_ld16(taddr + (uint32_t)(j0 + jb), v);
+        if (stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + j0 + jb), w);
         tmem_ld_wait();
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (u < nq) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int j = j0 + 16 * u + jj;
-              const float dist = fmaf(-2.0f, __uint_as_float(v[u][jj]), bias_s[j]);
-              if (dist < best) {
-                best = dist;
-                bl = j;
-              }
-            }
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = j0 + jb + jj;
+          float dot = __uint_as_float(v[jj]);
+          if (stacked) dot += __uint_as_float(w[jj]);
+          const float dist = fmaf(-2.0f, dot, bias_s[j]);
+          if (dist < bd[jj & 3]) {
+            bd[jj & 3] = dist;
+            bi[jj & 3] = j;
           }
         }
       }
       tc_fence_before();
       mbar_arrive(bar(B_ACC_EMPTY(a)));
+      float best = bd[0];
+      int bl = bi[0];
+#pragma unroll
+      for (int u = 1; u < 4; ++u)
+        if (better(bd[u], bi[u], best, bl)) {
+          best = bd[u];
+          bl = bi[u];
+        }
+      const int slot = (i & 1) * BM + row;
+      if (h == 1) {
+        ep_best[slot] = best;
+        ep_idx[slot] = bl;
+        named_bar(1 + q, 64);
+        continue;
+      }
+      named_bar(1 + q, 64);
+      if (better(ep_best[slot], ep_idx[slot], best, bl)) {
+        best = ep_best[slot];
+        bl = ep_idx[slot];
+      }
+      if (bl >= p.k) bl = 0;  // only reachable when every distance is +inf or NaN
       bool ch = false;
       if (grow < p.n) {
         ch = p.changed && old != bl;
@@ -737,13 +752,15 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->k = k;
   plan->k_pad = (int)round_up((size_t)k, 16);
   plan->k_steps = (ld + tc::KC - 1) / tc::KC;
-  // TMEM: x buffers (32-column aligned), one x_lo buffer, accumulators
+  // TMEM: accumulators (2k columns when [C_hi | C_lo] is one N <= 256 operand,
+  // else k) and x_lo buffers (32-column aligned); double-buffer what fits
   plan->xcols = (int)round_up((size_t)plan->k_steps * tc::KC, 32);
-  plan->nbx = 2;
+  const int acc_cols = 2 * plan->k_pad <= 256 ? 2 * plan->k_pad : plan->k_pad;
+  plan->nbl = 2;
   plan->nba = 2;
-  auto cols = [&]() { return (plan->nbx + 1) * plan->xcols + plan->nba * plan->k_pad; };
+  auto cols = [&]() { return plan->nba * acc_cols + plan->nbl * plan->xcols; };
   if (cols() > 512) plan->nba = 1;
-  if (cols() > 512) plan->nbx = 1;
+  if (cols() > 512) plan->nbl = 1;
   if (cols() > 512) return OK;
   int tcols = 32;
   while (tcols < cols()) tcols *= 2;
@@ -785,7 +802,7 @@ int tc_estep(const TcPlan& plan, const float* bias, int32_t* labels, unsigned lo
   p.k_pad = plan.k_pad;
   p.nk = plan.k_steps;
   p.stages = plan.stages;
-  p.nbx = plan.nbx;
+  p.nbl = plan.nbl;
   p.nba = plan.nba;
   p.xcols = plan.xcols;
   p.tmem_cols = plan.tmem_cols;

@@ -1,6 +1,6 @@
-// Tensor-core (tcgen05, sm_100a) E-step: TMA-fed X tiles copied into tensor
-// memory, 3xTF32 distance tiles accumulated in tensor memory, running argmin
-// in registers, incremental fixed-point deltas for rows that change label.
+// Tensor-core (tcgen05, sm_100a) E-step: bulk-copied X tiles, 3xTF32 distance
+// tiles accumulated in tensor memory, running argmin in registers, incremental
+// fixed-point deltas for rows that change label.
 #pragma once
 
 #include <cuda.h>
@@ -22,9 +22,9 @@ struct TcPlan {
   int k_pad = 0;       // clusters padded to the MMA N granularity (16)
   int k_steps = 0;     // K = ld in chunks of 8 columns
   int stages = 0;      // X stages in shared memory
-  int nbx = 0;         // x buffers in tensor memory
+  int nbl = 0;         // x_lo buffers in tensor memory
   int nba = 0;         // accumulator buffers in tensor memory
-  int xcols = 0;       // tensor-memory columns per x buffer
+  int xcols = 0;       // tensor-memory columns per x_lo buffer
   int tmem_cols = 0;   // tensor-memory allocation
   int round_mode = 0;  // tensor-core fp32->tf32 conversion (probe result)
   int grid = 0;

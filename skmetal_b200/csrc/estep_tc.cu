@@ -27,8 +27,12 @@
 // per CTA by TMA in the SWIZZLE_32B layout, C_hi and C_lo of chunk c side by
 // side so that [C_hi | C_lo] is one 2k-row operand.
 //
-// Warp roles (576 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer,
-// 2-9 converter, 10-17 epilogue. Warp w owns TMEM lanes 32*(w%4) .. +31 (= tile
+// Warp roles (608 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer
+// of even tiles, 18 MMA issuer of odd tiles, 2-9 converter, 10-17 epilogue.
+// A single thread issues tcgen05.mma at roughly one instruction per ~120
+// cycles whatever N is, while issuers on different SM sub-partitions overlap,
+// so tiles alternate between two issuing warps (each with its own
+// accumulator and x_lo buffer). Warp w owns TMEM lanes 32*(w%4) .. +31 (= tile
 // rows); the two converter (epilogue) warps of a lane quarter split the K
 // chunks (the clusters) between them.
 //
@@ -58,7 +62,7 @@ constexpr int KC = 8;                     // fp32 columns per K chunk (UMMA K fo
 constexpr int CHUNK_BYTES = BM * KC * 4;  // 4096
 constexpr int MAX_NK = 16;                // d <= 128
 constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
-constexpr int THREADS = 576;
+constexpr int THREADS = 608;
 constexpr int MAX_STAGES = 4;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
 
@@ -262,8 +266,9 @@ __host__ __device__ constexpr int B_XLO_FREE(int b) { return 2 * MAX_STAGES + 2 
 __host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + 4 + a; }
 __host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + 6 + a; }
 constexpr int B_C_FULL = 2 * MAX_STAGES + 8;
-constexpr int B_DONE = 2 * MAX_STAGES + 9;
-constexpr int NUM_BARS = 2 * MAX_STAGES + 10;
+__host__ __device__ constexpr int B_DONE(int t) { return 2 * MAX_STAGES + 9 + t; }  // drain of MMA issuer t
+constexpr int NUM_BARS = 2 * MAX_STAGES + 11;
+constexpr int MMA_W1 = 18;  // second MMA issuer warp (sub-partition 2)
 
 constexpr int CONV_WARPS = 8;
 constexpr int EPI_WARPS = 8;
@@ -328,7 +333,8 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
       mbar_init(bar(B_ACC_EMPTY(b)), 32 * EPI_WARPS);
     }
     mbar_init(bar(B_C_FULL), 1);
-    mbar_init(bar(B_DONE), 1);
+    mbar_init(bar(B_DONE(0)), 1);
+    mbar_init(bar(B_DONE(1)), 1);
     misc[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -378,13 +384,17 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
       for (int i = (armed > p.stages ? armed - p.stages : 0); i < armed; ++i)
         mbar_wait(bar(B_FULL(i % p.stages)), (i / p.stages) & 1, &no_abort, p.err, 2103);
     }
-  } else if (warp == 1) {
-    // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+  } else if (warp == 1 || warp == MMA_W1) {
+    // ---------------------------------------------------------- MMA issuers
+    // two issuers when every tile has its own accumulator and x_lo buffer
+    // (nba == nbl == 2), else warp 1 issues everything
+    const int n_iss = (p.nba == 2 && p.nbl == 2) ? 2 : 1;
+    const int t = warp == 1 ? 0 : 1;
+    if (lane == 0 && t < n_iss) {
       const uint32_t idesc_k = idesc_tf32(p.k_pad);
       const uint32_t idesc_2k = idesc_tf32(stacked ? 2 * p.k_pad : p.k_pad);
       bool ok = mbar_wait(bar(B_C_FULL), 0, abort_flag, p.err, 2201);
-      for (int i = 0; ok && i < my_tiles; ++i) {
+      for (int i = t; ok && i < my_tiles; i += n_iss) {
         const int s = i % p.stages, a = i % p.nba, b = i % p.nbl;
         if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nba) & 1) ^ 1, abort_flag, p.err, 2203)) break;
         if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) break;
@@ -410,11 +420,11 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
         tc_commit(bar(B_XLO_FREE(b)));
       }
       // every tcgen05 operation issued by this thread is complete once DONE fires
-      tc_commit(bar(B_DONE));
+      tc_commit(bar(B_DONE(t)));
       volatile int no_abort = 0;
-      mbar_wait(bar(B_DONE), 0, &no_abort, p.err, 2206);
+      mbar_wait(bar(B_DONE(t)), 0, &no_abort, p.err, 2206);
     }
-  } else if (warp < EPI_W0) {
+  } else if (warp >= CONV_W0 && warp < EPI_W0) {
     // ---------------------------------------------------------------- converter
     // thread = tile row: reads its row's 16-byte quads of its K chunks from the
     // shared-memory stage (a warp reads 512 contiguous bytes per quad) and
@@ -451,7 +461,7 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
       tc_fence_before();
       mbar_arrive(bar(B_XLO_FULL(b)));
     }
-  } else {
+  } else if (warp >= EPI_W0 && warp < EPI_W0 + EPI_WARPS) {
     // ----------------------------------------------------------------- epilogue
     // the two warps of a lane quarter take the clusters [0, k/2) and
     // [k/2, k); the upper warp hands its (min, index) to the lower one
@@ -459,8 +469,10 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
     const int h = (warp - EPI_W0) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const int kh = p.k_pad >> 1;  // multiple of 8
-    const int j0 = h * kh;
+    // split at a multiple of 16 (the TMEM load width): [0, kh0) and [kh0, k_pad)
+    const int kh0 = ((p.k_pad >> 1) + 15) & ~15;
+    const int j0 = h ? kh0 : 0;
+    const int kh = h ? p.k_pad - kh0 : kh0;
     float* ep_best = reinterpret_cast<float*>(base + L.ep);
     int* ep_idx = reinterpret_cast<int*>(base + L.ep + 2 * BM * 4);
     int old_next = -1;

@@ -156,12 +156,15 @@ def test_lloyd_step_relocation_lockstep():
 
 @pytest.mark.parametrize("name,n", [("c1", 30000), ("c2", 30000)])
 def test_tc_fit_matches_simt_fit(name, n):
+    """Tensor-core and SIMT E-steps agree (one Lloyd iteration plus the final
+    E-step, so that the comparison is not amplified by later iterations)."""
     w = scaled(name, n)
     X, init = make_workload(w)
-    c_tc, l_tc, i_tc, n_tc = _bridge.kmeans_fit(X, init, 5, 0.0)
-    c_si, l_si, i_si, n_si = _bridge.kmeans_fit(X, init, 5, 0.0, simt=True)
+    c_tc, l_tc, i_tc, n_tc = _bridge.kmeans_fit(X, init, 1, 0.0)
+    c_si, l_si, i_si, n_si = _bridge.kmeans_fit(X, init, 1, 0.0, simt=True)
     mean, Xc, _ = ora.center_data(X)
     check_labels(Xc, c_si - mean, l_tc, l_si, "tc vs simt")
+    np.testing.assert_allclose(c_tc, c_si, rtol=CENTER_RTOL, atol=1e-4)
     assert i_tc == pytest.approx(i_si, rel=1e-5)
 
 

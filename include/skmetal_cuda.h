@@ -173,6 +173,44 @@ int skmetal_dataset_fit_shard(void* handle, const float* init, size_t k, int32_t
                               uint32_t flags, uint64_t row_base, uint64_t n_total, float* centers_out,
                               int32_t* labels_out, double* inertia_out, int32_t* n_iter_out);
 
+/* ---- no-allocation entry point -------------------------------------------- */
+
+/* Size of the static device scratch behind skmetal_kmeans_update_centers_noalloc
+ * (2 MiB, held on every device that loads the library until the process exits). */
+#define SKMETAL_NOALLOC_SCRATCH_BYTES 2097152u
+
+/* No counterpart in the reference: an addition for callers that must not
+ * allocate device memory while they run -- a process whose free device memory
+ * is already claimed by another allocator's pool, where a cudaMalloc would
+ * fail, or a loop that cannot afford the device-wide waits that cudaMalloc and
+ * cudaFree may cause. It calls no cudaMalloc, cudaFree or allocating library
+ * routine; its scratch is one static device array of
+ * SKMETAL_NOALLOC_SCRATCH_BYTES.
+ *
+ * Centroid update from given labels: for every cluster c with at least one
+ * row, centers[c] = mean of the rows i with labels[i] == c, computed with the
+ * fit's exact fixed-point sums, so the result is bit-identical to the
+ * centres of skmetal_kmeans_lloyd_iter for the same labels when no cluster is
+ * empty. Rows of empty clusters are left unchanged (no relocation). weight,
+ * if not NULL, receives the per-cluster row counts.
+ *
+ * X (n x d row-major float32), labels (n int32 in [0, k)), centers (k x d)
+ * and weight (k float32) must be device memory of the current device. The
+ * work runs on `stream` (a cudaStream_t; NULL is the default stream) and the
+ * call returns once it has completed. Sizes with k * (d + 1) above
+ * SKMETAL_NOALLOC_SCRATCH_BYTES / 8 - 1 (262143) do not fit the scratch and
+ * return 1 (invalid argument) with a message; so do labels outside [0, k) and
+ * non-finite X, which leave centers and weight untouched.
+ *
+ * The first call on each device looks up the scratch's device address
+ * (cudaGetSymbolAddress, with that device current), which can load the
+ * library's device code there; make that first call before any stream capture
+ * begins. All callers on a device share the one scratch array: calls on the
+ * same device that overlap in time (from several threads, or on several
+ * streams) race on it and corrupt each other's results, so serialise them. */
+int skmetal_kmeans_update_centers_noalloc(const float* X, const int32_t* labels, size_t n, size_t d, size_t k,
+                                          float* centers, float* weight, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

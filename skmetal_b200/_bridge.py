@@ -83,6 +83,8 @@ _SIGNATURES = [
     ("skmetal_dataset_fit_shard", _c_int, [_c_void_p, _c_void_p, _c_size_t, _c_i32, _c_double, _c_u32, _c_u64,
                                            _c_u64, _c_void_p, _c_void_p, ctypes.POINTER(_c_double),
                                            ctypes.POINTER(_c_i32)]),
+    ("skmetal_kmeans_update_centers_noalloc", _c_int, [_c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t,
+                                                       _c_void_p, _c_void_p, _c_void_p]),
 ]
 EXPORTED_SYMBOLS = [s[0] for s in _SIGNATURES]
 

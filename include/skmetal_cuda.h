@@ -62,13 +62,14 @@ unsigned long long skmetal_launch_count(void);
  * point from now fails with `code` before doing any GPU work. */
 int skmetal_debug_inject_failure(int code, int after_calls);
 
-/* Tensor-core self-check (no reference counterpart): runs a 128 x 8 tf32 MMA
- * probe on the current device. *mode = 0 when the tensor core truncates fp32
- * operands to tf32, 1 when it rounds to nearest even, -1 when the result
- * matches neither (the library then uses its SIMT E-step). raw3072, if not
- * NULL, receives the probe's raw output (copied operand, products with the
- * operand read from tensor memory, products with it read from shared memory). */
-int skmetal_debug_tc_probe(int* mode, uint32_t* raw3072);
+/* Tensor-core self-check (no reference counterpart): pushes exactly
+ * representable operands through the E-step's fp16 split, centre image and
+ * tcgen05.mma sequences on the current device and compares the products with
+ * their exact values. *mode = 0 when they match, -1 otherwise (the library
+ * then uses its SIMT E-step). raw4096, if not NULL, receives the products
+ * (float bits): 128 x 16 for the stacked layout, then 128 x 16 for the
+ * two-segment layout. */
+int skmetal_debug_tc_probe(int* mode, uint32_t* raw4096);
 
 /* ---- KMeans path: reference entry points -------------------------------- */
 

@@ -397,9 +397,13 @@ def device_info() -> dict:
 
 
 def debug_tc_probe(raw: bool = False):
-    """Tensor-core self-check: (mode, raw) with mode 0 truncation, 1 rounding, -1 unusable."""
+    """Tensor-core self-check: (mode, raw) with mode 0 exact, -1 unusable (SIMT E-step).
+
+    ``raw`` (4096 uint32 bit patterns of float32): [0, 2048) the stacked-layout
+    products, [2048, 4096) the two-segment-layout products, each 128 x 16.
+    """
     mode = _c_int(-3)
-    out = np.zeros(3072, dtype=np.uint32) if raw else None
+    out = np.zeros(4096, dtype=np.uint32) if raw else None
     rc = _fn("skmetal_debug_tc_probe")(ctypes.byref(mode), out.ctypes.data if raw else None)
     if rc != 0:
         raise RuntimeError(f"skmetal_debug_tc_probe failed with code {rc}: {_last_error()}")

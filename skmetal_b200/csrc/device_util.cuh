@@ -1,6 +1,7 @@
 // Device helpers shared by the kernel translation units.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -75,6 +76,70 @@ __device__ __forceinline__ void warp_apply_changed(const float* __restrict__ X, 
     const int o = __shfl_sync(0xffffffffu, old, src);
     const int nn = __shfl_sync(0xffffffffu, neu, src);
     warp_apply_delta(X, ld, d, k, r, o, nn, D, scale);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split-fp16 operands of the tensor-core E-step.
+// x . c is computed as x_hi.c_hi + x_lo.c_hi + x_hi.c_lo with fp16 parts of
+// power-of-two scaled values (v * 2^e = v_hi + v_lo, v_hi = fp16(v * 2^e),
+// v_lo = fp16(v * 2^e - v_hi)) multiplied exactly and accumulated in fp32 by
+// the tensor core. fp16 keeps 11 significant bits, as many as tf32, so this is
+// 3xTF32 with the exponent range fixed by the scale; the dropped x_lo.c_lo
+// term is below 2^-22 of |x||c|.
+// ---------------------------------------------------------------------------
+
+// Scale exponent for values bounded by the float whose bits are given: with
+// max |v| < 2^E, v * 2^(14 - E) < 2^14 (fp16 reaches 65504, so centres may be
+// up to 4x larger than the bound). Clamped so that 2^(1 - 2e) stays a normal
+// float; zero or non-finite bounds give 0.
+__device__ __forceinline__ int split_exp(unsigned int maxabs_bits) {
+  const float mx = __uint_as_float(maxabs_bits);
+  if (!(mx > 0.0f) || mx > 3.0e38f) return 0;
+  int E = 0;
+  frexpf(mx, &E);
+  return max(-50, min(63, 14 - E));
+}
+
+// Centre image: the exact shared-memory bytes of the E-step's B operand (fp16,
+// K-major, no swizzle: core matrices of 8 rows x 16 bytes, 8-row groups 128
+// bytes apart, the two 8-element K halves N * 16 bytes apart), K chunk c (8
+// columns) at c * N * 32 bytes. Its K half 0 multiplies x_hi, half 1 x_lo.
+//  stacked (2 k_pad <= 256): N = 2 k_pad; rows j < k_pad hold (c_hi | c_hi),
+//    rows k_pad + j hold (c_lo | 0), so acc[j] + acc[k_pad + j] = x . c_j.
+//  otherwise: N = k_pad; segment 1 holds (c_hi | c_hi) per chunk, segment 2
+//    (after nk chunks) holds c_lo of chunk pairs (2m | 2m + 1), multiplied by
+//    x_hi of the same pair; both accumulate into one accumulator.
+// Entries of padding rows and columns are zero.
+struct CentreImage {
+  uint16_t* img;  // fp16 bit patterns; null when the tensor-core path is off
+  int k_pad;      // clusters padded to 16
+  int nk;         // K chunks of 8 columns
+  int stacked;
+};
+
+__host__ __device__ inline size_t cimg_halves(int k_pad, int nk, int stacked) {
+  return stacked ? (size_t)nk * 2 * k_pad * 16 : (size_t)nk * k_pad * 16 + (size_t)((nk + 1) / 2) * k_pad * 16;
+}
+
+// Writes centre c, column j (value v, scale s = 2^e) into the image.
+__device__ __forceinline__ void cimg_put(const CentreImage& ci, int c, int j, float v, float s) {
+  const float vs = v * s;
+  const __half hi = __float2half_rn(vs);
+  const __half lo = __float2half_rn(vs - __half2float(hi));
+  const uint16_t hb = __half_as_ushort(hi), lb = __half_as_ushort(lo);
+  const int chunk = j >> 3, e = j & 7;
+  const int N = ci.stacked ? 2 * ci.k_pad : ci.k_pad;
+  const size_t base = (size_t)chunk * N * 16;
+  const size_t r = (size_t)(c >> 3) * 64 + (size_t)(c & 7) * 8 + e;
+  ci.img[base + r] = hb;
+  ci.img[base + (size_t)N * 8 + r] = hb;
+  if (ci.stacked) {
+    const int cl = ci.k_pad + c;
+    ci.img[base + (size_t)(cl >> 3) * 64 + (size_t)(cl & 7) * 8 + e] = lb;
+  } else {
+    const size_t seg2 = (size_t)ci.nk * ci.k_pad * 16;
+    ci.img[seg2 + (size_t)(chunk >> 1) * ci.k_pad * 16 + (size_t)(chunk & 1) * ci.k_pad * 8 + r] = lb;
   }
 }
 

@@ -1,45 +1,45 @@
 // Tensor-core E-step for sm_100a: labels[i] = argmin_j (||c_j||^2 - 2 x_i . c_j)
 // over 128-row tiles of X, with the dot products computed by tcgen05.mma in
-// 3xTF32 split precision and accumulated in fp32 in tensor memory (TMEM):
-//     x . c  ~=  T(x).T(c) + T(x).c_lo + x_lo.T(c)
-// where T is the tensor core's own fp32 -> tf32 conversion (measured once per
-// device by tc_probe), x_lo = x - T(x) and c_lo = c - T(c). The n x k
-// distance matrix never leaves the SM: the epilogue reads each row's k
-// accumulators from TMEM and keeps a running argmin in registers (strict '<',
-// lowest index first, as sklearn/cluster/_k_means_lloyd.pyx:205-213). Rows
-// whose label changed add their exact fixed-point deltas to the centroid sums
-// (the incremental M-step input).
+// split-fp16 precision (x_hi.c_hi + x_lo.c_hi + x_hi.c_lo, the 3xTF32 scheme
+// with fp16 parts of power-of-two scaled values; see CentreImage) and
+// accumulated in fp32 in tensor memory (TMEM). The n x k distance matrix never
+// leaves the SM: the epilogue reads each row's accumulators from TMEM and keeps
+// a running argmin in registers (strict '<', lowest index first, as
+// sklearn/cluster/_k_means_lloyd.pyx:205-213). Rows whose label changed add
+// their exact fixed-point deltas to the centroid sums (the incremental M-step
+// input).
 //
-// Data path of one tile (all asynchronous, one CTA per SM, persistent):
-//   HBM --bulk copy--> smem stage (x, the A operand of the first MMAs)
-//   MMA thread : acc  = x.[C_hi | C_lo]     (A = smem stage, B = smem; one MMA
-//                                            per K chunk with N = 2k, or two)
-//   converter  : smem stage --> x_lo = x - T(x) --tcgen05.st--> TMEM (2 buffers)
-//   MMA thread : acc += x_lo.C_hi           (A = TMEM, B = smem)
+// Data path of one tile (all asynchronous, one persistent CTA per SM):
+//   HBM --bulk copy--> smem stage (fp32 x in the blocked layout)
+//   converter  : rewrites the stage in place: the two fp32 column quads of each
+//                8-column chunk become (x_hi | x_lo) in fp16, i.e. one K = 16
+//                slice of the kind::f16 A operand in the canonical layout
+//   MMA thread : acc = A . B   (A = stage, B = centre image; one MMA per chunk)
 //   epilogue   : TMEM acc --tcgen05.ld--> argmin --> labels, deltas
 // X is read from HBM exactly once per iteration.
 //
 // X is the fit's blocked working copy (xblk_index): a 128-row tile is one
-// contiguous region already in the tensor core's canonical no-swizzle K-major
-// layout (8-column chunk c = 4 KB at c * 4096: two 2 KB halves of 4 columns,
-// 8-row core matrices of 16-byte rows 128 bytes apart), so one bulk copy per
-// tile lands it ready for the MMAs. The centres (B operand) are loaded once
-// per CTA by TMA in the SWIZZLE_32B layout, C_hi and C_lo of chunk c side by
-// side so that [C_hi | C_lo] is one 2k-row operand.
+// contiguous region in the tensor core's canonical no-swizzle K-major layout
+// (8-column chunk c = 4 KB at c * 4096: two 2 KB halves of 4 columns, 8-row
+// core matrices of 16-byte rows 128 bytes apart), so one bulk copy per tile
+// lands it, and after the in-place split the same descriptor geometry (K
+// halves 2048 bytes apart) addresses (x_hi | x_lo) of the chunk. The centre
+// image (B) is written by the M-step in exactly its shared-memory layout and
+// loaded once per CTA.
 //
-// Warp roles (608 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer
-// of even tiles, 18 MMA issuer of odd tiles, 2-9 converter, 10-17 epilogue.
-// A single thread issues tcgen05.mma at roughly one instruction per ~120
+// Warp roles (640 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer
+// of even tiles, 2 MMA issuer of odd tiles, 3 idle, 4-11 converter, 12-19
+// epilogue. One thread issues tcgen05.mma at roughly one instruction per ~120
 // cycles whatever N is, while issuers on different SM sub-partitions overlap,
-// so tiles alternate between two issuing warps (each with its own
-// accumulator and x_lo buffer). Warp w owns TMEM lanes 32*(w%4) .. +31 (= tile
-// rows); the two converter (epilogue) warps of a lane quarter split the K
-// chunks (the clusters) between them.
+// so tiles alternate between two issuing warps. Warp w reads TMEM lanes
+// 32*(w%4) .. +31 (= tile rows); the epilogue warps form two groups of one
+// warp per lane quarter that take alternate tiles.
 //
 // Every mbarrier wait is bounded in time; on timeout the CTA records an error
 // code, stops issuing work, waits (bounded) for its own in-flight copies and
 // tensor-core operations, frees its tensor memory and returns.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -58,12 +58,13 @@ namespace skm {
 namespace tc {
 
 constexpr int BM = 128;                   // rows per tile (UMMA M)
-constexpr int KC = 8;                     // fp32 columns per K chunk (UMMA K for tf32)
+constexpr int KC = 8;                     // fp32 columns per K chunk (one kind::f16 MMA, K = 16)
 constexpr int CHUNK_BYTES = BM * KC * 4;  // 4096
 constexpr int MAX_NK = 16;                // d <= 128
 constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
-constexpr int THREADS = 608;
+constexpr int THREADS = 640;
 constexpr int MAX_STAGES = 4;
+constexpr int MAX_ACC = 4;
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
 
 struct Params {
@@ -71,22 +72,26 @@ struct Params {
   long long n;
   int k;
   int k_pad;
-  int nk;      // K chunks of 8 columns
-  int stages;  // X stages in shared memory
-  int nbl;     // x_lo buffers in TMEM (1 or 2)
-  int nba;     // accumulator buffers in TMEM (1 or 2)
-  int xcols;   // TMEM columns of one x_lo buffer (>= 8 nk, multiple of 32)
+  int nk;         // K chunks of 8 columns
+  int nq;         // fp32 column quads present in a tile (ld / 4)
+  int stacked;    // centre image layout (CentreImage)
+  int stages;     // X stages in shared memory
+  int nacc;       // accumulators in TMEM
+  int acc_cols;   // TMEM columns of one accumulator
   int tmem_cols;
-  int round_mode;  // fp32->tf32 conversion of the tensor core: 0 truncate, 1 nearest-even
-  const float* bias;  // ||c||^2, k entries
+  uint32_t stage_bytes;  // >= nk (even nk when not stacked) chunks
+  uint32_t img_bytes;
+  const uint16_t* img;   // centre image
+  const int* sexp;       // {xexp, cexp}: operand scales 2^xexp, 2^cexp
+  const float* bias;     // ||c||^2, k entries
   int32_t* labels;
   unsigned long long* changed;
-  long long* D;  // nullable: incremental deltas of rows that changed label
-  const float* X;  // blocked layout
+  long long* D;     // nullable: incremental deltas of rows that changed label
+  const float* X;   // blocked layout
   int ld;
   int d;
   uint32_t tile_bytes;  // 512 * ld: one tile of blocked X
-  const FitState* st;  // nullable: skip when st->done
+  const FitState* st;   // nullable: skip when st->done; scale for D
   int* err;
 };
 
@@ -142,91 +147,42 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_fla
   }
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(src)), "r"(bytes), "r"(bar)
                : "memory");
 }
 
-// K-major no-swizzle shared-memory matrix descriptor for one 128 x 8 fp32
-// chunk of a blocked tile: core matrices of 8 rows x 16 bytes, 8-row groups
-// 128 bytes apart (stride byte offset), the two 4-column halves 2048 bytes
-// apart (leading byte offset), descriptor version 1, layout type 0.
-__device__ __forceinline__ uint64_t blk_desc(uint32_t saddr) {
+// K-major no-swizzle shared-memory matrix descriptor: core matrices of 8 rows
+// x 16 bytes; `lbo` = bytes between the two K halves of a K = 16 slice, `sbo`
+// = bytes between 8-row groups; descriptor version 1, layout type 0.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)(2048u >> 4) << 16;
-  d |= (uint64_t)(128u >> 4) << 32;
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;
   return d;
 }
 
-// K-major SWIZZLE_32B shared-memory matrix descriptor: rows of 32 bytes,
-// 8-row atoms of 256 bytes (stride byte offset), leading byte offset unused
-// (1), descriptor version 1 (sm_100), layout type 6 (SWIZZLE_32B).
-__device__ __forceinline__ uint64_t sw32_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;
-  d |= (uint64_t)(256u >> 4) << 32;
-  d |= (uint64_t)1u << 46;
-  d |= (uint64_t)6u << 61;
-  return d;
-}
-
-// kind::tf32 instruction descriptor: D fp32, A/B tf32, both K-major, M=128, N.
-__host__ __device__ constexpr uint32_t idesc_tf32(int N) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, M = 128, N.
+__host__ __device__ constexpr uint32_t idesc_f16(int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem] . B[smem]^T
-__device__ __forceinline__ void mma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// D[tmem] (+)= A[tmem] . B[smem]^T
-__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// 128 rows x 8 fp32 (one chunk) from shared memory into TMEM lanes 0..127
-__device__ __forceinline__ void tmem_cp_chunk(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
 
@@ -239,56 +195,86 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void named_bar(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Rewrites one row of one 8-column chunk of a blocked fp32 tile in place as a
+// K = 16 slice of the kind::f16 A operand: the 16 bytes of column quad 2c
+// become the fp16 high parts of the row's 8 values scaled by s, those of quad
+// 2c + 1 the fp16 remainders. Quads at or past nq (beyond the last column)
+// read as zero.
+__device__ __forceinline__ void split_chunk_row(unsigned char* tile, int row, int c, int nq, float s) {
+  float4* q0 = reinterpret_cast<float4*>(tile + (size_t)(2 * c) * 2048 + (size_t)row * 16);
+  float4* q1 = reinterpret_cast<float4*>(tile + (size_t)(2 * c + 1) * 2048 + (size_t)row * 16);
+  const float4 a = *q0;
+  const float4 b = (2 * c + 1 < nq) ? *q1 : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float v[8] = {a.x * s, a.y * s, a.z * s, a.w * s, b.x * s, b.y * s, b.z * s, b.w * s};
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const __half2 h = __floats2half2_rn(v[2 * p], v[2 * p + 1]);
+    const float2 hf = __half22float2(h);
+    hi[p] = h2_bits(h);
+    lo[p] = h2_bits(__floats2half2_rn(v[2 * p] - hf.x, v[2 * p + 1] - hf.y));
+  }
+  *reinterpret_cast<uint4*>(q0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(q1) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
-// The tensor core's fp32 -> tf32 conversion: 0 = truncate the low 13 mantissa
-// bits, 1 = round to nearest even at bit 13 (finite inputs).
-__host__ __device__ __forceinline__ uint32_t to_tf32_bits(uint32_t u, int mode) {
-  if (mode == 0) return u & 0xffffe000u;
-  const uint32_t lsb = (u >> 13) & 1u;
-  return (u + 0x0fffu + lsb) & 0xffffe000u;
+// The MMAs of one tile: A = stage (split in place), B = centre image in smem.
+__device__ __forceinline__ void issue_tile_mmas(uint32_t tacc, uint32_t stage, uint32_t img, int nk, int k_pad,
+                                                int stacked) {
+  if (stacked) {
+    const int N = 2 * k_pad;
+    const uint32_t idesc = idesc_f16(N);
+    for (int c = 0; c < nk; ++c)
+      mma_f16(tacc, kmajor_desc(stage + (uint32_t)c * CHUNK_BYTES, 2048u, 128u),
+              kmajor_desc(img + (uint32_t)(c * N * 32), (uint32_t)(N * 16), 128u), idesc, c > 0 ? 1u : 0u);
+  } else {
+    const uint32_t idesc = idesc_f16(k_pad);
+    for (int c = 0; c < nk; ++c)
+      mma_f16(tacc, kmajor_desc(stage + (uint32_t)c * CHUNK_BYTES, 2048u, 128u),
+              kmajor_desc(img + (uint32_t)(c * k_pad * 32), (uint32_t)(k_pad * 16), 128u), idesc, c > 0 ? 1u : 0u);
+    // x_hi of chunk pairs (2m | 2m + 1) times c_lo of the same pair
+    const uint32_t seg2 = img + (uint32_t)(nk * k_pad * 32);
+    for (int m = 0; 2 * m < nk; ++m)
+      mma_f16(tacc, kmajor_desc(stage + (uint32_t)(2 * m) * CHUNK_BYTES, (uint32_t)CHUNK_BYTES, 128u),
+              kmajor_desc(seg2 + (uint32_t)(m * k_pad * 32), (uint32_t)(k_pad * 16), 128u), idesc, 1u);
+  }
 }
 
+// stages at s * stage_bytes from 0, then the centre image, bias, barriers and
+// misc words
 struct Smem {
-  uint32_t x[MAX_STAGES], c, bias, ep, bars, misc, total;
+  uint32_t c, bias, bars, misc, total;
 };
 
 // barrier indices
-__host__ __device__ constexpr int B_FULL(int s) { return s; }
-__host__ __device__ constexpr int B_EMPTY(int s) { return MAX_STAGES + s; }
-__host__ __device__ constexpr int B_XLO_FULL(int b) { return 2 * MAX_STAGES + b; }
-__host__ __device__ constexpr int B_XLO_FREE(int b) { return 2 * MAX_STAGES + 2 + b; }
-__host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + 4 + a; }
-__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + 6 + a; }
-constexpr int B_C_FULL = 2 * MAX_STAGES + 8;
-__host__ __device__ constexpr int B_DONE(int t) { return 2 * MAX_STAGES + 9 + t; }  // drain of MMA issuer t
-constexpr int NUM_BARS = 2 * MAX_STAGES + 11;
-constexpr int MMA_W1 = 18;  // second MMA issuer warp (sub-partition 2)
+__host__ __device__ constexpr int B_FULL(int s) { return s; }                    // stage loaded
+__host__ __device__ constexpr int B_SPLIT(int s) { return MAX_STAGES + s; }      // stage converted
+__host__ __device__ constexpr int B_EMPTY(int s) { return 2 * MAX_STAGES + s; }  // stage consumed by the MMAs
+__host__ __device__ constexpr int B_ACC_FULL(int a) { return 3 * MAX_STAGES + a; }
+__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 3 * MAX_STAGES + MAX_ACC + a; }
+constexpr int B_C_FULL = 3 * MAX_STAGES + 2 * MAX_ACC;
+__host__ __device__ constexpr int B_DONE(int t) { return B_C_FULL + 1 + t; }  // drain of MMA issuer t
+constexpr int NUM_BARS = B_C_FULL + 3;
 
+constexpr int MMA_W0 = 1, MMA_W1 = 2;
 constexpr int CONV_WARPS = 8;
 constexpr int EPI_WARPS = 8;
-constexpr int CONV_W0 = 2;
+constexpr int CONV_W0 = 4;
 constexpr int EPI_W0 = CONV_W0 + CONV_WARPS;
+static_assert((EPI_W0 + EPI_WARPS) * 32 == THREADS, "warp roles must fill the block");
 
-__host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
+__host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_bytes, int k_pad, int stages) {
   Smem s;
-  uint32_t off = 0;
-  const uint32_t stage = (uint32_t)nk * CHUNK_BYTES;
-  for (int i = 0; i < MAX_STAGES; ++i) {
-    s.x[i] = off;
-    if (i < stages) off += stage;
-  }
-  s.c = off;  // chunk c: C_hi (k_pad rows) then C_lo (k_pad rows), 32 bytes each
-  off += (uint32_t)nk * 2 * k_pad * 32;
+  uint32_t off = (uint32_t)stages * stage_bytes;
+  s.c = off;
+  off += img_bytes;
   s.bias = off;
   off += (uint32_t)k_pad * 4;
-  s.ep = off;  // epilogue pair exchange: [2 parities][128 rows] (float, int)
-  off += 2 * BM * 8;
   off = (off + 15) & ~15u;
   s.bars = off;
   off += NUM_BARS * 8;
@@ -300,14 +286,12 @@ __host__ __device__ inline Smem smem_layout(int nk, int k_pad, int stages) {
 
 __device__ __forceinline__ bool better(float d, int i, float bd, int bi) { return d < bd || (d == bd && i < bi); }
 
-__global__ void __launch_bounds__(THREADS, 1)
-estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_constant__ CUtensorMap tmap_clo,
-                Params p) {
+__global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
   if (p.st && p.st->done) return;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Smem L = smem_layout(p.nk, p.k_pad, p.stages);
+  const Smem L = smem_layout(p.stage_bytes, p.img_bytes, p.k_pad, p.stages);
   const uint32_t sbase = smem_u32(base);
   const uint32_t bar0 = sbase + L.bars;
   auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
@@ -316,21 +300,21 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
   float* bias_s = reinterpret_cast<float*>(base + L.bias);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int my_tiles = (p.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  const uint32_t stage_bytes = (uint32_t)p.nk * CHUNK_BYTES;
-  const uint32_t cstride = (uint32_t)(2 * p.k_pad * 32);  // bytes per K chunk of [C_hi | C_lo]
-  const bool stacked = 2 * p.k_pad <= 256;
-  const int acc_cols = stacked ? 2 * p.k_pad : p.k_pad;
+  // two MMA issuers and two epilogue groups when there are 2 or 4
+  // accumulators (issuer / group t owns the accumulators a = t mod 2, so each
+  // accumulator barrier has one producer and one consumer), else one of each
+  const int n_iss = p.nacc >= 2 ? 2 : 1;
+  const int n_grp = n_iss;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < MAX_STAGES; ++s) {
       mbar_init(bar(B_FULL(s)), 1);
-      mbar_init(bar(B_EMPTY(s)), 1 + CONV_WARPS);  // first MMAs done + every converter warp
+      mbar_init(bar(B_SPLIT(s)), CONV_WARPS);
+      mbar_init(bar(B_EMPTY(s)), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(B_XLO_FULL(b)), 32 * CONV_WARPS);
-      mbar_init(bar(B_XLO_FREE(b)), 1);
-      mbar_init(bar(B_ACC_FULL(b)), 1);
-      mbar_init(bar(B_ACC_EMPTY(b)), 32 * EPI_WARPS);
+    for (int a = 0; a < MAX_ACC; ++a) {
+      mbar_init(bar(B_ACC_FULL(a)), 1);
+      mbar_init(bar(B_ACC_EMPTY(a)), 4);  // the four warps of one epilogue group
     }
     mbar_init(bar(B_C_FULL), 1);
     mbar_init(bar(B_DONE(0)), 1);
@@ -338,35 +322,31 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
     misc[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == MMA_W0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + L.misc),
                  "r"(p.tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   for (int j = threadIdx.x; j < p.k_pad; j += blockDim.x) bias_s[j] = j < p.k ? p.bias[j] : INFINITY;
-  if (p.tile_bytes < stage_bytes) {
-    // 4-column tail of the last chunk (d % 8 in 1..4): never copied, must be zero
+  if (p.nk * CHUNK_BYTES < (int)p.stage_bytes) {
+    // the extra chunk of an odd nk (read as x_hi by the last pair MMA): zero
     for (int s = 0; s < p.stages; ++s)
-      for (uint32_t o = p.tile_bytes + 16u * threadIdx.x; o < stage_bytes; o += 16u * blockDim.x)
-        *reinterpret_cast<uint4*>(base + L.x[s] + o) = make_uint4(0, 0, 0, 0);
+      for (uint32_t o = (uint32_t)p.nk * CHUNK_BYTES + 16u * threadIdx.x; o < p.stage_bytes; o += 16u * blockDim.x)
+        *reinterpret_cast<uint4*>(base + (uint32_t)s * p.stage_bytes + o) = make_uint4(0, 0, 0, 0);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = misc[0];
-  // TMEM column map: acc[0..nba) | x_lo[0..nbl)
-  const uint32_t col_xlo = (uint32_t)(p.nba * acc_cols);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      mbar_expect_tx(bar(B_C_FULL), 2u * (uint32_t)p.nk * p.k_pad * 32u);
-      for (int c = 0; c < p.nk; ++c) {
-        tma_load_2d(sbase + L.c + (uint32_t)c * cstride, &tmap_chi, c * KC, 0, bar(B_C_FULL));
-        tma_load_2d(sbase + L.c + (uint32_t)c * cstride + (uint32_t)p.k_pad * 32, &tmap_clo, c * KC, 0,
-                    bar(B_C_FULL));
-      }
+      mbar_expect_tx(bar(B_C_FULL), p.img_bytes);
+      for (uint32_t o = 0; o < p.img_bytes; o += 8192u)
+        bulk_load(sbase + L.c + o, reinterpret_cast<const char*>(p.img) + o, min(8192u, p.img_bytes - o),
+                  bar(B_C_FULL));
       int armed = 0;
       for (int i = 0; i < my_tiles; ++i) {
         const int s = i % p.stages;
@@ -375,7 +355,7 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
         const char* src = reinterpret_cast<const char*>(p.X) + (size_t)tile * p.tile_bytes;
         mbar_expect_tx(bar(B_FULL(s)), p.tile_bytes);
         for (uint32_t o = 0; o < p.tile_bytes; o += 8192u)
-          bulk_load(sbase + L.x[s] + o, src + o, min(8192u, p.tile_bytes - o), bar(B_FULL(s)));
+          bulk_load(sbase + (uint32_t)s * p.stage_bytes + o, src + o, min(8192u, p.tile_bytes - o), bar(B_FULL(s)));
         armed = i + 1;
       }
       // our own copies must land before the CTA may exit
@@ -384,40 +364,20 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
       for (int i = (armed > p.stages ? armed - p.stages : 0); i < armed; ++i)
         mbar_wait(bar(B_FULL(i % p.stages)), (i / p.stages) & 1, &no_abort, p.err, 2103);
     }
-  } else if (warp == 1 || warp == MMA_W1) {
+  } else if (warp == MMA_W0 || warp == MMA_W1) {
     // ---------------------------------------------------------- MMA issuers
-    // two issuers when every tile has its own accumulator and x_lo buffer
-    // (nba == nbl == 2), else warp 1 issues everything
-    const int n_iss = (p.nba == 2 && p.nbl == 2) ? 2 : 1;
-    const int t = warp == 1 ? 0 : 1;
+    const int t = warp == MMA_W0 ? 0 : 1;
     if (lane == 0 && t < n_iss) {
-      const uint32_t idesc_k = idesc_tf32(p.k_pad);
-      const uint32_t idesc_2k = idesc_tf32(stacked ? 2 * p.k_pad : p.k_pad);
       bool ok = mbar_wait(bar(B_C_FULL), 0, abort_flag, p.err, 2201);
       for (int i = t; ok && i < my_tiles; i += n_iss) {
-        const int s = i % p.stages, a = i % p.nba, b = i % p.nbl;
-        if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nba) & 1) ^ 1, abort_flag, p.err, 2203)) break;
-        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) break;
+        const int s = i % p.stages, a = i % p.nacc;
+        if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nacc) & 1) ^ 1, abort_flag, p.err, 2203)) break;
+        if (!mbar_wait(bar(B_SPLIT(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) break;
         tc_fence_after();
-        const uint32_t tacc = tmem_base + (uint32_t)(a * acc_cols);
-        for (int c = 0; c < p.nk; ++c) {
-          const uint64_t a_desc = blk_desc(sbase + L.x[s] + (uint32_t)c * CHUNK_BYTES);
-          const uint32_t cb = sbase + L.c + (uint32_t)c * cstride;
-          if (stacked) {
-            mma_ss(tacc, a_desc, sw32_desc(cb), idesc_2k, c > 0 ? 1u : 0u);
-          } else {
-            mma_ss(tacc, a_desc, sw32_desc(cb + (uint32_t)p.k_pad * 32), idesc_k, c > 0 ? 1u : 0u);
-            mma_ss(tacc, a_desc, sw32_desc(cb), idesc_k, 1u);
-          }
-        }
+        issue_tile_mmas(tmem_base + (uint32_t)(a * p.acc_cols), sbase + (uint32_t)s * p.stage_bytes, sbase + L.c, p.nk, p.k_pad,
+                        p.stacked);
         tc_commit(bar(B_EMPTY(s)));  // the stage is no longer read by the tensor core
-        if (!mbar_wait(bar(B_XLO_FULL(b)), (i / p.nbl) & 1, abort_flag, p.err, 2204)) break;
-        tc_fence_after();
-        const uint32_t txl = tmem_base + col_xlo + (uint32_t)(b * p.xcols);
-        for (int c = 0; c < p.nk; ++c)
-          mma_ts(tacc, txl + (uint32_t)(c * KC), sw32_desc(sbase + L.c + (uint32_t)c * cstride), idesc_k, 1u);
         tc_commit(bar(B_ACC_FULL(a)));
-        tc_commit(bar(B_XLO_FREE(b)));
       }
       // every tcgen05 operation issued by this thread is complete once DONE fires
       tc_commit(bar(B_DONE(t)));
@@ -426,85 +386,65 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
     }
   } else if (warp >= CONV_W0 && warp < EPI_W0) {
     // ---------------------------------------------------------------- converter
-    // thread = tile row: reads its row's 16-byte quads of its K chunks from the
-    // shared-memory stage (a warp reads 512 contiguous bytes per quad) and
-    // writes x - T(x) to its TMEM lane
-    const int q = warp & 3;
-    const int h = (warp - CONV_W0) >> 2;
-    const int row = q * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // thread = tile row; the two threads of a row split its chunks. A warp
+    // reads and writes 512 contiguous bytes per quad (conflict-free).
+    const int t = (warp - CONV_W0) * 32 + lane;
+    const int row = t & (BM - 1);
+    const int h = t >> 7;
     const int half = (p.nk + 1) >> 1;
     const int c0 = h ? half : 0, c1 = h ? p.nk : half;
+    const float sx = ldexpf(1.0f, p.sexp[0]);
     for (int i = 0; i < my_tiles; ++i) {
-      const int s = i % p.stages, b = i % p.nbl;
+      const int s = i % p.stages;
       if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2301)) break;
-      if (!mbar_wait(bar(B_XLO_FREE(b)), ((i / p.nbl) & 1) ^ 1, abort_flag, p.err, 2302)) break;
-      tc_fence_after();
-      const float4* stg = reinterpret_cast<const float4*>(base + L.x[s]) + row;  // quad j at stg[128 j]
-      const uint32_t tl = tmem_base + lane_off + col_xlo + (uint32_t)(b * p.xcols);
+      unsigned char* stg = base + (uint32_t)s * p.stage_bytes;
 #pragma unroll 2
-      for (int c = c0; c < c1; ++c) {
-        const float4 a0 = stg[(2 * c) * 128];
-        const float4 a1 = stg[(2 * c + 1) * 128];  // zero past the last column (stage tail is zero)
-        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        uint32_t r[8];
-#pragma unroll
-        for (int e2 = 0; e2 < 8; ++e2)
-          r[e2] = __float_as_uint(v[e2] - __uint_as_float(to_tf32_bits(__float_as_uint(v[e2]), p.round_mode)));
-        tmem_st8(tl + (uint32_t)(c * KC), r);
-      }
-      // the stage may be refilled once the first MMAs and all converter warps are done
+      for (int c = c0; c < c1; ++c) split_chunk_row(stg, row, c, p.nq, sx);
+      // generic-proxy writes -> visible to the tensor core (async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_EMPTY(s)));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar(B_XLO_FULL(b)));
+      if (lane == 0) mbar_arrive(bar(B_SPLIT(s)));
     }
-  } else if (warp >= EPI_W0 && warp < EPI_W0 + EPI_WARPS) {
+  } else if (warp >= EPI_W0) {
     // ----------------------------------------------------------------- epilogue
-    // the two warps of a lane quarter take the clusters [0, k/2) and
-    // [k/2, k); the upper warp hands its (min, index) to the lower one
+    // two groups of four warps (one per TMEM lane quarter) take alternate
+    // tiles; each warp scans all clusters of its 32 rows
     const int q = warp & 3;
-    const int h = (warp - EPI_W0) >> 2;
+    const int g = (warp - EPI_W0) >> 2;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    // split at a multiple of 16 (the TMEM load width): [0, kh0) and [kh0, k_pad)
-    const int kh0 = ((p.k_pad >> 1) + 15) & ~15;
-    const int j0 = h ? kh0 : 0;
-    const int kh = h ? p.k_pad - kh0 : kh0;
-    float* ep_best = reinterpret_cast<float*>(base + L.ep);
-    int* ep_idx = reinterpret_cast<int*>(base + L.ep + 2 * BM * 4);
+    // dist = ||c||^2 - 2 x.c with x.c = acc * 2^-(xexp + cexp)
+    const float negscale = -ldexpf(1.0f, 1 - p.sexp[0] - p.sexp[1]);
     int old_next = -1;
-    if (h == 0 && p.changed && my_tiles > 0) {
-      const long long g0 = (long long)blockIdx.x * BM + row;
+    if (g < n_grp && p.changed && g < my_tiles) {
+      const long long g0 = (long long)((int)blockIdx.x + g * (int)gridDim.x) * BM + row;
       old_next = g0 < p.n ? p.labels[g0] : -1;
     }
-    for (int i = 0; i < my_tiles; ++i) {
-      const int a = i % p.nba;
+    for (int i = g; g < n_grp && i < my_tiles; i += n_grp) {
+      const int a = i % p.nacc;
       const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
       const int old = old_next;
-      if (h == 0 && p.changed && i + 1 < my_tiles) {  // prefetch the next tile's previous labels
-        const long long g1 = grow + (long long)gridDim.x * BM;
+      if (p.changed && i + n_grp < my_tiles) {  // prefetch the next tile's previous labels
+        const long long g1 = grow + (long long)n_grp * gridDim.x * BM;
         old_next = g1 < p.n ? p.labels[g1] : -1;
       }
-      if (!mbar_wait(bar(B_ACC_FULL(a)), (i / p.nba) & 1, abort_flag, p.err, 2401)) break;
+      if (!mbar_wait(bar(B_ACC_FULL(a)), (i / p.nacc) & 1, abort_flag, p.err, 2401)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + lane_off + (uint32_t)(a * acc_cols);
+      const uint32_t taddr = tmem_base + lane_off + (uint32_t)(a * p.acc_cols);
       // four independent running minima (columns j = 4m + u), merged in index order
       float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
       int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
-      for (int jb = 0; jb < kh; jb += 16) {
+      for (int jb = 0; jb < p.k_pad; jb += 16) {
         uint32_t v[16], w[16];
-        tmem_ld16(taddr + (uint32_t)(j0 + jb), v);
-        if (stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + j0 + jb), w);
+        tmem_ld16(taddr + (uint32_t)jb, v);
+        if (p.stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + jb), w);
         tmem_ld_wait();
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
-          const int j = j0 + jb + jj;
+          const int j = jb + jj;
           float dot = __uint_as_float(v[jj]);
-          if (stacked) dot += __uint_as_float(w[jj]);
-          const float dist = fmaf(-2.0f, dot, bias_s[j]);
+          if (p.stacked) dot += __uint_as_float(w[jj]);
+          const float dist = fmaf(dot, negscale, bias_s[j]);
           if (dist < bd[jj & 3]) {
             bd[jj & 3] = dist;
             bi[jj & 3] = j;
@@ -512,7 +452,8 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
         }
       }
       tc_fence_before();
-      mbar_arrive(bar(B_ACC_EMPTY(a)));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_ACC_EMPTY(a)));
       float best = bd[0];
       int bl = bi[0];
 #pragma unroll
@@ -521,18 +462,6 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
           best = bd[u];
           bl = bi[u];
         }
-      const int slot = (i & 1) * BM + row;
-      if (h == 1) {
-        ep_best[slot] = best;
-        ep_idx[slot] = bl;
-        named_bar(1 + q, 64);
-        continue;
-      }
-      named_bar(1 + q, 64);
-      if (better(ep_best[slot], ep_idx[slot], best, bl)) {
-        best = ep_best[slot];
-        bl = ep_idx[slot];
-      }
       if (bl >= p.k) bl = 0;  // only reachable when every distance is +inf or NaN
       bool ch = false;
       if (grow < p.n) {
@@ -549,40 +478,62 @@ estep_tc_kernel(const __grid_constant__ CUtensorMap tmap_chi, const __grid_const
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == MMA_W0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols));
   }
 }
 
 // ---------------------------------------------------------------------------
-// probe: tcgen05.cp layout and the tensor core's fp32 -> tf32 conversion
+// probe: operand layouts of the split-fp16 path, checked on exact values
 // ---------------------------------------------------------------------------
-// A (128 x 8) holds fp32 values whose dropped mantissa bits distinguish
-// truncation from rounding (rows 64..127 negative); B (16 x 8) is the identity
-// on its first 8 rows, so D[m][n] = tf32(A[m][n]) for n < 8. out: [0,1024) the
-// TMEM copy of A made by tcgen05.cp, [1024,2048) D with A read from TMEM,
-// [2048,3072) D with A read from shared memory, [3072] error code.
-__host__ __device__ __forceinline__ uint32_t probe_bits(int m, int k) {
-  const uint32_t low = 0x1000u | ((uint32_t)(m * 8 + k) & 0x0fffu);
-  return 0x3f800000u | ((uint32_t)k << 13) | low | (m >= 64 ? 0x80000000u : 0u);
+// A 128 x 16 tile (two chunks) and 16 centres whose fp16 splits are exact
+// (x = p + q 2^-12, c = r + s 2^-12 with |p|, |r| in [8, 16), |q|, |s| <= 8),
+// so that x_hi.c_hi + x_lo.c_hi + x_hi.c_lo is exact in fp32. The tile goes
+// through split_chunk_row and the centres through cimg_put, as in the fit;
+// the stacked (N = 32) and two-segment (N = 16) MMA sequences then run on
+// them. out: [0, 2048) stacked x.c (acc[j] + acc[16 + j]), [2048, 4096)
+// two-segment x.c, row-major 128 x 16; [4096] error code.
+constexpr int PROBE_K = 16, PROBE_NK = 2;
+
+__host__ __device__ inline float probe_x(int m, int j) {
+  const int p = 8 + ((m * 7 + j * 3) % 8);
+  const int q = ((m * 5 + j * 11) % 17) - 8;
+  return (float)(((m + j) & 1) ? -p : p) + (float)q * (1.0f / 4096.0f);
 }
 
-__global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
-  __shared__ __align__(1024) unsigned char sm[CHUNK_BYTES + 512 + 64];
-  const uint32_t sa = smem_u32(sm), sb = sa + CHUNK_BYTES, sbar = sb + 512;
-  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + CHUNK_BYTES + 512 + 16);
+__host__ __device__ inline float probe_c(int c, int j) {
+  const int r = 8 + ((c * 3 + j * 5) % 8);
+  const int s = ((c * 13 + j * 7) % 17) - 8;
+  return (float)(((c + 2 * j) % 3 == 0) ? -r : r) + (float)s * (1.0f / 4096.0f);
+}
+
+__global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint16_t* img_st, uint16_t* img_2s, uint32_t* out) {
+  constexpr uint32_t TILE = PROBE_NK * CHUNK_BYTES;                 // 8 KB
+  constexpr uint32_t IMG_ST = PROBE_NK * 2 * PROBE_K * 32;          // 2 KB
+  constexpr uint32_t IMG_2S = PROBE_NK * PROBE_K * 32 + PROBE_K * 32;  // 1.5 KB
+  __shared__ __align__(1024) unsigned char sm[TILE + IMG_ST + IMG_2S + 64];
+  const uint32_t sa = smem_u32(sm), sb1 = sa + TILE, sb2 = sb1 + IMG_ST, sbar = sb2 + IMG_2S;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(sm + TILE + IMG_ST + IMG_2S + 16);
   const uint32_t smisc = smem_u32(misc);
-  int* err = reinterpret_cast<int*>(out + 3072);
+  int* err = reinterpret_cast<int*>(out + 4096);
   const int tid = threadIdx.x, warp = tid >> 5;
-  // A in the blocked no-swizzle layout (column quad q at q * 2048, row m at
-  // m * 16); B in SWIZZLE_32B (bit 4 of the byte offset XORed with bit 7)
-  auto sw32 = [](uint32_t off) { return off ^ (((off >> 7) & 1u) << 4); };
-  for (int k = 0; k < 8; ++k)
-    *reinterpret_cast<uint32_t*>(sm + (uint32_t)((k >> 2) * 2048 + tid * 16 + (k & 3) * 4)) = probe_bits(tid, k);
-  if (tid < 16)
-    for (int k = 0; k < 8; ++k)
-      *reinterpret_cast<float*>(sm + CHUNK_BYTES + sw32((uint32_t)(tid * 32 + k * 4))) = (tid == k) ? 1.0f : 0.0f;
+  // fp32 tile in the blocked layout, split in place
+  for (int j = 0; j < PROBE_NK * KC; ++j)
+    *reinterpret_cast<float*>(sm + (j >> 2) * 2048 + tid * 16 + (j & 3) * 4) = probe_x(tid, j);
+  for (int c = 0; c < PROBE_NK; ++c) split_chunk_row(sm, tid, c, 2 * PROBE_NK, 1.0f);
+  // centre images: built in global memory by cimg_put, copied to smem
+  const CentreImage st{img_st, PROBE_K, PROBE_NK, 1}, two{img_2s, PROBE_K, PROBE_NK, 0};
+  for (int e = tid; e < PROBE_K * PROBE_NK * KC; e += blockDim.x) {
+    const int c = e / (PROBE_NK * KC), j = e % (PROBE_NK * KC);
+    cimg_put(st, c, j, probe_c(c, j), 1.0f);
+    cimg_put(two, c, j, probe_c(c, j), 1.0f);
+  }
+  __syncthreads();
+  for (uint32_t o = tid * 2; o < IMG_ST / 2; o += 2 * blockDim.x)
+    *reinterpret_cast<uint32_t*>(sm + TILE + o * 2) = *reinterpret_cast<const uint32_t*>(img_st + o);
+  for (uint32_t o = tid * 2; o < IMG_2S / 2; o += 2 * blockDim.x)
+    *reinterpret_cast<uint32_t*>(sm + TILE + IMG_ST + o * 2) = *reinterpret_cast<const uint32_t*>(img_2s + o);
   if (tid == 0) {
     mbar_init(sbar, 1);
     misc[1] = 0;
@@ -590,7 +541,7 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smisc), "r"(32));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smisc), "r"(64));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -598,43 +549,30 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
   tc_fence_after();
   const uint32_t tb = misc[0];
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
-  // TMEM columns: [0,8) copy of A, [8,24) D (A from TMEM); then [16,32) D (A from smem)
+  // TMEM columns: [0, 32) stacked accumulator, [32, 48) two-segment accumulator
   if (tid == 0) {
-    const uint32_t idesc = idesc_tf32(16);
-    tmem_cp_chunk(tb, blk_desc(sa));
-    mma_ts(tb + 8, tb, sw32_desc(sb), idesc, 0u);
+    issue_tile_mmas(tb, sa, sb1, PROBE_NK, PROBE_K, 1);
+    issue_tile_mmas(tb + 32, sa, sb2, PROBE_NK, PROBE_K, 0);
     tc_commit(sbar);
   }
   __syncwarp();
   mbar_wait(sbar, 0, abort_flag, err, 2501);
   tc_fence_after();
   const uint32_t lo = (uint32_t)(warp * 32) << 16;
-  uint32_t r[8];
-  tmem_ld8(tb + lo, r);
+  uint32_t v[16], w[16], u[16];
+  tmem_ld16(tb + lo, v);
+  tmem_ld16(tb + lo + 16, w);
+  tmem_ld16(tb + lo + 32, u);
   tmem_ld_wait();
-  for (int e = 0; e < 8; ++e) out[tid * 8 + e] = r[e];
-  tmem_ld8(tb + lo + 8, r);
-  tmem_ld_wait();
-  for (int e = 0; e < 8; ++e) out[1024 + tid * 8 + e] = r[e];
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (tid == 0) {
-    const uint32_t idesc = idesc_tf32(16);
-    mma_ss(tb + 16, blk_desc(sa), sw32_desc(sb), idesc, 0u);
-    tc_commit(sbar);
+  for (int j = 0; j < PROBE_K; ++j) {
+    out[tid * PROBE_K + j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+    out[2048 + tid * PROBE_K + j] = u[j];
   }
-  __syncwarp();
-  mbar_wait(sbar, 1, abort_flag, err, 2502);
-  tc_fence_after();
-  tmem_ld8(tb + lo + 16, r);
-  tmem_ld_wait();
-  for (int e = 0; e < 8; ++e) out[2048 + tid * 8 + e] = r[e];
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tb), "r"(32));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tb), "r"(64));
   }
 }
 
@@ -644,50 +582,21 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint32_t* out) {
 // host side
 // ---------------------------------------------------------------------------
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-// 2-D fp32 tensor map over a rows x ld matrix, box = 8 columns x box_rows rows,
-// 32-byte swizzle, out-of-bounds elements read as zero.
-static int make_map(CUtensorMap* m, const float* ptr, int ld, long long rows, int box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) {
-    set_error(ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
-    return ERR_UNSUPPORTED;
-  }
-  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)tc::KC, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error(ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) ld=%d rows=%lld box_rows=%d", (int)r, ld, rows,
-              box_rows);
-    return ERR_CUDA;
-  }
-  return OK;
-}
-
-// Per-device probe result: -2 not run, -1 unusable, 0 truncation, 1 rounding.
+// Per-device probe result: -2 not run, -1 unusable, 0 exact.
 static int g_probe_mode[64];
 static bool g_probe_init = false;
+
+// Exact value of x_hi.c_hi + x_lo.c_hi + x_hi.c_lo for the probe operands
+// (p r + q r 2^-12 + p s 2^-12 summed over 16 columns, exact in double).
+static double probe_expected(int m, int c) {
+  double t = 0.0;
+  for (int j = 0; j < tc::PROBE_NK * tc::KC; ++j) {
+    const double x = tc::probe_x(m, j), cc = tc::probe_c(c, j);
+    const double xh = std::nearbyint(x), ch = std::nearbyint(cc);
+    t += xh * ch + (x - xh) * ch + xh * (cc - ch);
+  }
+  return t;
+}
 
 int tc_probe(int* mode_out, uint32_t* raw_out) {
   int dev = 0;
@@ -702,41 +611,47 @@ int tc_probe(int* mode_out, uint32_t* raw_out) {
   }
   cudaStream_t s;
   SKM_TRY(thread_stream(&s, nullptr));
+  const size_t out_words = 4097;
+  const size_t img_halves = cimg_halves(tc::PROBE_K, tc::PROBE_NK, 1) + cimg_halves(tc::PROBE_K, tc::PROBE_NK, 0);
   uint32_t* d_out = nullptr;
-  SKM_CUDA(cudaMallocAsync(&d_out, 3073 * 4, s));
-  SKM_CUDA(cudaMemsetAsync(d_out, 0, 3073 * 4, s));
-  tc::tc_probe_kernel<<<1, 128, 0, s>>>(d_out);
-  int rc = check_launch("tc_probe_kernel");
-  std::vector<uint32_t> h(3073, 0);
+  uint16_t* d_img = nullptr;
+  SKM_CUDA(cudaMallocAsync(&d_out, out_words * 4, s));
+  int rc = OK;
+  if (cudaMallocAsync(&d_img, img_halves * 2, s) != cudaSuccess) {
+    cudaGetLastError();
+    rc = ERR_OOM;
+  }
+  if (rc == OK && (cudaMemsetAsync(d_out, 0, out_words * 4, s) != cudaSuccess ||
+                   cudaMemsetAsync(d_img, 0, img_halves * 2, s) != cudaSuccess))
+    rc = ERR_CUDA;
   if (rc == OK) {
-    cudaMemcpyAsync(h.data(), d_out, 3073 * 4, cudaMemcpyDeviceToHost, s);
+    tc::tc_probe_kernel<<<1, 128, 0, s>>>(d_img, d_img + cimg_halves(tc::PROBE_K, tc::PROBE_NK, 1), d_out);
+    rc = check_launch("tc_probe_kernel");
+  }
+  std::vector<uint32_t> h(out_words, 0);
+  if (rc == OK) {
+    cudaMemcpyAsync(h.data(), d_out, out_words * 4, cudaMemcpyDeviceToHost, s);
     if (cudaStreamSynchronize(s) != cudaSuccess) rc = ERR_CUDA;
   }
   cudaFreeAsync(d_out, s);
+  if (d_img) cudaFreeAsync(d_img, s);
   if (rc != OK) {
-    set_error(ERR_CUDA, "tensor-core probe failed to run");
+    set_error(rc, "tensor-core probe failed to run");
     return rc;
   }
-  if (raw_out) memcpy(raw_out, h.data(), 3072 * 4);
-  int mode = -1;
-  bool copy_ok = h[3072] == 0;
-  for (int m = 0; m < 128 && copy_ok; ++m)
-    for (int k = 0; k < 8; ++k)
-      if (h[m * 8 + k] != tc::probe_bits(m, k)) copy_ok = false;
-  if (copy_ok) {
-    for (int cand = 0; cand < 2 && mode < 0; ++cand) {
-      bool ok = true;
-      for (int m = 0; m < 128 && ok; ++m)
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t want = tc::to_tf32_bits(h[m * 8 + k], cand);
-          if (h[1024 + m * 8 + k] != want || h[2048 + m * 8 + k] != want) {
-            ok = false;
-            break;
-          }
-        }
-      if (ok) mode = cand;
+  if (raw_out) memcpy(raw_out, h.data(), 4096 * 4);
+  int mode = h[4096] == 0 ? 0 : -1;
+  for (int m = 0; m < tc::BM && mode == 0; ++m)
+    for (int c = 0; c < tc::PROBE_K; ++c) {
+      const float want = (float)probe_expected(m, c);
+      float a, b;
+      memcpy(&a, &h[m * tc::PROBE_K + c], 4);
+      memcpy(&b, &h[2048 + m * tc::PROBE_K + c], 4);
+      if (a != want || b != want) {
+        mode = -1;
+        break;
+      }
     }
-  }
   if (dev < 64) g_probe_mode[dev] = mode;
   *mode_out = mode;
   return OK;
@@ -745,7 +660,6 @@ int tc_probe(int* mode_out, uint32_t* raw_out) {
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->supported = false;
   if (getenv("SKMETAL_DISABLE_TC")) return OK;
-  if (!encode_fn()) return OK;
   if (d > tc::MAX_NK * tc::KC || k > tc::MAX_KPAD || n < 1) return OK;
   if ((reinterpret_cast<uintptr_t>(X) & 15) || ((ld * 4) & 15)) return OK;
   int dev = 0, optin = 0, major = 0;
@@ -756,7 +670,6 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   int mode = -1;
   SKM_TRY(tc_probe(&mode, nullptr));
   if (mode < 0) return OK;  // unexpected tensor-core behaviour: use the SIMT E-step
-  plan->round_mode = mode;
   plan->X = X;
   plan->ld = ld;
   plan->n = n;
@@ -764,30 +677,32 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->k = k;
   plan->k_pad = (int)round_up((size_t)k, 16);
   plan->k_steps = (ld + tc::KC - 1) / tc::KC;
-  // TMEM: accumulators (2k columns when [C_hi | C_lo] is one N <= 256 operand,
-  // else k) and x_lo buffers (32-column aligned); double-buffer what fits
-  plan->xcols = (int)round_up((size_t)plan->k_steps * tc::KC, 32);
-  const int acc_cols = 2 * plan->k_pad <= 256 ? 2 * plan->k_pad : plan->k_pad;
-  plan->nbl = 2;
-  plan->nba = 2;
-  auto cols = [&]() { return plan->nba * acc_cols + plan->nbl * plan->xcols; };
-  if (cols() > 512) plan->nba = 1;
-  if (cols() > 512) plan->nbl = 1;
-  if (cols() > 512) return OK;
-  int tcols = 32;
-  while (tcols < cols()) tcols *= 2;
-  plan->tmem_cols = tcols;
-  // shared memory: as many X stages as fit (2..4)
+  plan->nq = ld / 4;
+  // prefer one stacked operand (one MMA per chunk); both layouts need >= 2 stages
   plan->stages = 0;
-  for (int st = tc::MAX_STAGES; st >= 2; --st) {
-    const tc::Smem L = tc::smem_layout(plan->k_steps, plan->k_pad, st);
-    if ((int)L.total <= optin) {
-      plan->stages = st;
-      plan->smem = L.total;
-      break;
+  for (int stacked = (2 * plan->k_pad <= 256) ? 1 : 0; stacked >= 0 && plan->stages == 0; --stacked) {
+    const int nkx = stacked ? plan->k_steps : (plan->k_steps + 1) & ~1;
+    const uint32_t stage_bytes = (uint32_t)nkx * tc::CHUNK_BYTES;
+    const uint32_t img_bytes = (uint32_t)(cimg_halves(plan->k_pad, plan->k_steps, stacked) * 2);
+    for (int st = tc::MAX_STAGES; st >= 2; --st) {
+      const tc::Smem L = tc::smem_layout(stage_bytes, img_bytes, plan->k_pad, st);
+      if ((int)L.total <= optin) {
+        plan->stacked = stacked;
+        plan->stages = st;
+        plan->stage_bytes = stage_bytes;
+        plan->img_bytes = img_bytes;
+        plan->smem = L.total;
+        break;
+      }
     }
   }
   if (plan->stages == 0) return OK;
+  plan->acc_cols = plan->stacked ? 2 * plan->k_pad : plan->k_pad;
+  // 4, 2 or 1 accumulators (see the issuer / epilogue pairing in the kernel)
+  plan->nacc = 4 * plan->acc_cols <= 512 ? 4 : (2 * plan->acc_cols <= 512 ? 2 : 1);
+  int tcols = 32;
+  while (tcols < plan->nacc * plan->acc_cols) tcols *= 2;
+  plan->tmem_cols = tcols;
   const int n_tiles = (int)((n + tc::BM - 1) / tc::BM);
   plan->grid = std::min(n_tiles, sm_count());
   static bool attr = false;
@@ -799,26 +714,28 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   return OK;
 }
 
-int tc_set_centres(TcPlan* plan, const float* Chi, const float* Clo) {
-  SKM_TRY(make_map(&plan->tmap_chi, Chi, plan->ld, plan->k, plan->k_pad));
-  SKM_TRY(make_map(&plan->tmap_clo, Clo, plan->ld, plan->k, plan->k_pad));
-  return OK;
+CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img) {
+  return CentreImage{img, plan.k_pad, plan.k_steps, plan.stacked};
 }
 
-int tc_estep(const TcPlan& plan, const float* bias, int32_t* labels, unsigned long long* changed, long long* D,
-             const FitState* st, int* err, cudaStream_t s) {
+int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,
+             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s) {
   tc::Params p;
   p.n_tiles = (int)((plan.n + tc::BM - 1) / tc::BM);
   p.n = plan.n;
   p.k = plan.k;
   p.k_pad = plan.k_pad;
   p.nk = plan.k_steps;
+  p.nq = plan.nq;
+  p.stacked = plan.stacked;
   p.stages = plan.stages;
-  p.nbl = plan.nbl;
-  p.nba = plan.nba;
-  p.xcols = plan.xcols;
+  p.nacc = plan.nacc;
+  p.acc_cols = plan.acc_cols;
   p.tmem_cols = plan.tmem_cols;
-  p.round_mode = plan.round_mode;
+  p.stage_bytes = plan.stage_bytes;
+  p.img_bytes = plan.img_bytes;
+  p.img = img;
+  p.sexp = sexp;
   p.bias = bias;
   p.labels = labels;
   p.changed = changed;
@@ -829,10 +746,10 @@ int tc_estep(const TcPlan& plan, const float* bias, int32_t* labels, unsigned lo
   p.tile_bytes = (uint32_t)(512 * plan.ld);
   p.st = st;
   p.err = err;
-  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(plan.tmap_chi, plan.tmap_clo, p);
+  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(p);
   return check_launch("estep_tc_kernel");
 }
 
 }  // namespace skm
 
-extern "C" int skmetal_debug_tc_probe(int* mode, uint32_t* raw3072) { return skm::tc_probe(mode, raw3072); }
+extern "C" int skmetal_debug_tc_probe(int* mode, uint32_t* raw4096) { return skm::tc_probe(mode, raw4096); }

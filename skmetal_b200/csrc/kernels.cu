@@ -79,6 +79,15 @@ __device__ double block_sum_f64(double v, double* scratch /* >= 32 */) {
   return r;
 }
 
+// Sum of v[0, n) in a fixed order for a given block size: thread t adds v[t],
+// v[t + blockDim.x], ... in index order, then the fixed block tree; result
+// valid in thread 0. All threads of the block must call it.
+__device__ double block_ordered_sum(const double* v, int n, double* scratch) {
+  double t = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) t += v[i];
+  return block_sum_f64(t, scratch);
+}
+
 // ---------------------------------------------------------------------------
 // data preparation
 // ---------------------------------------------------------------------------
@@ -322,6 +331,8 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
   if (tol_mode == 1) t = (tol == 0.0 || sumsq == nullptr) ? 0.0 : (*sumsq / (n_total * (double)d)) * tol;
   st->tol = t;
   st->maxabs_bits = *maxabs_bits;
+  st->xexp = split_exp(*maxabs_bits);
+  st->cexp = st->xexp;
   st->scale = fixed_scale(*maxabs_bits, n_total);
   st->inv_scale = 1.0 / st->scale;
 }
@@ -568,6 +579,11 @@ __device__ bool select_farthest(const float* __restrict__ mind, long long n, lon
   return grid_barrier(st, nblocks);
 }
 
+// Mean of a cluster's column from its exact fixed-point sum.
+__device__ __forceinline__ float centre_from_sum(long long s, double inv_scale, long long count) {
+  return (float)((double)s * inv_scale / (double)count);
+}
+
 // Averaged centre value of a non-empty cluster c (after relocation), column j.
 __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, int n_reloc) {
   for (int i = 0; i < n_reloc; ++i)
@@ -575,15 +591,16 @@ __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, 
   long long s = a.S[(long long)c * a.ld + j];
   for (int i = 0; i < n_reloc; ++i)
     if (a.reloc_label[i] == c) s -= to_fixed(a.reloc_x[(long long)i * a.ld + j], a.st->scale);
-  return (float)((double)s * a.st->inv_scale / (double)a.cnt_adj[c]);
+  return centre_from_sum(s, a.st->inv_scale, a.cnt_adj[c]);
 }
 
 // One centre (cluster c, columns strided over the calling warp's lanes):
-// writes C_new, the tf32 split and returns (shift^2, ||c||^2) summed in a
-// fixed order (lane partials, then a fixed butterfly).
+// writes C_new, its centre-image entries and returns (shift^2, ||c||^2)
+// summed in a fixed order (lane partials, then a fixed butterfly).
 __device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, int src, int n_reloc, double* dsq_out,
                                             double* nrm_out) {
   const int lane = threadIdx.x & 31;
+  const float cs = ldexpf(1.0f, a.st->xexp);  // centres are bounded by max |x|
   double dsq = 0.0, nrm = 0.0;
   for (int j = lane; j < a.ld; j += 32) {
     float v = 0.0f;
@@ -592,21 +609,52 @@ __device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, int src, 
       const double df = (double)v - (double)a.C_old[(long long)c * a.ld + j];
       dsq += df * df;
       nrm += (double)v * v;
+      if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
     }
     a.C_new[(long long)c * a.ld + j] = v;
-    if (a.Chi) {
-      const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
-      a.Chi[(long long)c * a.ld + j] = hi;
-      a.Clo[(long long)c * a.ld + j] = v - hi;
-    }
   }
   *dsq_out = warp_sum(dsq);
   *nrm_out = warp_sum(nrm);
 }
 
-// Convergence bookkeeping (_kmeans.py:723-741) from per-cluster squared
-// shifts summed in cluster order; one thread.
+// Fast-path centre (no relocation): folds this iteration's deltas of cluster
+// c into S while computing the centre, so that S, D and C_old are read once
+// with independent loads. counts must already be folded into cnt_adj.
+__device__ __forceinline__ void warp_centre_fold(const MStepArgs& a, int c, double* dsq_out, double* nrm_out) {
+  const int lane = threadIdx.x & 31;
+  const float cs = ldexpf(1.0f, a.st->xexp);
+  const double inv_scale = a.st->inv_scale;
+  const long long cnt = a.cnt_adj[c];
+  long long* S = const_cast<long long*>(a.S);
+  double dsq = 0.0, nrm = 0.0;
+  for (int j = lane; j < a.ld; j += 32) {
+    const long long i = (long long)c * a.ld + j;
+    const long long dv = a.D[i];
+    const long long sv = S[i] + dv;
+    const float old = a.C_old[i];
+    if (dv != 0) {
+      S[i] = sv;
+      a.D[i] = 0;
+    }
+    float v = 0.0f;
+    if (j < a.d) {
+      v = centre_from_sum(sv, inv_scale, cnt);
+      const double df = (double)v - (double)old;
+      dsq += df * df;
+      nrm += (double)v * v;
+      if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
+    }
+    a.C_new[i] = v;
+  }
+  *dsq_out = warp_sum(dsq);
+  *nrm_out = warp_sum(nrm);
+}
+
+// Convergence bookkeeping (_kmeans.py:723-741) from the per-cluster squared
+// shifts summed in a fixed order; one thread. The centre image now holds
+// centres scaled by 2^xexp.
 __device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long long changed_now, double tot) {
+  st->cexp = st->xexp;
   st->shift_tot = tot;
   st->iter += 1;
   if (changed_now == 0) {
@@ -619,7 +667,7 @@ __device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long
   *const_cast<unsigned long long*>(a.changed) = 0;
 }
 
-__global__ void mstep_kernel(MStepArgs a) {
+__global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   FitState* st = a.st;
   if (st->done) return;  // uniform: `done` is only written at the very end
   const unsigned long long changed_now = *a.changed;  // cleared at the end
@@ -659,18 +707,17 @@ __global__ void mstep_kernel(MStepArgs a) {
   if (n_empty == 0) {
     // ---------------- fast path: no relocation, one block does the update
     if (blockIdx.x != 0) return;
-    long long* S = const_cast<long long*>(a.S);
+    __shared__ double red_scratch[32];
     long long* cnt = const_cast<long long*>(a.counts);
-    for (long long i = threadIdx.x; i < ks + a.k; i += blockDim.x) {
-      const long long v = a.D[i];
-      if (v != 0) {
-        if (i < ks) S[i] += v;
-        else cnt[i - ks] += v;
-        a.D[i] = 0;
+    for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
+      const long long dv = dcnt[c];
+      const long long v = cnt[c] + dv;
+      a.cnt_adj[c] = v;
+      if (dv != 0) {
+        cnt[c] = v;
+        a.D[ks + c] = 0;
       }
     }
-    __syncthreads();
-    for (int c = threadIdx.x; c < a.k; c += blockDim.x) a.cnt_adj[c] = cnt[c];
     if (threadIdx.x == 0) {
       st->n_empty = 0;
       st->relocated = 0;
@@ -679,7 +726,7 @@ __global__ void mstep_kernel(MStepArgs a) {
     double* dsq_s = a.shift_partial;  // k entries (scratch sized for max(k, grid))
     for (int c = warp; c < a.k; c += nwarps) {
       double dsq, nrm;
-      warp_centre(a, c, c, 0, &dsq, &nrm);
+      warp_centre_fold(a, c, &dsq, &nrm);
       if (lane == 0) {
         dsq_s[c] = dsq;
         if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
@@ -687,11 +734,8 @@ __global__ void mstep_kernel(MStepArgs a) {
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      double tot = 0.0;
-      for (int c = 0; c < a.k; ++c) tot += dsq_s[c];
-      finish_iteration(a, st, changed_now, tot);
-    }
+    const double tot = block_ordered_sum(dsq_s, a.k, red_scratch);
+    if (threadIdx.x == 0) finish_iteration(a, st, changed_now, tot);
     return;
   }
 
@@ -838,11 +882,11 @@ __global__ void mstep_kernel(MStepArgs a) {
   }
   if (!grid_barrier(st, nb)) return;
 
-  // 5. convergence bookkeeping, cluster order
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    double tot = 0.0;
-    for (int c = 0; c < a.k; ++c) tot += dsq_s[c];
-    finish_iteration(a, st, changed_now, tot);
+  // 5. convergence bookkeeping
+  if (blockIdx.x == 0) {
+    __shared__ double red_scratch[32];
+    const double tot = block_ordered_sum(dsq_s, a.k, red_scratch);
+    if (threadIdx.x == 0) finish_iteration(a, st, changed_now, tot);
   }
 }
 
@@ -850,21 +894,31 @@ __global__ void counts_to_float_kernel(const long long* __restrict__ c, int k, f
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x) out[i] = (float)c[i];
 }
 
-// bias[c] = ||c||^2 (float64 sum, rounded) and the tf32 split of the centres
-// for the tensor-core E-step: Chi = C with the low 13 mantissa bits cleared,
-// Clo = C - Chi (exact in float32).
+// bias[c] = ||c||^2 (float64 sum, rounded) and the centre image of C for the
+// tensor-core E-step, scaled by 2^cexp with cexp = split_exp(max |C|) (stored
+// in st->cexp). One block (the initial centres of a fit, k x d is small).
 __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, int d, float* __restrict__ bias,
-                                   float* __restrict__ Chi, float* __restrict__ Clo, const FitState* st) {
-  if (st && st->done) return;
+                                   CentreImage ci, FitState* st) {
+  if (st->done || blockIdx.x != 0) return;
   __shared__ double scratch[32];
-  for (int c = blockIdx.x; c < k; c += gridDim.x) {
+  __shared__ unsigned int mx_s;
+  if (threadIdx.x == 0) mx_s = 0;
+  __syncthreads();
+  unsigned int m = 0;
+  for (long long i = threadIdx.x; i < (long long)k * ld; i += blockDim.x)
+    if ((int)(i % ld) < d) m = max(m, __float_as_uint(C[i]) & 0x7fffffffu);
+  m = min(m, 0x7f800000u);
+  atomicMax(&mx_s, m);
+  __syncthreads();
+  const int cexp = split_exp(mx_s);
+  const float cs = ldexpf(1.0f, cexp);
+  if (threadIdx.x == 0) st->cexp = cexp;
+  for (int c = 0; c < k; ++c) {
     double acc = 0.0;
-    for (int j = threadIdx.x; j < ld; j += blockDim.x) {
-      const float v = j < d ? C[(long long)c * ld + j] : 0.0f;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      const float v = C[(long long)c * ld + j];
       acc += (double)v * v;
-      const float hi = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
-      if (Chi) Chi[(long long)c * ld + j] = hi;
-      if (Clo) Clo[(long long)c * ld + j] = v - hi;
+      if (ci.img) cimg_put(ci, c, j, v, cs);
     }
     acc = block_sum_f64(acc, scratch);
     if (threadIdx.x == 0 && bias) bias[c] = (float)acc;

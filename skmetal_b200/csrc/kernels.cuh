@@ -1,6 +1,7 @@
 // Kernel declarations shared by the host driver and the kernel files.
 #pragma once
 
+#include "device_util.cuh"
 #include "skm.cuh"
 
 namespace skm {
@@ -33,10 +34,9 @@ struct MStepArgs {
   float* reloc_x;       // min(k, kMaxEmptyCap) x ld
   double* shift_partial;  // max(k, gridDim.x) entries
   float* shift_out;       // per-centre shift (nullable)
-  // operands of the next tensor-core E-step (nullable): C_new split into
-  // tf32-exact high parts and remainders, and ||C_new||^2
-  float* Chi;
-  float* Clo;
+  // operands of the next tensor-core E-step: the fp16 split image of C_new
+  // (img nullable) and ||C_new||^2 (nullable)
+  CentreImage cimg;
   float* bias;
   // exchanged relocation candidates (multi-GPU); null on one GPU
   int n_cand;
@@ -69,9 +69,8 @@ bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream
 __global__ void bulk_sums_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
                                  long long* D, const FitState* st, int smem_acc);
 
-__global__ void mstep_kernel(MStepArgs a);
-__global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, float* Chi, float* Clo,
-                                   const FitState* st);
+__global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a);
+__global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, CentreImage ci, FitState* st);
 __global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
                                        const int32_t* labels, double* partial, int blocked);
 __global__ void ordered_sum_kernel(const double* partial, int m, double* out);

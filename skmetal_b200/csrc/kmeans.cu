@@ -296,14 +296,17 @@ static int run_fit(const FitParams& p) {
     int rc = tc_plan(X, ld, n, d, k, &plan.tcp);
     plan.tc = (rc == OK) && plan.tcp.supported;
   }
-  float *bias = nullptr, *chi = nullptr, *clo = nullptr;
+  float* bias = nullptr;
+  CentreImage cimg{};
   if (plan.tc) {
     SKM_TRY(buf.alloc_n(&bias, (size_t)plan.tcp.k_pad));
-    SKM_TRY(buf.alloc_n(&chi, (size_t)k * ld));
-    SKM_TRY(buf.alloc_n(&clo, (size_t)k * ld));
-    SKM_TRY(tc_set_centres(&plan.tcp, chi, clo));
+    const size_t halves = plan.tcp.img_bytes / 2;
+    uint16_t* img = nullptr;
+    SKM_TRY(buf.alloc_n(&img, halves));
+    SKM_CUDA(cudaMemsetAsync(img, 0, plan.tcp.img_bytes, s));  // padding entries stay zero
+    cimg = tc_centre_image(plan.tcp, img);
     // operands of the first E-step; later ones come out of the M-step
-    centre_prep_kernel<<<std::min(k, 1024), 128, 0, s>>>(Cb0, k, ld, d, bias, chi, clo, st);
+    centre_prep_kernel<<<1, 1024, 0, s>>>(Cb0, k, ld, d, bias, cimg, st);
     SKM_TRY(check_launch("centre_prep_kernel"));
   }
   int* dev_err = &st->error;
@@ -337,8 +340,7 @@ static int run_fit(const FitParams& p) {
   ma.reloc_dist = reloc_dist;
   ma.reloc_x = reloc_x;
   ma.shift_partial = shift_partial;
-  ma.Chi = chi;
-  ma.Clo = clo;
+  ma.cimg = cimg;
   ma.bias = bias;
   const int mstep_blocks = nsm;
   const int mstep_threads = 1024;
@@ -390,7 +392,7 @@ static int run_fit(const FitParams& p) {
       long long* Dinc = bulk ? nullptr : D;
       if (bulk && it > 0) SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
       if (plan.tc) {
-        SKM_TRY(tc_estep(plan.tcp, bias, labels, changed, Dinc, st, dev_err, s));
+        SKM_TRY(tc_estep(plan.tcp, cimg.img, &st->xexp, bias, labels, changed, Dinc, st, dev_err, s));
       } else {
         SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, Dinc, 0, 1, s));
       }
@@ -455,8 +457,8 @@ static int run_fit(const FitParams& p) {
   // ---- final E-step, inertia, outputs ----------------------------------------
   if (!hs.strict) {
     if (plan.tc) {
-      // chi / clo / bias of the final centres were written by the last M-step
-      SKM_TRY(tc_estep(plan.tcp, bias, labels, nullptr, nullptr, nullptr, dev_err, s));
+      // centre image and bias of the final centres were written by the last M-step
+      SKM_TRY(tc_estep(plan.tcp, cimg.img, &st->xexp, bias, labels, nullptr, nullptr, nullptr, dev_err, s));
     } else {
       SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, nullptr, 0, 1, s));
     }

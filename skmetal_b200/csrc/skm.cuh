@@ -54,6 +54,8 @@ struct FitState {
   unsigned int barrier_count;  // software grid barrier
   unsigned int barrier_gen;
   unsigned int maxabs_bits;    // max |x| (float bits) of centred X
+  int32_t xexp;        // tensor-core operand scale of X: x * 2^xexp (split_exp)
+  int32_t cexp;        // same for the centres of the current centre image
   int32_t pad0;
 };
 

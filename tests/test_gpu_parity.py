@@ -55,24 +55,31 @@ def test_compute_mindists_and_inertia_golden():
     np.testing.assert_allclose(_bridge.row_norm_sq(X), [0, 2, 200, 162], rtol=1e-6)
 
 
+def _probe_x(m, j):
+    p = 8 + (m * 7 + j * 3) % 8
+    q = (m * 5 + j * 11) % 17 - 8
+    return np.where((m + j) & 1, -p, p) + q / 4096.0
+
+
+def _probe_c(c, j):
+    r = 8 + (c * 3 + j * 5) % 8
+    s = (c * 13 + j * 7) % 17 - 8
+    return np.where((c + 2 * j) % 3 == 0, -r, r) + s / 4096.0
+
+
 def test_tensor_core_probe():
-    """tcgen05.cp copies the SW32 tile unpermuted and the tensor core's
-    fp32 -> tf32 conversion is one of the two the E-step can compensate."""
+    """The fp16 split of X, the centre image and both MMA sequences give the
+    exact x_hi.c_hi + x_lo.c_hi + x_hi.c_lo on exactly representable operands."""
     mode, raw = _bridge.debug_tc_probe(raw=True)
-    print(f"tensor-core fp32->tf32 conversion: {['truncation', 'round-to-nearest-even'][mode] if mode >= 0 else mode}")
-    assert mode in (0, 1), mode
-    m = np.arange(128)[:, None]
-    k = np.arange(8)[None, :]
-    low = 0x1000 | ((m * 8 + k) & 0x0FFF)
-    bits = (0x3F800000 | (k << 13) | low | np.where(m >= 64, 0x80000000, 0)).astype(np.uint32)
-    np.testing.assert_array_equal(raw[:1024].reshape(128, 8), bits)
-    if mode == 0:
-        want = bits & np.uint32(0xFFFFE000)
-    else:
-        lsb = (bits >> 13) & 1
-        want = (bits + np.uint32(0x0FFF) + lsb) & np.uint32(0xFFFFE000)
-    np.testing.assert_array_equal(raw[1024:2048].reshape(128, 8), want)
-    np.testing.assert_array_equal(raw[2048:].reshape(128, 8), want)
+    assert mode == 0, mode
+    j = np.arange(16)
+    x = _probe_x(np.arange(128)[:, None], j[None, :])          # 128 x 16, exact in float32
+    c = _probe_c(np.arange(16)[:, None], j[None, :])           # 16 x 16
+    xh, ch = np.round(x), np.round(c)
+    want = (xh @ ch.T + (x - xh) @ ch.T + xh @ (c - ch).T).astype(np.float32)
+    got = raw.view(np.float32)
+    np.testing.assert_array_equal(got[:2048].reshape(128, 16), want)
+    np.testing.assert_array_equal(got[2048:].reshape(128, 16), want)
 
 
 # ---------------------------------------------------------------------------

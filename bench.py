@@ -12,7 +12,9 @@ iterations, the final E-step and the inertia).
 * ``e2e``: the same metric through the public C-ABI call with host buffers
   (pinned X in, labels/centres out, host<->device copies inside the timed region).
 * ``roofline``: the E-step kernel (dominant) against the measured HBM copy
-  bandwidth; algorithmic bytes = 4 n d per launch (X read once).
+  bandwidth; algorithmic bytes = 4 n d per launch (X read once); its duration
+  is the CUDA-event time of the E-step launches of every 10th iteration of the
+  timed fits (the library's profile mode samples them to keep its cost low).
 * ``cpu_baseline`` (rank 0, N = 1): scikit-learn's Lloyd (the reference's CPU
   path) on a bounded sample of the same workload.
 
@@ -27,7 +29,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -51,55 +52,78 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """SM clock and clock-event (throttle) reasons of one GPU, read through NVML
+    every 5 ms on a background thread while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.sm: list[float] = []
+        self.reasons: set[str] = set()
+        self.sm_max = None
+        self.error = None
+        self._stop = threading.Event()
+        self.t = None
+
+    def _handle(self, nv):
+        import torch
+
+        props = torch.cuda.get_device_properties(self.cuda_index)
+        try:
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:  # noqa: BLE001
-            self.proc = None
+            import pynvml as nv
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = self._handle(nv)
+            self.sm_max = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        except Exception as e:  # noqa: BLE001
+            self.error = f"nvml unavailable: {e}"
+
+    def _sample(self):
+        nv = self.nv
+        self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+        bits = int(self.get_reasons(self.h))
+        for name, const in self.REASONS:
+            if bits & int(getattr(nv, const, 0)):
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.wait(self.period):
+            try:
+                self._sample()
+            except Exception:  # noqa: BLE001
+                return
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
+        if self.error:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error], "samples": 0}
+        self._stop.set()
+        if self.t is not None:
+            self.t.join(timeout=5)
         try:
-            self.proc.wait(timeout=5)
+            self._sample()
         except Exception:  # noqa: BLE001
-            self.proc.kill()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+            pass
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.sm_max,
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 5 ms"}
 
 
 def _traffic_for(config: str, launches_rows: int):
@@ -172,7 +196,7 @@ def run_reference(args, w, X, init):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2")

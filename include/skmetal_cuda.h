@@ -30,7 +30,7 @@ extern "C" {
 /* ---- flags for the fit entry points ------------------------------------ */
 #define SKMETAL_FIT_CENTER      0x1u  /* centre X and init by the column mean (KMeans.fit semantics) */
 #define SKMETAL_FIT_SIMT        0x2u  /* force the SIMT E-step instead of the tensor-core one */
-#define SKMETAL_FIT_PROFILE     0x4u  /* time every E-step launch with CUDA events (see fit stats) */
+#define SKMETAL_FIT_PROFILE     0x4u  /* time the E-step launches of every 10th iteration with CUDA events (see fit stats) */
 #define SKMETAL_FIT_DISTRIBUTED 0x8u  /* X is this rank's shard; sums are all-reduced over the communicator */
 #define SKMETAL_FIT_TOL_ABS     0x10u /* tol is the absolute threshold on the sum of squared centre shifts */
 #define SKMETAL_FIT_BULK_SUMS   0x20u /* recompute the centroid sums from all rows every iteration (diagnostic) */
@@ -147,8 +147,9 @@ int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t 
 /* Statistics of the calling thread's last fit / predict: device times in
  * milliseconds measured with CUDA events on the library's stream
  * (total, preparation, Lloyd loop, final E-step + inertia), the number of
- * E-step launches timed individually (SKMETAL_FIT_PROFILE) and their summed
- * duration, the kernel launches issued, and the iterations run. */
+ * E-step launches timed individually (SKMETAL_FIT_PROFILE: iterations 0, 10,
+ * 20, ...) and their summed duration, the kernel launches issued, and the
+ * iterations run. */
 int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,
                            int32_t* estep_launches, double* estep_ms_sum, uint64_t* launches, int32_t* iterations);
 

@@ -89,6 +89,31 @@ __device__ __forceinline__ void warp_apply_changed(const float* __restrict__ X, 
 // term is below 2^-22 of |x||c|.
 // ---------------------------------------------------------------------------
 
+// The split of 8 consecutive columns of one row (two fp32 column quads a, b)
+// scaled by s: hi = fp16 of the 8 scaled values, lo = fp16 of their remainders,
+// each packed as 8 halves (16 bytes), element e at bytes 2e.
+__device__ __forceinline__ void split8(const float4& a, const float4& b, float s, uint4* hi, uint4* lo) {
+  const float v[8] = {a.x * s, a.y * s, a.z * s, a.w * s, b.x * s, b.y * s, b.z * s, b.w * s};
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    __half2 hh = __floats2half2_rn(v[2 * p], v[2 * p + 1]);
+    const float2 hf = __half22float2(hh);
+    __half2 ll = __floats2half2_rn(v[2 * p] - hf.x, v[2 * p + 1] - hf.y);
+    h[p] = *reinterpret_cast<uint32_t*>(&hh);
+    l[p] = *reinterpret_cast<uint32_t*>(&ll);
+  }
+  *hi = make_uint4(h[0], h[1], h[2], h[3]);
+  *lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Split working copy of X for the tensor-core E-step: tile t (128 rows) at
+// t * nk * 4096 bytes; its 8-column chunk c at c * 4096 holds x_hi of the
+// chunk's 8 columns for rows 0..127 (2 KB, 16 bytes per row) then x_lo (2 KB):
+// exactly one K = 16 slice of the kind::f16 A operand in the canonical
+// no-swizzle K-major layout (8-row groups 128 bytes apart, K halves 2048 bytes
+// apart). Columns past d and rows past n are zero.
+
 // Scale exponent for values bounded by the float whose bits are given: with
 // max |v| < 2^E, v * 2^(14 - E) < 2^14 (fp16 reaches 65504, so centres may be
 // up to 4x larger than the bound). Clamped so that 2^(1 - 2e) stays a normal

@@ -9,31 +9,26 @@
 // their exact fixed-point deltas to the centroid sums (the incremental M-step
 // input).
 //
-// Data path of one tile (all asynchronous, one persistent CTA per SM):
-//   HBM --bulk copy--> smem stage (fp32 x in the blocked layout)
-//   converter  : rewrites the stage in place: the two fp32 column quads of each
-//                8-column chunk become (x_hi | x_lo) in fp16, i.e. one K = 16
-//                slice of the kind::f16 A operand in the canonical layout
-//   MMA thread : acc = A . B   (A = stage, B = centre image; one MMA per chunk)
-//   epilogue   : TMEM acc --tcgen05.ld--> argmin --> labels, deltas
-// X is read from HBM exactly once per iteration.
+// Operands: the fit keeps a split working copy of X (split_x_kernel, once per
+// fit) whose 128-row tiles are, byte for byte, the kind::f16 A operand
+// (x_hi | x_lo per 8-column chunk, canonical no-swizzle K-major layout), and a
+// centre image written by the M-step in exactly the B operand's shared-memory
+// layout. A tile therefore goes HBM -> shared memory in bulk copies and
+// straight into the MMAs; the image is loaded once per CTA.
 //
-// X is the fit's blocked working copy (xblk_index): a 128-row tile is one
-// contiguous region in the tensor core's canonical no-swizzle K-major layout
-// (8-column chunk c = 4 KB at c * 4096: two 2 KB halves of 4 columns, 8-row
-// core matrices of 16-byte rows 128 bytes apart), so one bulk copy per tile
-// lands it, and after the in-place split the same descriptor geometry (K
-// halves 2048 bytes apart) addresses (x_hi | x_lo) of the chunk. The centre
-// image (B) is written by the M-step in exactly its shared-memory layout and
-// loaded once per CTA.
+// Data path of one tile (all asynchronous, one persistent CTA per SM):
+//   producer   : HBM --bulk copy--> smem stage
+//   MMA thread : acc = A . B   (one MMA per 8-column chunk)
+//   epilogue   : TMEM acc --tcgen05.ld--> argmin --> labels, deltas
+// X is read from HBM once per iteration (4 bytes per element, as fp32).
 //
 // Warp roles (640 threads): 0 bulk-copy producer, 1 TMEM owner + MMA issuer
-// of even tiles, 2 MMA issuer of odd tiles, 3 idle, 4-11 converter, 12-19
-// epilogue. One thread issues tcgen05.mma at roughly one instruction per ~120
-// cycles whatever N is, while issuers on different SM sub-partitions overlap,
-// so tiles alternate between two issuing warps. Warp w reads TMEM lanes
-// 32*(w%4) .. +31 (= tile rows); the epilogue warps form two groups of one
-// warp per lane quarter that take alternate tiles.
+// of even tiles, 2 MMA issuer of odd tiles, 3 idle, 4-19 epilogue. One thread
+// issues tcgen05.mma at roughly one instruction per ~120 cycles whatever N is,
+// while issuers on different SM sub-partitions overlap, so tiles alternate
+// between two issuing warps. Warp w reads TMEM lanes 32*(w%4) .. +31 (= tile
+// rows); the epilogue warps form up to four groups of one warp per lane
+// quarter, group g taking the tiles of accumulator g.
 //
 // Every mbarrier wait is bounded in time; on timeout the CTA records an error
 // code, stops issuing work, waits (bounded) for its own in-flight copies and
@@ -73,24 +68,24 @@ struct Params {
   int k;
   int k_pad;
   int nk;         // K chunks of 8 columns
-  int nq;         // fp32 column quads present in a tile (ld / 4)
   int stacked;    // centre image layout (CentreImage)
   int stages;     // X stages in shared memory
-  int nacc;       // accumulators in TMEM
+  int nacc;       // accumulators in TMEM (1, 2 or 4)
   int acc_cols;   // TMEM columns of one accumulator
   int tmem_cols;
-  uint32_t stage_bytes;  // >= nk (even nk when not stacked) chunks
+  uint32_t stage_bytes;  // >= tile_bytes (an even number of chunks when not stacked)
+  uint32_t tile_bytes;   // nk * 4096: one tile of the split copy
   uint32_t img_bytes;
-  const uint16_t* img;   // centre image
-  const int* sexp;       // {xexp, cexp}: operand scales 2^xexp, 2^cexp
-  const float* bias;     // ||c||^2, k entries
+  const unsigned char* Xs;  // split working copy
+  const uint16_t* img;      // centre image
+  const int* sexp;          // {xexp, cexp}: operand scales 2^xexp, 2^cexp
+  const float* bias;        // ||c||^2, k entries
   int32_t* labels;
   unsigned long long* changed;
   long long* D;     // nullable: incremental deltas of rows that changed label
-  const float* X;   // blocked layout
+  const float* X;   // fp32 blocked copy (the deltas read exact values from it)
   int ld;
   int d;
-  uint32_t tile_bytes;  // 512 * ld: one tile of blocked X
   const FitState* st;   // nullable: skip when st->done; scale for D
   int* err;
 };
@@ -198,50 +193,28 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
-// Rewrites one row of one 8-column chunk of a blocked fp32 tile in place as a
-// K = 16 slice of the kind::f16 A operand: the 16 bytes of column quad 2c
-// become the fp16 high parts of the row's 8 values scaled by s, those of quad
-// 2c + 1 the fp16 remainders. Quads at or past nq (beyond the last column)
-// read as zero.
-__device__ __forceinline__ void split_chunk_row(unsigned char* tile, int row, int c, int nq, float s) {
-  float4* q0 = reinterpret_cast<float4*>(tile + (size_t)(2 * c) * 2048 + (size_t)row * 16);
-  float4* q1 = reinterpret_cast<float4*>(tile + (size_t)(2 * c + 1) * 2048 + (size_t)row * 16);
-  const float4 a = *q0;
-  const float4 b = (2 * c + 1 < nq) ? *q1 : make_float4(0.f, 0.f, 0.f, 0.f);
-  const float v[8] = {a.x * s, a.y * s, a.z * s, a.w * s, b.x * s, b.y * s, b.z * s, b.w * s};
-  uint32_t hi[4], lo[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const __half2 h = __floats2half2_rn(v[2 * p], v[2 * p + 1]);
-    const float2 hf = __half22float2(h);
-    hi[p] = h2_bits(h);
-    lo[p] = h2_bits(__floats2half2_rn(v[2 * p] - hf.x, v[2 * p + 1] - hf.y));
-  }
-  *reinterpret_cast<uint4*>(q0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-  *reinterpret_cast<uint4*>(q1) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-}
-
-// The MMAs of one tile: A = stage (split in place), B = centre image in smem.
+// The MMAs of one tile: A = stage (split copy of X), B = centre image in smem.
+// The start address sits in the low 14 bits of a descriptor (address / 16,
+// shared memory < 256 KB), so later chunks advance a descriptor by addition.
 __device__ __forceinline__ void issue_tile_mmas(uint32_t tacc, uint32_t stage, uint32_t img, int nk, int k_pad,
                                                 int stacked) {
+  const uint64_t a0 = kmajor_desc(stage, 2048u, 128u);
+  const uint64_t a_step = CHUNK_BYTES >> 4;
   if (stacked) {
     const int N = 2 * k_pad;
     const uint32_t idesc = idesc_f16(N);
-    for (int c = 0; c < nk; ++c)
-      mma_f16(tacc, kmajor_desc(stage + (uint32_t)c * CHUNK_BYTES, 2048u, 128u),
-              kmajor_desc(img + (uint32_t)(c * N * 32), (uint32_t)(N * 16), 128u), idesc, c > 0 ? 1u : 0u);
+    const uint64_t b0 = kmajor_desc(img, (uint32_t)(N * 16), 128u);
+    const uint64_t b_step = (uint64_t)(N * 32) >> 4;
+    for (int c = 0; c < nk; ++c) mma_f16(tacc, a0 + c * a_step, b0 + c * b_step, idesc, c > 0 ? 1u : 0u);
   } else {
     const uint32_t idesc = idesc_f16(k_pad);
-    for (int c = 0; c < nk; ++c)
-      mma_f16(tacc, kmajor_desc(stage + (uint32_t)c * CHUNK_BYTES, 2048u, 128u),
-              kmajor_desc(img + (uint32_t)(c * k_pad * 32), (uint32_t)(k_pad * 16), 128u), idesc, c > 0 ? 1u : 0u);
+    const uint64_t b0 = kmajor_desc(img, (uint32_t)(k_pad * 16), 128u);
+    const uint64_t b_step = (uint64_t)(k_pad * 32) >> 4;
+    for (int c = 0; c < nk; ++c) mma_f16(tacc, a0 + c * a_step, b0 + c * b_step, idesc, c > 0 ? 1u : 0u);
     // x_hi of chunk pairs (2m | 2m + 1) times c_lo of the same pair
-    const uint32_t seg2 = img + (uint32_t)(nk * k_pad * 32);
-    for (int m = 0; 2 * m < nk; ++m)
-      mma_f16(tacc, kmajor_desc(stage + (uint32_t)(2 * m) * CHUNK_BYTES, (uint32_t)CHUNK_BYTES, 128u),
-              kmajor_desc(seg2 + (uint32_t)(m * k_pad * 32), (uint32_t)(k_pad * 16), 128u), idesc, 1u);
+    const uint64_t p0 = kmajor_desc(stage, (uint32_t)CHUNK_BYTES, 128u);
+    const uint64_t q0 = kmajor_desc(img + (uint32_t)(nk * k_pad * 32), (uint32_t)(k_pad * 16), 128u);
+    for (int m = 0; 2 * m < nk; ++m) mma_f16(tacc, p0 + 2 * m * a_step, q0 + m * b_step, idesc, 1u);
   }
 }
 
@@ -252,21 +225,18 @@ struct Smem {
 };
 
 // barrier indices
-__host__ __device__ constexpr int B_FULL(int s) { return s; }                    // stage loaded
-__host__ __device__ constexpr int B_SPLIT(int s) { return MAX_STAGES + s; }      // stage converted
-__host__ __device__ constexpr int B_EMPTY(int s) { return 2 * MAX_STAGES + s; }  // stage consumed by the MMAs
-__host__ __device__ constexpr int B_ACC_FULL(int a) { return 3 * MAX_STAGES + a; }
-__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 3 * MAX_STAGES + MAX_ACC + a; }
-constexpr int B_C_FULL = 3 * MAX_STAGES + 2 * MAX_ACC;
+__host__ __device__ constexpr int B_FULL(int s) { return s; }               // stage loaded
+__host__ __device__ constexpr int B_EMPTY(int s) { return MAX_STAGES + s; }  // stage consumed by the MMAs
+__host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + a; }
+__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + MAX_ACC + a; }
+constexpr int B_C_FULL = 2 * MAX_STAGES + 2 * MAX_ACC;
 __host__ __device__ constexpr int B_DONE(int t) { return B_C_FULL + 1 + t; }  // drain of MMA issuer t
 constexpr int NUM_BARS = B_C_FULL + 3;
 
 constexpr int MMA_W0 = 1, MMA_W1 = 2;
-constexpr int CONV_WARPS = 8;
-constexpr int EPI_WARPS = 8;
-constexpr int CONV_W0 = 4;
-constexpr int EPI_W0 = CONV_W0 + CONV_WARPS;
-static_assert((EPI_W0 + EPI_WARPS) * 32 == THREADS, "warp roles must fill the block");
+constexpr int EPI_W0 = 4;
+constexpr int EPI_GROUPS = 4;  // one warp per TMEM lane quarter each
+static_assert((EPI_W0 + 4 * EPI_GROUPS) * 32 == THREADS, "warp roles must fill the block");
 
 __host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_bytes, int k_pad, int stages) {
   Smem s;
@@ -300,16 +270,15 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
   float* bias_s = reinterpret_cast<float*>(base + L.bias);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int my_tiles = (p.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  // two MMA issuers and two epilogue groups when there are 2 or 4
-  // accumulators (issuer / group t owns the accumulators a = t mod 2, so each
-  // accumulator barrier has one producer and one consumer), else one of each
+  // issuer t owns the accumulators a = t mod n_iss and epilogue group g those
+  // with a = g mod n_grp (n_iss and n_grp divide nacc), so each accumulator
+  // barrier has exactly one producer and one consumer
   const int n_iss = p.nacc >= 2 ? 2 : 1;
-  const int n_grp = n_iss;
+  const int n_grp = p.nacc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < MAX_STAGES; ++s) {
       mbar_init(bar(B_FULL(s)), 1);
-      mbar_init(bar(B_SPLIT(s)), CONV_WARPS);
       mbar_init(bar(B_EMPTY(s)), 1);
     }
     for (int a = 0; a < MAX_ACC; ++a) {
@@ -328,10 +297,10 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   for (int j = threadIdx.x; j < p.k_pad; j += blockDim.x) bias_s[j] = j < p.k ? p.bias[j] : INFINITY;
-  if (p.nk * CHUNK_BYTES < (int)p.stage_bytes) {
+  if (p.tile_bytes < p.stage_bytes) {
     // the extra chunk of an odd nk (read as x_hi by the last pair MMA): zero
     for (int s = 0; s < p.stages; ++s)
-      for (uint32_t o = (uint32_t)p.nk * CHUNK_BYTES + 16u * threadIdx.x; o < p.stage_bytes; o += 16u * blockDim.x)
+      for (uint32_t o = p.tile_bytes + 16u * threadIdx.x; o < p.stage_bytes; o += 16u * blockDim.x)
         *reinterpret_cast<uint4*>(base + (uint32_t)s * p.stage_bytes + o) = make_uint4(0, 0, 0, 0);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -352,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
         const int s = i % p.stages;
         if (!mbar_wait(bar(B_EMPTY(s)), ((i / p.stages) & 1) ^ 1, abort_flag, p.err, 2101)) break;
         const int tile = (int)blockIdx.x + i * (int)gridDim.x;
-        const char* src = reinterpret_cast<const char*>(p.X) + (size_t)tile * p.tile_bytes;
+        const unsigned char* src = p.Xs + (size_t)tile * p.tile_bytes;
         mbar_expect_tx(bar(B_FULL(s)), p.tile_bytes);
         for (uint32_t o = 0; o < p.tile_bytes; o += 8192u)
           bulk_load(sbase + (uint32_t)s * p.stage_bytes + o, src + o, min(8192u, p.tile_bytes - o), bar(B_FULL(s)));
@@ -372,7 +341,16 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
       for (int i = t; ok && i < my_tiles; i += n_iss) {
         const int s = i % p.stages, a = i % p.nacc;
         if (!mbar_wait(bar(B_ACC_EMPTY(a)), ((i / p.nacc) & 1) ^ 1, abort_flag, p.err, 2203)) break;
-        if (!mbar_wait(bar(B_SPLIT(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) break;
+        // A parity wait is only exact while the waiter is at most one phase
+        // away from the barrier. With two issuers and an odd number of stages,
+        // the previous use of stage s belongs to the other issuer, and copies
+        // can land out of order, so FULL(s) alone could still show the phase
+        // of use u - 2. Waiting first for the previous use to be consumed
+        // (EMPTY(s), phase u - 1, as the producer does; this issuer's own MMAs
+        // of use u - 2 completed before its accumulator of tile i was freed)
+        // pins FULL(s) to phase u - 1 or u.
+        if (!mbar_wait(bar(B_EMPTY(s)), ((i / p.stages) & 1) ^ 1, abort_flag, p.err, 2204)) break;
+        if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2202)) break;
         tc_fence_after();
         issue_tile_mmas(tmem_base + (uint32_t)(a * p.acc_cols), sbase + (uint32_t)s * p.stage_bytes, sbase + L.c, p.nk, p.k_pad,
                         p.stacked);
@@ -384,31 +362,10 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
       volatile int no_abort = 0;
       mbar_wait(bar(B_DONE(t)), 0, &no_abort, p.err, 2206);
     }
-  } else if (warp >= CONV_W0 && warp < EPI_W0) {
-    // ---------------------------------------------------------------- converter
-    // thread = tile row; the two threads of a row split its chunks. A warp
-    // reads and writes 512 contiguous bytes per quad (conflict-free).
-    const int t = (warp - CONV_W0) * 32 + lane;
-    const int row = t & (BM - 1);
-    const int h = t >> 7;
-    const int half = (p.nk + 1) >> 1;
-    const int c0 = h ? half : 0, c1 = h ? p.nk : half;
-    const float sx = ldexpf(1.0f, p.sexp[0]);
-    for (int i = 0; i < my_tiles; ++i) {
-      const int s = i % p.stages;
-      if (!mbar_wait(bar(B_FULL(s)), (i / p.stages) & 1, abort_flag, p.err, 2301)) break;
-      unsigned char* stg = base + (uint32_t)s * p.stage_bytes;
-#pragma unroll 2
-      for (int c = c0; c < c1; ++c) split_chunk_row(stg, row, c, p.nq, sx);
-      // generic-proxy writes -> visible to the tensor core (async proxy)
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_SPLIT(s)));
-    }
   } else if (warp >= EPI_W0) {
     // ----------------------------------------------------------------- epilogue
-    // two groups of four warps (one per TMEM lane quarter) take alternate
-    // tiles; each warp scans all clusters of its 32 rows
+    // groups of four warps (one per TMEM lane quarter) take the tiles of their
+    // accumulator; each warp scans all clusters of its 32 rows
     const int q = warp & 3;
     const int g = (warp - EPI_W0) >> 2;
     const int row = q * 32 + lane;
@@ -485,12 +442,42 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
 }
 
 // ---------------------------------------------------------------------------
+// split working copy of X (see the layout note at split8)
+// ---------------------------------------------------------------------------
+// One thread per (tile, chunk, row): reads the row's two fp32 column quads of
+// the chunk from the blocked copy and writes its x_hi and x_lo (16 bytes each)
+// at the same row position of the chunk's two halves; consecutive threads take
+// consecutive rows, so reads and writes are coalesced 512-byte runs per warp.
+__global__ void split_x_kernel(const float* __restrict__ X, int ld, int nk, long long n_tiles,
+                               const int* __restrict__ sexp, uint4* __restrict__ Xs) {
+  const float s = ldexpf(1.0f, sexp[0]);
+  const int nq = ld >> 2;
+  const long long total = n_tiles * nk * BM;
+  const float4* X4 = reinterpret_cast<const float4*>(X);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i & (BM - 1));
+    const long long tc = i >> 7;  // tile * nk + chunk
+    const long long t = tc / nk;
+    const int c = (int)(tc - t * nk);
+    const float4* xt = X4 + t * (32LL * ld);  // tile t of the blocked copy: quad j at xt[128 j]
+    const float4 a = xt[(long long)(2 * c) * 128 + row];
+    const float4 b = (2 * c + 1 < nq) ? xt[(long long)(2 * c + 1) * 128 + row] : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint4 hi, lo;
+    split8(a, b, s, &hi, &lo);
+    uint4* dst = Xs + tc * (CHUNK_BYTES / 16);
+    dst[row] = hi;
+    dst[BM + row] = lo;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // probe: operand layouts of the split-fp16 path, checked on exact values
 // ---------------------------------------------------------------------------
 // A 128 x 16 tile (two chunks) and 16 centres whose fp16 splits are exact
 // (x = p + q 2^-12, c = r + s 2^-12 with |p|, |r| in [8, 16), |q|, |s| <= 8),
 // so that x_hi.c_hi + x_lo.c_hi + x_hi.c_lo is exact in fp32. The tile goes
-// through split_chunk_row and the centres through cimg_put, as in the fit;
+// through split8 and the centres through cimg_put, as in the fit;
 // the stacked (N = 32) and two-segment (N = 16) MMA sequences then run on
 // them. out: [0, 2048) stacked x.c (acc[j] + acc[16 + j]), [2048, 4096)
 // two-segment x.c, row-major 128 x 16; [4096] error code.
@@ -521,7 +508,12 @@ __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint16_t* img_st, uint
   // fp32 tile in the blocked layout, split in place
   for (int j = 0; j < PROBE_NK * KC; ++j)
     *reinterpret_cast<float*>(sm + (j >> 2) * 2048 + tid * 16 + (j & 3) * 4) = probe_x(tid, j);
-  for (int c = 0; c < PROBE_NK; ++c) split_chunk_row(sm, tid, c, 2 * PROBE_NK, 1.0f);
+  for (int c = 0; c < PROBE_NK; ++c) {
+    uint4* q0 = reinterpret_cast<uint4*>(sm + (2 * c) * 2048 + tid * 16);
+    uint4* q1 = reinterpret_cast<uint4*>(sm + (2 * c + 1) * 2048 + tid * 16);
+    const float4 a = *reinterpret_cast<const float4*>(q0), b = *reinterpret_cast<const float4*>(q1);
+    split8(a, b, 1.0f, q0, q1);
+  }
   // centre images: built in global memory by cimg_put, copied to smem
   const CentreImage st{img_st, PROBE_K, PROBE_NK, 1}, two{img_2s, PROBE_K, PROBE_NK, 0};
   for (int e = tid; e < PROBE_K * PROBE_NK * KC; e += blockDim.x) {
@@ -677,7 +669,6 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->k = k;
   plan->k_pad = (int)round_up((size_t)k, 16);
   plan->k_steps = (ld + tc::KC - 1) / tc::KC;
-  plan->nq = ld / 4;
   // prefer one stacked operand (one MMA per chunk); both layouts need >= 2 stages
   plan->stages = 0;
   for (int stacked = (2 * plan->k_pad <= 256) ? 1 : 0; stacked >= 0 && plan->stages == 0; --stacked) {
@@ -714,6 +705,21 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   return OK;
 }
 
+size_t tc_split_bytes(const TcPlan& plan) {
+  return (size_t)((plan.n + tc::BM - 1) / tc::BM) * plan.k_steps * tc::CHUNK_BYTES;
+}
+
+int tc_split_x(TcPlan* plan, void* Xs, const int* sexp, cudaStream_t s) {
+  const long long n_tiles = (plan->n + tc::BM - 1) / tc::BM;
+  const long long work = n_tiles * plan->k_steps * tc::BM;
+  const int blocks = (int)std::max(1LL, std::min((work + 255) / 256, (long long)sm_count() * 8));
+  tc::split_x_kernel<<<blocks, 256, 0, s>>>(plan->X, plan->ld, plan->k_steps, n_tiles, sexp,
+                                            reinterpret_cast<uint4*>(Xs));
+  SKM_TRY(check_launch("split_x_kernel"));
+  plan->Xs = static_cast<const unsigned char*>(Xs);
+  return OK;
+}
+
 CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img) {
   return CentreImage{img, plan.k_pad, plan.k_steps, plan.stacked};
 }
@@ -726,7 +732,6 @@ int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const flo
   p.k = plan.k;
   p.k_pad = plan.k_pad;
   p.nk = plan.k_steps;
-  p.nq = plan.nq;
   p.stacked = plan.stacked;
   p.stages = plan.stages;
   p.nacc = plan.nacc;
@@ -734,6 +739,8 @@ int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const flo
   p.tmem_cols = plan.tmem_cols;
   p.stage_bytes = plan.stage_bytes;
   p.img_bytes = plan.img_bytes;
+  p.tile_bytes = (uint32_t)(plan.k_steps * tc::CHUNK_BYTES);
+  p.Xs = plan.Xs;
   p.img = img;
   p.sexp = sexp;
   p.bias = bias;
@@ -743,7 +750,6 @@ int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const flo
   p.X = plan.X;
   p.ld = plan.ld;
   p.d = plan.d;
-  p.tile_bytes = (uint32_t)(512 * plan.ld);
   p.st = st;
   p.err = err;
   tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(p);

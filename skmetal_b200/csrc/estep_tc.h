@@ -1,7 +1,7 @@
-// Tensor-core (tcgen05, sm_100a) E-step: bulk-copied X tiles split in shared
-// memory into fp16 (high | remainder) operands, split-fp16 distance tiles
-// accumulated in tensor memory, running argmin in registers, incremental
-// fixed-point deltas for rows that change label.
+// Tensor-core (tcgen05, sm_100a) E-step: tiles of a split-fp16 working copy
+// of X bulk-copied into shared memory, distance tiles accumulated in tensor
+// memory, running argmin in registers, incremental fixed-point deltas for rows
+// that change label.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -22,12 +22,12 @@ struct TcPlan {
   int k = 0;
   int k_pad = 0;     // clusters padded to the MMA N granularity (16)
   int k_steps = 0;   // K = ld in chunks of 8 columns
-  int nq = 0;        // fp32 column quads per row (ld / 4)
   int stacked = 0;   // centre image layout (CentreImage)
   int stages = 0;    // X stages in shared memory
   int nacc = 0;      // accumulators in tensor memory
   int acc_cols = 0;  // tensor-memory columns per accumulator
   int tmem_cols = 0; // tensor-memory allocation
+  const unsigned char* Xs = nullptr;  // split working copy (tc_split_x)
   uint32_t stage_bytes = 0;
   uint32_t img_bytes = 0;
   int grid = 0;
@@ -43,6 +43,12 @@ int tc_probe(int* mode, uint32_t* raw4096);
 
 // X: the fit's blocked working copy (xblk_index), round_up(n, 128) rows.
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan);
+
+// Bytes of the split working copy of X for this plan, and the launch that
+// builds it from the fp32 blocked copy with the scale 2^sexp[0] (device int);
+// the plan then reads its tiles from Xs.
+size_t tc_split_bytes(const TcPlan& plan);
+int tc_split_x(TcPlan* plan, void* Xs, const int* sexp, cudaStream_t s);
 
 // Geometry of the centre image the plan's kernel reads (img: cimg_halves(...)
 // fp16 entries, zero-initialised by the caller).

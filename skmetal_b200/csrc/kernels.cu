@@ -617,39 +617,6 @@ __device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, int src, 
   *nrm_out = warp_sum(nrm);
 }
 
-// Fast-path centre (no relocation): folds this iteration's deltas of cluster
-// c into S while computing the centre, so that S, D and C_old are read once
-// with independent loads. counts must already be folded into cnt_adj.
-__device__ __forceinline__ void warp_centre_fold(const MStepArgs& a, int c, double* dsq_out, double* nrm_out) {
-  const int lane = threadIdx.x & 31;
-  const float cs = ldexpf(1.0f, a.st->xexp);
-  const double inv_scale = a.st->inv_scale;
-  const long long cnt = a.cnt_adj[c];
-  long long* S = const_cast<long long*>(a.S);
-  double dsq = 0.0, nrm = 0.0;
-  for (int j = lane; j < a.ld; j += 32) {
-    const long long i = (long long)c * a.ld + j;
-    const long long dv = a.D[i];
-    const long long sv = S[i] + dv;
-    const float old = a.C_old[i];
-    if (dv != 0) {
-      S[i] = sv;
-      a.D[i] = 0;
-    }
-    float v = 0.0f;
-    if (j < a.d) {
-      v = centre_from_sum(sv, inv_scale, cnt);
-      const double df = (double)v - (double)old;
-      dsq += df * df;
-      nrm += (double)v * v;
-      if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
-    }
-    a.C_new[i] = v;
-  }
-  *dsq_out = warp_sum(dsq);
-  *nrm_out = warp_sum(nrm);
-}
-
 // Convergence bookkeeping (_kmeans.py:723-741) from the per-cluster squared
 // shifts summed in a fixed order; one thread. The centre image now holds
 // centres scaled by 2^xexp.
@@ -669,12 +636,22 @@ __device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long
 
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   FitState* st = a.st;
-  if (st->done) return;  // uniform: `done` is only written at the very end
-  const unsigned long long changed_now = *a.changed;  // cleared at the end
   const unsigned int nb = gridDim.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const long long ks = (long long)a.k * a.ld;
   const long long* dcnt = a.D + ks;
+  // Every global value the no-relocation path needs is loaded here at once,
+  // so that its chain of dependent memory round trips stays short.
+  const int done = st->done;  // uniform: `done` is only written at the very end
+  const unsigned long long changed_now = *a.changed;  // cleared at the end
+  const double inv_scale = st->inv_scale;
+  const int xexp = st->xexp;
+  long long cnt0 = 0, dcnt0 = 0;  // cluster threadIdx.x
+  if ((int)threadIdx.x < a.k) {
+    cnt0 = a.counts[threadIdx.x];
+    dcnt0 = dcnt[threadIdx.x];
+  }
+  if (done) return;
   __shared__ int n_empty_s;
   __shared__ int wcount[32];
   __shared__ long long hv_cnt[32];
@@ -686,7 +663,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   __syncthreads();
   for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
     const int c = c0 + threadIdx.x;
-    const bool e = c < a.k && a.counts[c] + dcnt[c] == 0;
+    const bool e = c < a.k && (c0 == 0 ? cnt0 + dcnt0 : a.counts[c] + dcnt[c]) == 0;
     const unsigned int b = __ballot_sync(0xffffffffu, e);
     if (lane == 0) wcount[warp] = __popc(b);
     __syncthreads();
@@ -708,34 +685,100 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     // ---------------- fast path: no relocation, one block does the update
     if (blockIdx.x != 0) return;
     __shared__ double red_scratch[32];
+    extern __shared__ long long cnt_smem[];  // k entries when k <= kFoldSmemK
+    long long* cnt_k = a.k <= kFoldSmemK ? cnt_smem : a.cnt_adj;
+    int iter = 0, max_iter = 0;
+    double tol = 0.0;
+    if (threadIdx.x == 0) {
+      iter = st->iter;
+      max_iter = st->max_iter;
+      tol = st->tol;
+    }
     long long* cnt = const_cast<long long*>(a.counts);
     for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
-      const long long dv = dcnt[c];
-      const long long v = cnt[c] + dv;
+      const long long dv = c < (int)blockDim.x ? dcnt0 : dcnt[c];
+      const long long v = (c < (int)blockDim.x ? cnt0 : cnt[c]) + dv;
+      cnt_k[c] = v;
       a.cnt_adj[c] = v;
       if (dv != 0) {
         cnt[c] = v;
         a.D[ks + c] = 0;
       }
     }
-    if (threadIdx.x == 0) {
-      st->n_empty = 0;
-      st->relocated = 0;
-    }
     __syncthreads();
-    double* dsq_s = a.shift_partial;  // k entries (scratch sized for max(k, grid))
+    // 2. S += dS and the centres, one warp per cluster, lanes over columns
+    //    in batches of 128 whose loads are all issued before any store
+    long long* S = const_cast<long long*>(a.S);
+    const float cs = ldexpf(1.0f, xexp);  // centres are bounded by max |x|
+    double wdsq = 0.0;  // this warp's squared shifts, in cluster order
     for (int c = warp; c < a.k; c += nwarps) {
-      double dsq, nrm;
-      warp_centre_fold(a, c, &dsq, &nrm);
+      const long long count = cnt_k[c];
+      double dsq = 0.0, nrm = 0.0;
+      for (int j0 = 0; j0 < a.ld; j0 += 128) {
+        long long dv[4], sv[4];
+        float old[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = j0 + 32 * u + lane;
+          dv[u] = 0;
+          sv[u] = 0;
+          old[u] = 0.0f;
+          if (j < a.ld) {
+            const long long i = (long long)c * a.ld + j;
+            dv[u] = a.D[i];
+            sv[u] = S[i];
+            old[u] = a.C_old[i];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = j0 + 32 * u + lane;
+          if (j < a.ld) {
+            const long long i = (long long)c * a.ld + j;
+            const long long sum = sv[u] + dv[u];
+            if (dv[u] != 0) {
+              S[i] = sum;
+              a.D[i] = 0;
+            }
+            float v = 0.0f;
+            if (j < a.d) {
+              v = centre_from_sum(sum, inv_scale, count);
+              const double df = (double)v - (double)old[u];
+              dsq += df * df;
+              nrm += (double)v * v;
+              if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
+            }
+            a.C_new[i] = v;
+          }
+        }
+      }
+      dsq = warp_sum(dsq);
+      nrm = warp_sum(nrm);
       if (lane == 0) {
-        dsq_s[c] = dsq;
         if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
         if (a.bias) a.bias[c] = (float)nrm;
       }
+      wdsq += dsq;
     }
+    // 3. total squared shift: warp partials in warp order (a fixed order)
+    if (lane == 0) red_scratch[warp] = wdsq;
     __syncthreads();
-    const double tot = block_ordered_sum(dsq_s, a.k, red_scratch);
-    if (threadIdx.x == 0) finish_iteration(a, st, changed_now, tot);
+    if (threadIdx.x == 0) {
+      double tot = 0.0;
+      for (int w = 0; w < nwarps; ++w) tot += red_scratch[w];
+      st->n_empty = 0;
+      st->relocated = 0;
+      st->cexp = xexp;
+      st->shift_tot = tot;
+      st->iter = iter + 1;
+      if (changed_now == 0) {
+        st->strict = 1;
+        st->done = 1;
+      } else if (tot <= tol || iter + 1 >= max_iter) {
+        st->done = 1;
+      }
+      *const_cast<unsigned long long*>(a.changed) = 0;
+    }
     return;
   }
 
@@ -900,7 +943,6 @@ __global__ void counts_to_float_kernel(const long long* __restrict__ c, int k, f
 __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, int d, float* __restrict__ bias,
                                    CentreImage ci, FitState* st) {
   if (st->done || blockIdx.x != 0) return;
-  __shared__ double scratch[32];
   __shared__ unsigned int mx_s;
   if (threadIdx.x == 0) mx_s = 0;
   __syncthreads();
@@ -913,15 +955,16 @@ __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, i
   const int cexp = split_exp(mx_s);
   const float cs = ldexpf(1.0f, cexp);
   if (threadIdx.x == 0) st->cexp = cexp;
-  for (int c = 0; c < k; ++c) {
+  const int lane = threadIdx.x & 31;
+  for (int c = threadIdx.x >> 5; c < k; c += blockDim.x >> 5) {
     double acc = 0.0;
-    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    for (int j = lane; j < d; j += 32) {
       const float v = C[(long long)c * ld + j];
       acc += (double)v * v;
       if (ci.img) cimg_put(ci, c, j, v, cs);
     }
-    acc = block_sum_f64(acc, scratch);
-    if (threadIdx.x == 0 && bias) bias[c] = (float)acc;
+    acc = warp_sum(acc);
+    if (lane == 0 && bias) bias[c] = (float)acc;
   }
 }
 

@@ -7,6 +7,7 @@
 namespace skm {
 
 constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
+constexpr int kFoldSmemK = 4096;          // M-step keeps up to this many folded counts in shared memory
 
 struct MStepArgs {
   FitState* st;

@@ -29,6 +29,11 @@
 
 namespace skm {
 
+// SKMETAL_FIT_PROFILE times the E-step launches of iterations 0, 10, 20, ...
+// with CUDA events: one event pair per iteration costs a few microseconds of
+// device time, so timing a sample keeps the measured loop representative.
+constexpr int kProfileEvery = 10;
+
 struct FitStats {
   double ms_total = 0, ms_prep = 0, ms_loop = 0, ms_final = 0;
   int estep_launches = 0;
@@ -299,6 +304,9 @@ static int run_fit(const FitParams& p) {
   float* bias = nullptr;
   CentreImage cimg{};
   if (plan.tc) {
+    void* Xs = nullptr;
+    SKM_TRY(buf.alloc(&Xs, tc_split_bytes(plan.tcp)));
+    SKM_TRY(tc_split_x(&plan.tcp, Xs, &st->xexp, s));
     SKM_TRY(buf.alloc_n(&bias, (size_t)plan.tcp.k_pad));
     const size_t halves = plan.tcp.img_bytes / 2;
     uint16_t* img = nullptr;
@@ -344,6 +352,7 @@ static int run_fit(const FitParams& p) {
   ma.bias = bias;
   const int mstep_blocks = nsm;
   const int mstep_threads = 1024;
+  const size_t mstep_smem = k <= kFoldSmemK ? sizeof(long long) * (size_t)k : 0;
 
   std::vector<cudaEvent_t> prof_ev;
   if (p.profile) {
@@ -385,7 +394,8 @@ static int run_fit(const FitParams& p) {
     for (; it < end; ++it) {
       const float* Cin = (it & 1) ? Cb1 : Cb0;
       float* Cout = (it & 1) ? Cb0 : Cb1;
-      if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
+      const bool timed = p.profile && it % kProfileEvery == 0;
+      if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
       // iteration 0 has no previous labels: sums are built in bulk afterwards;
       // later iterations add the deltas of the rows that changed label
       const bool bulk = it == 0 || p.bulk_sums;
@@ -396,13 +406,13 @@ static int run_fit(const FitParams& p) {
       } else {
         SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, Dinc, 0, 1, s));
       }
-      if (p.profile) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
+      if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
       if (bulk) SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, D, st, s));
       if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
       ma.C_old = Cin;
       ma.C_new = Cout;
       void* args[] = {&ma};
-      SKM_CUDA(cudaLaunchCooperativeKernel((void*)mstep_kernel, dim3(mstep_blocks), dim3(mstep_threads), args, 0, s));
+      SKM_CUDA(cudaLaunchCooperativeKernel((void*)mstep_kernel, dim3(mstep_blocks), dim3(mstep_threads), args, mstep_smem, s));
       SKM_TRY(check_launch("mstep_kernel"));
     }
     const int slot = chunk_idx & 63;
@@ -496,7 +506,7 @@ static int run_fit(const FitParams& p) {
   cudaEventElapsedTime(&ms, ev2, ev3);
   fs.ms_final = ms;
   if (p.profile) {
-    for (int i = 0; i < iters; ++i) {
+    for (int i = 0; i < iters; i += kProfileEvery) {
       float m = 0;
       if (cudaEventElapsedTime(&m, prof_ev[2 * i], prof_ev[2 * i + 1]) == cudaSuccess) {
         fs.estep_ms_sum += m;

@@ -157,6 +157,18 @@ def test_lloyd_step_relocation_lockstep():
     _lockstep(X, init, 5)
 
 
+@pytest.mark.parametrize("n,d,k", [(300_000, 36, 24), (200_000, 100, 50), (150_000, 64, 256)])
+def test_estep_many_tiles_per_cta(n, d, k):
+    """Sizes at which every CTA of the persistent tensor-core E-step runs many
+    tiles, so its shared-memory stages, accumulators and both MMA issuers wrap
+    around many times: one Lloyd step against the oracle's E-step."""
+    X, init = gaussian_mixture(n, d, k, seed=n + d + k)
+    lab, cnew, weight, shift = _bridge.kmeans_lloyd_iter(X, init)
+    want, _ = ora.assign(X, init, "fp32")
+    check_labels(X, init, lab, want, "many-tile E-step")
+    np.testing.assert_array_equal(weight.astype(np.int64), np.bincount(lab, minlength=k))
+
+
 # ---------------------------------------------------------------------------
 # tensor-core vs SIMT E-step, full fits
 # ---------------------------------------------------------------------------

@@ -3,7 +3,7 @@
 // skmetal_kmeans_update_centers_noalloc computes, for rows and labels that
 // already live in device memory, every cluster's mean with the same exact
 // fixed-point sums as the fit's M-step (max |x| -> scale 2^F, integer sums,
-// mean = sum / (2^F * count)), so its centres are bit-identical to the ones
+// mean = sum * (2^-F / count)), so its centres are bit-identical to the ones
 // skmetal_kmeans_lloyd_iter returns for the same labels when no cluster is
 // empty. It exists for callers that cannot allocate device memory at the time
 // they call: a process whose free device memory is already claimed by another
@@ -95,8 +95,9 @@ __global__ void noalloc_sums_kernel(const float* __restrict__ X, long long n, in
   }
 }
 
-// centres[c][j] = S[c][j] / (2^F * count[c]) for every non-empty cluster (the
-// fit's averaging expression); rows of empty clusters are left as they are.
+// centres[c][j] = S[c][j] * (2^-F / count[c]) for every non-empty cluster (the
+// fit's averaging expression, centre_from_sum); rows of empty clusters are
+// left as they are.
 // Nothing is written when the sums reported an error.
 __global__ void noalloc_centres_kernel(const long long* __restrict__ S, const long long* __restrict__ counts,
                                        long long n, int d, int k, const unsigned int* __restrict__ hdr,
@@ -107,7 +108,7 @@ __global__ void noalloc_centres_kernel(const long long* __restrict__ S, const lo
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
     const long long cnt = counts[i / d];
-    if (cnt > 0) centres[i] = (float)((double)S[i] * inv_scale / (double)cnt);
+    if (cnt > 0) centres[i] = centre_from_sum(S[i], centre_factor(inv_scale, cnt));
   }
   if (weight)
     for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < k; c += stride)

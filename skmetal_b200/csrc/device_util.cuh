@@ -34,6 +34,23 @@ __device__ __forceinline__ long long to_fixed(float v, double scale) {
   return __double2ll_rn(static_cast<double>(v) * scale);
 }
 
+// Centres from exact fixed-point sums: c = s * (2^-F / count), the factor
+// computed once per cluster (one float64 division per cluster, not per
+// element).
+__device__ __forceinline__ double centre_factor(double inv_scale, long long count) {
+  return inv_scale / (double)count;
+}
+__device__ __forceinline__ float centre_from_sum(long long s, double factor) { return (float)((double)s * factor); }
+
+// Programmatic dependent launch (kernels launched with the programmatic
+// stream-serialization attribute): allow the next kernel of the stream to be
+// scheduled now, and wait until every write of the previous kernel is
+// visible. Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
   atomicAdd(reinterpret_cast<unsigned long long*>(p), static_cast<unsigned long long>(v));
 }
@@ -41,41 +58,63 @@ __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
 // ---------------------------------------------------------------------------
 // incremental update: a row whose label moved from `old` to `neu` adds its
 // fixed-point coordinates to cluster `neu` and removes them from `old` in the
-// delta buffer D = [dS (k x ld) | dcount (k) | changed]. Called by all 32
-// lanes of a warp with the row index and labels of one lane (`src_lane`);
-// lanes stride over the columns, so loads and reductions are coalesced.
+// delta buffer D = [dS (k x ld) | dcount (k) | changed]. In the blocked layout
+// a row's column quads are 16-byte pieces 2 KB apart, so lane q loads quad q
+// (one float4) and a warp fetches a whole row (ld <= 128) in one round trip.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void warp_apply_delta(const float* __restrict__ X, int ld, int d, int k, long long row, int old, int neu,
-                                 long long* __restrict__ D, double scale) {
-  const int lane = threadIdx.x & 31;
-  const float* xr = X + xblk_index(row, 0, ld);  // X is blocked: column j at xr[(j/4)*512 + j%4]
-  long long* dn = D + (long long)neu * ld;
-  long long* dold = old >= 0 ? D + (long long)old * ld : nullptr;
-  for (int j = lane; j < d; j += 32) {
-    const long long v = to_fixed(__ldg(xr + (j >> 2) * 512 + (j & 3)), scale);
-    if (v != 0) {
-      red_add_s64(dn + j, v);
-      if (dold) red_add_s64(dold + j, -v);
+__device__ __forceinline__ void quad_delta(const float4& v, int q, int d, long long* __restrict__ dn,
+                                           long long* __restrict__ dold, double scale) {
+  const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = 4 * q + u;
+    const long long f = to_fixed(x[u], scale);
+    if (j < d && f != 0) {
+      red_add_s64(dn + j, f);
+      if (dold) red_add_s64(dold + j, -f);
     }
-  }
-  if (lane == 0) {
-    long long* cnt = D + (long long)k * ld;
-    red_add_s64(cnt + neu, 1);
-    if (old >= 0) red_add_s64(cnt + old, -1);
   }
 }
 
+__device__ __forceinline__ void count_delta(int k, int ld, int old, int neu, long long* __restrict__ D) {
+  long long* cnt = D + (long long)k * ld;
+  red_add_s64(cnt + neu, 1);
+  if (old >= 0) red_add_s64(cnt + old, -1);
+}
+
 // For every lane of the calling warp whose row changed label, apply its delta.
-__device__ __forceinline__ void warp_apply_changed(const float* __restrict__ X, int ld, int d, int k, long long row, int old, int neu,
-                                   bool changed, long long* __restrict__ D, double scale) {
+// Rows are taken two at a time so that both rows' loads are in flight together.
+__device__ __forceinline__ void warp_apply_changed(const float* __restrict__ X, int ld, int d, int k, long long row,
+                                                   int old, int neu, bool changed, long long* __restrict__ D,
+                                                   double scale) {
+  const int lane = threadIdx.x & 31;
+  const int nq = ld >> 2;
   unsigned int m = __ballot_sync(0xffffffffu, changed);
   while (m) {
-    const int src = __ffs(m) - 1;
+    const int s1 = __ffs(m) - 1;
     m &= m - 1;
-    const long long r = __shfl_sync(0xffffffffu, row, src);
-    const int o = __shfl_sync(0xffffffffu, old, src);
-    const int nn = __shfl_sync(0xffffffffu, neu, src);
-    warp_apply_delta(X, ld, d, k, r, o, nn, D, scale);
+    const int s2 = m ? __ffs(m) - 1 : s1;
+    if (m) m &= m - 1;
+    const bool two = s2 != s1;
+    const long long r1 = __shfl_sync(0xffffffffu, row, s1), r2 = __shfl_sync(0xffffffffu, row, s2);
+    const int o1 = __shfl_sync(0xffffffffu, old, s1), o2 = __shfl_sync(0xffffffffu, old, s2);
+    const int n1 = __shfl_sync(0xffffffffu, neu, s1), n2 = __shfl_sync(0xffffffffu, neu, s2);
+    const float4* x1 = reinterpret_cast<const float4*>(X + xblk_index(r1, 0, ld));  // quad q at x1[128 q]
+    const float4* x2 = reinterpret_cast<const float4*>(X + xblk_index(r2, 0, ld));
+    long long* dn1 = D + (long long)n1 * ld;
+    long long* do1 = o1 >= 0 ? D + (long long)o1 * ld : nullptr;
+    long long* dn2 = D + (long long)n2 * ld;
+    long long* do2 = o2 >= 0 ? D + (long long)o2 * ld : nullptr;
+    for (int q = lane; q < nq; q += 32) {
+      const float4 v1 = __ldg(x1 + (long long)q * 128);
+      const float4 v2 = two ? __ldg(x2 + (long long)q * 128) : v1;
+      quad_delta(v1, q, d, dn1, do1, scale);
+      if (two) quad_delta(v2, q, d, dn2, do2, scale);
+    }
+    if (lane == 0) {
+      count_delta(k, ld, o1, n1, D);
+      if (two) count_delta(k, ld, o2, n2, D);
+    }
   }
 }
 

@@ -257,7 +257,13 @@ __host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_b
 __device__ __forceinline__ bool better(float d, int i, float bd, int bi) { return d < bd || (d == bd && i < bi); }
 
 __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
+  // the M-step that follows may be scheduled as soon as SMs free up; the
+  // previous M-step's centres, bias, image and flags must be visible first
+  pdl_launch_dependents();
+  pdl_wait();
   if (p.st && p.st->done) return;
+  // bulk iterations rebuild the sums from all rows in the M-step
+  long long* const deltas = (p.st && p.st->bulk) ? nullptr : p.D;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -428,7 +434,7 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
       if (p.changed) {
         const unsigned int m = __ballot_sync(0xffffffffu, ch);
         if (lane == 0 && m) atomicAdd(p.changed, (unsigned long long)__popc(m));
-        if (p.D) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, p.D, p.st->scale);
+        if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st->scale);
       }
     }
   }
@@ -725,7 +731,7 @@ CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img) {
 }
 
 int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,
-             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s) {
+             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s, bool pdl) {
   tc::Params p;
   p.n_tiles = (int)((plan.n + tc::BM - 1) / tc::BM);
   p.n = plan.n;
@@ -752,7 +758,21 @@ int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const flo
   p.d = plan.d;
   p.st = st;
   p.err = err;
-  tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(p);
+  if (pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(tc::THREADS);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SKM_CUDA(cudaLaunchKernelEx(&cfg, tc::estep_tc_kernel, p));
+  } else {
+    tc::estep_tc_kernel<<<plan.grid, tc::THREADS, plan.smem, s>>>(p);
+  }
   return check_launch("estep_tc_kernel");
 }
 

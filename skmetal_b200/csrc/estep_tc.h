@@ -60,7 +60,11 @@ CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img);
 // fixed-point deltas of those rows; `st` (nullable) makes the launch a no-op
 // once st->done is set; `err` receives a nonzero code if a pipeline wait
 // times out.
+// `pdl`: launch with programmatic stream serialization (the kernel waits for
+// the previous kernel's writes itself). In bulk iterations (st->bulk) no
+// deltas are written.
 int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,
-             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s);
+             unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s,
+             bool pdl = false);
 
 }  // namespace skm

@@ -311,7 +311,7 @@ __global__ void scale_kernel(const unsigned int* __restrict__ maxabs_bits, doubl
 // Initialise the fit state. tol_mode 0: `tol` is already absolute; 1: `tol` is
 // relative and is scaled by the mean column variance sumsq / (n_total * d).
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
-                                  double n_total, int d, const unsigned int* maxabs_bits) {
+                                  double n_total, int d, const unsigned int* maxabs_bits, int bulk_always) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   st->iter = 0;
   st->done = max_iter <= 0;
@@ -331,6 +331,10 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
   if (tol_mode == 1) t = (tol == 0.0 || sumsq == nullptr) ? 0.0 : (*sumsq / (n_total * (double)d)) * tol;
   st->tol = t;
   st->maxabs_bits = *maxabs_bits;
+  st->bulk = 1;  // the first iteration starts from labels -1: every row changes
+  st->bulk_always = bulk_always;
+  // above ~n/10 changed rows the per-row deltas cost more than a bulk pass
+  st->bulk_threshold = (long long)fmax(1.0, n_total / 10.0);
   st->xexp = split_exp(*maxabs_bits);
   st->cexp = st->xexp;
   st->scale = fixed_scale(*maxabs_bits, n_total);
@@ -411,7 +415,7 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
   if (changed) {
     const unsigned int b = __ballot_sync(0xffffffffu, ch);
     if ((threadIdx.x & 31) == 0 && b) atomicAdd(changed, (unsigned long long)__popc(b));
-    if (D) warp_apply_changed(X, ld, d, k, r, old, bl, ch, D, st->scale);
+    if (D && !st->bulk) warp_apply_changed(X, ld, d, k, r, old, bl, ch, D, st->scale);
   }
 }
 
@@ -469,45 +473,80 @@ bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream
 // and flushes it with one global reduction per nonzero entry; otherwise it
 // adds straight into D. Integer sums are exact, so the result does not depend
 // on the order or the grid.
-__global__ void bulk_sums_kernel(const float* __restrict__ X, int ld, long long n, int d,
-                                 const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                 const FitState* __restrict__ st, int smem_acc) {
-  extern __shared__ long long acc[];
-  if (st->done) return;
-  const double scale = st->scale;
+// Fixed-point sums and counts of all rows by label, added into
+// D = [dS (k x ld) | dcount (k)], which must be zero. A warp takes 8
+// consecutive rows at a time; lane (rsub, qsub) = (lane % 8, lane / 8) reads
+// column quad 4 m + qsub of row rsub, so each load instruction fetches four
+// whole 128-byte lines of the blocked layout (8 rows x 16 bytes per quad) and
+// uses them at once. With `acc` (shared, k*ld + k int64) the block
+// accumulates privately in the layout [u][c][q] (column 4q + u of cluster c)
+// and adds its non-zero entries to D at the end; without, it adds to D
+// directly. Integer additions are exact, so the result does not depend on
+// their order.
+__device__ __forceinline__ void bulk_pass(const float* __restrict__ X, int ld, long long n,
+                                          const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
+                                          double scale, long long* acc) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int rsub = lane & 7, qsub = lane >> 3;
+  const int nq = ld >> 2;
   const long long ks = (long long)k * ld;
-  long long* A = smem_acc ? acc : D;
-  if (smem_acc) {
+  if (acc) {
     for (long long i = threadIdx.x; i < ks + k; i += blockDim.x) acc[i] = 0;
     __syncthreads();
   }
-  const int q4 = ld >> 2;
-  const long long items = (n + 31) / 32;  // 32-row groups (4 per tile)
   const float4* X4 = reinterpret_cast<const float4*>(X);
-  for (long long it = (long long)blockIdx.x * nw + warp; it < items; it += (long long)gridDim.x * nw) {
-    const long long r = it * 32 + lane;
-    if (r >= n) continue;
-    const int l = labels[r];
-    const float4* xp = X4 + (r >> 7) * (32LL * ld) + (r & 127);  // quad q at xp[q * 128]
-    long long* a = A + (long long)l * ld;
-    for (int q = 0; q < q4; ++q) {
-      const float4 v = __ldcs(xp + (long long)q * 128);
-      const long long v0 = to_fixed(v.x, scale), v1 = to_fixed(v.y, scale);
-      const long long v2 = to_fixed(v.z, scale), v3 = to_fixed(v.w, scale);
-      if (v0) red_add_s64(a + 4 * q + 0, v0);
-      if (v1) red_add_s64(a + 4 * q + 1, v1);
-      if (v2) red_add_s64(a + 4 * q + 2, v2);
-      if (v3) red_add_s64(a + 4 * q + 3, v3);
+  const long long blocks8 = (n + 7) / 8;
+  for (long long b = (long long)blockIdx.x * nw + warp; b < blocks8; b += (long long)gridDim.x * nw) {
+    const long long r = b * 8 + rsub;
+    const bool valid = r < n;
+    const int c = valid ? labels[r] : 0;
+    const float4* xr = X4 + (r >> 7) * (32LL * ld) + (r & 127);  // quad q of row r at xr[128 q]
+    for (int q0 = 0; q0 < nq; q0 += 4) {
+      const int q = q0 + qsub;
+      if (!valid || q >= nq) continue;
+      const float4 v = __ldcs(xr + (long long)q * 128);
+      const long long f[4] = {to_fixed(v.x, scale), to_fixed(v.y, scale), to_fixed(v.z, scale),
+                              to_fixed(v.w, scale)};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (f[u] == 0) continue;
+        if (acc)
+          atomicAdd(reinterpret_cast<unsigned long long*>(&acc[((long long)u * k + c) * nq + q]),
+                    static_cast<unsigned long long>(f[u]));
+        else
+          red_add_s64(D + (long long)c * ld + 4 * q + u, f[u]);
+      }
     }
-    red_add_s64(&A[ks + l], 1);
+    if (valid && qsub == 0) {
+      if (acc)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&acc[ks + c]), 1ull);
+      else
+        red_add_s64(D + ks + c, 1);
+    }
   }
-  (void)d;
-  if (smem_acc) {
+  if (acc) {
     __syncthreads();
-    for (long long i = threadIdx.x; i < ks + k; i += blockDim.x)
-      if (acc[i] != 0) red_add_s64(&D[i], acc[i]);
+    for (long long i = threadIdx.x; i < ks + k; i += blockDim.x) {
+      const long long v = acc[i];
+      if (v == 0) continue;
+      long long dst = i;
+      if (i < ks) {  // i = (u * k + c) * nq + q
+        const long long q = i % nq, uc = i / nq;
+        const long long c = uc % k, u = uc / k;
+        dst = c * ld + 4 * q + u;
+      }
+      red_add_s64(D + dst, v);
+    }
   }
+}
+
+__global__ void bulk_pass_kernel(const float* __restrict__ X, int ld, long long n, int d,
+                                 const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
+                                 const FitState* __restrict__ st) {
+  extern __shared__ __align__(16) long long bulk_acc[];
+  (void)d;
+  if (st->done || !st->bulk) return;
+  bulk_pass(X, ld, n, labels, k, D, st->scale, bulk_in_smem(k, ld) ? bulk_acc : nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -579,11 +618,6 @@ __device__ bool select_farthest(const float* __restrict__ mind, long long n, lon
   return grid_barrier(st, nblocks);
 }
 
-// Mean of a cluster's column from its exact fixed-point sum.
-__device__ __forceinline__ float centre_from_sum(long long s, double inv_scale, long long count) {
-  return (float)((double)s * inv_scale / (double)count);
-}
-
 // Averaged centre value of a non-empty cluster c (after relocation), column j.
 __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, int n_reloc) {
   for (int i = 0; i < n_reloc; ++i)
@@ -591,7 +625,7 @@ __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, 
   long long s = a.S[(long long)c * a.ld + j];
   for (int i = 0; i < n_reloc; ++i)
     if (a.reloc_label[i] == c) s -= to_fixed(a.reloc_x[(long long)i * a.ld + j], a.st->scale);
-  return centre_from_sum(s, a.st->inv_scale, a.cnt_adj[c]);
+  return centre_from_sum(s, centre_factor(a.st->inv_scale, a.cnt_adj[c]));
 }
 
 // One centre (cluster c, columns strided over the calling warp's lanes):
@@ -622,6 +656,7 @@ __device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, int src, 
 // centres scaled by 2^xexp.
 __device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long long changed_now, double tot) {
   st->cexp = st->xexp;
+  st->bulk = st->bulk_always || changed_now > (unsigned long long)st->bulk_threshold;
   st->shift_tot = tot;
   st->iter += 1;
   if (changed_now == 0) {
@@ -632,9 +667,18 @@ __device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long
   }
   if (st->iter >= st->max_iter) st->done = 1;
   *const_cast<unsigned long long*>(a.changed) = 0;
+  if (a.host_done) *a.host_done = st->done;
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();  // the E-step's labels, deltas and counters
   FitState* st = a.st;
   const unsigned int nb = gridDim.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -646,12 +690,39 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   const unsigned long long changed_now = *a.changed;  // cleared at the end
   const double inv_scale = st->inv_scale;
   const int xexp = st->xexp;
+  const int bulk = st->bulk;  // D holds the sums of all rows (replace S), not deltas
   long long cnt0 = 0, dcnt0 = 0;  // cluster threadIdx.x
   if ((int)threadIdx.x < a.k) {
     cnt0 = a.counts[threadIdx.x];
     dcnt0 = dcnt[threadIdx.x];
   }
   if (done) return;
+  extern __shared__ __align__(16) long long dyn_smem[];
+  if (bulk) {
+    if (!a.bulk_external) {
+      bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, bulk_in_smem(a.k, a.ld) ? dyn_smem : nullptr);
+      if (!grid_barrier(st, nb)) return;
+      if ((int)threadIdx.x < a.k) dcnt0 = dcnt[threadIdx.x];
+    }
+    cnt0 = 0;
+  }
+  // Block 0 stages S, D and C_old in shared memory when they fit: the copies
+  // run while the empty clusters are counted and the centres are then
+  // computed without a global round trip per cluster (these arrays are cold:
+  // the E-step streamed X through L2 since they were last touched).
+  const long long kld = (long long)a.k * a.ld;
+  const bool staged = blockIdx.x == 0 && !bulk && kld <= kStageElems;
+  long long* cnt_smem = dyn_smem;               // k entries when k <= kFoldSmemK
+  long long* sS = dyn_smem + ((a.k + 1) & ~1);  // staged: k*ld sums
+  long long* sD = sS + kld;                     //         k*ld deltas
+  float* sC = reinterpret_cast<float*>(sD + kld);  //      k*ld old centres
+  if (staged) {
+    for (long long i = threadIdx.x; i < kld / 2; i += blockDim.x) {
+      cp_async16(sS + 2 * i, a.S + 2 * i);
+      cp_async16(sD + 2 * i, a.D + 2 * i);
+    }
+    for (long long i = threadIdx.x; i < kld / 4; i += blockDim.x) cp_async16(sC + 4 * i, a.C_old + 4 * i);
+  }
   __shared__ int n_empty_s;
   __shared__ int wcount[32];
   __shared__ long long hv_cnt[32];
@@ -663,7 +734,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   __syncthreads();
   for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
     const int c = c0 + threadIdx.x;
-    const bool e = c < a.k && (c0 == 0 ? cnt0 + dcnt0 : a.counts[c] + dcnt[c]) == 0;
+    const bool e = c < a.k && (c0 == 0 ? cnt0 + dcnt0 : (bulk ? 0 : a.counts[c]) + dcnt[c]) == 0;
     const unsigned int b = __ballot_sync(0xffffffffu, e);
     if (lane == 0) wcount[warp] = __popc(b);
     __syncthreads();
@@ -685,7 +756,6 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     // ---------------- fast path: no relocation, one block does the update
     if (blockIdx.x != 0) return;
     __shared__ double red_scratch[32];
-    extern __shared__ long long cnt_smem[];  // k entries when k <= kFoldSmemK
     long long* cnt_k = a.k <= kFoldSmemK ? cnt_smem : a.cnt_adj;
     int iter = 0, max_iter = 0;
     double tol = 0.0;
@@ -697,22 +767,22 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     long long* cnt = const_cast<long long*>(a.counts);
     for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
       const long long dv = c < (int)blockDim.x ? dcnt0 : dcnt[c];
-      const long long v = (c < (int)blockDim.x ? cnt0 : cnt[c]) + dv;
+      const long long v = (c < (int)blockDim.x ? cnt0 : (bulk ? 0 : cnt[c])) + dv;
       cnt_k[c] = v;
       a.cnt_adj[c] = v;
-      if (dv != 0) {
-        cnt[c] = v;
-        a.D[ks + c] = 0;
-      }
+      if (bulk || dv != 0) cnt[c] = v;
+      if (dv != 0) a.D[ks + c] = 0;
     }
+    if (staged) cp_async_wait_all();
     __syncthreads();
-    // 2. S += dS and the centres, one warp per cluster, lanes over columns
-    //    in batches of 128 whose loads are all issued before any store
+    // 2. S += dS (bulk: S = D) and the centres, one warp per cluster, lanes
+    //    over columns in batches of 128 whose loads are all issued before any
+    //    store
     long long* S = const_cast<long long*>(a.S);
     const float cs = ldexpf(1.0f, xexp);  // centres are bounded by max |x|
     double wdsq = 0.0;  // this warp's squared shifts, in cluster order
     for (int c = warp; c < a.k; c += nwarps) {
-      const long long count = cnt_k[c];
+      const double fct = centre_factor(inv_scale, cnt_k[c]);
       double dsq = 0.0, nrm = 0.0;
       for (int j0 = 0; j0 < a.ld; j0 += 128) {
         long long dv[4], sv[4];
@@ -725,9 +795,9 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
           old[u] = 0.0f;
           if (j < a.ld) {
             const long long i = (long long)c * a.ld + j;
-            dv[u] = a.D[i];
-            sv[u] = S[i];
-            old[u] = a.C_old[i];
+            dv[u] = staged ? sD[i] : a.D[i];
+            sv[u] = bulk ? 0 : (staged ? sS[i] : S[i]);
+            old[u] = staged ? sC[i] : a.C_old[i];
           }
         }
 #pragma unroll
@@ -736,13 +806,11 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
           if (j < a.ld) {
             const long long i = (long long)c * a.ld + j;
             const long long sum = sv[u] + dv[u];
-            if (dv[u] != 0) {
-              S[i] = sum;
-              a.D[i] = 0;
-            }
+            if (bulk || dv[u] != 0) S[i] = sum;
+            if (dv[u] != 0) a.D[i] = 0;
             float v = 0.0f;
             if (j < a.d) {
-              v = centre_from_sum(sum, inv_scale, count);
+              v = centre_from_sum(sum, fct);
               const double df = (double)v - (double)old[u];
               dsq += df * df;
               nrm += (double)v * v;
@@ -752,8 +820,11 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
           }
         }
       }
-      dsq = warp_sum(dsq);
-      nrm = warp_sum(nrm);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {  // both butterflies interleaved
+        dsq += __shfl_xor_sync(0xffffffffu, dsq, o);
+        nrm += __shfl_xor_sync(0xffffffffu, nrm, o);
+      }
       if (lane == 0) {
         if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
         if (a.bias) a.bias[c] = (float)nrm;
@@ -771,6 +842,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
       st->cexp = xexp;
       st->shift_tot = tot;
       st->iter = iter + 1;
+      st->bulk = st->bulk_always || changed_now > (unsigned long long)st->bulk_threshold;
       if (changed_now == 0) {
         st->strict = 1;
         st->done = 1;
@@ -778,19 +850,26 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
         st->done = 1;
       }
       *const_cast<unsigned long long*>(a.changed) = 0;
+      if (a.host_done) *a.host_done = st->done;
     }
     return;
   }
 
   // ---------------- relocation path (cooperative, all blocks)
-  // 0. S += dS, counts += dcount; clear the deltas (all but `changed`)
+  if (staged) cp_async_wait_all();  // the staged copies are not used here
+  // 0. S += dS, counts += dcount (bulk: S = dS, counts = dcount); clear the
+  //    deltas (all but `changed`)
   {
     long long* S = const_cast<long long*>(a.S);
     long long* cnt = const_cast<long long*>(a.counts);
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + a.k;
          i += (long long)nb * blockDim.x) {
       const long long v = a.D[i];
-      if (v != 0) {
+      if (bulk) {
+        if (i < ks) S[i] = v;
+        else cnt[i - ks] = v;
+        if (v != 0) a.D[i] = 0;
+      } else if (v != 0) {
         if (i < ks) S[i] += v;
         else cnt[i - ks] += v;
         a.D[i] = 0;

@@ -4,10 +4,27 @@
 #include "device_util.cuh"
 #include "skm.cuh"
 
+#include <algorithm>
+
 namespace skm {
 
 constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
 constexpr int kFoldSmemK = 4096;          // M-step keeps up to this many folded counts in shared memory
+constexpr int kStageElems = 8192;         // M-step stages S, D, C_old (k*ld <= this) in shared memory
+constexpr size_t kBulkSmemBytes = 160 * 1024;  // bulk pass accumulates privately when (k*ld + k) int64 fit
+
+__host__ __device__ inline bool bulk_in_smem(int k, int ld) {
+  return sizeof(long long) * ((size_t)k * ld + k) <= kBulkSmemBytes;
+}
+
+// Dynamic shared memory of mstep_kernel for k clusters of ld columns.
+inline size_t mstep_smem_bytes(int k, int ld) {
+  const size_t kk = (size_t)((k + 1) & ~1);
+  size_t b = k <= kFoldSmemK ? sizeof(long long) * kk : 0;
+  if ((long long)k * ld <= kStageElems) b = sizeof(long long) * kk + (size_t)k * ld * (8 + 8 + 4);
+  if (bulk_in_smem(k, ld)) b = std::max(b, sizeof(long long) * ((size_t)k * ld + k));
+  return b;
+}
 
 struct MStepArgs {
   FitState* st;
@@ -39,6 +56,12 @@ struct MStepArgs {
   // (img nullable) and ||C_new||^2 (nullable)
   CentreImage cimg;
   float* bias;
+  // mapped pinned host word (nullable): receives st->done after each update,
+  // so that the host can poll the loop without a copy in the stream
+  volatile int* host_done;
+  // bulk iterations: the sums were already added into D before the M-step
+  // (multi-GPU: before the all-reduce), so the M-step only replaces S by D
+  int bulk_external;
   // exchanged relocation candidates (multi-GPU); null on one GPU
   int n_cand;
   const float* cand_dist;
@@ -52,7 +75,7 @@ __global__ void colsum_fixed_kernel(const float* X, int ld, long long n, int d, 
 __global__ void mean_from_colsum_kernel(const long long* colsum, int d, const double* scale, double n_total, float* mean);
 __global__ void scale_kernel(const unsigned int* maxabs_bits, double n_total, double* out);
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
-                                  double n_total, int d, const unsigned int* maxabs_bits);
+                                  double n_total, int d, const unsigned int* maxabs_bits, int bulk_always);
 __global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits,
                               double* partial);
 __global__ void sumsq_partial_kernel(const float* X, int ld, long long n, int d, double* partial);
@@ -67,8 +90,11 @@ __global__ void counts_to_float_kernel(const long long* c, int k, float* out);
 // returns false when d has no specialisation.
 bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
                          long long n, const float* C, int k, int32_t* labels, float* mind);
-__global__ void bulk_sums_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
-                                 long long* D, const FitState* st, int smem_acc);
+// The bulk pass of a bulk iteration as its own launch (multi-GPU: before the
+// all-reduce); a no-op unless st->bulk. Dynamic shared memory: (k*ld + k)
+// int64 when bulk_in_smem(k, ld), else 0.
+__global__ void bulk_pass_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
+                                 long long* D, const FitState* st);
 
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, CentreImage ci, FitState* st);

@@ -121,22 +121,34 @@ static int launch_assign_simt(const float* X, int ld, long long n, int d, const 
   return check_launch("assign_simt_kernel");
 }
 
-static int launch_bulk_sums(const float* X, int ld, long long n, int d, const int32_t* labels, int k, long long* D,
+// The bulk pass as its own launch (multi-GPU fits, before the all-reduce).
+static int launch_bulk_pass(const float* X, int ld, long long n, int d, const int32_t* labels, int k, long long* D,
                             const FitState* st, cudaStream_t s) {
-  static int optin = 0;
-  if (!optin) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncSetAttribute(bulk_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
-  }
-  const size_t need = sizeof(long long) * ((size_t)k * ld + k);
-  if (need + 2048 <= (size_t)optin) {
-    bulk_sums_kernel<<<sm_count(), 1024, need, s>>>(X, ld, n, d, labels, k, D, st, 1);
-  } else {
-    bulk_sums_kernel<<<sm_count() * 4, 256, 0, s>>>(X, ld, n, d, labels, k, D, st, 0);
-  }
-  return check_launch("bulk_sums_kernel");
+  const size_t smem = bulk_in_smem(k, ld) ? sizeof(long long) * ((size_t)k * ld + k) : 0;
+  if (smem > 48 * 1024)
+    SKM_CUDA(cudaFuncSetAttribute(bulk_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  bulk_pass_kernel<<<sm_count(), 1024, smem, s>>>(X, ld, n, d, labels, k, D, st);
+  return check_launch("bulk_pass_kernel");
+}
+
+// The cooperative M-step; with `pdl` it is launched with programmatic stream
+// serialization so that its launch overlaps the E-step's tail (the kernel
+// waits for the E-step's writes itself).
+static int launch_mstep(MStepArgs& ma, int blocks, int threads, size_t smem, bool pdl, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  SKM_CUDA(cudaLaunchKernelEx(&cfg, mstep_kernel, ma));
+  return check_launch("mstep_kernel");
 }
 
 // ---------------------------------------------------------------------------
@@ -289,7 +301,7 @@ static int run_fit(const FitParams& p) {
     if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, sumsq, 1, s));
   }
   init_state_kernel<<<1, 32, 0, s>>>(st, p.max_iter, p.tol, tol_rel ? 1 : 0, tol_rel ? sumsq : nullptr,
-                                     (double)n_total, d, &u32s[1]);
+                                     (double)n_total, d, &u32s[1], p.bulk_sums ? 1 : 0);
   SKM_TRY(check_launch("init_state_kernel"));
   SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n, s));  // label -1: every row changes in iteration 1
   SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
@@ -352,7 +364,9 @@ static int run_fit(const FitParams& p) {
   ma.bias = bias;
   const int mstep_blocks = nsm;
   const int mstep_threads = 1024;
-  const size_t mstep_smem = k <= kFoldSmemK ? sizeof(long long) * (size_t)k : 0;
+  const size_t mstep_smem = mstep_smem_bytes(k, ld);
+  if (mstep_smem > 48 * 1024)
+    SKM_CUDA(cudaFuncSetAttribute(mstep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mstep_smem));
 
   std::vector<cudaEvent_t> prof_ev;
   if (p.profile) {
@@ -366,7 +380,13 @@ static int run_fit(const FitParams& p) {
     }
   } pg{&prof_ev};
 
-  int32_t* flags = reinterpret_cast<int32_t*>(pinned);  // done snapshot per chunk (slots 0..63)
+  // done flag written by the M-steps straight into mapped pinned memory
+  volatile int* host_done = reinterpret_cast<volatile int*>(pinned);
+  *host_done = 0;
+  int* host_done_dev = nullptr;
+  SKM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_done_dev), pinned, 0));
+  ma.host_done = host_done_dev;
+  ma.bulk_external = comm ? 1 : 0;
   const int chunk = 8;
   int it = 0, chunk_idx = 0, pending = -1;
   bool done_seen = false;
@@ -396,31 +416,29 @@ static int run_fit(const FitParams& p) {
       float* Cout = (it & 1) ? Cb0 : Cb1;
       const bool timed = p.profile && it % kProfileEvery == 0;
       if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
-      // iteration 0 has no previous labels: sums are built in bulk afterwards;
-      // later iterations add the deltas of the rows that changed label
-      const bool bulk = it == 0 || p.bulk_sums;
-      long long* Dinc = bulk ? nullptr : D;
-      if (bulk && it > 0) SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
+      // Iterations flagged `bulk` on the device (the first one, and those
+      // after an iteration that changed many rows) rebuild the sums from all
+      // rows; the others add the deltas of the rows that changed label.
       if (plan.tc) {
-        SKM_TRY(tc_estep(plan.tcp, cimg.img, &st->xexp, bias, labels, changed, Dinc, st, dev_err, s));
+        SKM_TRY(tc_estep(plan.tcp, cimg.img, &st->xexp, bias, labels, changed, D, st, dev_err, s, !comm && !timed));
       } else {
-        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, Dinc, 0, 1, s));
+        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, D, 0, 1, s));
       }
       if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
-      if (bulk) SKM_TRY(launch_bulk_sums(X, ld, n, d, labels, k, D, st, s));
-      if (comm) SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
+      if (comm) {
+        // bulk sums must be local before the all-reduce (a no-op unless bulk)
+        SKM_TRY(launch_bulk_pass(X, ld, n, d, labels, k, D, st, s));
+        SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
+      }
       ma.C_old = Cin;
       ma.C_new = Cout;
-      void* args[] = {&ma};
-      SKM_CUDA(cudaLaunchCooperativeKernel((void*)mstep_kernel, dim3(mstep_blocks), dim3(mstep_threads), args, mstep_smem, s));
-      SKM_TRY(check_launch("mstep_kernel"));
+      SKM_TRY(launch_mstep(ma, mstep_blocks, mstep_threads, mstep_smem, !comm && !timed, s));
     }
-    const int slot = chunk_idx & 63;
-    SKM_CUDA(cudaMemcpyAsync(&flags[slot], &st->done, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     SKM_CUDA(cudaEventRecord(chunk_ev[chunk_idx & 1], s));
     if (pending >= 0) {
       SKM_TRY(wait_event(chunk_ev[pending & 1]));
-      if (flags[pending & 63]) done_seen = true;
+      // written by the M-steps (monotone: a later iteration's value is as good)
+      if (*host_done) done_seen = true;
     }
     pending = chunk_idx++;
   }

@@ -56,7 +56,10 @@ struct FitState {
   unsigned int maxabs_bits;    // max |x| (float bits) of centred X
   int32_t xexp;        // tensor-core operand scale of X: x * 2^xexp (split_exp)
   int32_t cexp;        // same for the centres of the current centre image
+  int32_t bulk;        // this iteration rebuilds the sums from all rows (no per-row deltas)
+  int32_t bulk_always; // every iteration does (diagnostic flag)
   int32_t pad0;
+  long long bulk_threshold;  // changed rows above which the next iteration is a bulk one
 };
 
 constexpr int kMaxEmptyCap = 4096;  // upper bound on relocations per iteration

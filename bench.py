@@ -229,13 +229,13 @@ def main():
 
     _bridge.set_device(local)
     _bridge.ensure_warmed_up()
+    from skmetal_b200.distributed import init_library_comm, max_over_ranks, shard_range
+
     if world > 1:
-        uid = [_bridge.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        _bridge.comm_init(uid[0], world, rank)
+        init_library_comm(_bridge, dist, rank, world)
 
     n = X.shape[0]
-    lo, hi = (n * rank) // world, (n * (rank + 1)) // world
+    lo, hi = shard_range(n, rank, world)
     Xs = np.ascontiguousarray(X[lo:hi])
     shard = (lo, n) if world > 1 else None
     ds = _bridge.Dataset(Xs)
@@ -269,9 +269,7 @@ def main():
     clk = clocks.stop()
     t_dev = ms_total / 1e3
     if dist is not None:
-        tt = torch.tensor([t_dev, wall], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_dev, wall = float(tt[0]), float(tt[1])
+        t_dev, wall = max_over_ranks(dist, [t_dev, wall], device="cuda")
     rows_iters = n * iters  # every rank ran the same iterations over its shard of n rows
     value = rows_iters / t_dev
 
@@ -291,9 +289,7 @@ def main():
         e2e_iters += n_iter
     e2e_t = time.perf_counter() - t0
     if dist is not None:
-        tt = torch.tensor([e2e_t], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_t = float(tt[0])
+        (e2e_t,) = max_over_ranks(dist, [e2e_t], device="cuda")
     e2e_value = n * e2e_iters / e2e_t
 
     hbm, bf16, src = _peaks()

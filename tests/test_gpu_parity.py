@@ -107,6 +107,40 @@ def test_transform_matches_fp64():
 
 
 # ---------------------------------------------------------------------------
+# golden fixtures produced by the reference's own API (tests/golden)
+# ---------------------------------------------------------------------------
+
+def _golden_case(name):
+    import importlib.util
+    import json
+    from pathlib import Path
+
+    g = Path(__file__).resolve().parent / "golden"
+    spec = importlib.util.spec_from_file_location("make_golden", g / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    z = np.load(g / "golden_kmeans.npz")
+    c = json.loads(str(z["meta"]))["cases"][name]
+    X, init = mg.case_inputs(c["gen"])
+    assert mg.digest(X, init) == c["sha256"]
+    return X, init, c, z
+
+
+@pytest.mark.parametrize("name", ["c1_small", "c2_small", "c3_small", "c4_small", "tol_rel", "relocation",
+                                  "odd_shape"])
+def test_fit_matches_reference_golden(name):
+    """Full fits against the reference's outputs on the same inputs."""
+    X, init, c, z = _golden_case(name)
+    centers, labels, inertia, n_iter = _bridge.kmeans_fit(X, init, c["max_iter"], c["tol"])
+    mean, Xc, _ = ora.center_data(X)
+    check_labels(Xc, centers - mean, labels, z[f"{name}/full/labels"], f"{name} labels")
+    scale = float(np.abs(X).max())
+    np.testing.assert_allclose(centers, z[f"{name}/full/centers"], rtol=CENTER_RTOL, atol=1e-5 * scale)
+    assert inertia == pytest.approx(float(z[f"{name}/full/inertia"]), rel=INERTIA_RTOL)
+    assert n_iter == int(z[f"{name}/full/n_iter"])
+
+
+# ---------------------------------------------------------------------------
 # lockstep Lloyd steps
 # ---------------------------------------------------------------------------
 

@@ -126,16 +126,22 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 5 ms"}
 
 
-def _traffic_for(config: str, launches_rows: int):
-    p = ROOT / "profiles" / "traffic.json"
+def _traffic_for(config: str, rows: int):
+    """DRAM bytes (read + write) per E-step launch from the committed ncu
+    summary of the full-size capture (profiles/estep_tc_<config>.md), scaled
+    by rows when the bench runs a different row count; None without one."""
+    import re
+
+    p = ROOT / "profiles" / f"estep_tc_{config}.md"
     if not p.exists():
         return None
-    d = json.loads(p.read_text())
-    e = d.get(config)
-    if not e:
+    text = p.read_text()
+    m = re.search(r"traffic_bytes_per_launch = (\d+)", text)
+    n = re.search(r"\((\d[\d,]*) x \d+, k = \d+\)", text)
+    if not m or not n:
         return None
-    # bytes per row measured by ncu on a smaller case, scaled to this launch
-    return float(e["dram_bytes_per_row"]) * launches_rows
+    ref_rows = int(n.group(1).replace(",", ""))
+    return float(m.group(1)) * rows / ref_rows
 
 
 def cpu_baseline(X, init, k, sample_iters: int):

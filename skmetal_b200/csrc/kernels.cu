@@ -667,7 +667,49 @@ __device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long
   }
   if (st->iter >= st->max_iter) st->done = 1;
   *const_cast<unsigned long long*>(a.changed) = 0;
-  if (a.host_done) *a.host_done = st->done;
+  if (a.host_done) *a.host_done = st->done ? st->iter : 0;
+}
+
+// Direct float32 squared distance of every local row to its (new) label's old
+// centre, ((X - centers_old[labels])**2).sum(axis=1) (_k_means_common.pyx:185),
+// into a.mind. Blocked X: lane per row of a 32-row group, columns in order.
+__device__ void rows_dist_to_old_centres(const MStepArgs& a, unsigned int nb) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  float* mind = const_cast<float*>(a.mind);
+  const long long items = (a.n + 31) / 32;
+  const float4* X4 = reinterpret_cast<const float4*>(a.X);
+  for (long long it = blockIdx.x * (long long)nwarps + warp; it < items; it += (long long)nb * nwarps) {
+    const long long r = it * 32 + lane;
+    if (r >= a.n) continue;
+    const float4* xp = X4 + (r >> 7) * (32LL * a.ld) + (r & 127);
+    const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
+    float s = 0.0f;
+    for (int q = 0; q < (a.ld >> 2); ++q) {
+      const float4 v = xp[(long long)q * 128];
+      float t = v.x - cr[4 * q];
+      s = fmaf(t, t, s);
+      t = v.y - cr[4 * q + 1];
+      s = fmaf(t, t, s);
+      t = v.z - cr[4 * q + 2];
+      s = fmaf(t, t, s);
+      t = v.w - cr[4 * q + 3];
+      s = fmaf(t, t, s);
+    }
+    mind[r] = s;
+  }
+}
+
+// Number of empty clusters after this iteration's sums (bulk iterations: the
+// sums in D alone); every block of the caller computes the same value.
+__device__ int count_empty(const MStepArgs& a, int bulk) {
+  const long long* dcnt = a.D + (long long)a.k * a.ld;
+  int total = 0;
+  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
+    const int c = c0 + threadIdx.x;
+    const bool e = c < a.k && (bulk ? 0 : a.counts[c]) + dcnt[c] == 0;
+    total += __syncthreads_count(e);
+  }
+  return total;
 }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
@@ -850,7 +892,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
         st->done = 1;
       }
       *const_cast<unsigned long long*>(a.changed) = 0;
-      if (a.host_done) *a.host_done = st->done;
+      if (a.host_done) *a.host_done = st->done ? st->iter : 0;
     }
     return;
   }
@@ -886,66 +928,60 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
 
   // 2. the n_empty rows farthest from their centre, paired in decreasing
   //    (distance, -row) order with the ascending empty ids
-  int m_cand = n_empty;
-  if (a.cand_row == nullptr) {
-    // distances of every row to its (new) label's old centre, float32 direct
-    // differences: ((X - centers_old[labels])**2).sum(axis=1) (_k_means_common.pyx:185)
-    // (X blocked: lane per row of a 32-row group, columns in order)
-    float* mind = const_cast<float*>(a.mind);
-    const long long items = (a.n + 31) / 32;
-    const float4* X4 = reinterpret_cast<const float4*>(a.X);
-    for (long long it = blockIdx.x * (long long)nwarps + warp; it < items; it += (long long)nb * nwarps) {
-      const long long r = it * 32 + lane;
-      if (r >= a.n) continue;
-      const float4* xp = X4 + (r >> 7) * (32LL * a.ld) + (r & 127);
-      const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
-      float s = 0.0f;
-      for (int q = 0; q < (a.ld >> 2); ++q) {
-        const float4 v = xp[(long long)q * 128];
-        float t = v.x - cr[4 * q];
-        s = fmaf(t, t, s);
-        t = v.y - cr[4 * q + 1];
-        s = fmaf(t, t, s);
-        t = v.z - cr[4 * q + 2];
-        s = fmaf(t, t, s);
-        t = v.w - cr[4 * q + 3];
-        s = fmaf(t, t, s);
-      }
-      mind[r] = s;
-    }
+  if (a.cand == nullptr) {
+    rows_dist_to_old_centres(a, nb);
     if (!grid_barrier(st, nb)) return;
     if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i < n_empty; i += blockDim.x) {
+        const float di = a.mind[a.sel[i]];
+        const unsigned long long ki = reloc_key(di, a.row_base + a.sel[i]);
+        int rank = 0;
+        for (int j = 0; j < n_empty; ++j)
+          if (reloc_key(a.mind[a.sel[j]], a.row_base + a.sel[j]) > ki) ++rank;
+        const long long r = a.sel[i];
+        a.reloc_dist[rank] = di;
+        a.reloc_label[rank] = a.labels[r];
+        for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
+      }
+    }
   } else {
-    m_cand = a.n_cand;
-    if (a.n_cand < n_empty) {  // exchanged candidates cannot cover this many empties
+    // candidates of every rank (the same bytes on every rank): rank r's block
+    // at cand + r * cand_block_bytes; its first `count` entries are valid
+    const size_t cb = cand_block_bytes(a.cand_cap, a.ld);
+    const int total = a.cand_ranks * a.cand_cap;
+    int valid_total = 0, overflow = 0;
+    for (int r = 0; r < a.cand_ranks; ++r) {
+      const int cnt = *reinterpret_cast<const int*>(a.cand + r * cb);
+      if (cnt < 0) overflow = 1;
+      else valid_total += cnt;
+    }
+    if (overflow || valid_total < n_empty) {  // uniform over blocks and ranks
       if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&st->error, 1003);
       return;
     }
-  }
-  if (blockIdx.x == 0) {
-    for (int i = threadIdx.x; i < m_cand; i += blockDim.x) {
-      float di;
-      long long gi;
-      if (a.cand_row) { di = a.cand_dist[i]; gi = a.cand_row[i]; }
-      else { di = a.mind[a.sel[i]]; gi = a.row_base + a.sel[i]; }
-      const unsigned long long ki = reloc_key(di, gi);
-      int rank = 0;
-      for (int j = 0; j < m_cand; ++j) {
-        float dj;
-        long long gj;
-        if (a.cand_row) { dj = a.cand_dist[j]; gj = a.cand_row[j]; }
-        else { dj = a.mind[a.sel[j]]; gj = a.row_base + a.sel[j]; }
-        if (reloc_key(dj, gj) > ki) ++rank;
-      }
-      if (rank < n_empty) {
-        a.reloc_dist[rank] = di;
-        if (a.cand_row) {
-          a.reloc_label[rank] = a.cand_label[i];
-          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.cand_x[(long long)i * a.ld + j];
-        } else {
-          const long long r = a.sel[i];
-          a.reloc_label[rank] = a.labels[r];
-          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
+    if (blockIdx.x == 0) {
+      for (int t = threadIdx.x; t < total; t += blockDim.x) {
+        const int r = t / a.cand_cap, i = t % a.cand_cap;
+        const unsigned char* blk = a.cand + r * cb;
+        if (i >= *reinterpret_cast<const int*>(blk)) continue;
+        const float di = reinterpret_cast<const float*>(blk + cand_dist_off(a.cand_cap))[i];
+        const long long gi = reinterpret_cast<const long long*>(blk + cand_row_off(a.cand_cap))[i];
+        const unsigned long long ki = reloc_key(di, gi);
+        int rank = 0;
+        for (int u = 0; u < total; ++u) {
+          const int r2 = u / a.cand_cap, i2 = u % a.cand_cap;
+          const unsigned char* b2 = a.cand + r2 * cb;
+          if (i2 >= *reinterpret_cast<const int*>(b2)) continue;
+          const float dj = reinterpret_cast<const float*>(b2 + cand_dist_off(a.cand_cap))[i2];
+          const long long gj = reinterpret_cast<const long long*>(b2 + cand_row_off(a.cand_cap))[i2];
+          if (reloc_key(dj, gj) > ki) ++rank;
+        }
+        if (rank < n_empty) {
+          a.reloc_dist[rank] = di;
+          a.reloc_label[rank] = reinterpret_cast<const int*>(blk + cand_label_off(a.cand_cap))[i];
+          const float* xs = reinterpret_cast<const float*>(blk + cand_x_off(a.cand_cap)) + (long long)i * a.ld;
+          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = xs[j];
         }
       }
     }
@@ -1009,6 +1045,48 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     __shared__ double red_scratch[32];
     const double tot = block_ordered_sum(dsq_s, a.k, red_scratch);
     if (threadIdx.x == 0) finish_iteration(a, st, changed_now, tot);
+  }
+}
+
+// Multi-GPU relocation, first half: this rank's n_empty rows farthest from
+// their centre (or all its rows if it has fewer), written to `send` for the
+// all-gather; count 0 when no cluster is empty, -1 when more than cand_cap
+// are. The M-step then ranks the gathered candidates of all ranks with the
+// single-GPU rule, so every rank relocates the same rows.
+__global__ void __launch_bounds__(1024, 1) reloc_candidates_kernel(MStepArgs a, unsigned char* send) {
+  FitState* st = a.st;
+  const unsigned int nb = gridDim.x;
+  const int done = st->done;
+  const int bulk = st->bulk;
+  int* count_out = reinterpret_cast<int*>(send);
+  if (done) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *count_out = 0;
+    return;
+  }
+  const int n_empty = count_empty(a, bulk);
+  if (n_empty == 0 || n_empty > a.cand_cap) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *count_out = n_empty == 0 ? 0 : -1;
+    return;
+  }
+  const int m = (int)min((long long)n_empty, a.n);
+  if (blockIdx.x == 0 && threadIdx.x == 0) st->sel_count = 0;
+  rows_dist_to_old_centres(a, nb);
+  if (!grid_barrier(st, nb)) return;
+  if (m > 0 && !select_farthest(a.mind, a.n, a.row_base, m, st, a.hist, a.sel, nb)) return;
+  if (blockIdx.x == 0) {
+    const int cap = a.cand_cap;
+    float* dist = reinterpret_cast<float*>(send + cand_dist_off(cap));
+    long long* row = reinterpret_cast<long long*>(send + cand_row_off(cap));
+    int* label = reinterpret_cast<int*>(send + cand_label_off(cap));
+    float* x = reinterpret_cast<float*>(send + cand_x_off(cap));
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      const long long r = a.sel[i];
+      dist[i] = a.mind[r];
+      row[i] = a.row_base + r;
+      label[i] = a.labels[r];
+      for (int j = 0; j < a.ld; ++j) x[(long long)i * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
+    }
+    if (threadIdx.x == 0) *count_out = m;
   }
 }
 

@@ -17,6 +17,19 @@ __host__ __device__ inline bool bulk_in_smem(int k, int ld) {
   return sizeof(long long) * ((size_t)k * ld + k) <= kBulkSmemBytes;
 }
 
+// Relocation candidates of one rank (multi-GPU fits), exchanged by an
+// all-gather: [count int32, 3 x int32 padding | dist float[cap] | global row
+// int64[cap] | label int32[cap] | x float[cap][ld]]. count = -1 when the
+// iteration has more empty clusters than `cap`.
+constexpr int kCandCap = 32;
+__host__ __device__ inline size_t cand_block_bytes(int cap, int ld) {
+  return (16 + (size_t)cap * 16 + (size_t)cap * ld * 4 + 15) & ~(size_t)15;
+}
+__host__ __device__ inline size_t cand_dist_off(int) { return 16; }
+__host__ __device__ inline size_t cand_row_off(int cap) { return 16 + (size_t)cap * 4; }
+__host__ __device__ inline size_t cand_label_off(int cap) { return 16 + (size_t)cap * 12; }
+__host__ __device__ inline size_t cand_x_off(int cap) { return 16 + (size_t)cap * 16; }
+
 // Dynamic shared memory of mstep_kernel for k clusters of ld columns.
 inline size_t mstep_smem_bytes(int k, int ld) {
   const size_t kk = (size_t)((k + 1) & ~1);
@@ -56,18 +69,18 @@ struct MStepArgs {
   // (img nullable) and ||C_new||^2 (nullable)
   CentreImage cimg;
   float* bias;
-  // mapped pinned host word (nullable): receives st->done after each update,
-  // so that the host can poll the loop without a copy in the stream
+  // mapped pinned host word (nullable): receives the iteration count once
+  // the loop has converged (0 while it runs), so that the host can poll the
+  // loop without a copy in the stream
   volatile int* host_done;
   // bulk iterations: the sums were already added into D before the M-step
   // (multi-GPU: before the all-reduce), so the M-step only replaces S by D
   int bulk_external;
-  // exchanged relocation candidates (multi-GPU); null on one GPU
-  int n_cand;
-  const float* cand_dist;
-  const long long* cand_row;
-  const int* cand_label;
-  const float* cand_x;
+  // relocation candidates gathered from every rank (multi-GPU); null on one
+  // GPU: cand_ranks blocks of cand_block_bytes(cand_cap, ld) bytes each
+  const unsigned char* cand;
+  int cand_ranks;
+  int cand_cap;
 };
 
 __global__ void maxabs_kernel(const float* X, int ld, long long n, int d, unsigned int* out_bits);
@@ -97,6 +110,9 @@ __global__ void bulk_pass_kernel(const float* X, int ld, long long n, int d, con
                                  long long* D, const FitState* st);
 
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a);
+// Multi-GPU: this rank's relocation candidates for the current iteration
+// (cooperative; writes one candidate block to `send`).
+__global__ void __launch_bounds__(1024, 1) reloc_candidates_kernel(MStepArgs a, unsigned char* send);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, CentreImage ci, FitState* st);
 __global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
                                        const int32_t* labels, double* partial, int blocked);

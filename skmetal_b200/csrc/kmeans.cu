@@ -387,6 +387,18 @@ static int run_fit(const FitParams& p) {
   SKM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_done_dev), pinned, 0));
   ma.host_done = host_done_dev;
   ma.bulk_external = comm ? 1 : 0;
+  // multi-GPU relocation: this rank's candidate block and everyone's
+  unsigned char* cand_send = nullptr;
+  unsigned char* cand_all = nullptr;
+  size_t cand_bytes = 0;
+  if (comm) {
+    cand_bytes = cand_block_bytes(kCandCap, ld);
+    SKM_TRY(buf.alloc_n(&cand_send, cand_bytes));
+    SKM_TRY(buf.alloc_n(&cand_all, cand_bytes * (size_t)comm_nranks(comm)));
+    ma.cand = cand_all;
+    ma.cand_ranks = comm_nranks(comm);
+    ma.cand_cap = kCandCap;
+  }
   const int chunk = 8;
   int it = 0, chunk_idx = 0, pending = -1;
   bool done_seen = false;
@@ -425,20 +437,31 @@ static int run_fit(const FitParams& p) {
         SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, D, 0, 1, s));
       }
       if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
+      ma.C_old = Cin;
+      ma.C_new = Cout;
       if (comm) {
         // bulk sums must be local before the all-reduce (a no-op unless bulk)
         SKM_TRY(launch_bulk_pass(X, ld, n, d, labels, k, D, st, s));
         SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
+        // relocation candidates of every rank (count 0 unless a cluster is empty)
+        void* cargs[] = {&ma, &cand_send};
+        SKM_CUDA(cudaLaunchCooperativeKernel((void*)reloc_candidates_kernel, dim3(mstep_blocks), dim3(mstep_threads),
+                                             cargs, 0, s));
+        SKM_TRY(check_launch("reloc_candidates_kernel"));
+        SKM_TRY(comm_allgather_bytes(comm, cand_send, cand_all, cand_bytes, s));
       }
-      ma.C_old = Cin;
-      ma.C_new = Cout;
       SKM_TRY(launch_mstep(ma, mstep_blocks, mstep_threads, mstep_smem, !comm && !timed, s));
     }
     SKM_CUDA(cudaEventRecord(chunk_ev[chunk_idx & 1], s));
     if (pending >= 0) {
       SKM_TRY(wait_event(chunk_ev[pending & 1]));
-      // written by the M-steps (monotone: a later iteration's value is as good)
-      if (*host_done) done_seen = true;
+      // The M-steps publish the iteration count at convergence (0 while
+      // running). One GPU may stop as soon as it is seen; ranks of a sharded
+      // fit stop only once it falls in a chunk they have all waited for, so
+      // that every rank enqueues the same collectives.
+      const int at = *host_done;
+      const int pending_end = std::min(p.max_iter, (pending + 1) * chunk);
+      if (at > 0 && (!comm || at <= pending_end)) done_seen = true;
     }
     pending = chunk_idx++;
   }

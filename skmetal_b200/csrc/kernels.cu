@@ -324,6 +324,7 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
   st->changed = 0;
   st->sel_count = 0;
   st->barrier_count = 0;
+  st->ticket = 0;
   st->barrier_gen = 0;
   st->shift_tot = 0.0;
   st->inertia = 0.0;
@@ -333,8 +334,7 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
   st->maxabs_bits = *maxabs_bits;
   st->bulk = 1;  // the first iteration starts from labels -1: every row changes
   st->bulk_always = bulk_always;
-  // above ~n/10 changed rows the per-row deltas cost more than a bulk pass
-  st->bulk_threshold = (long long)fmax(1.0, n_total / 10.0);
+  st->bulk_threshold = (long long)fmax(1.0, n_total / (double)kBulkDivisor);
   st->xexp = split_exp(*maxabs_bits);
   st->cexp = st->xexp;
   st->scale = fixed_scale(*maxabs_bits, n_total);
@@ -712,12 +712,6 @@ __device__ int count_empty(const MStepArgs& a, int bulk) {
   return total;
 }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // the E-step's labels, deltas and counters
@@ -726,12 +720,8 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const long long ks = (long long)a.k * a.ld;
   const long long* dcnt = a.D + ks;
-  // Every global value the no-relocation path needs is loaded here at once,
-  // so that its chain of dependent memory round trips stays short.
   const int done = st->done;  // uniform: `done` is only written at the very end
   const unsigned long long changed_now = *a.changed;  // cleared at the end
-  const double inv_scale = st->inv_scale;
-  const int xexp = st->xexp;
   const int bulk = st->bulk;  // D holds the sums of all rows (replace S), not deltas
   long long cnt0 = 0, dcnt0 = 0;  // cluster threadIdx.x
   if ((int)threadIdx.x < a.k) {
@@ -748,27 +738,11 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     }
     cnt0 = 0;
   }
-  // Block 0 stages S, D and C_old in shared memory when they fit: the copies
-  // run while the empty clusters are counted and the centres are then
-  // computed without a global round trip per cluster (these arrays are cold:
-  // the E-step streamed X through L2 since they were last touched).
-  const long long kld = (long long)a.k * a.ld;
-  const bool staged = blockIdx.x == 0 && !bulk && kld <= kStageElems;
-  long long* cnt_smem = dyn_smem;               // k entries when k <= kFoldSmemK
-  long long* sS = dyn_smem + ((a.k + 1) & ~1);  // staged: k*ld sums
-  long long* sD = sS + kld;                     //         k*ld deltas
-  float* sC = reinterpret_cast<float*>(sD + kld);  //      k*ld old centres
-  if (staged) {
-    for (long long i = threadIdx.x; i < kld / 2; i += blockDim.x) {
-      cp_async16(sS + 2 * i, a.S + 2 * i);
-      cp_async16(sD + 2 * i, a.D + 2 * i);
-    }
-    for (long long i = threadIdx.x; i < kld / 4; i += blockDim.x) cp_async16(sC + 4 * i, a.C_old + 4 * i);
-  }
   __shared__ int n_empty_s;
   __shared__ int wcount[32];
   __shared__ long long hv_cnt[32];
   __shared__ int hv_idx[32];
+  __shared__ double red_scratch[32];
 
   // 1. empty clusters of the new assignment (counts + this iteration's
   //    deltas), ascending ids; every block computes the same answer
@@ -795,110 +769,90 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   const int n_empty = n_empty_s;
 
   if (n_empty == 0) {
-    // ---------------- fast path: no relocation, one block does the update
-    if (blockIdx.x != 0) return;
-    __shared__ double red_scratch[32];
-    long long* cnt_k = a.k <= kFoldSmemK ? cnt_smem : a.cnt_adj;
-    int iter = 0, max_iter = 0;
-    double tol = 0.0;
-    if (threadIdx.x == 0) {
-      iter = st->iter;
-      max_iter = st->max_iter;
-      tol = st->tol;
-    }
-    long long* cnt = const_cast<long long*>(a.counts);
-    for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
-      const long long dv = c < (int)blockDim.x ? dcnt0 : dcnt[c];
-      const long long v = (c < (int)blockDim.x ? cnt0 : (bulk ? 0 : cnt[c])) + dv;
-      cnt_k[c] = v;
-      a.cnt_adj[c] = v;
-      if (bulk || dv != 0) cnt[c] = v;
-      if (dv != 0) a.D[ks + c] = 0;
-    }
-    if (staged) cp_async_wait_all();
-    __syncthreads();
-    // 2. S += dS (bulk: S = D) and the centres, one warp per cluster, lanes
-    //    over columns in batches of 128 whose loads are all issued before any
-    //    store
-    long long* S = const_cast<long long*>(a.S);
+    // ---------------- fast path: no relocation. Units of (cluster, column
+    // part) spread over the blocks; each block folds its units' sums (S + D;
+    // bulk: D) and computes their centres; the last block to finish reduces
+    // the per-unit partials in a fixed order, folds the counts and sets the
+    // loop flags.
+    const double inv_scale = st->inv_scale;
+    const int xexp = st->xexp;
     const float cs = ldexpf(1.0f, xexp);  // centres are bounded by max |x|
-    double wdsq = 0.0;  // this warp's squared shifts, in cluster order
-    for (int c = warp; c < a.k; c += nwarps) {
-      const double fct = centre_factor(inv_scale, cnt_k[c]);
+    const int nq = a.ld >> 2;
+    const int parts = max(1, min(nq, (int)nb / a.k));
+    const int units = a.k * parts;
+    long long* S = const_cast<long long*>(a.S);
+    long long* cnt = const_cast<long long*>(a.counts);
+    for (int u = blockIdx.x; u < units; u += nb) {
+      const int c = u / parts, pt = u % parts;
+      const int q0 = (int)((long long)nq * pt / parts), q1 = (int)((long long)nq * (pt + 1) / parts);
+      const int j0 = 4 * q0, j1 = 4 * q1;
+      const long long dcc = dcnt[c];
+      const long long cnew = (bulk ? 0 : cnt[c]) + dcc;
+      const double fct = centre_factor(inv_scale, cnew);
       double dsq = 0.0, nrm = 0.0;
-      for (int j0 = 0; j0 < a.ld; j0 += 128) {
-        long long dv[4], sv[4];
-        float old[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = j0 + 32 * u + lane;
-          dv[u] = 0;
-          sv[u] = 0;
-          old[u] = 0.0f;
-          if (j < a.ld) {
-            const long long i = (long long)c * a.ld + j;
-            dv[u] = staged ? sD[i] : a.D[i];
-            sv[u] = bulk ? 0 : (staged ? sS[i] : S[i]);
-            old[u] = staged ? sC[i] : a.C_old[i];
-          }
+      for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+        const long long i = (long long)c * a.ld + j;
+        const long long dv = a.D[i];
+        const long long sum = (bulk ? 0 : S[i]) + dv;
+        const float old = a.C_old[i];
+        S[i] = sum;
+        if (dv != 0) a.D[i] = 0;
+        float v = 0.0f;
+        if (j < a.d) {
+          v = centre_from_sum(sum, fct);
+          const double df = (double)v - (double)old;
+          dsq += df * df;
+          nrm += (double)v * v;
+          if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
         }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = j0 + 32 * u + lane;
-          if (j < a.ld) {
-            const long long i = (long long)c * a.ld + j;
-            const long long sum = sv[u] + dv[u];
-            if (bulk || dv[u] != 0) S[i] = sum;
-            if (dv[u] != 0) a.D[i] = 0;
-            float v = 0.0f;
-            if (j < a.d) {
-              v = centre_from_sum(sum, fct);
-              const double df = (double)v - (double)old[u];
-              dsq += df * df;
-              nrm += (double)v * v;
-              if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
-            }
-            a.C_new[i] = v;
-          }
-        }
+        a.C_new[i] = v;
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {  // both butterflies interleaved
-        dsq += __shfl_xor_sync(0xffffffffu, dsq, o);
-        nrm += __shfl_xor_sync(0xffffffffu, nrm, o);
+      dsq = block_sum_f64(dsq, red_scratch);
+      nrm = block_sum_f64(nrm, red_scratch);
+      if (threadIdx.x == 0) {
+        a.unit_dsq[u] = dsq;
+        a.unit_nrm[u] = nrm;
       }
-      if (lane == 0) {
-        if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
-        if (a.bias) a.bias[c] = (float)nrm;
-      }
-      wdsq += dsq;
+      __syncthreads();
     }
-    // 3. total squared shift: warp partials in warp order (a fixed order)
-    if (lane == 0) red_scratch[warp] = wdsq;
-    __syncthreads();
+    // the last block to get here reduces and finishes the iteration
+    __shared__ int last_s;
     if (threadIdx.x == 0) {
-      double tot = 0.0;
-      for (int w = 0; w < nwarps; ++w) tot += red_scratch[w];
+      __threadfence();
+      last_s = atomicAdd(&st->ticket, 1u) == nb - 1;
+    }
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    double* dsq_c = a.shift_partial;  // k entries
+    for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
+      // counts are folded only now: every unit of the cluster has read them
+      const long long dcc = __ldcg(&dcnt[c]);
+      const long long cnew = (bulk ? 0 : __ldcg(&cnt[c])) + dcc;
+      cnt[c] = cnew;
+      a.cnt_adj[c] = cnew;
+      if (dcc != 0) a.D[ks + c] = 0;
+      double dsq = 0.0, nrm = 0.0;
+      for (int pt = 0; pt < parts; ++pt) {  // written by other blocks: read through L2
+        dsq += __ldcg(&a.unit_dsq[c * parts + pt]);
+        nrm += __ldcg(&a.unit_nrm[c * parts + pt]);
+      }
+      dsq_c[c] = dsq;
+      if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
+      if (a.bias) a.bias[c] = (float)nrm;
+    }
+    __syncthreads();
+    const double tot = block_ordered_sum(dsq_c, a.k, red_scratch);
+    if (threadIdx.x == 0) {
+      st->ticket = 0;
       st->n_empty = 0;
       st->relocated = 0;
-      st->cexp = xexp;
-      st->shift_tot = tot;
-      st->iter = iter + 1;
-      st->bulk = st->bulk_always || changed_now > (unsigned long long)st->bulk_threshold;
-      if (changed_now == 0) {
-        st->strict = 1;
-        st->done = 1;
-      } else if (tot <= tol || iter + 1 >= max_iter) {
-        st->done = 1;
-      }
-      *const_cast<unsigned long long*>(a.changed) = 0;
-      if (a.host_done) *a.host_done = st->done ? st->iter : 0;
+      finish_iteration(a, st, changed_now, tot);
     }
     return;
   }
 
   // ---------------- relocation path (cooperative, all blocks)
-  if (staged) cp_async_wait_all();  // the staged copies are not used here
   // 0. S += dS, counts += dcount (bulk: S = dS, counts = dcount); clear the
   //    deltas (all but `changed`)
   {

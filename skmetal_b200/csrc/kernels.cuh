@@ -9,8 +9,6 @@
 namespace skm {
 
 constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
-constexpr int kFoldSmemK = 4096;          // M-step keeps up to this many folded counts in shared memory
-constexpr int kStageElems = 8192;         // M-step stages S, D, C_old (k*ld <= this) in shared memory
 constexpr size_t kBulkSmemBytes = 160 * 1024;  // bulk pass accumulates privately when (k*ld + k) int64 fit
 
 __host__ __device__ inline bool bulk_in_smem(int k, int ld) {
@@ -30,14 +28,19 @@ __host__ __device__ inline size_t cand_row_off(int cap) { return 16 + (size_t)ca
 __host__ __device__ inline size_t cand_label_off(int cap) { return 16 + (size_t)cap * 12; }
 __host__ __device__ inline size_t cand_x_off(int cap) { return 16 + (size_t)cap * 16; }
 
+// The M-step's fast path splits the centre update into units of (cluster,
+// column part): parts = max(1, min(ld / 4, blocks / k)), so that the k * parts
+// units spread over the blocks.
+// Above n / 10 changed rows in an iteration, per-row deltas (about 2 d
+// contended reductions per row) cost more than rebuilding the sums from all
+// rows, so the next iteration is a bulk one.
+constexpr int kBulkDivisor = 10;
+
 // Dynamic shared memory of mstep_kernel for k clusters of ld columns.
 inline size_t mstep_smem_bytes(int k, int ld) {
-  const size_t kk = (size_t)((k + 1) & ~1);
-  size_t b = k <= kFoldSmemK ? sizeof(long long) * kk : 0;
-  if ((long long)k * ld <= kStageElems) b = sizeof(long long) * kk + (size_t)k * ld * (8 + 8 + 4);
-  if (bulk_in_smem(k, ld)) b = std::max(b, sizeof(long long) * ((size_t)k * ld + k));
-  return b;
+  return bulk_in_smem(k, ld) ? sizeof(long long) * ((size_t)k * ld + k) : 0;
 }
+
 
 struct MStepArgs {
   FitState* st;
@@ -76,6 +79,9 @@ struct MStepArgs {
   // bulk iterations: the sums were already added into D before the M-step
   // (multi-GPU: before the all-reduce), so the M-step only replaces S by D
   int bulk_external;
+  // per (cluster, column part) partial squared shift and squared norm
+  double* unit_dsq;
+  double* unit_nrm;
   // relocation candidates gathered from every rank (multi-GPU); null on one
   // GPU: cand_ranks blocks of cand_block_bytes(cand_cap, ld) bytes each
   const unsigned char* cand;

@@ -387,6 +387,11 @@ static int run_fit(const FitParams& p) {
   SKM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_done_dev), pinned, 0));
   ma.host_done = host_done_dev;
   ma.bulk_external = comm ? 1 : 0;
+  {
+    const size_t nunit = (size_t)std::max(k, mstep_blocks);
+    SKM_TRY(buf.alloc_n(&ma.unit_dsq, nunit));
+    SKM_TRY(buf.alloc_n(&ma.unit_nrm, nunit));
+  }
   // multi-GPU relocation: this rank's candidate block and everyone's
   unsigned char* cand_send = nullptr;
   unsigned char* cand_all = nullptr;

@@ -53,6 +53,8 @@ struct FitState {
   double inertia;
   unsigned int barrier_count;  // software grid barrier
   unsigned int barrier_gen;
+  unsigned int ticket;         // M-step: blocks done with their clusters (the last one finishes)
+  unsigned int pad_ticket;
   unsigned int maxabs_bits;    // max |x| (float bits) of centred X
   int32_t xexp;        // tensor-core operand scale of X: x * 2^xexp (split_exp)
   int32_t cexp;        // same for the centres of the current centre image

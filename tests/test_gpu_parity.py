@@ -255,7 +255,10 @@ def test_tolerance_decision_lockstep():
     X, init = gaussian_mixture(20000, 16, 6, seed=5)
     res = ora.kmeans_lloyd(X, init, 300, 1e-4, keep_centers=True)
     km = KMeans(6, init=init, n_init=1, max_iter=300, tol=1e-4, algorithm="lloyd").fit(X)
-    assert res.n_iter == km.n_iter_  # the oracle's loop is scikit-learn's
+    # the oracle's loop is scikit-learn's, but when the relative tolerance stops
+    # it depends on float32 summation order, which depends on the host's thread
+    # count: the exact pinning is test_oracle.py's, on fixed fixtures
+    assert abs(res.n_iter - km.n_iter_) <= 5
     tol_abs = ora.tolerance(X, 1e-4)
     mean, Xc, _ = ora.center_data(X)
     for i, h in enumerate(res.history):

@@ -18,9 +18,11 @@ iterations, the final E-step and the inertia).
 * ``cpu_baseline`` (rank 0, N = 1): scikit-learn's Lloyd (the reference's CPU
   path) on a bounded sample of the same workload.
 
-Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): rows are split
-into N contiguous shards (strong scaling of the same dataset); the per-iteration
-k x d sums and k counts are all-reduced with NCCL inside the library.
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): weak scaling.
+Every GPU holds as many rows as the N = 1 workload (500,000 for C2) of one
+dataset of N times that size drawn with the same recipe; rank r fits its
+contiguous shard and the library all-reduces the per-iteration k x d sums and
+k counts with NCCL. ``value`` counts the rows of all GPUs.
 """
 
 from __future__ import annotations
@@ -173,7 +175,9 @@ def run_reference(args, w, X, init):
     from sklearn.cluster import KMeans
     from sklearn.utils._openmp_helpers import _openmp_effective_n_threads
 
-    sample_iters = 20
+    # a bounded sample per step: about 20 x 500k row-iterations whatever N is
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    sample_iters = max(2, round(20 / world))
     for _ in range(args.warmup):
         KMeans(w.k, init=init, n_init=1, max_iter=sample_iters, tol=0, algorithm="lloyd").fit(X)
     rows_iters, t_total = 0, 0.0
@@ -187,7 +191,7 @@ def run_reference(args, w, X, init):
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_total / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture, BASELINE configs[1])",
         "config": {"workload": w.name, "n": w.n, "d": w.d, "k": w.k, "max_iter": sample_iters, "tol": 0,
                    "parallelism": "cpu threads"},
@@ -212,7 +216,11 @@ def main():
 
     from skmetal_b200._synthetic import WORKLOADS, make_workload, scaled
 
-    w = WORKLOADS[args.config] if not args.rows else scaled(args.config, args.rows)
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    rows_per_gpu = args.rows or WORKLOADS[args.config].n
+    # Weak scaling: every GPU holds rows_per_gpu rows of the same recipe; at
+    # N = 1 the workload is exactly the metric's configuration.
+    w = scaled(args.config, rows_per_gpu * world_env) if (args.rows or world_env > 1) else WORKLOADS[args.config]
     X, init = make_workload(w)
     if args.impl == "reference":
         run_reference(args, w, X, init)
@@ -306,10 +314,11 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture, BASELINE configs[1]); X resident in HBM",
-        "config": {"workload": w.name, "n": n, "d": w.d, "k": w.k, "max_iter": w.max_iter, "tol": 0,
-                   "iters_per_step": iters / args.steps, "parallelism": f"rows sharded x{world}",
+        "config": {"workload": w.name, "n": n, "n_per_gpu": n // world, "d": w.d, "k": w.k,
+                   "max_iter": w.max_iter, "tol": 0, "iters_per_step": iters / args.steps,
+                   "parallelism": f"rows sharded x{world} (weak scaling: {n // world} rows per GPU)",
                    "l2": "X (%.0f MB per GPU) > L2 (126 MB) between iterations" % (alg_bytes / 1e6)},
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": int(Xs.nbytes + init.nbytes),

@@ -540,14 +540,6 @@ __device__ __forceinline__ void bulk_pass(const float* __restrict__ X, int ld, l
   }
 }
 
-__global__ void bulk_pass_kernel(const float* __restrict__ X, int ld, long long n, int d,
-                                 const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                 const FitState* __restrict__ st) {
-  extern __shared__ __align__(16) long long bulk_acc[];
-  (void)d;
-  if (st->done || !st->bulk) return;
-  bulk_pass(X, ld, n, labels, k, D, st->scale, bulk_in_smem(k, ld) ? bulk_acc : nullptr);
-}
 
 // ---------------------------------------------------------------------------
 // M-step (cooperative): empty clusters, relocation, averaging, shift, flags
@@ -910,7 +902,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
       if (cnt < 0) overflow = 1;
       else valid_total += cnt;
     }
-    if (overflow || valid_total < n_empty) {  // uniform over blocks and ranks
+    if (overflow || n_empty > a.cand_cap || valid_total < n_empty) {  // uniform over blocks and ranks
       if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&st->error, 1003);
       return;
     }
@@ -1002,37 +994,54 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   }
 }
 
-// Multi-GPU relocation, first half: this rank's n_empty rows farthest from
-// their centre (or all its rows if it has fewer), written to `send` for the
-// all-gather; count 0 when no cluster is empty, -1 when more than cand_cap
-// are. The M-step then ranks the gathered candidates of all ranks with the
-// single-GPU rule, so every rank relocates the same rows.
-__global__ void __launch_bounds__(1024, 1) reloc_candidates_kernel(MStepArgs a, unsigned char* send) {
+// Multi-GPU fits, between the E-step and the all-reduce of the payload
+// [D | one candidate slot per rank]: the bulk pass of a bulk iteration; the
+// rank's own cluster counts; and, when one of them is empty after this
+// iteration, the rank's farthest rows as relocation candidates in its slot.
+// A cluster can only be empty globally if it is empty on every rank, so every
+// rank then supplies its min(local empties, cap) farthest rows, which contain
+// its share of the global farthest rows. The other ranks' slots are zeroed
+// here, so the integer all-reduce delivers each rank's slot unchanged.
+__global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long long* local_counts, int rank) {
   FitState* st = a.st;
   const unsigned int nb = gridDim.x;
-  const int done = st->done;
+  const size_t cb = cand_block_bytes(a.cand_cap, a.ld);
+  unsigned char* slots = const_cast<unsigned char*>(a.cand);
+  unsigned char* mine = slots + (size_t)rank * cb;
+  // every slot starts at zero (the payload's other parts are D)
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < cb * a.cand_ranks / 8;
+       i += (size_t)nb * blockDim.x)
+    reinterpret_cast<long long*>(slots)[i] = 0;
+  if (st->done) return;
   const int bulk = st->bulk;
-  int* count_out = reinterpret_cast<int*>(send);
-  if (done) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) *count_out = 0;
-    return;
+  extern __shared__ __align__(16) long long dyn_smem[];
+  if (bulk) bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, bulk_in_smem(a.k, a.ld) ? dyn_smem : nullptr);
+  if (!grid_barrier(st, nb)) return;
+  // local counts after this iteration, and how many clusters this rank has empty
+  const long long* dcnt = a.D + (long long)a.k * a.ld;
+  int n_local_empty = 0;
+  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
+    const int c = c0 + threadIdx.x;
+    long long v = 0;
+    if (c < a.k) v = (bulk ? 0 : local_counts[c]) + dcnt[c];
+    n_local_empty += __syncthreads_count(c < a.k && v == 0);
+    if (blockIdx.x == 0 && c < a.k) a.cnt_adj[c] = v;  // staged: written back after the barrier
   }
-  const int n_empty = count_empty(a, bulk);
-  if (n_empty == 0 || n_empty > a.cand_cap) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) *count_out = n_empty == 0 ? 0 : -1;
-    return;
-  }
-  const int m = (int)min((long long)n_empty, a.n);
   if (blockIdx.x == 0 && threadIdx.x == 0) st->sel_count = 0;
+  if (!grid_barrier(st, nb)) return;
+  if (blockIdx.x == 0)
+    for (int c = threadIdx.x; c < a.k; c += blockDim.x) local_counts[c] = a.cnt_adj[c];
+  if (n_local_empty == 0) return;  // the slot's count stays 0
+  const int m = (int)min((long long)min(n_local_empty, a.cand_cap), a.n);
   rows_dist_to_old_centres(a, nb);
   if (!grid_barrier(st, nb)) return;
-  if (m > 0 && !select_farthest(a.mind, a.n, a.row_base, m, st, a.hist, a.sel, nb)) return;
+  if (!select_farthest(a.mind, a.n, a.row_base, m, st, a.hist, a.sel, nb)) return;
   if (blockIdx.x == 0) {
     const int cap = a.cand_cap;
-    float* dist = reinterpret_cast<float*>(send + cand_dist_off(cap));
-    long long* row = reinterpret_cast<long long*>(send + cand_row_off(cap));
-    int* label = reinterpret_cast<int*>(send + cand_label_off(cap));
-    float* x = reinterpret_cast<float*>(send + cand_x_off(cap));
+    float* dist = reinterpret_cast<float*>(mine + cand_dist_off(cap));
+    long long* row = reinterpret_cast<long long*>(mine + cand_row_off(cap));
+    int* label = reinterpret_cast<int*>(mine + cand_label_off(cap));
+    float* x = reinterpret_cast<float*>(mine + cand_x_off(cap));
     for (int i = threadIdx.x; i < m; i += blockDim.x) {
       const long long r = a.sel[i];
       dist[i] = a.mind[r];
@@ -1040,7 +1049,7 @@ __global__ void __launch_bounds__(1024, 1) reloc_candidates_kernel(MStepArgs a, 
       label[i] = a.labels[r];
       for (int j = 0; j < a.ld; ++j) x[(long long)i * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
     }
-    if (threadIdx.x == 0) *count_out = m;
+    if (threadIdx.x == 0) *reinterpret_cast<int*>(mine) = m;
   }
 }
 

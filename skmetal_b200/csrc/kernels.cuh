@@ -15,11 +15,11 @@ __host__ __device__ inline bool bulk_in_smem(int k, int ld) {
   return sizeof(long long) * ((size_t)k * ld + k) <= kBulkSmemBytes;
 }
 
-// Relocation candidates of one rank (multi-GPU fits), exchanged by an
-// all-gather: [count int32, 3 x int32 padding | dist float[cap] | global row
-// int64[cap] | label int32[cap] | x float[cap][ld]]. count = -1 when the
-// iteration has more empty clusters than `cap`.
-constexpr int kCandCap = 32;
+// Relocation candidates of one rank (multi-GPU fits), one slot per rank after
+// D in the all-reduced payload: [count int32, 3 x int32 padding | dist
+// float[cap] | global row int64[cap] | label int32[cap] | x float[cap][ld]].
+// count = min(clusters this rank has empty, cap).
+constexpr int kCandCap = 16;
 __host__ __device__ inline size_t cand_block_bytes(int cap, int ld) {
   return (16 + (size_t)cap * 16 + (size_t)cap * ld * 4 + 15) & ~(size_t)15;
 }
@@ -109,16 +109,11 @@ __global__ void counts_to_float_kernel(const long long* c, int k, float* out);
 // returns false when d has no specialisation.
 bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
                          long long n, const float* C, int k, int32_t* labels, float* mind);
-// The bulk pass of a bulk iteration as its own launch (multi-GPU: before the
-// all-reduce); a no-op unless st->bulk. Dynamic shared memory: (k*ld + k)
-// int64 when bulk_in_smem(k, ld), else 0.
-__global__ void bulk_pass_kernel(const float* X, int ld, long long n, int d, const int32_t* labels, int k,
-                                 long long* D, const FitState* st);
 
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a);
-// Multi-GPU: this rank's relocation candidates for the current iteration
-// (cooperative; writes one candidate block to `send`).
-__global__ void __launch_bounds__(1024, 1) reloc_candidates_kernel(MStepArgs a, unsigned char* send);
+// Multi-GPU, before the all-reduce (cooperative): bulk pass, the rank's
+// local counts and its relocation-candidate slot (see kernels.cu).
+__global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long long* local_counts, int rank);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, CentreImage ci, FitState* st);
 __global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
                                        const int32_t* labels, double* partial, int blocked);

@@ -121,16 +121,6 @@ static int launch_assign_simt(const float* X, int ld, long long n, int d, const 
   return check_launch("assign_simt_kernel");
 }
 
-// The bulk pass as its own launch (multi-GPU fits, before the all-reduce).
-static int launch_bulk_pass(const float* X, int ld, long long n, int d, const int32_t* labels, int k, long long* D,
-                            const FitState* st, cudaStream_t s) {
-  const size_t smem = bulk_in_smem(k, ld) ? sizeof(long long) * ((size_t)k * ld + k) : 0;
-  if (smem > 48 * 1024)
-    SKM_CUDA(cudaFuncSetAttribute(bulk_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  bulk_pass_kernel<<<sm_count(), 1024, smem, s>>>(X, ld, n, d, labels, k, D, st);
-  return check_launch("bulk_pass_kernel");
-}
-
 // The cooperative M-step; with `pdl` it is launched with programmatic stream
 // serialization so that its launch overlaps the E-step's tail (the kernel
 // waits for the E-step's writes itself).
@@ -222,7 +212,12 @@ static int run_fit(const FitParams& p) {
   SKM_TRY(buf.alloc_n(&S, (size_t)k * ld + k));
   long long* counts = S + (size_t)k * ld;
   // per-iteration deltas (the all-reduced payload): dS (k*ld) | dcount (k) | changed (1)
-  const size_t payload_len = (size_t)k * ld + k + 1;
+  // all-reduced payload: D = [dS (k x ld) | dcount (k) | changed], then on
+  // multi-GPU fits one relocation-candidate slot per rank (16-byte aligned)
+  const size_t d_len = (size_t)k * ld + k + 1;
+  const size_t cand_off = (d_len + 1) & ~(size_t)1;
+  const size_t cand_bytes = comm ? cand_block_bytes(kCandCap, ld) : 0;
+  const size_t payload_len = comm ? cand_off + cand_bytes / 8 * (size_t)comm_nranks(comm) : d_len;
   long long* D = nullptr;
   SKM_TRY(buf.alloc_n(&D, payload_len));
   unsigned long long* changed = reinterpret_cast<unsigned long long*>(D + (size_t)k * ld + k);
@@ -366,7 +361,10 @@ static int run_fit(const FitParams& p) {
   const int mstep_threads = 1024;
   const size_t mstep_smem = mstep_smem_bytes(k, ld);
   if (mstep_smem > 48 * 1024)
+  {
     SKM_CUDA(cudaFuncSetAttribute(mstep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mstep_smem));
+    SKM_CUDA(cudaFuncSetAttribute(shard_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mstep_smem));
+  }
 
   std::vector<cudaEvent_t> prof_ev;
   if (p.profile) {
@@ -392,18 +390,16 @@ static int run_fit(const FitParams& p) {
     SKM_TRY(buf.alloc_n(&ma.unit_dsq, nunit));
     SKM_TRY(buf.alloc_n(&ma.unit_nrm, nunit));
   }
-  // multi-GPU relocation: this rank's candidate block and everyone's
-  unsigned char* cand_send = nullptr;
-  unsigned char* cand_all = nullptr;
-  size_t cand_bytes = 0;
+  // multi-GPU: candidate slots after D, and this rank's own cluster counts
+  long long* local_counts = nullptr;
   if (comm) {
-    cand_bytes = cand_block_bytes(kCandCap, ld);
-    SKM_TRY(buf.alloc_n(&cand_send, cand_bytes));
-    SKM_TRY(buf.alloc_n(&cand_all, cand_bytes * (size_t)comm_nranks(comm)));
-    ma.cand = cand_all;
+    ma.cand = reinterpret_cast<const unsigned char*>(D + cand_off);
     ma.cand_ranks = comm_nranks(comm);
     ma.cand_cap = kCandCap;
+    SKM_TRY(buf.alloc_n(&local_counts, (size_t)k));
+    SKM_CUDA(cudaMemsetAsync(local_counts, 0, sizeof(long long) * k, s));
   }
+
   const int chunk = 8;
   int it = 0, chunk_idx = 0, pending = -1;
   bool done_seen = false;
@@ -445,15 +441,13 @@ static int run_fit(const FitParams& p) {
       ma.C_old = Cin;
       ma.C_new = Cout;
       if (comm) {
-        // bulk sums must be local before the all-reduce (a no-op unless bulk)
-        SKM_TRY(launch_bulk_pass(X, ld, n, d, labels, k, D, st, s));
+        // bulk pass, local counts and relocation candidates, then one all-reduce
+        int rank = comm_rank(comm);
+        void* pargs[] = {&ma, &local_counts, &rank};
+        SKM_CUDA(cudaLaunchCooperativeKernel((void*)shard_prep_kernel, dim3(mstep_blocks), dim3(mstep_threads), pargs,
+                                             mstep_smem, s));
+        SKM_TRY(check_launch("shard_prep_kernel"));
         SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
-        // relocation candidates of every rank (count 0 unless a cluster is empty)
-        void* cargs[] = {&ma, &cand_send};
-        SKM_CUDA(cudaLaunchCooperativeKernel((void*)reloc_candidates_kernel, dim3(mstep_blocks), dim3(mstep_threads),
-                                             cargs, 0, s));
-        SKM_TRY(check_launch("reloc_candidates_kernel"));
-        SKM_TRY(comm_allgather_bytes(comm, cand_send, cand_all, cand_bytes, s));
       }
       SKM_TRY(launch_mstep(ma, mstep_blocks, mstep_threads, mstep_smem, !comm && !timed, s));
     }

@@ -150,6 +150,14 @@ int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t 
  * E-step launches timed individually (SKMETAL_FIT_PROFILE: iterations 0, 10,
  * 20, ...) and their summed duration, the kernel launches issued, and the
  * iterations run. */
+/* Debug: the device timestamps (ns) of the last profiled fit that ran the
+ * persistent loop kernel on this thread: per iteration t, [4t] start, [4t+1]
+ * E-step done, [4t+2] bulk sums and empty clusters done, [4t+3] centres
+ * done, and a final end stamp. Copies up to `cap` and returns how many there
+ * are (0 when the last profiled fit used the multi-launch loop). No
+ * reference counterpart. */
+int skmetal_debug_loop_stamps(uint64_t* out, int cap);
+
 int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,
                            int32_t* estep_launches, double* estep_ms_sum, uint64_t* launches, int32_t* iterations);
 

@@ -25,7 +25,7 @@ __all__ = [
     "ensure_warmed_up", "kmeans_assign", "kmeans_batch_fused", "compute_mindists", "kmeans_inertia",
     "row_norm_sq", "kmeans_fit", "kmeans_lloyd_iter", "kmeans_transform", "Dataset", "last_fit_stats",
     "launch_count", "device_info", "device_count", "set_device", "comm_unique_id", "comm_init",
-    "comm_destroy", "kmeans_fit_shard", "debug_inject_failure", "FIT_CENTER", "FIT_SIMT", "FIT_PROFILE",
+    "comm_destroy", "kmeans_fit_shard", "debug_inject_failure", "debug_loop_stamps", "FIT_CENTER", "FIT_SIMT", "FIT_PROFILE",
     "FIT_DISTRIBUTED", "FIT_TOL_ABS", "EXPORTED_SYMBOLS",
 ]
 
@@ -52,6 +52,7 @@ _SIGNATURES = [
     ("skmetal_launch_count", ctypes.c_ulonglong, []),
     ("skmetal_debug_inject_failure", _c_int, [_c_int, _c_int]),
     ("skmetal_debug_tc_probe", _c_int, [ctypes.POINTER(_c_int), _c_void_p]),
+    ("skmetal_debug_loop_stamps", _c_int, [_c_void_p, _c_int]),
     ("skmetal_kmeans_assign", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t]),
     ("skmetal_kmeans_batch_fused", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t,
                                             _c_size_t, _c_size_t, _c_float, ctypes.POINTER(_c_i32)]),
@@ -408,6 +409,17 @@ def debug_tc_probe(raw: bool = False):
     if rc != 0:
         raise RuntimeError(f"skmetal_debug_tc_probe failed with code {rc}: {_last_error()}")
     return int(mode.value), out
+
+
+def debug_loop_stamps() -> np.ndarray:
+    """Device timestamps (ns) of the last profiled persistent-loop fit on this
+    thread: per iteration [start, E-step done, sums and empties done, centres
+    done], then the end stamp; empty when that fit used the multi-launch loop."""
+    n = int(_fn("skmetal_debug_loop_stamps")(None, 0))
+    out = np.zeros(max(n, 0), dtype=np.uint64)
+    if n > 0:
+        _fn("skmetal_debug_loop_stamps")(out.ctypes.data, n)
+    return out
 
 
 def debug_inject_failure(code: int, after_calls: int = 0) -> None:

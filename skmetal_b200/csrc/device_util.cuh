@@ -51,6 +51,16 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Block barrier for code in which lanes of a warp may arrive separately
+// (warp-specialised roles where one elected lane runs a loop, or
+// `if (threadIdx.x == 0) { ... }` sections with loops and early exits):
+// bar.sync is the .aligned form, which a diverged warp must not execute, so
+// the warp first reconverges on __syncwarp.
+__device__ __forceinline__ void block_sync() {
+  __syncwarp();
+  __syncthreads();
+}
+
 __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
   atomicAdd(reinterpret_cast<unsigned long long*>(p), static_cast<unsigned long long>(v));
 }

@@ -1,0 +1,527 @@
+// Device code of the tensor-core E-step pipeline (sm_100a), shared by the
+// stand-alone E-step kernel (estep_tc.cu) and the persistent Lloyd loop
+// kernel (loop_tc.cu): mbarrier / bulk-copy / tcgen05 wrappers, the shared
+// memory layout, and one pass of the warp-specialised pipeline over a CTA's
+// tiles (estep_pass), which a persistent kernel may run once per iteration.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "device_util.cuh"
+#include "estep_tc.h"
+#include "skm.cuh"
+
+namespace skm {
+
+namespace tc {
+
+constexpr int BM = 128;                   // rows per tile (UMMA M)
+constexpr int KC = 8;                     // fp32 columns per K chunk (one kind::f16 MMA, K = 16)
+constexpr int CHUNK_BYTES = BM * KC * 4;  // 4096
+constexpr int MAX_NK = 16;                // d <= 128
+constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
+constexpr int THREADS = 640;
+constexpr int MAX_STAGES = 4;
+constexpr int MAX_ACC = 4;
+constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
+
+struct Params {
+  int n_tiles;
+  long long n;
+  int k;
+  int k_pad;
+  int nk;         // K chunks of 8 columns
+  int stacked;    // centre image layout (CentreImage)
+  int stages;     // X stages in shared memory
+  int nacc;       // accumulators in TMEM (1, 2 or 4)
+  int acc_cols;   // TMEM columns of one accumulator
+  int tmem_cols;
+  uint32_t stage_bytes;  // >= tile_bytes (an even number of chunks when not stacked)
+  uint32_t tile_bytes;   // nk * 4096: one tile of the split copy
+  uint32_t img_bytes;
+  const unsigned char* Xs;  // split working copy
+  const uint16_t* img;      // centre image
+  const int* sexp;          // {xexp, cexp}: operand scales 2^xexp, 2^cexp
+  const float* bias;        // ||c||^2, k entries
+  int32_t* labels;
+  unsigned long long* changed;
+  long long* D;     // nullable: incremental deltas of rows that changed label
+  const float* X;   // fp32 blocked copy (the deltas read exact values from it)
+  int ld;
+  int d;
+  const FitState* st;   // nullable: skip when st->done; scale for D
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false on timeout (after recording `code`) or when another
+// thread of the CTA aborted.
+static __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > TIMEOUT_NS) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// K-major no-swizzle shared-memory matrix descriptor: core matrices of 8 rows
+// x 16 bytes; `lbo` = bytes between the two K halves of a K = 16 slice, `sbo`
+// = bytes between 8-row groups; descriptor version 1, layout type 0. Kept as
+// two 32-bit words: lo = start address >> 4 (bits 0-13) | lbo >> 4 (bits
+// 16-29), hi = sbo >> 4 (bits 32-45) | version (bit 46). Only lo changes
+// along K, and the MMA wrapper joins the words in PTX.
+struct SmemDesc {
+  uint32_t lo, hi;
+};
+__device__ __forceinline__ SmemDesc kmajor_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  SmemDesc d;
+  d.lo = ((saddr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+  d.hi = ((sbo >> 4) & 0x3FFFu) | (1u << 14);
+  return d;
+}
+// the descriptor of the matrix `bytes` further along (start address field)
+__device__ __forceinline__ SmemDesc desc_advance(SmemDesc d, uint32_t bytes) {
+  d.lo += bytes >> 4;
+  return d;
+}
+
+// kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, M = 128, N.
+__host__ __device__ constexpr uint32_t idesc_f16(int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] . B[smem]^T
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, SmemDesc a, SmemDesc b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}"
+      ::"r"(tmem_d), "r"(a.lo), "r"(a.hi), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// tcgen05.ld is asynchronous: its destination registers hold the data only
+// after tcgen05.wait::ld. The wait takes the registers of a load as in/out
+// operands, so the compiler cannot schedule their uses before it.
+__device__ __forceinline__ void tmem_ld_wait16(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+// Orders the uses of r after the preceding volatile asm (a second load's
+// registers after tmem_ld_wait16 of the first).
+__device__ __forceinline__ void reg_pin16(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// The MMAs of one tile: A = stage (split copy of X), B = centre image in smem.
+// The start address sits in the low 14 bits of a descriptor (address / 16,
+// shared memory < 256 KB), so later chunks advance a descriptor by addition.
+__device__ __forceinline__ void issue_tile_mmas(uint32_t tacc, uint32_t stage, uint32_t img, int nk, int k_pad,
+                                                int stacked) {
+  const SmemDesc a0 = kmajor_desc(stage, 2048u, 128u);
+  if (stacked) {
+    const int N = 2 * k_pad;
+    const uint32_t idesc = idesc_f16(N);
+    const SmemDesc b0 = kmajor_desc(img, (uint32_t)(N * 16), 128u);
+    for (int c = 0; c < nk; ++c)
+      mma_f16(tacc, desc_advance(a0, (uint32_t)c * CHUNK_BYTES), desc_advance(b0, (uint32_t)(c * N * 32)), idesc,
+              c > 0 ? 1u : 0u);
+  } else {
+    const uint32_t idesc = idesc_f16(k_pad);
+    const SmemDesc b0 = kmajor_desc(img, (uint32_t)(k_pad * 16), 128u);
+    for (int c = 0; c < nk; ++c)
+      mma_f16(tacc, desc_advance(a0, (uint32_t)c * CHUNK_BYTES), desc_advance(b0, (uint32_t)(c * k_pad * 32)), idesc,
+              c > 0 ? 1u : 0u);
+    // x_hi of chunk pairs (2m | 2m + 1) times c_lo of the same pair
+    const SmemDesc p0 = kmajor_desc(stage, (uint32_t)CHUNK_BYTES, 128u);
+    const SmemDesc q0 = kmajor_desc(img + (uint32_t)(nk * k_pad * 32), (uint32_t)(k_pad * 16), 128u);
+    for (int m = 0; 2 * m < nk; ++m)
+      mma_f16(tacc, desc_advance(p0, (uint32_t)(2 * m) * CHUNK_BYTES), desc_advance(q0, (uint32_t)(m * k_pad * 32)),
+              idesc, 1u);
+  }
+}
+
+// stages at s * stage_bytes from 0, then the centre image, bias, barriers and
+// misc words
+struct Smem {
+  uint32_t c, bias, bars, misc, total;
+};
+
+// barrier indices
+__host__ __device__ constexpr int B_FULL(int s) { return s; }               // stage loaded
+__host__ __device__ constexpr int B_EMPTY(int s) { return MAX_STAGES + s; }  // stage consumed by the MMAs
+__host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + a; }
+__host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + MAX_ACC + a; }
+constexpr int B_C_FULL = 2 * MAX_STAGES + 2 * MAX_ACC;
+__host__ __device__ constexpr int B_DONE(int t) { return B_C_FULL + 1 + t; }  // drain of MMA issuer t
+constexpr int NUM_BARS = B_C_FULL + 3;
+
+constexpr int MMA_W0 = 1, MMA_W1 = 2;
+constexpr int EPI_W0 = 4;
+constexpr int EPI_GROUPS = 4;  // one warp per TMEM lane quarter each
+static_assert((EPI_W0 + 4 * EPI_GROUPS) * 32 == THREADS, "warp roles must fill the block");
+
+__host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_bytes, int k_pad, int stages) {
+  Smem s;
+  uint32_t off = (uint32_t)stages * stage_bytes;
+  s.c = off;
+  off += img_bytes;
+  s.bias = off;
+  off += (uint32_t)k_pad * 4;
+  off = (off + 15) & ~15u;
+  s.bars = off;
+  off += NUM_BARS * 8;
+  s.misc = off;
+  off += 16;             // [0] tmem base, [1] abort flag
+  s.total = off + 1024;  // slack for aligning the base to 1024
+  return s;
+}
+
+__device__ __forceinline__ bool better(float d, int i, float bd, int bi) { return d < bd || (d == bd && i < bi); }
+
+// Per-CTA view of a launch's shared memory, barriers and tensor memory.
+struct Cta {
+  unsigned char* base;  // dynamic shared memory, aligned to 1024
+  uint32_t sbase;
+  Smem L;
+  uint32_t bar0;
+  uint32_t* misc;  // [0] tensor-memory base, [1] abort flag
+  volatile int* abort_flag;
+  float* bias_s;  // ||c||^2, k_pad entries (+inf beyond k)
+  uint32_t tmem_base;
+  int my_tiles;  // tiles blockIdx.x + i * gridDim.x, i < my_tiles
+  int n_iss;     // MMA issuers (1 or 2)
+  int n_grp;     // epilogue groups (= accumulators)
+  __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * (uint32_t)i; }
+};
+
+// The extra chunk of an odd nk (read as x_hi by the last pair MMA of the
+// two-segment layout) is zero in every stage. All threads; the caller
+// synchronises the block before the next bulk copy into the stages.
+__device__ __forceinline__ void zero_stage_padding(const Params& p, const Cta& c) {
+  if (p.tile_bytes < p.stage_bytes) {
+    for (int s = 0; s < p.stages; ++s)
+      for (uint32_t o = p.tile_bytes + 16u * threadIdx.x; o < p.stage_bytes; o += 16u * blockDim.x)
+        *reinterpret_cast<uint4*>(c.base + (uint32_t)s * p.stage_bytes + o) = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+}
+
+// ||c||^2 into shared memory (+inf for the padding clusters). All threads.
+__device__ __forceinline__ void load_bias(const Params& p, const Cta& c, const float* bias) {
+  for (int j = threadIdx.x; j < p.k_pad; j += blockDim.x) c.bias_s[j] = j < p.k ? __ldcg(bias + j) : INFINITY;
+}
+
+// All threads, once per launch: layout, barriers, tensor-memory allocation
+// (warp MMA_W0), bias (nullable), zeroed stage padding; ends with a block
+// barrier after which c.tmem_base is valid.
+__device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_raw, const float* bias, Cta& c) {
+  c.base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  c.L = smem_layout(p.stage_bytes, p.img_bytes, p.k_pad, p.stages);
+  c.sbase = smem_u32(c.base);
+  c.bar0 = c.sbase + c.L.bars;
+  c.misc = reinterpret_cast<uint32_t*>(c.base + c.L.misc);
+  c.abort_flag = reinterpret_cast<volatile int*>(c.misc + 1);
+  c.bias_s = reinterpret_cast<float*>(c.base + c.L.bias);
+  c.my_tiles = (p.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  // issuer t owns the accumulators a = t mod n_iss and epilogue group g those
+  // with a = g mod n_grp (n_iss and n_grp divide nacc), so each accumulator
+  // barrier has exactly one producer and one consumer
+  c.n_iss = p.nacc >= 2 ? 2 : 1;
+  c.n_grp = p.nacc;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < MAX_STAGES; ++s) {
+      mbar_init(c.bar(B_FULL(s)), 1);
+      mbar_init(c.bar(B_EMPTY(s)), 1);
+    }
+    for (int a = 0; a < MAX_ACC; ++a) {
+      mbar_init(c.bar(B_ACC_FULL(a)), 1);
+      mbar_init(c.bar(B_ACC_EMPTY(a)), 4);  // the four warps of one epilogue group
+    }
+    mbar_init(c.bar(B_C_FULL), 1);
+    mbar_init(c.bar(B_DONE(0)), 1);
+    mbar_init(c.bar(B_DONE(1)), 1);
+    c.misc[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == MMA_W0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(c.sbase + c.L.misc),
+                 "r"(p.tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (bias) load_bias(p, c, bias);
+  zero_stage_padding(p, c);
+  tc_fence_before();
+  block_sync();
+  tc_fence_after();
+  c.tmem_base = c.misc[0];
+}
+
+// All threads, once per launch, after the last pass: frees the tensor memory.
+__device__ __forceinline__ void cta_teardown(const Params& p, const Cta& c) {
+  tc_fence_before();
+  block_sync();
+  if ((threadIdx.x >> 5) == MMA_W0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(c.tmem_base), "r"(p.tmem_cols));
+  }
+}
+
+// One pass of the pipeline over this CTA's tiles, every thread in its warp
+// role: the producer loads the centre image and the tiles, the issuers run
+// the MMAs, the epilogue writes labels, counts changed rows into `changed`
+// (nullable) and, with `deltas` non-null, adds their fixed-point deltas.
+// ig0 = tiles this CTA processed in earlier passes of the launch: stage and
+// accumulator phases continue from there, so consecutive passes need no
+// barrier re-initialisation. par = parity of the pass (the image and drain
+// barriers complete once per pass). No block barrier at the end: a caller
+// that reuses shared memory synchronises first. On a timeout the CTA's abort
+// flag is set and every role stops issuing work after draining its own
+// copies and tensor-core operations.
+__device__ __forceinline__ void estep_pass(const Params& p, const Cta& c, int ig0, int par, long long* deltas,
+                                           unsigned long long* changed) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int my_tiles = c.my_tiles;
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      mbar_expect_tx(c.bar(B_C_FULL), p.img_bytes);
+      for (uint32_t o = 0; o < p.img_bytes; o += 8192u)
+        bulk_load(c.sbase + c.L.c + o, reinterpret_cast<const char*>(p.img) + o, min(8192u, p.img_bytes - o),
+                  c.bar(B_C_FULL));
+      int armed = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int ig = ig0 + i;
+        const int s = ig % p.stages;
+        if (!mbar_wait(c.bar(B_EMPTY(s)), ((ig / p.stages) & 1) ^ 1, c.abort_flag, p.err, 2101)) break;
+        const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+        const unsigned char* src = p.Xs + (size_t)tile * p.tile_bytes;
+        mbar_expect_tx(c.bar(B_FULL(s)), p.tile_bytes);
+        for (uint32_t o = 0; o < p.tile_bytes; o += 8192u)
+          bulk_load(c.sbase + (uint32_t)s * p.stage_bytes + o, src + o, min(8192u, p.tile_bytes - o),
+                    c.bar(B_FULL(s)));
+        armed = i + 1;
+      }
+      // our own copies must land before the CTA may go on
+      volatile int no_abort = 0;
+      mbar_wait(c.bar(B_C_FULL), par, &no_abort, p.err, 2102);
+      for (int i = (armed > p.stages ? armed - p.stages : 0); i < armed; ++i) {
+        const int ig = ig0 + i;
+        mbar_wait(c.bar(B_FULL(ig % p.stages)), (ig / p.stages) & 1, &no_abort, p.err, 2103);
+      }
+    }
+  } else if (warp == MMA_W0 || warp == MMA_W1) {
+    // ---------------------------------------------------------- MMA issuers
+    const int t = warp == MMA_W0 ? 0 : 1;
+    if (lane == 0 && t < c.n_iss) {
+      bool ok = mbar_wait(c.bar(B_C_FULL), par, c.abort_flag, p.err, 2201);
+      for (int i = (t - ig0 % c.n_iss + c.n_iss) % c.n_iss; ok && i < my_tiles; i += c.n_iss) {
+        const int ig = ig0 + i;
+        const int s = ig % p.stages, a = ig % p.nacc;
+        if (!mbar_wait(c.bar(B_ACC_EMPTY(a)), ((ig / p.nacc) & 1) ^ 1, c.abort_flag, p.err, 2203)) break;
+        // A parity wait is only exact while the waiter is at most one phase
+        // away from the barrier. With two issuers and an odd number of stages,
+        // the previous use of stage s belongs to the other issuer, and copies
+        // can land out of order, so FULL(s) alone could still show the phase
+        // of use u - 2. Waiting first for the previous use to be consumed
+        // (EMPTY(s), phase u - 1, as the producer does; this issuer's own MMAs
+        // of use u - 2 completed before its accumulator of tile i was freed)
+        // pins FULL(s) to phase u - 1 or u.
+        if (!mbar_wait(c.bar(B_EMPTY(s)), ((ig / p.stages) & 1) ^ 1, c.abort_flag, p.err, 2204)) break;
+        if (!mbar_wait(c.bar(B_FULL(s)), (ig / p.stages) & 1, c.abort_flag, p.err, 2202)) break;
+        tc_fence_after();
+        issue_tile_mmas(c.tmem_base + (uint32_t)(a * p.acc_cols), c.sbase + (uint32_t)s * p.stage_bytes,
+                        c.sbase + c.L.c, p.nk, p.k_pad, p.stacked);
+        tc_commit(c.bar(B_EMPTY(s)));  // the stage is no longer read by the tensor core
+        tc_commit(c.bar(B_ACC_FULL(a)));
+      }
+      // every tcgen05 operation issued by this thread is complete once DONE fires
+      tc_commit(c.bar(B_DONE(t)));
+      volatile int no_abort = 0;
+      mbar_wait(c.bar(B_DONE(t)), par, &no_abort, p.err, 2206);
+    }
+  } else if (warp >= EPI_W0) {
+    // ----------------------------------------------------------------- epilogue
+    // groups of four warps (one per TMEM lane quarter) take the tiles of their
+    // accumulator; each warp scans all clusters of its 32 rows
+    const int q = warp & 3;
+    const int g = (warp - EPI_W0) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // dist = ||c||^2 - 2 x.c with x.c = acc * 2^-(xexp + cexp)
+    const float negscale = -ldexpf(1.0f, 1 - __ldcg(p.sexp) - __ldcg(p.sexp + 1));
+    const int i0 = g < c.n_grp ? (g - ig0 % c.n_grp + c.n_grp) % c.n_grp : my_tiles;
+    int old_next = -1;
+    if (changed && i0 < my_tiles) {
+      const long long g0 = (long long)((int)blockIdx.x + i0 * (int)gridDim.x) * BM + row;
+      old_next = g0 < p.n ? p.labels[g0] : -1;
+    }
+    for (int i = i0; i < my_tiles; i += c.n_grp) {
+      const int ig = ig0 + i;
+      const int a = ig % p.nacc;
+      const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
+      const int old = old_next;
+      if (changed && i + c.n_grp < my_tiles) {  // prefetch the next tile's previous labels
+        const long long g1 = grow + (long long)c.n_grp * gridDim.x * BM;
+        old_next = g1 < p.n ? p.labels[g1] : -1;
+      }
+      if (!mbar_wait(c.bar(B_ACC_FULL(a)), (ig / p.nacc) & 1, c.abort_flag, p.err, 2401)) break;
+      tc_fence_after();
+      const uint32_t taddr = c.tmem_base + lane_off + (uint32_t)(a * p.acc_cols);
+      // four independent running minima (columns j = 4m + u), merged in index order
+      float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+      int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
+      for (int jb = 0; jb < p.k_pad; jb += 16) {
+        uint32_t v[16], w[16];
+        // tcgen05.ld / wait::ld are .sync.aligned: the running minima below
+        // branch per lane, so the warp reconverges before each load
+        __syncwarp();
+        tmem_ld16(taddr + (uint32_t)jb, v);
+        if (p.stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + jb), w);
+        tmem_ld_wait16(v);
+        if (p.stacked) reg_pin16(w);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = jb + jj;
+          float dot = __uint_as_float(v[jj]);
+          if (p.stacked) dot += __uint_as_float(w[jj]);
+          const float dist = fmaf(dot, negscale, c.bias_s[j]);
+          if (dist < bd[jj & 3]) {
+            bd[jj & 3] = dist;
+            bi[jj & 3] = j;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(c.bar(B_ACC_EMPTY(a)));
+      float best = bd[0];
+      int bl = bi[0];
+#pragma unroll
+      for (int u = 1; u < 4; ++u)
+        if (better(bd[u], bi[u], best, bl)) {
+          best = bd[u];
+          bl = bi[u];
+        }
+      if (bl >= p.k) bl = 0;  // only reachable when every distance is +inf or NaN
+      bool ch = false;
+      if (grow < p.n) {
+        ch = changed && old != bl;
+        p.labels[grow] = bl;
+      }
+      if (changed) {
+        const unsigned int m = __ballot_sync(0xffffffffu, ch);
+        if (lane == 0 && m) atomicAdd(changed, (unsigned long long)__popc(m));
+        if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st->scale);
+      }
+    }
+  }
+  // the single-lane roles leave warps 0-2 diverged: reconverge before the
+  // caller's block barriers
+  __syncwarp();
+}
+
+
+// Launch parameters of a plan; the per-launch operands (image, scales, bias,
+// labels, changed, D, fit state, error word) are filled in by the caller.
+inline Params make_params(const TcPlan& plan) {
+  Params p{};
+  p.n_tiles = (int)((plan.n + BM - 1) / BM);
+  p.n = plan.n;
+  p.k = plan.k;
+  p.k_pad = plan.k_pad;
+  p.nk = plan.k_steps;
+  p.stacked = plan.stacked;
+  p.stages = plan.stages;
+  p.nacc = plan.nacc;
+  p.acc_cols = plan.acc_cols;
+  p.tmem_cols = plan.tmem_cols;
+  p.stage_bytes = plan.stage_bytes;
+  p.img_bytes = plan.img_bytes;
+  p.tile_bytes = (uint32_t)(plan.k_steps * CHUNK_BYTES);
+  p.Xs = plan.Xs;
+  p.X = plan.X;
+  p.ld = plan.ld;
+  p.d = plan.d;
+  return p;
+}
+
+}  // namespace tc
+
+}  // namespace skm

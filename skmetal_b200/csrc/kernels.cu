@@ -12,81 +12,13 @@
 //   strict convergence / tol / max_iter       (_kmeans.py:705-758)
 #include "kernels.cuh"
 #include "device_util.cuh"
+#include "mstep_dev.cuh"
 
 #include <cfloat>
 #include <cmath>
 
 namespace skm {
 
-// ---------------------------------------------------------------------------
-// helpers
-// ---------------------------------------------------------------------------
-
-// Bounded software grid barrier for cooperative launches. Returns false (and
-// records an error in the fit state) if the other blocks do not arrive within
-// the spin limit, so that a broken launch ends instead of hanging the GPU.
-__device__ bool grid_barrier(FitState* st, unsigned int nblocks) {
-  __shared__ int ok_s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    volatile unsigned int* genp = &st->barrier_gen;
-    unsigned int gen = *genp;
-    __threadfence();
-    unsigned int arrived = atomicAdd(&st->barrier_count, 1u) + 1u;
-    if (arrived == nblocks) {
-      atomicExch(&st->barrier_count, 0u);
-      __threadfence();
-      atomicAdd(&st->barrier_gen, 1u);
-    } else {
-      long long spins = 0;
-      while (*genp == gen) {
-        if (++spins > (1LL << 25)) {
-          atomicExch(&st->error, 1001);
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    __threadfence();
-    ok_s = ok;
-  }
-  __syncthreads();
-  return ok_s != 0;
-}
-
-template <typename T>
-__device__ __forceinline__ T warp_sum(T v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// Deterministic block sum (fixed tree); result valid in thread 0.
-__device__ double block_sum_f64(double v, double* scratch /* >= 32 */) {
-  v = warp_sum(v);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  double r = 0.0;
-  if (warp == 0) {
-    const int nw = (blockDim.x + 31) >> 5;
-    r = lane < nw ? scratch[lane] : 0.0;
-    r = warp_sum(r);
-  }
-  __syncthreads();
-  return r;
-}
-
-// Sum of v[0, n) in a fixed order for a given block size: thread t adds v[t],
-// v[t + blockDim.x], ... in index order, then the fixed block tree; result
-// valid in thread 0. All threads of the block must call it.
-__device__ double block_ordered_sum(const double* v, int n, double* scratch) {
-  double t = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) t += v[i];
-  return block_sum_f64(t, scratch);
-}
 
 // ---------------------------------------------------------------------------
 // data preparation
@@ -161,14 +93,14 @@ __global__ void colsum_fixed_kernel(const float* __restrict__ X, int ld, long lo
     }
   }
   for (int i = threadIdx.x; i < ld; i += blockDim.x) cs_acc[i] = 0;
-  __syncthreads();
+  block_sync();
   if (rg < g) {
     atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 0]), (unsigned long long)a0);
     atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 1]), (unsigned long long)a1);
     atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 2]), (unsigned long long)a2);
     atomicAdd(reinterpret_cast<unsigned long long*>(&cs_acc[4 * c4 + 3]), (unsigned long long)a3);
   }
-  __syncthreads();
+  block_sync();
   for (int i = threadIdx.x; i < ld; i += blockDim.x)
     if (cs_acc[i] != 0) red_add_s64(&colsum[i], cs_acc[i]);
 }
@@ -375,9 +307,9 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
   int bl = 0;
   for (int c0 = 0; c0 < k; c0 += chunk) {
     const int cn = min(chunk, k - c0);
-    __syncthreads();
+    block_sync();
     for (int i = threadIdx.x; i < cn * ld; i += blockDim.x) csh[i] = C[(long long)c0 * ld + i];
-    __syncthreads();
+    block_sync();
     if (active) {
       for (int c = 0; c < cn; ++c) {
         const float* cr = csh + c * ld;
@@ -426,7 +358,7 @@ __global__ void assign_small_kernel(const float* __restrict__ X, int ld, long lo
                                     int32_t* __restrict__ labels, float* __restrict__ mind) {
   extern __shared__ float csh[];
   for (int i = threadIdx.x; i < k * D; i += blockDim.x) csh[i] = C[(i / D) * ld + (i % D)];
-  __syncthreads();
+  block_sync();
   for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n;
        r += (long long)gridDim.x * blockDim.x) {
     float x[D];
@@ -462,303 +394,27 @@ bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream
   }
 }
 
-// ---------------------------------------------------------------------------
-// bulk fixed-point sums from the labels into the delta buffer D (zero on entry)
-// ---------------------------------------------------------------------------
-
-// Bulk fixed-point sums of all rows by label, X blocked. A work item is a
-// group of 32 rows of one tile (lane = row) that walks the tile's quads, so
-// every warp load is 512 contiguous bytes. With `smem_acc` the block adds into
-// a private k x ld (+ k counts) int64 copy in shared memory (integer atomics)
-// and flushes it with one global reduction per nonzero entry; otherwise it
-// adds straight into D. Integer sums are exact, so the result does not depend
-// on the order or the grid.
-// Fixed-point sums and counts of all rows by label, added into
-// D = [dS (k x ld) | dcount (k)], which must be zero. A warp takes 8
-// consecutive rows at a time; lane (rsub, qsub) = (lane % 8, lane / 8) reads
-// column quad 4 m + qsub of row rsub, so each load instruction fetches four
-// whole 128-byte lines of the blocked layout (8 rows x 16 bytes per quad) and
-// uses them at once. With `acc` (shared, k*ld + k int64) the block
-// accumulates privately in the layout [u][c][q] (column 4q + u of cluster c)
-// and adds its non-zero entries to D at the end; without, it adds to D
-// directly. Integer additions are exact, so the result does not depend on
-// their order.
-__device__ __forceinline__ void bulk_pass(const float* __restrict__ X, int ld, long long n,
-                                          const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                          double scale, long long* acc) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int rsub = lane & 7, qsub = lane >> 3;
-  const int nq = ld >> 2;
-  const long long ks = (long long)k * ld;
-  if (acc) {
-    for (long long i = threadIdx.x; i < ks + k; i += blockDim.x) acc[i] = 0;
-    __syncthreads();
-  }
-  const float4* X4 = reinterpret_cast<const float4*>(X);
-  const long long blocks8 = (n + 7) / 8;
-  for (long long b = (long long)blockIdx.x * nw + warp; b < blocks8; b += (long long)gridDim.x * nw) {
-    const long long r = b * 8 + rsub;
-    const bool valid = r < n;
-    const int c = valid ? labels[r] : 0;
-    const float4* xr = X4 + (r >> 7) * (32LL * ld) + (r & 127);  // quad q of row r at xr[128 q]
-    for (int q0 = 0; q0 < nq; q0 += 4) {
-      const int q = q0 + qsub;
-      if (!valid || q >= nq) continue;
-      const float4 v = __ldcs(xr + (long long)q * 128);
-      const long long f[4] = {to_fixed(v.x, scale), to_fixed(v.y, scale), to_fixed(v.z, scale),
-                              to_fixed(v.w, scale)};
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (f[u] == 0) continue;
-        if (acc)
-          atomicAdd(reinterpret_cast<unsigned long long*>(&acc[((long long)u * k + c) * nq + q]),
-                    static_cast<unsigned long long>(f[u]));
-        else
-          red_add_s64(D + (long long)c * ld + 4 * q + u, f[u]);
-      }
-    }
-    if (valid && qsub == 0) {
-      if (acc)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&acc[ks + c]), 1ull);
-      else
-        red_add_s64(D + ks + c, 1);
-    }
-  }
-  if (acc) {
-    __syncthreads();
-    for (long long i = threadIdx.x; i < ks + k; i += blockDim.x) {
-      const long long v = acc[i];
-      if (v == 0) continue;
-      long long dst = i;
-      if (i < ks) {  // i = (u * k + c) * nq + q
-        const long long q = i % nq, uc = i / nq;
-        const long long c = uc % k, u = uc / k;
-        dst = c * ld + 4 * q + u;
-      }
-      red_add_s64(D + dst, v);
-    }
-  }
-}
-
-
-// ---------------------------------------------------------------------------
-// M-step (cooperative): empty clusters, relocation, averaging, shift, flags
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ unsigned long long reloc_key(float dist, long long row) {
-  unsigned int b = __float_as_uint(dist);
-  if (b & 0x80000000u) b = 0;  // -0.0 and (impossible) negatives sort as zero
-  return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - (unsigned int)row);
-}
-
-// Selection of the m rows farthest from their assigned centre (largest
-// (distance, -row) keys) by an exact 8-pass radix select over 64-bit keys.
-// Keys are unique, so exactly m rows are collected. Runs inside the
-// cooperative M-step; `hist` holds 2 x 256 counters.
-__device__ bool select_farthest(const float* __restrict__ mind, long long n, long long row_base, int m,
-                                FitState* st, unsigned int* hist, long long* sel, unsigned int nblocks) {
-  __shared__ unsigned int h[256];
-  __shared__ unsigned long long prefix_s, mask_s;
-  __shared__ int remaining_s;
-  unsigned long long prefix = 0, mask = 0;
-  int remaining = m;
-  for (int pass = 0; pass < 8; ++pass) {
-    const int shift = 56 - 8 * pass;
-    unsigned int* gh = hist + (pass & 1) * 256;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
-    __syncthreads();
-    for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)nblocks * blockDim.x) {
-      const unsigned long long key = reloc_key(mind[r], row_base + r);
-      if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < 256; i += blockDim.x)
-      if (h[i]) atomicAdd(&gh[i], h[i]);
-    if (!grid_barrier(st, nblocks)) return false;
-    if (threadIdx.x == 0) {
-      // every block computes the same choice from the same global histogram
-      int cum = 0, digit = 0;
-      for (int dgt = 255; dgt >= 0; --dgt) {
-        const int c = (int)gh[dgt];
-        if (cum + c >= remaining) { digit = dgt; break; }
-        cum += c;
-      }
-      prefix_s = prefix | ((unsigned long long)digit << shift);
-      mask_s = mask | (255ull << shift);
-      remaining_s = remaining - cum;
-    }
-    __syncthreads();
-    prefix = prefix_s;
-    mask = mask_s;
-    remaining = remaining_s;
-    // clear the other histogram for the next pass (nobody reads it until the
-    // next barrier)
-    if (blockIdx.x == 0) {
-      unsigned int* oh = hist + ((pass + 1) & 1) * 256;
-      for (int i = threadIdx.x; i < 256; i += blockDim.x) oh[i] = 0;
-    }
-    if (!grid_barrier(st, nblocks)) return false;
-  }
-  // prefix is now the m-th largest key: collect keys >= prefix (exactly m)
-  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)nblocks * blockDim.x) {
-    const unsigned long long key = reloc_key(mind[r], row_base + r);
-    if (key >= prefix) {
-      const int slot = atomicAdd(&st->sel_count, 1);
-      if (slot < m) sel[slot] = r;
-    }
-  }
-  return grid_barrier(st, nblocks);
-}
-
-// Averaged centre value of a non-empty cluster c (after relocation), column j.
-__device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, int n_reloc) {
-  for (int i = 0; i < n_reloc; ++i)
-    if (a.empty_ids[i] == c) return a.reloc_x[(long long)i * a.ld + j];  // exactly the far row
-  long long s = a.S[(long long)c * a.ld + j];
-  for (int i = 0; i < n_reloc; ++i)
-    if (a.reloc_label[i] == c) s -= to_fixed(a.reloc_x[(long long)i * a.ld + j], a.st->scale);
-  return centre_from_sum(s, centre_factor(a.st->inv_scale, a.cnt_adj[c]));
-}
-
-// One centre (cluster c, columns strided over the calling warp's lanes):
-// writes C_new, its centre-image entries and returns (shift^2, ||c||^2)
-// summed in a fixed order (lane partials, then a fixed butterfly).
-__device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, int src, int n_reloc, double* dsq_out,
-                                            double* nrm_out) {
-  const int lane = threadIdx.x & 31;
-  const float cs = ldexpf(1.0f, a.st->xexp);  // centres are bounded by max |x|
-  double dsq = 0.0, nrm = 0.0;
-  for (int j = lane; j < a.ld; j += 32) {
-    float v = 0.0f;
-    if (j < a.d) {
-      v = centre_value(a, src, j, n_reloc);
-      const double df = (double)v - (double)a.C_old[(long long)c * a.ld + j];
-      dsq += df * df;
-      nrm += (double)v * v;
-      if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
-    }
-    a.C_new[(long long)c * a.ld + j] = v;
-  }
-  *dsq_out = warp_sum(dsq);
-  *nrm_out = warp_sum(nrm);
-}
-
-// Convergence bookkeeping (_kmeans.py:723-741) from the per-cluster squared
-// shifts summed in a fixed order; one thread. The centre image now holds
-// centres scaled by 2^xexp.
-__device__ void finish_iteration(const MStepArgs& a, FitState* st, unsigned long long changed_now, double tot) {
-  st->cexp = st->xexp;
-  st->bulk = st->bulk_always || changed_now > (unsigned long long)st->bulk_threshold;
-  st->shift_tot = tot;
-  st->iter += 1;
-  if (changed_now == 0) {
-    st->strict = 1;
-    st->done = 1;
-  } else if (tot <= st->tol) {
-    st->done = 1;
-  }
-  if (st->iter >= st->max_iter) st->done = 1;
-  *const_cast<unsigned long long*>(a.changed) = 0;
-  if (a.host_done) *a.host_done = st->done ? st->iter : 0;
-}
-
-// Direct float32 squared distance of every local row to its (new) label's old
-// centre, ((X - centers_old[labels])**2).sum(axis=1) (_k_means_common.pyx:185),
-// into a.mind. Blocked X: lane per row of a 32-row group, columns in order.
-__device__ void rows_dist_to_old_centres(const MStepArgs& a, unsigned int nb) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  float* mind = const_cast<float*>(a.mind);
-  const long long items = (a.n + 31) / 32;
-  const float4* X4 = reinterpret_cast<const float4*>(a.X);
-  for (long long it = blockIdx.x * (long long)nwarps + warp; it < items; it += (long long)nb * nwarps) {
-    const long long r = it * 32 + lane;
-    if (r >= a.n) continue;
-    const float4* xp = X4 + (r >> 7) * (32LL * a.ld) + (r & 127);
-    const float* cr = a.C_old + (long long)a.labels[r] * a.ld;
-    float s = 0.0f;
-    for (int q = 0; q < (a.ld >> 2); ++q) {
-      const float4 v = xp[(long long)q * 128];
-      float t = v.x - cr[4 * q];
-      s = fmaf(t, t, s);
-      t = v.y - cr[4 * q + 1];
-      s = fmaf(t, t, s);
-      t = v.z - cr[4 * q + 2];
-      s = fmaf(t, t, s);
-      t = v.w - cr[4 * q + 3];
-      s = fmaf(t, t, s);
-    }
-    mind[r] = s;
-  }
-}
-
-// Number of empty clusters after this iteration's sums (bulk iterations: the
-// sums in D alone); every block of the caller computes the same value.
-__device__ int count_empty(const MStepArgs& a, int bulk) {
-  const long long* dcnt = a.D + (long long)a.k * a.ld;
-  int total = 0;
-  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
-    const int c = c0 + threadIdx.x;
-    const bool e = c < a.k && (bulk ? 0 : a.counts[c]) + dcnt[c] == 0;
-    total += __syncthreads_count(e);
-  }
-  return total;
-}
 
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // the E-step's labels, deltas and counters
   FitState* st = a.st;
   const unsigned int nb = gridDim.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const long long ks = (long long)a.k * a.ld;
   const long long* dcnt = a.D + ks;
   const int done = st->done;  // uniform: `done` is only written at the very end
   const unsigned long long changed_now = *a.changed;  // cleared at the end
   const int bulk = st->bulk;  // D holds the sums of all rows (replace S), not deltas
-  long long cnt0 = 0, dcnt0 = 0;  // cluster threadIdx.x
-  if ((int)threadIdx.x < a.k) {
-    cnt0 = a.counts[threadIdx.x];
-    dcnt0 = dcnt[threadIdx.x];
-  }
   if (done) return;
   extern __shared__ __align__(16) long long dyn_smem[];
-  if (bulk) {
-    if (!a.bulk_external) {
-      bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, bulk_in_smem(a.k, a.ld) ? dyn_smem : nullptr);
-      if (!grid_barrier(st, nb)) return;
-      if ((int)threadIdx.x < a.k) dcnt0 = dcnt[threadIdx.x];
-    }
-    cnt0 = 0;
+  if (bulk && !a.bulk_external) {
+    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale,
+              bulk_acc_bytes(a.k, a.ld, kBulkSmemBytes) ? dyn_smem : nullptr);
+    if (!grid_barrier(st, nb)) return;
   }
-  __shared__ int n_empty_s;
-  __shared__ int wcount[32];
-  __shared__ long long hv_cnt[32];
-  __shared__ int hv_idx[32];
   __shared__ double red_scratch[32];
-
-  // 1. empty clusters of the new assignment (counts + this iteration's
-  //    deltas), ascending ids; every block computes the same answer
-  if (threadIdx.x == 0) n_empty_s = 0;
-  __syncthreads();
-  for (int c0 = 0; c0 < a.k; c0 += blockDim.x) {
-    const int c = c0 + threadIdx.x;
-    const bool e = c < a.k && (c0 == 0 ? cnt0 + dcnt0 : (bulk ? 0 : a.counts[c]) + dcnt[c]) == 0;
-    const unsigned int b = __ballot_sync(0xffffffffu, e);
-    if (lane == 0) wcount[warp] = __popc(b);
-    __syncthreads();
-    int base = n_empty_s;
-    for (int w = 0; w < warp; ++w) base += wcount[w];
-    const int pos = base + __popc(b & ((1u << lane) - 1u));
-    if (e && blockIdx.x == 0 && pos < kMaxEmptyCap) a.empty_ids[pos] = c;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int t = 0;
-      for (int w = 0; w < nwarps; ++w) t += wcount[w];
-      n_empty_s += t;
-    }
-    __syncthreads();
-  }
-  const int n_empty = n_empty_s;
+  // 1. empty clusters of the new assignment; every block computes the same answer
+  const int n_empty = find_empty_clusters(a, bulk);
 
   if (n_empty == 0) {
     // ---------------- fast path: no relocation. Units of (cluster, column
@@ -805,7 +461,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
         a.unit_dsq[u] = dsq;
         a.unit_nrm[u] = nrm;
       }
-      __syncthreads();
+      block_sync();
     }
     // the last block to get here reduces and finishes the iteration
     __shared__ int last_s;
@@ -813,7 +469,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
       __threadfence();
       last_s = atomicAdd(&st->ticket, 1u) == nb - 1;
     }
-    __syncthreads();
+    block_sync();
     if (!last_s) return;
     __threadfence();
     double* dsq_c = a.shift_partial;  // k entries
@@ -833,7 +489,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
       if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
       if (a.bias) a.bias[c] = (float)nrm;
     }
-    __syncthreads();
+    block_sync();
     const double tot = block_ordered_sum(dsq_c, a.k, red_scratch);
     if (threadIdx.x == 0) {
       st->ticket = 0;
@@ -844,154 +500,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     return;
   }
 
-  // ---------------- relocation path (cooperative, all blocks)
-  // 0. S += dS, counts += dcount (bulk: S = dS, counts = dcount); clear the
-  //    deltas (all but `changed`)
-  {
-    long long* S = const_cast<long long*>(a.S);
-    long long* cnt = const_cast<long long*>(a.counts);
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + a.k;
-         i += (long long)nb * blockDim.x) {
-      const long long v = a.D[i];
-      if (bulk) {
-        if (i < ks) S[i] = v;
-        else cnt[i - ks] = v;
-        if (v != 0) a.D[i] = 0;
-      } else if (v != 0) {
-        if (i < ks) S[i] += v;
-        else cnt[i - ks] += v;
-        a.D[i] = 0;
-      }
-    }
-  }
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    st->n_empty = n_empty;
-    st->sel_count = 0;
-    if (n_empty > kMaxEmptyCap) atomicExch(&st->error, 1002);
-  }
-  if (n_empty > kMaxEmptyCap) return;  // uniform
-  if (!grid_barrier(st, nb)) return;
-
-  // 2. the n_empty rows farthest from their centre, paired in decreasing
-  //    (distance, -row) order with the ascending empty ids
-  if (a.cand == nullptr) {
-    rows_dist_to_old_centres(a, nb);
-    if (!grid_barrier(st, nb)) return;
-    if (!select_farthest(a.mind, a.n, a.row_base, n_empty, st, a.hist, a.sel, nb)) return;
-    if (blockIdx.x == 0) {
-      for (int i = threadIdx.x; i < n_empty; i += blockDim.x) {
-        const float di = a.mind[a.sel[i]];
-        const unsigned long long ki = reloc_key(di, a.row_base + a.sel[i]);
-        int rank = 0;
-        for (int j = 0; j < n_empty; ++j)
-          if (reloc_key(a.mind[a.sel[j]], a.row_base + a.sel[j]) > ki) ++rank;
-        const long long r = a.sel[i];
-        a.reloc_dist[rank] = di;
-        a.reloc_label[rank] = a.labels[r];
-        for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
-      }
-    }
-  } else {
-    // candidates of every rank (the same bytes on every rank): rank r's block
-    // at cand + r * cand_block_bytes; its first `count` entries are valid
-    const size_t cb = cand_block_bytes(a.cand_cap, a.ld);
-    const int total = a.cand_ranks * a.cand_cap;
-    int valid_total = 0, overflow = 0;
-    for (int r = 0; r < a.cand_ranks; ++r) {
-      const int cnt = *reinterpret_cast<const int*>(a.cand + r * cb);
-      if (cnt < 0) overflow = 1;
-      else valid_total += cnt;
-    }
-    if (overflow || n_empty > a.cand_cap || valid_total < n_empty) {  // uniform over blocks and ranks
-      if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&st->error, 1003);
-      return;
-    }
-    if (blockIdx.x == 0) {
-      for (int t = threadIdx.x; t < total; t += blockDim.x) {
-        const int r = t / a.cand_cap, i = t % a.cand_cap;
-        const unsigned char* blk = a.cand + r * cb;
-        if (i >= *reinterpret_cast<const int*>(blk)) continue;
-        const float di = reinterpret_cast<const float*>(blk + cand_dist_off(a.cand_cap))[i];
-        const long long gi = reinterpret_cast<const long long*>(blk + cand_row_off(a.cand_cap))[i];
-        const unsigned long long ki = reloc_key(di, gi);
-        int rank = 0;
-        for (int u = 0; u < total; ++u) {
-          const int r2 = u / a.cand_cap, i2 = u % a.cand_cap;
-          const unsigned char* b2 = a.cand + r2 * cb;
-          if (i2 >= *reinterpret_cast<const int*>(b2)) continue;
-          const float dj = reinterpret_cast<const float*>(b2 + cand_dist_off(a.cand_cap))[i2];
-          const long long gj = reinterpret_cast<const long long*>(b2 + cand_row_off(a.cand_cap))[i2];
-          if (reloc_key(dj, gj) > ki) ++rank;
-        }
-        if (rank < n_empty) {
-          a.reloc_dist[rank] = di;
-          a.reloc_label[rank] = reinterpret_cast<const int*>(blk + cand_label_off(a.cand_cap))[i];
-          const float* xs = reinterpret_cast<const float*>(blk + cand_x_off(a.cand_cap)) + (long long)i * a.ld;
-          for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = xs[j];
-        }
-      }
-    }
-  }
-  if (!grid_barrier(st, nb)) return;
-  // no relocation when every distance is zero (_k_means_common.pyx:192-194)
-  const int n_reloc = a.reloc_dist[0] > 0.0f ? n_empty : 0;
-
-  // 3. counts after relocation (block 0), then the heaviest cluster (first max)
-  if (blockIdx.x == 0) {
-    for (int c = threadIdx.x; c < a.k; c += blockDim.x) a.cnt_adj[c] = a.counts[c];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int i = 0; i < n_reloc; ++i) {
-        a.cnt_adj[a.reloc_label[i]] -= 1;
-        a.cnt_adj[a.empty_ids[i]] += 1;
-      }
-      st->relocated = n_reloc;
-    }
-  }
-  if (!grid_barrier(st, nb)) return;
-  long long bc = -1;
-  int bi = 0;
-  for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
-    const long long v = a.cnt_adj[c];
-    if (v > bc) { bc = v; bi = c; }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const long long ov = __shfl_xor_sync(0xffffffffu, bc, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bc || (ov == bc && oi < bi)) { bc = ov; bi = oi; }
-  }
-  if (lane == 0) { hv_cnt[warp] = bc; hv_idx[warp] = bi; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < nwarps; ++w)
-      if (hv_cnt[w] > hv_cnt[0] || (hv_cnt[w] == hv_cnt[0] && hv_idx[w] < hv_idx[0])) {
-        hv_cnt[0] = hv_cnt[w];
-        hv_idx[0] = hv_idx[w];
-      }
-  }
-  __syncthreads();
-  const int heavy = hv_idx[0];
-
-  // 4. new centres (one warp per cluster) and their squared shifts
-  double* dsq_s = a.shift_partial;
-  for (int c = blockIdx.x * nwarps + warp; c < a.k; c += nb * nwarps) {
-    double dsq, nrm;
-    warp_centre(a, c, a.cnt_adj[c] > 0 ? c : heavy, n_reloc, &dsq, &nrm);
-    if (lane == 0) {
-      dsq_s[c] = dsq;
-      if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
-      if (a.bias) a.bias[c] = (float)nrm;
-    }
-  }
-  if (!grid_barrier(st, nb)) return;
-
-  // 5. convergence bookkeeping
-  if (blockIdx.x == 0) {
-    __shared__ double red_scratch[32];
-    const double tot = block_ordered_sum(dsq_s, a.k, red_scratch);
-    if (threadIdx.x == 0) finish_iteration(a, st, changed_now, tot);
-  }
+  relocation_path(a, n_empty, bulk, changed_now);
 }
 
 // Multi-GPU fits, between the E-step and the all-reduce of the payload
@@ -1015,7 +524,9 @@ __global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long l
   if (st->done) return;
   const int bulk = st->bulk;
   extern __shared__ __align__(16) long long dyn_smem[];
-  if (bulk) bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, bulk_in_smem(a.k, a.ld) ? dyn_smem : nullptr);
+  if (bulk)
+    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale,
+              bulk_acc_bytes(a.k, a.ld, kBulkSmemBytes) ? dyn_smem : nullptr);
   if (!grid_barrier(st, nb)) return;
   // local counts after this iteration, and how many clusters this rank has empty
   const long long* dcnt = a.D + (long long)a.k * a.ld;
@@ -1024,6 +535,7 @@ __global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long l
     const int c = c0 + threadIdx.x;
     long long v = 0;
     if (c < a.k) v = (bulk ? 0 : local_counts[c]) + dcnt[c];
+    __syncwarp();
     n_local_empty += __syncthreads_count(c < a.k && v == 0);
     if (blockIdx.x == 0 && c < a.k) a.cnt_adj[c] = v;  // staged: written back after the barrier
   }
@@ -1065,13 +577,13 @@ __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, i
   if (st->done || blockIdx.x != 0) return;
   __shared__ unsigned int mx_s;
   if (threadIdx.x == 0) mx_s = 0;
-  __syncthreads();
+  block_sync();
   unsigned int m = 0;
   for (long long i = threadIdx.x; i < (long long)k * ld; i += blockDim.x)
     if ((int)(i % ld) < d) m = max(m, __float_as_uint(C[i]) & 0x7fffffffu);
   m = min(m, 0x7f800000u);
   atomicMax(&mx_s, m);
-  __syncthreads();
+  block_sync();
   const int cexp = split_exp(mx_s);
   const float cs = ldexpf(1.0f, cexp);
   if (threadIdx.x == 0) st->cexp = cexp;

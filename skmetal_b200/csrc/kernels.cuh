@@ -11,8 +11,11 @@ namespace skm {
 constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
 constexpr size_t kBulkSmemBytes = 160 * 1024;  // bulk pass accumulates privately when (k*ld + k) int64 fit
 
-__host__ __device__ inline bool bulk_in_smem(int k, int ld) {
-  return sizeof(long long) * ((size_t)k * ld + k) <= kBulkSmemBytes;
+// The bulk pass's private accumulator: (k*ld + k) int64 when they fit in
+// `avail` bytes of shared memory, else 0 (sums go straight to global memory).
+__host__ __device__ inline size_t bulk_acc_bytes(int k, int ld, size_t avail) {
+  const size_t b = sizeof(long long) * ((size_t)k * ld + k);
+  return b <= avail ? b : 0;
 }
 
 // Relocation candidates of one rank (multi-GPU fits), one slot per rank after
@@ -37,9 +40,7 @@ __host__ __device__ inline size_t cand_x_off(int cap) { return 16 + (size_t)cap 
 constexpr int kBulkDivisor = 10;
 
 // Dynamic shared memory of mstep_kernel for k clusters of ld columns.
-inline size_t mstep_smem_bytes(int k, int ld) {
-  return bulk_in_smem(k, ld) ? sizeof(long long) * ((size_t)k * ld + k) : 0;
-}
+inline size_t mstep_smem_bytes(int k, int ld) { return bulk_acc_bytes(k, ld, kBulkSmemBytes); }
 
 
 struct MStepArgs {

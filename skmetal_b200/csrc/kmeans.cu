@@ -25,6 +25,7 @@
 #include "driver.h"
 #include "estep_tc.h"
 #include "kernels.cuh"
+#include "loop_tc.h"
 #include "../../include/skmetal_cuda.h"
 
 namespace skm {
@@ -42,6 +43,8 @@ struct FitStats {
   int iterations = 0;
 };
 static thread_local FitStats t_stats;
+// globaltimer stamps of the last profiled persistent-loop fit (lloyd_loop_kernel)
+static thread_local std::vector<unsigned long long> t_loop_stamps;
 
 struct Dataset {
   int device = 0;
@@ -400,72 +403,110 @@ static int run_fit(const FitParams& p) {
     SKM_CUDA(cudaMemsetAsync(local_counts, 0, sizeof(long long) * k, s));
   }
 
-  const int chunk = 8;
-  int it = 0, chunk_idx = 0, pending = -1;
-  bool done_seen = false;
-  cudaEvent_t chunk_ev[2];
-  SKM_CUDA(cudaEventCreateWithFlags(&chunk_ev[0], cudaEventDisableTiming));
-  SKM_CUDA(cudaEventCreateWithFlags(&chunk_ev[1], cudaEventDisableTiming));
-  struct ChunkGuard {
-    cudaEvent_t* e;
-    ~ChunkGuard() {
-      cudaEventDestroy(e[0]);
-      cudaEventDestroy(e[1]);
+  // One GPU with the tensor-core E-step: the persistent loop kernel runs
+  // every iteration in one launch (SKMETAL_LOOP=launches selects the
+  // multi-launch loop instead; both give bit-identical fits).
+  const char* loop_env = getenv("SKMETAL_LOOP");
+  const bool launches_loop = loop_env && strcmp(loop_env, "launches") == 0;
+  const bool persistent = plan.tc && !comm && !p.single_step && !launches_loop && tc_loop_supported(plan.tcp);
+  std::vector<unsigned long long> prof_stamps;
+  if (persistent) {
+    long long *D2 = nullptr, *counts2 = nullptr;
+    SKM_TRY(buf.alloc_n(&D2, d_len));
+    SKM_TRY(buf.alloc_n(&counts2, (size_t)k));
+    SKM_CUDA(cudaMemsetAsync(D2, 0, sizeof(long long) * d_len, s));
+    SKM_CUDA(cudaMemsetAsync(counts2, 0, sizeof(long long) * k, s));
+    unsigned long long* prof_d = nullptr;
+    if (p.profile) {
+      prof_stamps.assign(4 * (size_t)p.max_iter + 1, 0);
+      SKM_TRY(buf.alloc_n(&prof_d, prof_stamps.size()));
+      SKM_CUDA(cudaMemsetAsync(prof_d, 0, sizeof(unsigned long long) * prof_stamps.size(), s));
     }
-  } cg{chunk_ev};
-
-  auto wait_event = [&](cudaEvent_t e) -> int {
-    if (!comm) {
-      SKM_CUDA(cudaEventSynchronize(e));
-      return OK;
-    }
-    return comm_wait_event(comm, e);
-  };
-
-  while (it < p.max_iter && !done_seen) {
-    const int end = std::min(p.max_iter, it + chunk);
-    for (; it < end; ++it) {
-      const float* Cin = (it & 1) ? Cb1 : Cb0;
-      float* Cout = (it & 1) ? Cb0 : Cb1;
-      const bool timed = p.profile && it % kProfileEvery == 0;
-      if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
-      // Iterations flagged `bulk` on the device (the first one, and those
-      // after an iteration that changed many rows) rebuild the sums from all
-      // rows; the others add the deltas of the rows that changed label.
-      if (plan.tc) {
-        SKM_TRY(tc_estep(plan.tcp, cimg.img, &st->xexp, bias, labels, changed, D, st, dev_err, s, !comm && !timed));
-      } else {
-        SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, D, 0, 1, s));
+    LoopInputs li{};
+    li.img = cimg.img;
+    li.sexp = &st->xexp;
+    li.bias = bias;
+    li.D[0] = D;
+    li.D[1] = D2;
+    li.counts[0] = counts;
+    li.counts[1] = counts2;
+    li.C[0] = Cb0;
+    li.C[1] = Cb1;
+    li.m = ma;
+    li.prof = prof_d;
+    SKM_TRY(tc_lloyd_loop(plan.tcp, li, s));
+    SKM_CUDA(cudaEventRecord(ev2, s));
+    if (prof_d)
+      SKM_CUDA(cudaMemcpyAsync(prof_stamps.data(), prof_d, sizeof(unsigned long long) * prof_stamps.size(),
+                               cudaMemcpyDeviceToHost, s));
+  } else {
+    const int chunk = 8;
+    int it = 0, chunk_idx = 0, pending = -1;
+    bool done_seen = false;
+    cudaEvent_t chunk_ev[2];
+    SKM_CUDA(cudaEventCreateWithFlags(&chunk_ev[0], cudaEventDisableTiming));
+    SKM_CUDA(cudaEventCreateWithFlags(&chunk_ev[1], cudaEventDisableTiming));
+    struct ChunkGuard {
+      cudaEvent_t* e;
+      ~ChunkGuard() {
+        cudaEventDestroy(e[0]);
+        cudaEventDestroy(e[1]);
       }
-      if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
-      ma.C_old = Cin;
-      ma.C_new = Cout;
-      if (comm) {
-        // bulk pass, local counts and relocation candidates, then one all-reduce
-        int rank = comm_rank(comm);
-        void* pargs[] = {&ma, &local_counts, &rank};
-        SKM_CUDA(cudaLaunchCooperativeKernel((void*)shard_prep_kernel, dim3(mstep_blocks), dim3(mstep_threads), pargs,
-                                             mstep_smem, s));
-        SKM_TRY(check_launch("shard_prep_kernel"));
-        SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
+    } cg{chunk_ev};
+
+    auto wait_event = [&](cudaEvent_t e) -> int {
+      if (!comm) {
+        SKM_CUDA(cudaEventSynchronize(e));
+        return OK;
       }
-      SKM_TRY(launch_mstep(ma, mstep_blocks, mstep_threads, mstep_smem, !comm && !timed, s));
+      return comm_wait_event(comm, e);
+    };
+
+    while (it < p.max_iter && !done_seen) {
+      const int end = std::min(p.max_iter, it + chunk);
+      for (; it < end; ++it) {
+        const float* Cin = (it & 1) ? Cb1 : Cb0;
+        float* Cout = (it & 1) ? Cb0 : Cb1;
+        const bool timed = p.profile && it % kProfileEvery == 0;
+        if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it], s));
+        // Iterations flagged `bulk` on the device (the first one, and those
+        // after an iteration that changed many rows) rebuild the sums from all
+        // rows; the others add the deltas of the rows that changed label.
+        if (plan.tc) {
+          SKM_TRY(tc_estep(plan.tcp, cimg.img, &st->xexp, bias, labels, changed, D, st, dev_err, s, !comm && !timed));
+        } else {
+          SKM_TRY(launch_assign_simt(X, ld, n, d, Cin, k, labels, nullptr, st, changed, D, 0, 1, s));
+        }
+        if (timed) SKM_CUDA(cudaEventRecord(prof_ev[2 * it + 1], s));
+        ma.C_old = Cin;
+        ma.C_new = Cout;
+        if (comm) {
+          // bulk pass, local counts and relocation candidates, then one all-reduce
+          int rank = comm_rank(comm);
+          void* pargs[] = {&ma, &local_counts, &rank};
+          SKM_CUDA(cudaLaunchCooperativeKernel((void*)shard_prep_kernel, dim3(mstep_blocks), dim3(mstep_threads), pargs,
+                                               mstep_smem, s));
+          SKM_TRY(check_launch("shard_prep_kernel"));
+          SKM_TRY(comm_allreduce_sum_s64(comm, D, payload_len, s));
+        }
+        SKM_TRY(launch_mstep(ma, mstep_blocks, mstep_threads, mstep_smem, !comm && !timed, s));
+      }
+      SKM_CUDA(cudaEventRecord(chunk_ev[chunk_idx & 1], s));
+      if (pending >= 0) {
+        SKM_TRY(wait_event(chunk_ev[pending & 1]));
+        // The M-steps publish the iteration count at convergence (0 while
+        // running). One GPU may stop as soon as it is seen; ranks of a sharded
+        // fit stop only once it falls in a chunk they have all waited for, so
+        // that every rank enqueues the same collectives.
+        const int at = *host_done;
+        const int pending_end = std::min(p.max_iter, (pending + 1) * chunk);
+        if (at > 0 && (!comm || at <= pending_end)) done_seen = true;
+      }
+      pending = chunk_idx++;
     }
-    SKM_CUDA(cudaEventRecord(chunk_ev[chunk_idx & 1], s));
-    if (pending >= 0) {
-      SKM_TRY(wait_event(chunk_ev[pending & 1]));
-      // The M-steps publish the iteration count at convergence (0 while
-      // running). One GPU may stop as soon as it is seen; ranks of a sharded
-      // fit stop only once it falls in a chunk they have all waited for, so
-      // that every rank enqueues the same collectives.
-      const int at = *host_done;
-      const int pending_end = std::min(p.max_iter, (pending + 1) * chunk);
-      if (at > 0 && (!comm || at <= pending_end)) done_seen = true;
-    }
-    pending = chunk_idx++;
+    if (pending >= 0) SKM_TRY(wait_event(chunk_ev[pending & 1]));
+    SKM_CUDA(cudaEventRecord(ev2, s));
   }
-  if (pending >= 0) SKM_TRY(wait_event(chunk_ev[pending & 1]));
-  SKM_CUDA(cudaEventRecord(ev2, s));
 
   FitState hs;
   SKM_CUDA(cudaMemcpyAsync(&hs, st, sizeof(FitState), cudaMemcpyDeviceToHost, s));
@@ -545,7 +586,17 @@ static int run_fit(const FitParams& p) {
   fs.ms_loop = ms;
   cudaEventElapsedTime(&ms, ev2, ev3);
   fs.ms_final = ms;
-  if (p.profile) {
+  if (p.profile && persistent) {
+    // E-step phases of the persistent loop from its globaltimer stamps
+    for (int i = 0; i < iters && 4 * i + 1 < (int)prof_stamps.size(); ++i) {
+      if (prof_stamps[4 * i + 1] > prof_stamps[4 * i]) {
+        fs.estep_ms_sum += (double)(prof_stamps[4 * i + 1] - prof_stamps[4 * i]) * 1e-6;
+        fs.estep_launches += 1;
+      }
+    }
+    prof_stamps.resize(std::min(prof_stamps.size(), 4 * (size_t)iters + 1));
+    t_loop_stamps = prof_stamps;
+  } else if (p.profile) {
     for (int i = 0; i < iters; i += kProfileEvery) {
       float m = 0;
       if (cudaEventElapsedTime(&m, prof_ev[2 * i], prof_ev[2 * i + 1]) == cudaSuccess) {
@@ -915,6 +966,12 @@ int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t 
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   return OK;
+}
+
+int skmetal_debug_loop_stamps(uint64_t* out, int cap) {
+  const int n = (int)std::min((size_t)std::max(cap, 0), t_loop_stamps.size());
+  for (int i = 0; i < n; ++i) out[i] = t_loop_stamps[i];
+  return (int)t_loop_stamps.size();
 }
 
 int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,

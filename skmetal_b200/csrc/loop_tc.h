@@ -1,0 +1,37 @@
+// Persistent Lloyd loop (single GPU, tensor-core E-step): one cooperative
+// launch runs every iteration of a fit, E-step and M-step alike, separated by
+// grid barriers instead of kernel boundaries.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "estep_tc.h"
+#include "kernels.cuh"
+
+namespace skm {
+
+struct LoopInputs {
+  const uint16_t* img;       // centre image of the current centres (B operand)
+  const int* sexp;           // {xexp, cexp} in the fit state
+  float* bias;               // ||c||^2 of the current centres (k floats); kept current by the loop
+  long long* D[2];           // delta buffers by iteration parity: dS (k x ld) | dcount (k) | changed; zero
+  long long* counts[2];      // cluster counts by iteration parity (counts[0] = those of the start labels)
+  float* C[2];               // centres by iteration parity: iteration t reads C[t & 1], writes C[(t + 1) & 1]
+  MStepArgs m;               // the M-step's state and scratch (D, counts, changed, C_old, C_new unused)
+  unsigned long long* prof;  // nullable: 4 * max_iter + 1 globaltimer stamps (see lloyd_loop_kernel)
+};
+
+// True when the plan's shared memory leaves room for the loop kernel's own.
+bool tc_loop_supported(const TcPlan& plan);
+
+// Static shared memory of the loop kernel (0 if it cannot be queried); plans
+// keep this much of a CTA's shared memory free.
+size_t tc_loop_static_smem();
+
+// Launches the loop (cooperative, plan.grid CTAs); runs until the fit state
+// says done. Errors of the device side are left in the fit state.
+int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s);
+
+}  // namespace skm

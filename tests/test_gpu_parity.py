@@ -365,6 +365,42 @@ def test_fit_is_deterministic():
     assert a[2] == b[2] and a[3] == b[3]
 
 
+def _golden_gen(gen):
+    import importlib.util
+    from pathlib import Path
+
+    spec = importlib.util.spec_from_file_location("make_golden", Path(__file__).parent / "golden" / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    return mg.case_inputs(gen)
+
+
+@pytest.mark.parametrize("gen,max_iter,tol,bulk_sums", [
+    ("reloc", 10, 0.0, False),                      # empty clusters relocated in the loop
+    ("mixture:60000:100:50:1", 30, 0.0, False),     # C2 recipe: bulk iterations, relocation, deltas
+    ("mixture:40000:32:8:0", 100, 1e-4, False),     # relative tolerance stop
+    ("mixture:30000:100:50:1", 12, 0.0, True),      # bulk sums in every iteration
+    ("mixture:20000:64:256:2", 15, 0.0, False),     # k = 256: two-segment centre image
+    ("dirichlet:40000:64:128:3", 20, 0.0, False),   # C4 recipe, two accumulators
+])
+def test_persistent_loop_matches_launch_loop(monkeypatch, gen, max_iter, tol, bulk_sums):
+    """The persistent loop kernel (one launch per fit) and the multi-launch
+    loop (E-step and M-step kernels per iteration) run the same arithmetic in
+    the same order: their fits are bit-identical."""
+    X, init = _golden_gen(gen)
+    a = _bridge.kmeans_fit(X, init, max_iter, tol, bulk_sums=bulk_sums)
+    la = _bridge.last_fit_stats()["launches"]
+    monkeypatch.setenv("SKMETAL_LOOP", "launches")
+    b = _bridge.kmeans_fit(X, init, max_iter, tol, bulk_sums=bulk_sums)
+    lb = _bridge.last_fit_stats()["launches"]
+    assert a[3] == b[3]
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+    assert a[2] == b[2]
+    # the persistent loop really ran: a fixed number of launches, not ~2 per iteration
+    assert la < 20 and lb >= 2 * b[3], (la, lb)
+
+
 def test_dataset_fit_matches_host_fit():
     X, init = make_workload(scaled("c1", 10000))
     a = _bridge.kmeans_fit(X, init, 15, 0.0)

@@ -116,6 +116,23 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 
+// L2 policy for data read once per pass (the tiles of X): evicted first, so
+// that streaming X through L2 does not push out the small state the M-step
+// reads back every iteration.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                               uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(src)), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+
 // K-major no-swizzle shared-memory matrix descriptor: core matrices of 8 rows
 // x 16 bytes; `lbo` = bytes between the two K halves of a K = 16 slice, `sbo`
 // = bytes between 8-row groups; descriptor version 1, layout type 0. Kept as
@@ -267,7 +284,21 @@ struct Cta {
   int my_tiles;  // tiles blockIdx.x + i * gridDim.x, i < my_tiles
   int n_iss;     // MMA issuers (1 or 2)
   int n_grp;     // epilogue groups (= accumulators)
+  int issued;    // producer thread: tiles of the CTA's sequence whose copies it issued
   __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * (uint32_t)i; }
+};
+
+// One pass of the pipeline (see estep_pass).
+struct Pass {
+  int ig0;       // tiles this CTA processed in earlier passes of the launch
+  int par;       // parity of the pass (the issuers' drain barriers complete once per pass)
+  int pre;       // tiles of this pass whose copies the previous pass already issued
+  int pre_next;  // tiles of the next pass to issue at the end of this one
+  int load_image;  // the producer copies the centre image from global memory (else it is in place)
+  int img_par;     // parity of that image load
+  float negscale;  // -2^(1 - xexp - cexp): dot products to distances
+  long long* deltas;            // nullable: fixed-point deltas of rows that change label
+  unsigned long long* changed;  // nullable: count of rows that change label
 };
 
 // The extra chunk of an odd nk (read as x_hi by the last pair MMA of the
@@ -304,6 +335,7 @@ __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_r
   // barrier has exactly one producer and one consumer
   c.n_iss = p.nacc >= 2 ? 2 : 1;
   c.n_grp = p.nacc;
+  c.issued = 0;
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int s = 0; s < MAX_STAGES; ++s) {
@@ -335,6 +367,14 @@ __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_r
 
 // All threads, once per launch, after the last pass: frees the tensor memory.
 __device__ __forceinline__ void cta_teardown(const Params& p, const Cta& c) {
+  if (threadIdx.x == 0) {
+    // copies still in flight (prefetched for a pass that did not run, or
+    // left by an abort) land before the CTA exits; at most `stages` are
+    // outstanding and each stage barrier is armed once per use
+    volatile int no_abort = 0;
+    for (int ig = (c.issued > p.stages ? c.issued - p.stages : 0); ig < c.issued; ++ig)
+      mbar_wait(c.bar(B_FULL(ig % p.stages)), (ig / p.stages) & 1, &no_abort, p.err, 2103);
+  }
   tc_fence_before();
   block_sync();
   if ((threadIdx.x >> 5) == MMA_W0) {
@@ -344,53 +384,60 @@ __device__ __forceinline__ void cta_teardown(const Params& p, const Cta& c) {
 }
 
 // One pass of the pipeline over this CTA's tiles, every thread in its warp
-// role: the producer loads the centre image and the tiles, the issuers run
-// the MMAs, the epilogue writes labels, counts changed rows into `changed`
-// (nullable) and, with `deltas` non-null, adds their fixed-point deltas.
-// ig0 = tiles this CTA processed in earlier passes of the launch: stage and
+// role: the producer copies the centre image (P.load_image) and the tiles,
+// the issuers run the MMAs, the epilogue writes labels, counts changed rows
+// into P.changed and, with P.deltas non-null, adds their fixed-point deltas.
+// P.ig0 = tiles this CTA processed in earlier passes of the launch: stage and
 // accumulator phases continue from there, so consecutive passes need no
-// barrier re-initialisation. par = parity of the pass (the image and drain
-// barriers complete once per pass). No block barrier at the end: a caller
-// that reuses shared memory synchronises first. On a timeout the CTA's abort
-// flag is set and every role stops issuing work after draining its own
-// copies and tensor-core operations.
-__device__ __forceinline__ void estep_pass(const Params& p, const Cta& c, int ig0, int par, long long* deltas,
-                                           unsigned long long* changed) {
+// barrier re-initialisation. The copies of the first P.pre tiles were issued
+// by the previous pass; at its end the producer issues the first P.pre_next
+// tiles of the next pass (X does not change between passes), which then land
+// while the caller runs other work that must leave the stages alone. Without
+// a copied image the caller has written it in place before the pass (then
+// fenced for the async proxy and synchronised the block). No block barrier at
+// the end. On a timeout the CTA's abort flag is set and every role stops
+// issuing work; the producer's copies are drained at teardown.
+__device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& P) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int my_tiles = c.my_tiles;
+  const int ig0 = P.ig0;
+  long long* const deltas = P.deltas;
+  unsigned long long* const changed = P.changed;
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      mbar_expect_tx(c.bar(B_C_FULL), p.img_bytes);
-      for (uint32_t o = 0; o < p.img_bytes; o += 8192u)
-        bulk_load(c.sbase + c.L.c + o, reinterpret_cast<const char*>(p.img) + o, min(8192u, p.img_bytes - o),
-                  c.bar(B_C_FULL));
-      int armed = 0;
-      for (int i = 0; i < my_tiles; ++i) {
-        const int ig = ig0 + i;
+      if (P.load_image) {
+        mbar_expect_tx(c.bar(B_C_FULL), p.img_bytes);
+        for (uint32_t o = 0; o < p.img_bytes; o += 8192u)
+          bulk_load(c.sbase + c.L.c + o, reinterpret_cast<const char*>(p.img) + o, min(8192u, p.img_bytes - o),
+                    c.bar(B_C_FULL));
+      }
+      // tiles i of this pass (i >= pre), then tiles i < pre_next of the next
+      const int n_issue = my_tiles - P.pre + min(P.pre_next, my_tiles);
+      const uint64_t pol = l2_evict_first_policy();
+      for (int q = 0; q < n_issue; ++q) {
+        const int ig = c.issued;
+        const int i = ig - ig0 < my_tiles ? ig - ig0 : ig - ig0 - my_tiles;
         const int s = ig % p.stages;
         if (!mbar_wait(c.bar(B_EMPTY(s)), ((ig / p.stages) & 1) ^ 1, c.abort_flag, p.err, 2101)) break;
         const int tile = (int)blockIdx.x + i * (int)gridDim.x;
         const unsigned char* src = p.Xs + (size_t)tile * p.tile_bytes;
         mbar_expect_tx(c.bar(B_FULL(s)), p.tile_bytes);
         for (uint32_t o = 0; o < p.tile_bytes; o += 8192u)
-          bulk_load(c.sbase + (uint32_t)s * p.stage_bytes + o, src + o, min(8192u, p.tile_bytes - o),
-                    c.bar(B_FULL(s)));
-        armed = i + 1;
+          bulk_load_hint(c.sbase + (uint32_t)s * p.stage_bytes + o, src + o, min(8192u, p.tile_bytes - o),
+                         c.bar(B_FULL(s)), pol);
+        c.issued = ig + 1;
       }
-      // our own copies must land before the CTA may go on
-      volatile int no_abort = 0;
-      mbar_wait(c.bar(B_C_FULL), par, &no_abort, p.err, 2102);
-      for (int i = (armed > p.stages ? armed - p.stages : 0); i < armed; ++i) {
-        const int ig = ig0 + i;
-        mbar_wait(c.bar(B_FULL(ig % p.stages)), (ig / p.stages) & 1, &no_abort, p.err, 2103);
+      if (P.load_image) {  // the image copy lands before the pass ends
+        volatile int no_abort = 0;
+        mbar_wait(c.bar(B_C_FULL), P.img_par, &no_abort, p.err, 2102);
       }
     }
   } else if (warp == MMA_W0 || warp == MMA_W1) {
     // ---------------------------------------------------------- MMA issuers
     const int t = warp == MMA_W0 ? 0 : 1;
     if (lane == 0 && t < c.n_iss) {
-      bool ok = mbar_wait(c.bar(B_C_FULL), par, c.abort_flag, p.err, 2201);
+      bool ok = !P.load_image || mbar_wait(c.bar(B_C_FULL), P.img_par, c.abort_flag, p.err, 2201);
       for (int i = (t - ig0 % c.n_iss + c.n_iss) % c.n_iss; ok && i < my_tiles; i += c.n_iss) {
         const int ig = ig0 + i;
         const int s = ig % p.stages, a = ig % p.nacc;
@@ -414,7 +461,7 @@ __device__ __forceinline__ void estep_pass(const Params& p, const Cta& c, int ig
       // every tcgen05 operation issued by this thread is complete once DONE fires
       tc_commit(c.bar(B_DONE(t)));
       volatile int no_abort = 0;
-      mbar_wait(c.bar(B_DONE(t)), par, &no_abort, p.err, 2206);
+      mbar_wait(c.bar(B_DONE(t)), P.par, &no_abort, p.err, 2206);
     }
   } else if (warp >= EPI_W0) {
     // ----------------------------------------------------------------- epilogue
@@ -425,7 +472,7 @@ __device__ __forceinline__ void estep_pass(const Params& p, const Cta& c, int ig
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     // dist = ||c||^2 - 2 x.c with x.c = acc * 2^-(xexp + cexp)
-    const float negscale = -ldexpf(1.0f, 1 - __ldcg(p.sexp) - __ldcg(p.sexp + 1));
+    const float negscale = P.negscale;
     const int i0 = g < c.n_grp ? (g - ig0 % c.n_grp + c.n_grp) % c.n_grp : my_tiles;
     int old_next = -1;
     if (changed && i0 < my_tiles) {

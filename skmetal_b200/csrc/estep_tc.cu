@@ -65,7 +65,12 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   Cta c;
   cta_setup(p, smem_raw, p.bias, c);
-  estep_pass(p, c, 0, 0, deltas, p.changed);
+  Pass P{};
+  P.load_image = 1;
+  P.negscale = -ldexpf(1.0f, 1 - __ldcg(p.sexp) - __ldcg(p.sexp + 1));
+  P.deltas = deltas;
+  P.changed = p.changed;
+  estep_pass(p, c, P);
   cta_teardown(p, c);
 }
 

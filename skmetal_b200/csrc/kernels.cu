@@ -412,59 +412,37 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
               bulk_acc_bytes(a.k, a.ld, kBulkSmemBytes) ? dyn_smem : nullptr);
     if (!grid_barrier(st, nb)) return;
   }
-  __shared__ double red_scratch[32];
   // 1. empty clusters of the new assignment; every block computes the same answer
   const int n_empty = find_empty_clusters(a, bulk);
 
   if (n_empty == 0) {
-    // ---------------- fast path: no relocation. Units of (cluster, column
-    // part) spread over the blocks; each block folds its units' sums (S + D;
-    // bulk: D) and computes their centres; the last block to finish reduces
-    // the per-unit partials in a fixed order, folds the counts and sets the
-    // loop flags.
+    // ---------------- fast path: no relocation. One warp per cluster folds
+    // its sums (S + D; bulk: D) and writes its centre; the last block to
+    // finish folds the counts, totals the shifts in the canonical order and
+    // sets the loop flags.
     const double inv_scale = st->inv_scale;
-    const int xexp = st->xexp;
-    const float cs = ldexpf(1.0f, xexp);  // centres are bounded by max |x|
-    const int nq = a.ld >> 2;
-    const int parts = max(1, min(nq, (int)nb / a.k));
-    const int units = a.k * parts;
+    const float cs = ldexpf(1.0f, st->xexp);  // centres are bounded by max |x|
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     long long* S = const_cast<long long*>(a.S);
     long long* cnt = const_cast<long long*>(a.counts);
-    for (int u = blockIdx.x; u < units; u += nb) {
-      const int c = u / parts, pt = u % parts;
-      const int q0 = (int)((long long)nq * pt / parts), q1 = (int)((long long)nq * (pt + 1) / parts);
-      const int j0 = 4 * q0, j1 = 4 * q1;
-      const long long dcc = dcnt[c];
-      const long long cnew = (bulk ? 0 : cnt[c]) + dcc;
-      const double fct = centre_factor(inv_scale, cnew);
-      double dsq = 0.0, nrm = 0.0;
-      for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
-        const long long i = (long long)c * a.ld + j;
-        const long long dv = a.D[i];
-        const long long sum = (bulk ? 0 : S[i]) + dv;
-        const float old = a.C_old[i];
-        S[i] = sum;
-        if (dv != 0) a.D[i] = 0;
-        float v = 0.0f;
-        if (j < a.d) {
-          v = centre_from_sum(sum, fct);
-          const double df = (double)v - (double)old;
-          dsq += df * df;
-          nrm += (double)v * v;
-          if (a.cimg.img) cimg_put(a.cimg, c, j, v, cs);
-        }
-        a.C_new[i] = v;
+    double* dsq_c = a.shift_partial;  // k entries
+    for (int c = blockIdx.x * nwarps + warp; c < a.k; c += nb * nwarps) {
+      const long long dcc = __ldcg(&dcnt[c]);
+      const long long cnew = (bulk ? 0 : __ldcg(&cnt[c])) + dcc;
+      double dsq, nrm;
+      warp_centre_from_sums(c, a.ld, a.d, S, a.D, bulk, cnew, inv_scale, a.C_old, cs, a.cimg, CentreImage{}, S,
+                            a.C_new, a.D, &dsq, &nrm);
+      if (lane == 0) {
+        dsq_c[c] = dsq;
+        if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
+        if (a.bias) a.bias[c] = (float)nrm;
       }
-      dsq = block_sum_f64(dsq, red_scratch);
-      nrm = block_sum_f64(nrm, red_scratch);
-      if (threadIdx.x == 0) {
-        a.unit_dsq[u] = dsq;
-        a.unit_nrm[u] = nrm;
-      }
-      block_sync();
     }
-    // the last block to get here reduces and finishes the iteration
+    // the last block to get here folds the counts (every block has read them
+    // in find_empty_clusters by now), totals the shifts and finishes the
+    // iteration
     __shared__ int last_s;
+    block_sync();
     if (threadIdx.x == 0) {
       __threadfence();
       last_s = atomicAdd(&st->ticket, 1u) == nb - 1;
@@ -472,25 +450,15 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
     block_sync();
     if (!last_s) return;
     __threadfence();
-    double* dsq_c = a.shift_partial;  // k entries
     for (int c = threadIdx.x; c < a.k; c += blockDim.x) {
-      // counts are folded only now: every unit of the cluster has read them
       const long long dcc = __ldcg(&dcnt[c]);
       const long long cnew = (bulk ? 0 : __ldcg(&cnt[c])) + dcc;
       cnt[c] = cnew;
       a.cnt_adj[c] = cnew;
       if (dcc != 0) a.D[ks + c] = 0;
-      double dsq = 0.0, nrm = 0.0;
-      for (int pt = 0; pt < parts; ++pt) {  // written by other blocks: read through L2
-        dsq += __ldcg(&a.unit_dsq[c * parts + pt]);
-        nrm += __ldcg(&a.unit_nrm[c * parts + pt]);
-      }
-      dsq_c[c] = dsq;
-      if (a.shift_out) a.shift_out[c] = (float)sqrt(dsq);
-      if (a.bias) a.bias[c] = (float)nrm;
     }
-    block_sync();
-    const double tot = block_ordered_sum(dsq_c, a.k, red_scratch);
+    if (threadIdx.x >= 32) return;
+    const double tot = warp_ordered_sum(dsq_c, a.k);
     if (threadIdx.x == 0) {
       st->ticket = 0;
       st->n_empty = 0;

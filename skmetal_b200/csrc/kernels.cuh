@@ -31,9 +31,6 @@ __host__ __device__ inline size_t cand_row_off(int cap) { return 16 + (size_t)ca
 __host__ __device__ inline size_t cand_label_off(int cap) { return 16 + (size_t)cap * 12; }
 __host__ __device__ inline size_t cand_x_off(int cap) { return 16 + (size_t)cap * 16; }
 
-// The M-step's fast path splits the centre update into units of (cluster,
-// column part): parts = max(1, min(ld / 4, blocks / k)), so that the k * parts
-// units spread over the blocks.
 // Above n / 10 changed rows in an iteration, per-row deltas (about 2 d
 // contended reductions per row) cost more than rebuilding the sums from all
 // rows, so the next iteration is a bulk one.
@@ -80,9 +77,6 @@ struct MStepArgs {
   // bulk iterations: the sums were already added into D before the M-step
   // (multi-GPU: before the all-reduce), so the M-step only replaces S by D
   int bulk_external;
-  // per (cluster, column part) partial squared shift and squared norm
-  double* unit_dsq;
-  double* unit_nrm;
   // relocation candidates gathered from every rank (multi-GPU); null on one
   // GPU: cand_ranks blocks of cand_block_bytes(cand_cap, ld) bytes each
   const unsigned char* cand;

@@ -388,11 +388,6 @@ static int run_fit(const FitParams& p) {
   SKM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_done_dev), pinned, 0));
   ma.host_done = host_done_dev;
   ma.bulk_external = comm ? 1 : 0;
-  {
-    const size_t nunit = (size_t)std::max(k, mstep_blocks);
-    SKM_TRY(buf.alloc_n(&ma.unit_dsq, nunit));
-    SKM_TRY(buf.alloc_n(&ma.unit_nrm, nunit));
-  }
   // multi-GPU: candidate slots after D, and this rank's own cluster counts
   long long* local_counts = nullptr;
   if (comm) {
@@ -411,11 +406,14 @@ static int run_fit(const FitParams& p) {
   const bool persistent = plan.tc && !comm && !p.single_step && !launches_loop && tc_loop_supported(plan.tcp);
   std::vector<unsigned long long> prof_stamps;
   if (persistent) {
-    long long *D2 = nullptr, *counts2 = nullptr;
-    SKM_TRY(buf.alloc_n(&D2, d_len));
-    SKM_TRY(buf.alloc_n(&counts2, (size_t)k));
-    SKM_CUDA(cudaMemsetAsync(D2, 0, sizeof(long long) * d_len, s));
-    SKM_CUDA(cudaMemsetAsync(counts2, 0, sizeof(long long) * k, s));
+    // second and third delta buffers, second sums + counts (the loop rotates them)
+    // (16-byte aligned: the loop reads and writes them as column quads)
+    const size_t d_stride = round_up(d_len, 4);
+    long long *D23 = nullptr, *S2 = nullptr;
+    SKM_TRY(buf.alloc_n(&D23, 2 * d_stride));
+    SKM_TRY(buf.alloc_n(&S2, (size_t)k * ld + k));
+    SKM_CUDA(cudaMemsetAsync(D23, 0, sizeof(long long) * 2 * d_stride, s));
+    SKM_CUDA(cudaMemsetAsync(S2, 0, sizeof(long long) * ((size_t)k * ld + k), s));
     unsigned long long* prof_d = nullptr;
     if (p.profile) {
       prof_stamps.assign(4 * (size_t)p.max_iter + 1, 0);
@@ -427,13 +425,17 @@ static int run_fit(const FitParams& p) {
     li.sexp = &st->xexp;
     li.bias = bias;
     li.D[0] = D;
-    li.D[1] = D2;
+    li.D[1] = D23;
+    li.D[2] = D23 + d_stride;
+    li.S[0] = S;
+    li.S[1] = S2;
     li.counts[0] = counts;
-    li.counts[1] = counts2;
+    li.counts[1] = S2 + (size_t)k * ld;
     li.C[0] = Cb0;
     li.C[1] = Cb1;
     li.m = ma;
     li.prof = prof_d;
+    SKM_TRY(buf.alloc_n(&li.part, 3 * (size_t)k));
     SKM_TRY(tc_lloyd_loop(plan.tcp, li, s));
     SKM_CUDA(cudaEventRecord(ev2, s));
     if (prof_d)

@@ -1,30 +1,33 @@
 // Persistent Lloyd loop for one GPU: a single cooperative launch of one CTA
-// per SM runs all iterations of a fit,
+// per SM runs all iterations of a fit. Iteration t:
 //
 //   E-step   the tensor-core pipeline of estep_dev.cuh over the CTA's tiles
-//            (labels, changed count, fixed-point deltas of changed rows)
-//   barrier
-//   M-step   [bulk iterations: fixed-point sums of all rows, barrier]
-//            empty clusters; fast path: (cluster, column part) units fold
-//            the sums and write the new centres, their image and partial
-//            shifts; relocation path: relocation_path of mstep_dev.cuh
-//   barrier
-//   every CTA reduces the unit partials in the same fixed order, so all of
-//   them reach the same convergence decision and refresh their ||c||^2
+//            (labels, changed count, fixed-point deltas of changed rows); at
+//            its end the producer already issues the copies of the next
+//            iteration's first tiles (X does not change)
+//   grid barrier
+//   M-step   [bulk iterations: fixed-point sums of all rows, grid barrier]
+//            the CTA owning cluster c (c mod CTAs) folds c's sums and count,
+//            writes its centre, centre image entries, squared shift and
+//            squared norm, or flags it empty, and clears c's deltas of
+//            iteration t - 1
+//   grid barrier
+//            every CTA reads the k shifts, norms and flags: ||c||^2 for its
+//            epilogue and, totalled in the canonical order, the same stop
+//            decision as every other CTA; the next E-step copies the centre
+//            image from global memory. With an empty cluster instead: the
+//            cooperative relocation path of mstep_dev.cuh and a grid barrier.
 //
-// which is the work of the E-step / M-step kernel pair of the multi-launch
-// loop, with the same arithmetic in the same order: both loops give
-// bit-identical fits. What the persistent loop removes is two kernel launches
-// per iteration, the pipeline's per-launch set-up (barrier initialisation,
-// tensor-memory allocation) and the host's polling of the done flag.
+// No kernel launches and no host round trips between iterations. The
+// arithmetic is that of the multi-launch loop (E-step and M-step kernels) in
+// the same order, so both give bit-identical fits.
 //
-// Buffers whose readers and writers would overlap across the iteration
-// boundary alternate by iteration parity: the delta buffer D (the next E-step
-// adds into the other one while this iteration's counts part is cleared), the
-// counts (units read the old, write the new) and the centres (as in the
-// multi-launch loop). The centre image is written by the units of iteration t
-// between the two barriers and read by the E-step of t + 1 after the second
-// one.
+// Buffers whose readers and writers overlap across iterations are rotated
+// (each 16-byte aligned, rows of ld entries): the delta buffers D by t mod 3
+// (written by E-step t, read by the owners in M-step t, cleared by them in
+// M-step t + 1, written again by E-step t + 3), the sums, counts and centres
+// by t mod 2 (the owners write the next ones while the relocation path may
+// still need the current ones).
 //
 // Every wait is bounded: mbarrier waits (estep_dev.cuh) and grid barriers
 // record an error code in the fit state and the CTAs leave the loop together
@@ -45,9 +48,11 @@ namespace {
 struct LoopArgs {
   tc::Params p;
   MStepArgs m;
-  long long* D[2];
+  long long* D[3];
+  long long* S[2];
   long long* cnt[2];
   float* C[2];
+  double* part;  // per cluster: squared shift [0, k), squared norm [k, 2k), empty flag [2k, 3k)
   unsigned long long* prof;
 };
 
@@ -57,8 +62,8 @@ __device__ __forceinline__ void proxy_fence_all() {
 }
 
 // Profile stamps (block 0, thread 0): per iteration t, [4t] start, [4t + 1]
-// E-step done (after the barrier), [4t + 2] bulk sums and empty clusters
-// done, [4t + 3] centres done (after the barrier); [4 T] the end.
+// E-step done (after the first barrier), [4t + 2] owners done (after the
+// second), [4t + 3] M-step done; [4 T] the end.
 __device__ __forceinline__ void stamp(unsigned long long* prof, int i) {
   if (prof && blockIdx.x == 0 && threadIdx.x == 0) prof[i] = tc::globaltimer();
 }
@@ -68,40 +73,54 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
   const Params& p = la.p;
   FitState* st = la.m.st;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ double dsq_s[MAX_KPAD];
-  __shared__ double red[32];
   __shared__ int flags_s[2];
   Cta c;
   cta_setup(p, smem_raw, p.bias, c);
 
   const unsigned int nb = gridDim.x;
-  const int k = p.k, ld = p.ld;
+  const int k = p.k, ld = p.ld, d = p.d;
   const long long ks = (long long)k * ld;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const double inv_scale = st->inv_scale;
-  const float cs = ldexpf(1.0f, st->xexp);  // centres are bounded by max |x|
-  const int nq = ld >> 2;
-  const int parts = max(1, min(nq, (int)nb / k));
-  const int units = k * parts;
-  long long* S = const_cast<long long*>(la.m.S);
+  const int xexp = st->xexp;
+  const float cs = ldexpf(1.0f, xexp);  // centres are bounded by max |x|
+  // the first image (centre_prep) is scaled by 2^cexp, those of the loop by 2^xexp
+  float negscale = -ldexpf(1.0f, 1 - xexp - st->cexp);
+  const float negscale_loop = -ldexpf(1.0f, 1 - 2 * xexp);
+  const int max_iter = st->max_iter;
   int bulk = st->bulk;
   int done = st->done;
+  int img_loads = 0, pre = 0;
   int t = 0;
   for (; !done; ++t) {
     const int par = t & 1;
-    long long* Dp = la.D[par];
+    long long* Dp = la.D[t % 3];
+    long long* D_prev = la.D[(t + 2) % 3];
     long long* dcnt = Dp + ks;
     unsigned long long* chg = reinterpret_cast<unsigned long long*>(Dp + ks + k);
-    const long long* cnt_in = la.cnt[par];
+    long long* S_in = la.S[par];
+    long long* S_out = la.S[par ^ 1];
+    long long* cnt_in = la.cnt[par];
     long long* cnt_out = la.cnt[par ^ 1];
     const float* C_old = la.C[par];
     float* C_new = la.C[par ^ 1];
     stamp(la.prof, 4 * t);
-    // the centre image written by other CTAs' generic stores is next read by
-    // this CTA's bulk copies (async proxy)
-    if (t > 0) proxy_fence_all();
 
     // ---------------------------------------------------------------- E-step
-    estep_pass(p, c, t * c.my_tiles, par, bulk ? nullptr : Dp, chg);
+    Pass P{};
+    P.ig0 = t * c.my_tiles;
+    P.par = par;
+    P.pre = pre;
+    // bulk iterations use the stages as the sums' workspace: nothing in flight
+    P.pre_next = (bulk || t + 1 >= max_iter) ? 0 : min(p.stages, c.my_tiles);
+    P.load_image = 1;  // the centre image of the previous M-step (or of centre_prep)
+    P.img_par = img_loads & 1;
+    P.negscale = negscale;
+    P.deltas = bulk ? nullptr : Dp;
+    P.changed = chg;
+    estep_pass(p, c, P);
+    ++img_loads;
+    pre = P.pre_next;
     proxy_fence_all();
     if (!grid_barrier(st, nb)) break;
     if (__ldcg(&st->error)) break;  // uniform: read after the barrier
@@ -110,6 +129,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
 
     // ---------------------------------------------------------------- M-step
     MStepArgs a = la.m;
+    a.S = S_in;
     a.D = Dp;
     a.changed = chg;
     a.counts = cnt_in;
@@ -123,108 +143,102 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       proxy_fence_all();
       if (!grid_barrier(st, nb)) break;
     }
-    const int n_empty = find_empty_clusters(a, bulk);
-    stamp(la.prof, 4 * t + 2);
-    if (n_empty == 0) {
-      // fast path: units of (cluster, column part) over the blocks
-      if (blockIdx.x == 0 && threadIdx.x == 0) st->cexp = st->xexp;  // read by the next E-step only
-      for (int u = blockIdx.x; u < units; u += nb) {
-        const int cl = u / parts, pt = u % parts;
-        const int q0 = (int)((long long)nq * pt / parts), q1 = (int)((long long)nq * (pt + 1) / parts);
-        const int j0 = 4 * q0, j1 = 4 * q1;
-        const long long cnew = (bulk ? 0 : __ldcg(&cnt_in[cl])) + __ldcg(&dcnt[cl]);
-        const double fct = centre_factor(inv_scale, cnew);
+    // (no block touches S_in, D or the counts before the barrier above)
+    // owners: cluster cl is CTA cl mod nb's, one warp per owned cluster
+    {
+      double* dsq_c = la.part;
+      double* nrm_c = la.part + k;
+      double* emp_c = la.part + 2 * k;
+      for (int m = warp; blockIdx.x + (long long)m * nb < (long long)k; m += nwarps) {
+        const int cl = (int)(blockIdx.x + (long long)m * nb);
+        const long long cnew = (bulk ? 0 : __ldcg(cnt_in + cl)) + __ldcg(dcnt + cl);
         double dsq = 0.0, nrm = 0.0;
-        for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
-          const long long i = (long long)cl * ld + j;
-          const long long dv = __ldcg(&Dp[i]);
-          const long long sum = (bulk ? 0 : __ldcg(&S[i])) + dv;
-          const float old = __ldcg(&C_old[i]);
-          S[i] = sum;
-          if (dv != 0) Dp[i] = 0;
-          float v = 0.0f;
-          if (j < p.d) {
-            v = centre_from_sum(sum, fct);
-            const double df = (double)v - (double)old;
-            dsq += df * df;
-            nrm += (double)v * v;
-            cimg_put(a.cimg, cl, j, v, cs);
+        if (cnew > 0)
+          warp_centre_from_sums(cl, ld, d, S_in, Dp, bulk, cnew, inv_scale, C_old, cs, la.m.cimg, CentreImage{},
+                                S_out, C_new, nullptr, &dsq, &nrm);
+        // cl's deltas of iteration t - 1: their readers finished before this
+        // iteration's first barrier; E-step t + 2 adds into them again
+        for (int j = 4 * lane; j < ld; j += 128) {
+          *reinterpret_cast<longlong2*>(D_prev + (long long)cl * ld + j) = make_longlong2(0, 0);
+          *reinterpret_cast<longlong2*>(D_prev + (long long)cl * ld + j + 2) = make_longlong2(0, 0);
+        }
+        if (lane == 0) {
+          D_prev[ks + cl] = 0;
+          cnt_out[cl] = cnew;
+          dsq_c[cl] = dsq;
+          nrm_c[cl] = nrm;
+          emp_c[cl] = cnew == 0 ? 1.0 : 0.0;
+          la.m.bias[cl] = (float)nrm;  // for the final E-step after the loop
+        }
+      }
+      if (blockIdx.x == 0 && threadIdx.x == 0) D_prev[ks + k] = 0;  // its changed counter
+      proxy_fence_all();
+      if (!grid_barrier(st, nb)) break;
+      stamp(la.prof, 4 * t + 2);
+      // every CTA: flags, ||c||^2, and the total shift in the canonical order
+      int n_empty_w = 0;
+      for (int cl = threadIdx.x; cl < p.k_pad; cl += blockDim.x) {
+        if (cl < k) {
+          c.bias_s[cl] = (float)__ldcg(nrm_c + cl);
+          n_empty_w += __ldcg(emp_c + cl) != 0.0;
+        } else {
+          c.bias_s[cl] = INFINITY;
+        }
+      }
+      __syncwarp();
+      const int n_empty = __syncthreads_count(n_empty_w != 0) ? 1 : 0;  // any empty cluster
+      if (n_empty == 0 && warp == 0) {
+        double tt = 0.0;
+        for (int cl = lane; cl < k; cl += 32) tt += __ldcg(dsq_c + cl);
+        const double tot = warp_sum(tt);
+        if (lane == 0) {
+          // _kmeans.py:723-741, as finish_iteration
+          const int it = t + 1;
+          const int strict = changed_now == 0;
+          const int dn = strict || tot <= st->tol || it >= max_iter;
+          const int bk = st->bulk_always || changed_now > (unsigned long long)st->bulk_threshold;
+          flags_s[0] = dn;
+          flags_s[1] = bk;
+          if (blockIdx.x == 0) {
+            st->shift_tot = tot;
+            st->iter = it;
+            st->bulk = bk;
+            st->n_empty = 0;
+            st->relocated = 0;
+            if (strict) st->strict = 1;
+            st->done = dn;
+            *chg = 0;
           }
-          C_new[i] = v;
         }
-        // one column per thread (ld <= 128 < blockDim): the block tree then
-        // sums the same terms in the same order as the 1024-thread M-step
-        dsq = block_sum_f64(dsq, red);
-        nrm = block_sum_f64(nrm, red);
-        if (threadIdx.x == 0) {
-          a.unit_dsq[u] = dsq;
-          a.unit_nrm[u] = nrm;
-          if (pt == 0) cnt_out[cl] = cnew;
+      }
+      block_sync();
+      if (n_empty == 0) {
+        done = flags_s[0];
+        bulk = flags_s[1];
+      } else {
+        // relocation: the empty clusters again with their ids, then the
+        // cooperative path, which folds this iteration's sums and counts into
+        // S_in and cnt_in and writes every centre, image entry and norm
+        const int ne = find_empty_clusters(a, bulk);
+        if (!relocation_path(a, ne, bulk, changed_now)) break;
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + k;
+             i += (long long)nb * blockDim.x) {
+          if (i < ks) S_out[i] = __ldcg(S_in + i);
+          else cnt_out[i - ks] = __ldcg(cnt_in + (i - ks));
         }
+        proxy_fence_all();
+        if (!grid_barrier(st, nb)) break;
+        load_bias(p, c, la.m.bias);
+        done = *reinterpret_cast<volatile int*>(&st->done);
+        bulk = *reinterpret_cast<volatile int*>(&st->bulk);
         block_sync();
       }
-      proxy_fence_all();
-      if (!grid_barrier(st, nb)) break;
-      stamp(la.prof, 4 * t + 3);
-      // every CTA: per-cluster shift and ||c||^2 from the unit partials in
-      // part order, then the total in the fixed order of block_ordered_sum
-      for (int cl = threadIdx.x; cl < p.k_pad; cl += blockDim.x) {
-        if (cl >= k) {  // padding clusters (the bulk sums may have used this memory)
-          c.bias_s[cl] = INFINITY;
-          continue;
-        }
-        double dsq = 0.0, nrm = 0.0;
-        for (int pt = 0; pt < parts; ++pt) {
-          dsq += __ldcg(&a.unit_dsq[cl * parts + pt]);
-          nrm += __ldcg(&a.unit_nrm[cl * parts + pt]);
-        }
-        dsq_s[cl] = dsq;
-        c.bias_s[cl] = (float)nrm;
-        if (blockIdx.x == 0) la.m.bias[cl] = (float)nrm;  // for the final E-step after the loop
-      }
-      block_sync();
-      const double tot = block_ordered_sum(dsq_s, k, red);
-      if (threadIdx.x == 0) {
-        // _kmeans.py:723-741, as finish_iteration
-        const int it = t + 1;
-        const int strict = changed_now == 0;
-        const int dn = strict || tot <= st->tol || it >= st->max_iter;
-        const int bk = st->bulk_always || changed_now > (unsigned long long)st->bulk_threshold;
-        flags_s[0] = dn;
-        flags_s[1] = bk;
-        if (blockIdx.x == 0) {
-          st->shift_tot = tot;
-          st->iter = it;
-          st->bulk = bk;
-          st->n_empty = 0;
-          st->relocated = 0;
-          if (strict) st->strict = 1;
-          st->done = dn;
-          *chg = 0;  // every CTA read it before the barrier
-        }
-      }
-      // this iteration's count deltas: read by the units before the barrier,
-      // next written by the E-step of iteration t + 2
-      if (blockIdx.x == 0)
-        for (int cl = threadIdx.x; cl < k; cl += blockDim.x) dcnt[cl] = 0;
-      block_sync();
-      done = flags_s[0];
-      bulk = flags_s[1];
-    } else {
-      if (!relocation_path(a, n_empty, bulk, changed_now)) break;
-      // the counts were folded into cnt_in (before a barrier of the path)
-      if (blockIdx.x == 0)
-        for (int cl = threadIdx.x; cl < k; cl += blockDim.x) cnt_out[cl] = __ldcg(&cnt_in[cl]);
-      proxy_fence_all();
-      if (!grid_barrier(st, nb)) break;
-      stamp(la.prof, 4 * t + 3);
-      load_bias(p, c, la.m.bias);
-      done = *reinterpret_cast<volatile int*>(&st->done);
-      bulk = *reinterpret_cast<volatile int*>(&st->bulk);
-      block_sync();
     }
+    negscale = negscale_loop;
+    stamp(la.prof, 4 * t + 3);
   }
   stamp(la.prof, 4 * t);
+  if (t > 0 && blockIdx.x == 0 && threadIdx.x == 0) st->cexp = xexp;  // scale of the final image
   cta_teardown(p, c);
 }
 
@@ -240,15 +254,10 @@ size_t tc_loop_static_smem() {
 }
 
 bool tc_loop_supported(const TcPlan& plan) {
-  cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, lloyd_loop_kernel) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  return plan.supported && plan.k <= tc::MAX_KPAD && fa.sharedSizeBytes + plan.smem <= (size_t)optin;
+  return plan.supported && plan.k <= tc::MAX_KPAD && tc_loop_static_smem() + plan.smem <= (size_t)optin;
 }
 
 int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
@@ -261,11 +270,13 @@ int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
   la.p.st = in.m.st;
   la.p.err = &in.m.st->error;
   la.m = in.m;
+  for (int i = 0; i < 3; ++i) la.D[i] = in.D[i];
   for (int i = 0; i < 2; ++i) {
-    la.D[i] = in.D[i];
+    la.S[i] = in.S[i];
     la.cnt[i] = in.counts[i];
     la.C[i] = in.C[i];
   }
+  la.part = in.part;
   la.prof = in.prof;
   static int attr_dev = -1;
   int dev = 0;
@@ -273,10 +284,8 @@ int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
   if (attr_dev != dev) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncAttributes fa{};
-    SKM_CUDA(cudaFuncGetAttributes(&fa, lloyd_loop_kernel));
     SKM_CUDA(cudaFuncSetAttribute(lloyd_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  optin - (int)fa.sharedSizeBytes));
+                                  optin - (int)tc_loop_static_smem()));
     attr_dev = dev;
   }
   void* args[] = {&la};

@@ -13,13 +13,15 @@
 namespace skm {
 
 struct LoopInputs {
-  const uint16_t* img;       // centre image of the current centres (B operand)
+  const uint16_t* img;       // centre image of the start centres (B operand)
   const int* sexp;           // {xexp, cexp} in the fit state
-  float* bias;               // ||c||^2 of the current centres (k floats); kept current by the loop
-  long long* D[2];           // delta buffers by iteration parity: dS (k x ld) | dcount (k) | changed; zero
+  float* bias;               // ||c||^2 of the start centres (k floats); kept current by the loop
+  long long* D[3];           // delta buffers, rotated by iteration mod 3: dS (k x ld) | dcount (k) | changed; zero
+  long long* S[2];           // fixed-point sums by iteration parity (S[0] = those of the start labels)
   long long* counts[2];      // cluster counts by iteration parity (counts[0] = those of the start labels)
   float* C[2];               // centres by iteration parity: iteration t reads C[t & 1], writes C[(t + 1) & 1]
-  MStepArgs m;               // the M-step's state and scratch (D, counts, changed, C_old, C_new unused)
+  MStepArgs m;               // the M-step's state and scratch (D, S, counts, changed, C_old, C_new unused)
+  double* part;              // 3 k doubles of per-cluster results of the owners
   unsigned long long* prof;  // nullable: 4 * max_iter + 1 globaltimer stamps (see lloyd_loop_kernel)
 };
 

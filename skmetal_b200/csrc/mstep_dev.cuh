@@ -265,6 +265,102 @@ static __device__ __forceinline__ void warp_centre(const MStepArgs& a, int c, in
   *nrm_out = warp_sum(nrm);
 }
 
+// New centres when no cluster is empty. Column j of cluster c's fixed-point
+// sum is (bulk ? 0 : S_in[j]) + D[j] and its centre value
+// centre_from_sum(sum, 2^-F / count). One warp handles a cluster, lane l its
+// column quads q = l, l + 32, ...; the squared shift against C_old and the
+// squared norm are accumulated by each lane in column order and then combined
+// by the xor butterfly of warp_sum. Every path of the library uses this
+// order, so all blocks, both loop drivers and every GPU count reach
+// bit-identical values. All arrays are k x ld with ld a multiple of 4 and
+// 16-byte aligned rows.
+struct QuadSums {
+  long long s[4];  // folded sums of the quad's columns
+  float4 old;      // previous centre values
+  bool dnz;        // some delta of the quad is non-zero
+};
+
+__device__ __forceinline__ QuadSums quad_load(const long long* S_in, const long long* D, const float* C_old,
+                                              long long i, int bulk) {
+  QuadSums r;
+  const longlong2 d01 = __ldcg(reinterpret_cast<const longlong2*>(D + i));
+  const longlong2 d23 = __ldcg(reinterpret_cast<const longlong2*>(D + i + 2));
+  longlong2 s01 = make_longlong2(0, 0), s23 = make_longlong2(0, 0);
+  if (!bulk) {
+    s01 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i));
+    s23 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i + 2));
+  }
+  r.old = __ldcg(reinterpret_cast<const float4*>(C_old + i));
+  r.s[0] = s01.x + d01.x;
+  r.s[1] = s01.y + d01.y;
+  r.s[2] = s23.x + d23.x;
+  r.s[3] = s23.y + d23.y;
+  r.dnz = (d01.x | d01.y | d23.x | d23.y) != 0;
+  return r;
+}
+
+// Centre values of quad q (columns 4q .. 4q + 3) of cluster c from its loaded
+// sums; adds the shift and norm terms of the columns < d in order; writes the
+// optional outputs (null to skip): centre image entries (img1, img2), folded
+// sums S_out, centre values C_new, and zeros over the non-zero deltas in
+// D_clear.
+__device__ __forceinline__ void quad_finish(const QuadSums& r, int c, int q, long long i, int d, double fct, float cs,
+                                            const CentreImage& img1, const CentreImage& img2, long long* S_out,
+                                            float* C_new, long long* D_clear, double& dsq, double& nrm) {
+  const float old[4] = {r.old.x, r.old.y, r.old.z, r.old.w};
+  float v[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int j = 4 * q + u;
+    v[u] = 0.0f;
+    if (j < d) {
+      v[u] = centre_from_sum(r.s[u], fct);
+      const double df = (double)v[u] - (double)old[u];
+      dsq += df * df;
+      nrm += (double)v[u] * v[u];
+      if (img1.img) cimg_put(img1, c, j, v[u], cs);
+      if (img2.img) cimg_put(img2, c, j, v[u], cs);
+    }
+  }
+  if (S_out) {
+    *reinterpret_cast<longlong2*>(S_out + i) = make_longlong2(r.s[0], r.s[1]);
+    *reinterpret_cast<longlong2*>(S_out + i + 2) = make_longlong2(r.s[2], r.s[3]);
+  }
+  if (C_new) *reinterpret_cast<float4*>(C_new + i) = make_float4(v[0], v[1], v[2], v[3]);
+  if (D_clear && r.dnz) {
+    *reinterpret_cast<longlong2*>(D_clear + i) = make_longlong2(0, 0);
+    *reinterpret_cast<longlong2*>(D_clear + i + 2) = make_longlong2(0, 0);
+  }
+}
+
+// One cluster, any ld (one warp; see above).
+static __device__ __forceinline__ void warp_centre_from_sums(int c, int ld, int d, const long long* S_in,
+                                                             const long long* D, int bulk, long long cnew,
+                                                             double inv_scale, const float* C_old, float cs,
+                                                             const CentreImage& img1, const CentreImage& img2,
+                                                             long long* S_out, float* C_new, long long* D_clear,
+                                                             double* dsq_out, double* nrm_out) {
+  const int lane = threadIdx.x & 31;
+  const double fct = centre_factor(inv_scale, cnew);
+  double dsq = 0.0, nrm = 0.0;
+  for (int q = lane; q < (ld >> 2); q += 32) {
+    const long long i = (long long)c * ld + 4 * q;
+    const QuadSums r = quad_load(S_in, D, C_old, i, bulk);
+    quad_finish(r, c, q, i, d, fct, cs, img1, img2, S_out, C_new, D_clear, dsq, nrm);
+  }
+  *dsq_out = warp_sum(dsq);
+  *nrm_out = warp_sum(nrm);
+}
+
+// Sum of v[0, n) in the canonical order (lane l adds v[l], v[l + 32], ... in
+// order, then the xor butterfly); every lane of the calling warp gets it. v
+// may be in global or shared memory.
+static __device__ __forceinline__ double warp_ordered_sum(const double* v, int n) {
+  double t = 0.0;
+  for (int i = threadIdx.x & 31; i < n; i += 32) t += v[i];
+  return warp_sum(t);
+}
+
 // Convergence bookkeeping (_kmeans.py:723-741) from the per-cluster squared
 // shifts summed in a fixed order; one thread. The centre image now holds
 // centres scaled by 2^xexp.
@@ -504,9 +600,8 @@ static __device__ bool relocation_path(const MStepArgs& a, int n_empty, int bulk
   if (!grid_barrier(st, nb)) return false;
 
   // 5. convergence bookkeeping
-  if (blockIdx.x == 0) {
-    __shared__ double red_scratch[32];
-    const double tot = block_ordered_sum(dsq_s, a.k, red_scratch);
+  if (blockIdx.x == 0 && threadIdx.x < 32) {
+    const double tot = warp_ordered_sum(dsq_s, a.k);
     if (threadIdx.x == 0) finish_iteration(a, st, changed_now, tot);
   }
   return true;

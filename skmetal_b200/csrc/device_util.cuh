@@ -196,6 +196,36 @@ __host__ __device__ inline size_t cimg_halves(int k_pad, int nk, int stacked) {
   return stacked ? (size_t)nk * 2 * k_pad * 16 : (size_t)nk * k_pad * 16 + (size_t)((nk + 1) / 2) * k_pad * 16;
 }
 
+// Writes centre c, columns 4q .. 4q + 3 (values v[0..3], scale s = 2^e) into
+// the image: the quad's entries are 4 consecutive halves in every segment
+// (8-byte aligned), so three 8-byte stores write them.
+__device__ __forceinline__ void cimg_put4(const CentreImage& ci, int c, int q, const float* v, float s) {
+  uint32_t h[2], l[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const __half2 hh = __floats2half2_rn(v[2 * p] * s, v[2 * p + 1] * s);
+    const float2 hf = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(v[2 * p] * s - hf.x, v[2 * p + 1] * s - hf.y);
+    h[p] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[p] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  const uint2 hv = make_uint2(h[0], h[1]), lv = make_uint2(l[0], l[1]);
+  const int chunk = q >> 1, e = (q & 1) * 4;
+  const int N = ci.stacked ? 2 * ci.k_pad : ci.k_pad;
+  const size_t base = (size_t)chunk * N * 16;
+  const size_t r = (size_t)(c >> 3) * 64 + (size_t)(c & 7) * 8 + e;
+  *reinterpret_cast<uint2*>(ci.img + base + r) = hv;
+  *reinterpret_cast<uint2*>(ci.img + base + (size_t)N * 8 + r) = hv;
+  if (ci.stacked) {
+    const int cl = ci.k_pad + c;
+    *reinterpret_cast<uint2*>(ci.img + base + (size_t)(cl >> 3) * 64 + (size_t)(cl & 7) * 8 + e) = lv;
+  } else {
+    const size_t seg2 = (size_t)ci.nk * ci.k_pad * 16;
+    *reinterpret_cast<uint2*>(ci.img + seg2 + (size_t)(chunk >> 1) * ci.k_pad * 16 + (size_t)(chunk & 1) * ci.k_pad * 8 +
+                              r) = lv;
+  }
+}
+
 // Writes centre c, column j (value v, scale s = 2^e) into the image.
 __device__ __forceinline__ void cimg_put(const CentreImage& ci, int c, int j, float v, float s) {
   const float vs = v * s;

@@ -294,8 +294,9 @@ struct Pass {
   int par;       // parity of the pass (the issuers' drain barriers complete once per pass)
   int pre;       // tiles of this pass whose copies the previous pass already issued
   int pre_next;  // tiles of the next pass to issue at the end of this one
-  int load_image;  // the producer copies the centre image from global memory (else it is in place)
-  int img_par;     // parity of that image load
+  int load_image;  // the producer issues the copy of the centre image from global memory
+  int wait_image;  // the pass waits for an image copy (issued by the producer or earlier by the caller)
+  int img_par;     // parity of that image copy
   float negscale;  // -2^(1 - xexp - cexp): dot products to distances
   long long* deltas;            // nullable: fixed-point deltas of rows that change label
   unsigned long long* changed;  // nullable: count of rows that change label
@@ -383,8 +384,17 @@ __device__ __forceinline__ void cta_teardown(const Params& p, const Cta& c) {
   }
 }
 
+// One thread: copies the centre image from global memory into the CTA's
+// image region, completing on B_C_FULL.
+__device__ __forceinline__ void issue_image_copy(const Params& p, const Cta& c) {
+  mbar_expect_tx(c.bar(B_C_FULL), p.img_bytes);  // < 1 MB: one copy, one transaction count
+  bulk_load(c.sbase + c.L.c, p.img, p.img_bytes, c.bar(B_C_FULL));
+}
+
 // One pass of the pipeline over this CTA's tiles, every thread in its warp
-// role: the producer copies the centre image (P.load_image) and the tiles,
+// role: the producer copies the centre image (P.load_image; the MMAs wait for
+// a copy when P.wait_image, which the caller may also have issued) and the
+// tiles,
 // the issuers run the MMAs, the epilogue writes labels, counts changed rows
 // into P.changed and, with P.deltas non-null, adds their fixed-point deltas.
 // P.ig0 = tiles this CTA processed in earlier passes of the launch: stage and
@@ -406,12 +416,7 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      if (P.load_image) {
-        mbar_expect_tx(c.bar(B_C_FULL), p.img_bytes);
-        for (uint32_t o = 0; o < p.img_bytes; o += 8192u)
-          bulk_load(c.sbase + c.L.c + o, reinterpret_cast<const char*>(p.img) + o, min(8192u, p.img_bytes - o),
-                    c.bar(B_C_FULL));
-      }
+      if (P.load_image) issue_image_copy(p, c);
       // tiles i of this pass (i >= pre), then tiles i < pre_next of the next
       const int n_issue = my_tiles - P.pre + min(P.pre_next, my_tiles);
       const uint64_t pol = l2_evict_first_policy();
@@ -422,13 +427,11 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
         if (!mbar_wait(c.bar(B_EMPTY(s)), ((ig / p.stages) & 1) ^ 1, c.abort_flag, p.err, 2101)) break;
         const int tile = (int)blockIdx.x + i * (int)gridDim.x;
         const unsigned char* src = p.Xs + (size_t)tile * p.tile_bytes;
-        mbar_expect_tx(c.bar(B_FULL(s)), p.tile_bytes);
-        for (uint32_t o = 0; o < p.tile_bytes; o += 8192u)
-          bulk_load_hint(c.sbase + (uint32_t)s * p.stage_bytes + o, src + o, min(8192u, p.tile_bytes - o),
-                         c.bar(B_FULL(s)), pol);
+        mbar_expect_tx(c.bar(B_FULL(s)), p.tile_bytes);  // <= 64 KB: one copy per tile
+        bulk_load_hint(c.sbase + (uint32_t)s * p.stage_bytes, src, p.tile_bytes, c.bar(B_FULL(s)), pol);
         c.issued = ig + 1;
       }
-      if (P.load_image) {  // the image copy lands before the pass ends
+      if (P.wait_image) {  // the image copy lands before the pass ends
         volatile int no_abort = 0;
         mbar_wait(c.bar(B_C_FULL), P.img_par, &no_abort, p.err, 2102);
       }
@@ -437,7 +440,7 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
     // ---------------------------------------------------------- MMA issuers
     const int t = warp == MMA_W0 ? 0 : 1;
     if (lane == 0 && t < c.n_iss) {
-      bool ok = !P.load_image || mbar_wait(c.bar(B_C_FULL), P.img_par, c.abort_flag, p.err, 2201);
+      bool ok = !P.wait_image || mbar_wait(c.bar(B_C_FULL), P.img_par, c.abort_flag, p.err, 2201);
       for (int i = (t - ig0 % c.n_iss + c.n_iss) % c.n_iss; ok && i < my_tiles; i += c.n_iss) {
         const int ig = ig0 + i;
         const int s = ig % p.stages, a = ig % p.nacc;

@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
   cta_setup(p, smem_raw, p.bias, c);
   Pass P{};
   P.load_image = 1;
+  P.wait_image = 1;
   P.negscale = -ldexpf(1.0f, 1 - __ldcg(p.sexp) - __ldcg(p.sexp + 1));
   P.deltas = deltas;
   P.changed = p.changed;

@@ -436,6 +436,8 @@ static int run_fit(const FitParams& p) {
     li.m = ma;
     li.prof = prof_d;
     SKM_TRY(buf.alloc_n(&li.part, 3 * (size_t)k));
+    SKM_TRY(buf.alloc_n(&li.bar, 1));
+    SKM_CUDA(cudaMemsetAsync(li.bar, 0, sizeof(unsigned int), s));
     SKM_TRY(tc_lloyd_loop(plan.tcp, li, s));
     SKM_CUDA(cudaEventRecord(ev2, s));
     if (prof_d)

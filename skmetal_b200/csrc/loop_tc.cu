@@ -53,8 +53,41 @@ struct LoopArgs {
   long long* cnt[2];
   float* C[2];
   double* part;  // per cluster: squared shift [0, k), squared norm [k, 2k), empty flag [2k, 3k)
+  unsigned int* bar;  // the loop's grid-barrier counter, zero at launch
   unsigned long long* prof;
 };
+
+// Grid barrier of the loop: every CTA adds 1 to a counter that only grows
+// during the launch (zero at launch) and waits until it reaches nb * (number
+// of barriers passed, this one included). The release add and the acquire
+// polls order the CTA's earlier writes (gathered by the block barrier) before
+// every other CTA's later reads. Bounded: after 2 s the CTA records error
+// 1001 and returns false.
+__device__ __forceinline__ bool loop_barrier(FitState* st, unsigned int* counter, unsigned int target) {
+  __shared__ int ok_s;
+  block_sync();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    if (v < target) {
+      const unsigned long long t0 = tc::globaltimer();
+      for (unsigned int i = 1;; ++i) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+        if (v >= target) break;
+        if ((i & 255) == 0 && tc::globaltimer() - t0 > 2000000000ull) {
+          atomicExch(&st->error, 1001);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    ok_s = ok;
+  }
+  block_sync();
+  return ok_s != 0;
+}
 
 __device__ __forceinline__ void proxy_fence_all() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -74,6 +107,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
   FitState* st = la.m.st;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ int flags_s[2];
+  __shared__ double dsq_s[MAX_KPAD];
   Cta c;
   cta_setup(p, smem_raw, p.bias, c);
 
@@ -90,7 +124,8 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
   const int max_iter = st->max_iter;
   int bulk = st->bulk;
   int done = st->done;
-  int img_loads = 0, pre = 0;
+  int img_loads = 0, pre = 0, image_issued = 0;
+  unsigned int n_bar = 0;  // loop barriers passed
   int t = 0;
   for (; !done; ++t) {
     const int par = t & 1;
@@ -105,6 +140,9 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     const float* C_old = la.C[par];
     float* C_new = la.C[par ^ 1];
     stamp(la.prof, 4 * t);
+    // an image copy issued by the producer below reads what other CTAs (or
+    // the relocation path) wrote through the generic proxy
+    if (t > 0) proxy_fence_all();
 
     // ---------------------------------------------------------------- E-step
     Pass P{};
@@ -113,7 +151,10 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     P.pre = pre;
     // bulk iterations use the stages as the sums' workspace: nothing in flight
     P.pre_next = (bulk || t + 1 >= max_iter) ? 0 : min(p.stages, c.my_tiles);
-    P.load_image = 1;  // the centre image of the previous M-step (or of centre_prep)
+    // the centre image of the previous M-step (or of centre_prep): after the
+    // fast path the M-step already issued its copy
+    P.load_image = !image_issued;
+    P.wait_image = 1;
     P.img_par = img_loads & 1;
     P.negscale = negscale;
     P.deltas = bulk ? nullptr : Dp;
@@ -122,7 +163,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     ++img_loads;
     pre = P.pre_next;
     proxy_fence_all();
-    if (!grid_barrier(st, nb)) break;
+    if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
     if (__ldcg(&st->error)) break;  // uniform: read after the barrier
     stamp(la.prof, 4 * t + 1);
     const unsigned long long changed_now = __ldcg(chg);
@@ -141,7 +182,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
                 bulk_acc_bytes(k, ld, c.L.bars) ? reinterpret_cast<long long*>(c.base) : nullptr);
       zero_stage_padding(p, c);
       proxy_fence_all();
-      if (!grid_barrier(st, nb)) break;
+      if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
     }
     // (no block touches S_in, D or the counts before the barrier above)
     // owners: cluster cl is CTA cl mod nb's, one warp per owned cluster
@@ -149,13 +190,20 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       double* dsq_c = la.part;
       double* nrm_c = la.part + k;
       double* emp_c = la.part + 2 * k;
+      const int nq = ld >> 2;  // <= 32: one column quad per lane
       for (int m = warp; blockIdx.x + (long long)m * nb < (long long)k; m += nwarps) {
         const int cl = (int)(blockIdx.x + (long long)m * nb);
+        const long long i0 = (long long)cl * ld + 4 * lane;
+        // the quad and the count loads go out together (one round trip)
+        QuadSums r{};
+        if (lane < nq) r = quad_load(S_in, Dp, C_old, i0, bulk);
         const long long cnew = (bulk ? 0 : __ldcg(cnt_in + cl)) + __ldcg(dcnt + cl);
         double dsq = 0.0, nrm = 0.0;
-        if (cnew > 0)
-          warp_centre_from_sums(cl, ld, d, S_in, Dp, bulk, cnew, inv_scale, C_old, cs, la.m.cimg, CentreImage{},
-                                S_out, C_new, nullptr, &dsq, &nrm);
+        if (cnew > 0 && lane < nq)  // the canonical order of warp_centre_from_sums
+          quad_finish(r, cl, lane, i0, d, centre_factor(inv_scale, cnew), cs, la.m.cimg, CentreImage{}, S_out, C_new,
+                      nullptr, dsq, nrm);
+        dsq = warp_sum(dsq);
+        nrm = warp_sum(nrm);
         // cl's deltas of iteration t - 1: their readers finished before this
         // iteration's first barrier; E-step t + 2 adds into them again
         for (int j = 4 * lane; j < ld; j += 128) {
@@ -173,24 +221,27 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       }
       if (blockIdx.x == 0 && threadIdx.x == 0) D_prev[ks + k] = 0;  // its changed counter
       proxy_fence_all();
-      if (!grid_barrier(st, nb)) break;
+      if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
       stamp(la.prof, 4 * t + 2);
-      // every CTA: flags, ||c||^2, and the total shift in the canonical order
-      int n_empty_w = 0;
-      for (int cl = threadIdx.x; cl < p.k_pad; cl += blockDim.x) {
-        if (cl < k) {
-          c.bias_s[cl] = (float)__ldcg(nrm_c + cl);
-          n_empty_w += __ldcg(emp_c + cl) != 0.0;
-        } else {
-          c.bias_s[cl] = INFINITY;
-        }
-      }
+      // every CTA: flags, ||c||^2, and the total shift in the canonical
+      // order (warp_ordered_sum); one load round (k <= 256 < threads)
+      const int cl_t = threadIdx.x;
+      const double dsq_t = cl_t < k ? __ldcg(dsq_c + cl_t) : 0.0;
+      const double nrm_t = cl_t < k ? __ldcg(nrm_c + cl_t) : 0.0;
+      const double emp_t = cl_t < k ? __ldcg(emp_c + cl_t) : 0.0;
+      if (cl_t < k) dsq_s[cl_t] = dsq_t;
+      if (cl_t < p.k_pad) c.bias_s[cl_t] = cl_t < k ? (float)nrm_t : INFINITY;
       __syncwarp();
-      const int n_empty = __syncthreads_count(n_empty_w != 0) ? 1 : 0;  // any empty cluster
+      const int n_empty = __syncthreads_count(emp_t != 0.0) ? 1 : 0;  // any empty cluster
+      // the owners' image is complete: its copy overlaps the decision
+      image_issued = n_empty == 0;
+      if (image_issued && threadIdx.x == MMA_W0 * 32) {  // an otherwise idle lane
+        // written by other CTAs' generic stores, read by this CTA's async proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        issue_image_copy(p, c);
+      }
       if (n_empty == 0 && warp == 0) {
-        double tt = 0.0;
-        for (int cl = lane; cl < k; cl += 32) tt += __ldcg(dsq_c + cl);
-        const double tot = warp_sum(tt);
+        const double tot = warp_ordered_sum(dsq_s, k);
         if (lane == 0) {
           // _kmeans.py:723-741, as finish_iteration
           const int it = t + 1;
@@ -227,7 +278,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
           else cnt_out[i - ks] = __ldcg(cnt_in + (i - ks));
         }
         proxy_fence_all();
-        if (!grid_barrier(st, nb)) break;
+        if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
         load_bias(p, c, la.m.bias);
         done = *reinterpret_cast<volatile int*>(&st->done);
         bulk = *reinterpret_cast<volatile int*>(&st->bulk);
@@ -277,6 +328,7 @@ int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
     la.C[i] = in.C[i];
   }
   la.part = in.part;
+  la.bar = in.bar;
   la.prof = in.prof;
   static int attr_dev = -1;
   int dev = 0;

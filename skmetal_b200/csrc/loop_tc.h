@@ -22,6 +22,7 @@ struct LoopInputs {
   float* C[2];               // centres by iteration parity: iteration t reads C[t & 1], writes C[(t + 1) & 1]
   MStepArgs m;               // the M-step's state and scratch (D, S, counts, changed, C_old, C_new unused)
   double* part;              // 3 k doubles of per-cluster results of the owners
+  unsigned int* bar;         // grid-barrier counter of the loop, zero at launch
   unsigned long long* prof;  // nullable: 4 * max_iter + 1 globaltimer stamps (see lloyd_loop_kernel)
 };
 

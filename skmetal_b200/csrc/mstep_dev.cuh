@@ -318,10 +318,11 @@ __device__ __forceinline__ void quad_finish(const QuadSums& r, int c, int q, lon
       const double df = (double)v[u] - (double)old[u];
       dsq += df * df;
       nrm += (double)v[u] * v[u];
-      if (img1.img) cimg_put(img1, c, j, v[u], cs);
-      if (img2.img) cimg_put(img2, c, j, v[u], cs);
     }
   }
+  // image entries of columns >= d are zero, as are v[u] there
+  if (img1.img) cimg_put4(img1, c, q, v, cs);
+  if (img2.img) cimg_put4(img2, c, q, v, cs);
   if (S_out) {
     *reinterpret_cast<longlong2*>(S_out + i) = make_longlong2(r.s[0], r.s[1]);
     *reinterpret_cast<longlong2*>(S_out + i + 2) = make_longlong2(r.s[2], r.s[3]);

@@ -28,9 +28,14 @@ __host__ __device__ __forceinline__ long long xblk_index(long long r, int j, int
   return (r >> 7) * (128LL * ld) + (long long)(j >> 2) * 512 + (r & 127) * 4 + (j & 3);
 }
 
-// value * 2^F rounded to the nearest integer (2^F = scale, a power of two, so
-// the product is exact in float64)
+// value * 2^F rounded to the nearest integer, ties to even (2^F = scale, a
+// power of two). When 2^F is a normal float the product v * 2^F is exact in
+// float32 (or below 2^-126, where it rounds to 0 either way) and the float32
+// conversion, twice the throughput of the float64 one, gives the same
+// integer; otherwise the product is formed in float64, where it is exact.
 __device__ __forceinline__ long long to_fixed(float v, double scale) {
+  const float fs = static_cast<float>(scale);
+  if (fs >= 1.17549435e-38f && fs <= 1.70141183e38f) return __float2ll_rn(v * fs);  // 2^-126 .. 2^127
   return __double2ll_rn(static_cast<double>(v) * scale);
 }
 
@@ -41,6 +46,67 @@ __device__ __forceinline__ double centre_factor(double inv_scale, long long coun
   return inv_scale / (double)count;
 }
 __device__ __forceinline__ float centre_from_sum(long long s, double factor) { return (float)((double)s * factor); }
+
+// ---------------------------------------------------------------------------
+// shared-memory barriers (mbarrier) and bulk copies (cp.async.bulk, the TMA
+// engine's untiled form), single-thread wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// L2 policy for data read once per pass (the tiles of X): evicted first, so
+// that streaming X through L2 does not push out the small state the M-step
+// reads back every iteration.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                               uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(dst), "l"(reinterpret_cast<unsigned long long>(src)), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
 
 // Programmatic dependent launch (kernels launched with the programmatic
 // stream-serialization attribute): allow the next kernel of the stream to be

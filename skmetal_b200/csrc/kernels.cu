@@ -408,8 +408,8 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   if (done) return;
   extern __shared__ __align__(16) long long dyn_smem[];
   if (bulk && !a.bulk_external) {
-    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale,
-              bulk_acc_bytes(a.k, a.ld, kBulkSmemBytes) ? dyn_smem : nullptr);
+    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, reinterpret_cast<unsigned char*>(dyn_smem),
+              mstep_smem_bytes(a.k, a.ld), &st->error);
     if (!grid_barrier(st, nb)) return;
   }
   // 1. empty clusters of the new assignment; every block computes the same answer
@@ -493,8 +493,8 @@ __global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long l
   const int bulk = st->bulk;
   extern __shared__ __align__(16) long long dyn_smem[];
   if (bulk)
-    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale,
-              bulk_acc_bytes(a.k, a.ld, kBulkSmemBytes) ? dyn_smem : nullptr);
+    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, reinterpret_cast<unsigned char*>(dyn_smem),
+              mstep_smem_bytes(a.k, a.ld), &st->error);
   if (!grid_barrier(st, nb)) return;
   // local counts after this iteration, and how many clusters this rank has empty
   const long long* dcnt = a.D + (long long)a.k * a.ld;

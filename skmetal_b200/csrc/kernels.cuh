@@ -11,11 +11,34 @@ namespace skm {
 constexpr int kAssignSmemFloats = 12288;  // 48 KB of centres per chunk
 constexpr size_t kBulkSmemBytes = 160 * 1024;  // bulk pass accumulates privately when (k*ld + k) int64 fit
 
-// The bulk pass's private accumulator: (k*ld + k) int64 when they fit in
-// `avail` bytes of shared memory, else 0 (sums go straight to global memory).
+// The atomic bulk pass's private accumulator: (k*ld + k) int64 when they fit
+// in `avail` bytes of shared memory, else 0 (sums go straight to global
+// memory).
 __host__ __device__ inline size_t bulk_acc_bytes(int k, int ld, size_t avail) {
   const size_t b = sizeof(long long) * ((size_t)k * ld + k);
   return b <= avail ? b : 0;
+}
+
+// The tiled bulk pass (bulk_pass_tiles) stages tiles of 128 rows of the
+// blocked X in shared memory with bulk copies, one per 2 KB column-quad block
+// at a stride of 2064 bytes (so that lanes reading consecutive quads of one
+// row hit distinct banks), two tiles in flight. Layout: 2 x [nq quad blocks |
+// 128 labels (int32)], 2 mbarriers, then the sort tables (hist 2 x k, offs
+// k + 1, cur k, rows 128; int32). Usable when each thread owns at most 2
+// (cluster, column quad) pairs and ld <= 128; the labels buffer must hold
+// round_up(n, 128) entries (-1 past n).
+constexpr int kBulkTileRows = 128;
+constexpr int kBulkMaxPairsPerThread = 2;
+constexpr int kBulkQuadStride = 2064;  // bytes between quad blocks of a staged tile
+__host__ __device__ inline size_t bulk_tile_bytes(int ld) {
+  return (size_t)(ld / 4) * kBulkQuadStride + 4 * kBulkTileRows;  // quads, then labels
+}
+__host__ __device__ inline size_t bulk_tiles_bytes(int k, int ld) {
+  return 2 * bulk_tile_bytes(ld) + 16 + 4 * (4 * (size_t)k + 1 + kBulkTileRows);
+}
+__host__ __device__ inline bool bulk_tiles_ok(int k, int ld, int threads, size_t avail) {
+  const long long pairs = (long long)k * (ld / 4);
+  return ld <= 128 && pairs <= (long long)kBulkMaxPairsPerThread * threads && bulk_tiles_bytes(k, ld) <= avail;
 }
 
 // Relocation candidates of one rank (multi-GPU fits), one slot per rank after
@@ -37,7 +60,9 @@ __host__ __device__ inline size_t cand_x_off(int cap) { return 16 + (size_t)cap 
 constexpr int kBulkDivisor = 10;
 
 // Dynamic shared memory of mstep_kernel for k clusters of ld columns.
-inline size_t mstep_smem_bytes(int k, int ld) { return bulk_acc_bytes(k, ld, kBulkSmemBytes); }
+__host__ __device__ inline size_t mstep_smem_bytes(int k, int ld) {
+  return bulk_tiles_ok(k, ld, 1024, kBulkSmemBytes) ? bulk_tiles_bytes(k, ld) : bulk_acc_bytes(k, ld, kBulkSmemBytes);
+}
 
 
 struct MStepArgs {

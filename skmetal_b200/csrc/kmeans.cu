@@ -210,7 +210,8 @@ static int run_fit(const FitParams& p) {
   SKM_TRY(buf.alloc_n(&mean, (size_t)ld));
   SKM_TRY(buf.alloc_n(&mind, (size_t)n));
   SKM_TRY(buf.alloc_n(&init_d, (size_t)k * d));
-  SKM_TRY(buf.alloc_n(&labels, (size_t)n));
+  // whole 128-row tiles (-1 past n): the tiled bulk pass copies them per tile
+  SKM_TRY(buf.alloc_n(&labels, (size_t)n_pad));
   // persistent sums of the current labels: S (k*ld) | counts (k)
   SKM_TRY(buf.alloc_n(&S, (size_t)k * ld + k));
   long long* counts = S + (size_t)k * ld;
@@ -301,7 +302,7 @@ static int run_fit(const FitParams& p) {
   init_state_kernel<<<1, 32, 0, s>>>(st, p.max_iter, p.tol, tol_rel ? 1 : 0, tol_rel ? sumsq : nullptr,
                                      (double)n_total, d, &u32s[1], p.bulk_sums ? 1 : 0);
   SKM_TRY(check_launch("init_state_kernel"));
-  SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n, s));  // label -1: every row changes in iteration 1
+  SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n_pad, s));  // label -1: every row changes in iteration 1
   SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
   SKM_CUDA(cudaMemsetAsync(D, 0, sizeof(long long) * payload_len, s));
 

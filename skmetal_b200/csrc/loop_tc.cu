@@ -72,11 +72,11 @@ __device__ __forceinline__ bool loop_barrier(FitState* st, unsigned int* counter
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
     if (v < target) {
-      const unsigned long long t0 = tc::globaltimer();
+      const unsigned long long t0 = globaltimer();
       for (unsigned int i = 1;; ++i) {
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
         if (v >= target) break;
-        if ((i & 255) == 0 && tc::globaltimer() - t0 > 2000000000ull) {
+        if ((i & 255) == 0 && globaltimer() - t0 > 2000000000ull) {
           atomicExch(&st->error, 1001);
           ok = 0;
           break;
@@ -98,7 +98,7 @@ __device__ __forceinline__ void proxy_fence_all() {
 // E-step done (after the first barrier), [4t + 2] owners done (after the
 // second), [4t + 3] M-step done; [4 T] the end.
 __device__ __forceinline__ void stamp(unsigned long long* prof, int i) {
-  if (prof && blockIdx.x == 0 && threadIdx.x == 0) prof[i] = tc::globaltimer();
+  if (prof && blockIdx.x == 0 && threadIdx.x == 0) prof[i] = globaltimer();
 }
 
 __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la) {
@@ -178,8 +178,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     a.C_new = C_new;
     a.host_done = nullptr;
     if (bulk) {
-      bulk_pass(p.X, ld, p.n, p.labels, k, Dp, st->scale,
-                bulk_acc_bytes(k, ld, c.L.bars) ? reinterpret_cast<long long*>(c.base) : nullptr);
+      bulk_pass(p.X, ld, p.n, p.labels, k, Dp, st->scale, c.base, c.L.bars, &st->error);
       zero_stage_padding(p, c);
       proxy_fence_all();
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;

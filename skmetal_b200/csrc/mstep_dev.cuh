@@ -154,13 +154,181 @@ static __device__ void bulk_pass_atomic(const float* __restrict__ X, int ld, lon
 }
 
 
-// The bulk pass with a shared accumulator `acc` of (k*ld + k) int64, or
-// straight to global memory with acc null; every thread of every block calls
-// it.
+// Tiled variant (bulk_tiles_ok): block b takes the tiles b, b + B, ... of 128
+// rows. Thread 0 copies each tile's quad blocks and labels into shared memory
+// with bulk copies (two tiles in flight, completion on one mbarrier per
+// buffer); the block counting-sorts the tile's rows by label, and thread t,
+// owner of the (cluster, column quad) pairs t, t + T, ... (pair p = cluster
+// p / nq, quad p % nq, so that a warp's lanes mostly share a cluster and read
+// consecutive quads of one row), adds the quad of every row of its cluster in
+// registers. The block adds its totals to D once at the end: no per-element
+// atomics. Waits are bounded (error 1004 in *err; the pass then stops).
+static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long long n,
+                                       const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
+                                       double scale, unsigned char* ws, int* err) {
+  constexpr int TR = kBulkTileRows;
+  const int nq = ld >> 2;
+  const size_t tb = bulk_tile_bytes(ld);
+  unsigned char* tile_s[2] = {ws, ws + tb};
+  const int* lab_s[2] = {reinterpret_cast<const int*>(ws + (size_t)nq * kBulkQuadStride),
+                         reinterpret_cast<const int*>(ws + tb + (size_t)nq * kBulkQuadStride)};
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ws + 2 * tb);
+  int* hist2 = reinterpret_cast<int*>(bars + 2);  // 2 x k
+  int* offs = hist2 + 2 * k;                      // k + 1
+  int* cur = offs + k + 1;                        // k
+  int* rows = cur + k;                            // 128
+  __shared__ int stop_sh;
+  volatile int& stop_s = stop_sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int T = blockDim.x;
+  const long long ks = (long long)k * ld;
+  const int pairs = k * nq;
+  const long long n_tiles = (n + TR - 1) / TR;
+  const uint32_t tx = (uint32_t)nq * 2048u + 4u * TR;
+  long long acc[kBulkMaxPairsPerThread][4];
+  long long cnt_acc[kBulkMaxPairsPerThread];
+#pragma unroll
+  for (int m = 0; m < kBulkMaxPairsPerThread; ++m) {
+    cnt_acc[m] = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[m][u] = 0;
+  }
+  // thread 0: copy tile t into buffer b
+  auto issue = [&](long long t, int b) {
+    const uint32_t bar = smem_u32(bars + b);
+    mbar_expect_tx(bar, tx);
+    const char* src = reinterpret_cast<const char*>(X + t * TR * ld);
+    const uint32_t dst = smem_u32(tile_s[b]);
+    for (int q = 0; q < nq; ++q) bulk_load(dst + (uint32_t)q * kBulkQuadStride, src + (size_t)q * 2048, 2048u, bar);
+    bulk_load(smem_u32(lab_s[b]), labels + t * TR, 4u * TR, bar);
+  };
+  if (tid == 0) {
+    mbar_init(smem_u32(bars), 1);
+    mbar_init(smem_u32(bars + 1), 1);
+    stop_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the buffers held other data
+  }
+  for (int c = tid; c < 2 * k; c += T) hist2[c] = 0;
+  block_sync();
+  const long long t0 = blockIdx.x;
+  if (tid == 0) {
+    if (t0 < n_tiles) issue(t0, 0);
+    if (t0 + gridDim.x < n_tiles) issue(t0 + gridDim.x, 1);
+  }
+  int i = 0;
+  for (long long t = t0; t < n_tiles; t += gridDim.x, ++i) {
+    const int b = i & 1;
+    int* hist = hist2 + b * k;
+    const unsigned char* cb = tile_s[b];
+    const int* lab = lab_s[b];
+    // wait for the tile (bounded)
+    {
+      const uint32_t bar = smem_u32(bars + b);
+      const uint32_t par = (uint32_t)(i >> 1) & 1u;
+      if (!mbar_try_wait(bar, par)) {
+        const unsigned long long w0 = globaltimer();
+        for (uint32_t it = 1; !mbar_try_wait(bar, par); ++it) {
+          if ((it & 63) == 0 && (stop_s || globaltimer() - w0 > 2000000000ull)) {
+            stop_s = 1;
+            atomicCAS(err, 0, 1004);
+            break;
+          }
+        }
+      }
+    }
+    if (tid < TR) {
+      const int c = lab[tid];  // in [0, k) (E-step output, -1 past n); anything else is left out
+      if ((unsigned)c < (unsigned)k) atomicAdd(&hist[c], 1);
+    }
+    block_sync();
+    if (stop_s) break;
+    if (warp == 0) {  // exclusive scan of the histogram
+      int carry = 0;
+      for (int b0 = 0; b0 < k; b0 += 32) {
+        const int c = b0 + lane;
+        const int h = c < k ? hist[c] : 0;
+        int x = h;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        if (c < k) {
+          offs[c] = carry + x - h;
+          cur[c] = carry + x - h;
+        }
+        carry += __shfl_sync(0xffffffffu, x, 31);
+      }
+      if (lane == 0) offs[k] = carry;
+    }
+#pragma unroll
+    for (int m = 0; m < kBulkMaxPairsPerThread; ++m)
+      if (tid + m * T < k) cnt_acc[m] += hist[tid + m * T];
+    block_sync();
+    if (tid < TR) {
+      const int c = lab[tid];
+      if ((unsigned)c < (unsigned)k) rows[atomicAdd(&cur[c], 1)] = tid;
+    }
+    for (int c = tid; c < k; c += T) hist[c] = 0;  // for the tile after next (this buffer's)
+    block_sync();
+#pragma unroll
+    for (int m = 0; m < kBulkMaxPairsPerThread; ++m) {
+      const int p = tid + m * T;
+      if (p >= pairs) break;
+      const int c = p / nq, q = p - c * nq;
+      const unsigned char* qb = cb + (size_t)q * kBulkQuadStride;
+      for (int j = offs[c]; j < offs[c + 1]; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(qb + rows[j] * 16);
+        acc[m][0] += to_fixed(v.x, scale);
+        acc[m][1] += to_fixed(v.y, scale);
+        acc[m][2] += to_fixed(v.z, scale);
+        acc[m][3] += to_fixed(v.w, scale);
+      }
+    }
+    // the buffer is read; the next copy into it goes through the async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    block_sync();
+    if (tid == 0 && t + 2 * (long long)gridDim.x < n_tiles) issue(t + 2 * (long long)gridDim.x, b);
+  }
+  // a stopped pass (at tile index i) lets its copies land before the
+  // workspace is reused: tile i in buffer i & 1 and, if it exists, tile i + 1
+  // in the other buffer (bounded)
+  if (tid == 0 && stop_s) {
+    for (int u = i; u <= i + 1; ++u) {
+      if (t0 + (long long)u * gridDim.x >= n_tiles) break;
+      const uint32_t bar = smem_u32(bars + (u & 1)), par = (uint32_t)(u >> 1) & 1u;
+      const unsigned long long w0 = globaltimer();
+      while (!mbar_try_wait(bar, par) && globaltimer() - w0 < 2000000000ull) {
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kBulkMaxPairsPerThread; ++m) {
+    const int p = tid + m * T;
+    if (p < pairs) {
+      const int c = p / nq, q = p - c * nq;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (acc[m][u] != 0) red_add_s64(D + (long long)c * ld + 4 * q + u, acc[m][u]);
+    }
+    if (tid + m * T < k && cnt_acc[m] != 0) red_add_s64(D + ks + tid + m * T, cnt_acc[m]);
+  }
+  block_sync();  // the workspace (and its barriers) may be reused after this
+}
+
+// The bulk pass with `ws_bytes` of shared workspace `ws` (16-byte aligned):
+// the tiled variant when it fits, else the atomic one with a shared
+// accumulator when that fits, else straight to global memory. Every thread
+// of every block calls it; `err` receives a code if a wait times out.
 static __device__ __forceinline__ void bulk_pass(const float* __restrict__ X, int ld, long long n,
                                                  const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                                 double scale, long long* acc) {
-  bulk_pass_atomic(X, ld, n, labels, k, D, scale, acc);
+                                                 double scale, unsigned char* ws, size_t ws_bytes, int* err) {
+  if (bulk_tiles_ok(k, ld, blockDim.x, ws_bytes))
+    bulk_pass_tiles(X, ld, n, labels, k, D, scale, ws, err);
+  else
+    bulk_pass_atomic(X, ld, n, labels, k, D, scale,
+                     bulk_acc_bytes(k, ld, ws_bytes) ? reinterpret_cast<long long*>(ws) : nullptr);
 }
 
 // ---------------------------------------------------------------------------

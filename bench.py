@@ -11,10 +11,15 @@ iterations, the final E-step and the inertia).
   (device time of the fit, CUDA events on the library's stream; max over ranks).
 * ``e2e``: the same metric through the public C-ABI call with host buffers
   (pinned X in, labels/centres out, host<->device copies inside the timed region).
-* ``roofline``: the E-step kernel (dominant) against the measured HBM copy
-  bandwidth; algorithmic bytes = 4 n d per launch (X read once); its duration
-  is the CUDA-event time of the E-step launches of every 10th iteration of the
-  timed fits (the library's profile mode samples them to keep its cost low).
+* ``roofline``: the dominant kernel against the measured HBM copy bandwidth;
+  algorithmic bytes = 4 n d per Lloyd iteration (X read once). On one GPU it
+  is the persistent loop kernel (one launch runs every iteration of a fit),
+  timed with CUDA events around its launch; ``e_phase`` splits out the E-step
+  part of an iteration from the kernel's device timestamps. With N > 1 GPUs
+  (multi-launch loop) it is the E-step kernel, timed with CUDA events on the
+  E-step launches of every 10th iteration. ``traffic`` = DRAM bytes per launch
+  from the committed ncu summary (profiles/), scaled to this run's rows and
+  iterations.
 * ``cpu_baseline`` (rank 0, N = 1): scikit-learn's Lloyd (the reference's CPU
   path) on a bounded sample of the same workload.
 
@@ -128,13 +133,14 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml, 5 ms"}
 
 
-def _traffic_for(config: str, rows: int):
-    """DRAM bytes (read + write) per E-step launch from the committed ncu
-    summary of the full-size capture (profiles/estep_tc_<config>.md), scaled
-    by rows when the bench runs a different row count; None without one."""
+def _traffic_for(kernel: str, config: str, rows: int, iters: float = 1.0):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    summary profiles/<kernel>_<config>.md, scaled by rows (and by Lloyd
+    iterations for the loop kernel, whose launch runs all of them) when this
+    run differs from the captured one; None without a summary."""
     import re
 
-    p = ROOT / "profiles" / f"estep_tc_{config}.md"
+    p = ROOT / "profiles" / f"{kernel}_{config}.md"
     if not p.exists():
         return None
     text = p.read_text()
@@ -142,8 +148,11 @@ def _traffic_for(config: str, rows: int):
     n = re.search(r"\((\d[\d,]*) x \d+, k = \d+\)", text)
     if not m or not n:
         return None
-    ref_rows = int(n.group(1).replace(",", ""))
-    return float(m.group(1)) * rows / ref_rows
+    scale = rows / int(n.group(1).replace(",", ""))
+    it = re.search(r"iterations_per_launch = (\d+)", text)
+    if it:
+        scale *= iters / int(it.group(1))
+    return float(m.group(1)) * scale
 
 
 def cpu_baseline(X, init, k, sample_iters: int):
@@ -279,6 +288,7 @@ def main():
         iters += n_iter
     wall = time.perf_counter() - t0
     launches = _bridge.launch_count() - l0
+    persistent = len(_bridge.debug_loop_stamps()) > 0  # the profiled fits ran the loop kernel
     barrier()
     clk = clocks.stop()
     t_dev = ms_total / 1e3
@@ -307,10 +317,28 @@ def main():
     e2e_value = n * e2e_iters / e2e_t
 
     hbm, bf16, src = _peaks()
+    alg_bytes = 4.0 * Xs.shape[0] * w.d  # X read once per Lloyd iteration
     est_avg_s = est_ms / max(1, est_n) / 1e3
-    alg_bytes = 4.0 * Xs.shape[0] * w.d
-    achieved = alg_bytes / est_avg_s / 1e9 if est_avg_s > 0 else None
-    traffic = _traffic_for(w.name, Xs.shape[0])
+    e_achieved = alg_bytes / est_avg_s / 1e9 if est_avg_s > 0 else None
+    if persistent:
+        per_launch = alg_bytes * iters / args.steps  # one launch per fit, all its iterations
+        dur_s = ms_loop / 1e3 / args.steps
+        achieved = per_launch / dur_s / 1e9 if dur_s > 0 else None
+        traffic = _traffic_for("lloyd_loop", w.name, Xs.shape[0], iters / args.steps)
+        kernel = "lloyd_loop_kernel (persistent: every Lloyd iteration of a fit in one launch)"
+        e_timing = "device globaltimer stamps of every iteration (E-step through the grid barrier)"
+    else:
+        per_launch = alg_bytes
+        achieved = e_achieved
+        traffic = _traffic_for("estep_tc", w.name, Xs.shape[0])
+        kernel = "E-step (estep_tc_kernel)"
+        e_timing = "CUDA events on the E-step launches of every 10th iteration"
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": (achieved / hbm) if achieved else None, "traffic": traffic, "kernel": kernel,
+                "peak_source": src, "algorithmic_bytes_per_launch": per_launch,
+                "e_phase": {"achieved": e_achieved, "frac": (e_achieved / hbm) if e_achieved else None,
+                            "timing": e_timing},
+                "loop_frac": (alg_bytes * iters / (ms_loop / 1e3)) / 1e9 / hbm if ms_loop > 0 else None}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True,
@@ -324,10 +352,7 @@ def main():
                 "h2d_bytes_per_step": int(Xs.nbytes + init.nbytes),
                 "d2h_bytes_per_step": int(Xs.shape[0] * 4 + init.nbytes + 12)},
         "gpu_launches": int(launches),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
-                     "kernel": "E-step (estep_tc_kernel)", "peak_source": src,
-                     "loop_frac": (alg_bytes * iters / (ms_loop / 1e3)) / 1e9 / hbm if ms_loop > 0 else None},
+        "roofline": roofline,
         "clocks": clk,
         "wall_s": wall,
     }

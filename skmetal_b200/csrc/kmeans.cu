@@ -591,6 +591,7 @@ static int run_fit(const FitParams& p) {
   fs.ms_loop = ms;
   cudaEventElapsedTime(&ms, ev2, ev3);
   fs.ms_final = ms;
+  if (!(p.profile && persistent)) t_loop_stamps.clear();  // stamps describe the last profiled loop-kernel fit only
   if (p.profile && persistent) {
     // E-step phases of the persistent loop from its globaltimer stamps
     for (int i = 0; i < iters && 4 * i + 1 < (int)prof_stamps.size(); ++i) {

@@ -16,34 +16,37 @@ namespace skm {
 // helpers
 // ---------------------------------------------------------------------------
 
-// Bounded software grid barrier for cooperative launches. Returns false (and
-// records an error in the fit state) if the other blocks do not arrive within
-// the spin limit, so that a broken launch ends instead of hanging the GPU.
+// Bounded software grid barrier for cooperative launches: arrival is an
+// acq_rel add on a counter, the last arrival resets it and releases a
+// generation number the others poll with acquire loads. Returns false (and
+// records error 1001 in the fit state) if the other blocks do not arrive
+// within 2 s, so that a broken launch ends instead of hanging the GPU.
 static __device__ bool grid_barrier(FitState* st, unsigned int nblocks) {
   __shared__ int ok_s;
   block_sync();
   if (threadIdx.x == 0) {
     int ok = 1;
-    volatile unsigned int* genp = &st->barrier_gen;
-    unsigned int gen = *genp;
-    __threadfence();
-    unsigned int arrived = atomicAdd(&st->barrier_count, 1u) + 1u;
-    if (arrived == nblocks) {
-      atomicExch(&st->barrier_count, 0u);
-      __threadfence();
-      atomicAdd(&st->barrier_gen, 1u);
+    unsigned int gen, arrived;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(&st->barrier_gen) : "memory");
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(&st->barrier_count) : "memory");
+    if (arrived + 1u == nblocks) {
+      // the last arrival resets the count for the next barrier, then releases
+      // the generation (the release orders the reset before it)
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(&st->barrier_count) : "memory");
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&st->barrier_gen) : "memory");
     } else {
-      long long spins = 0;
-      while (*genp == gen) {
-        if (++spins > (1LL << 25)) {
+      const unsigned long long t0 = globaltimer();
+      for (unsigned int it = 1;; ++it) {
+        unsigned int g;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(&st->barrier_gen) : "memory");
+        if (g != gen) break;
+        if ((it & 255) == 0 && globaltimer() - t0 > 2000000000ull) {
           atomicExch(&st->error, 1001);
           ok = 0;
           break;
         }
-        __nanosleep(64);
       }
     }
-    __threadfence();
     ok_s = ok;
   }
   block_sync();
@@ -349,10 +352,11 @@ static __device__ bool select_farthest(const float* __restrict__ mind, long long
                                 FitState* st, unsigned int* hist, long long* sel, unsigned int nblocks) {
   __shared__ unsigned int h[256];
   __shared__ unsigned long long prefix_s, mask_s;
-  __shared__ int remaining_s;
+  __shared__ int remaining_s, whole_s;
   unsigned long long prefix = 0, mask = 0;
   int remaining = m;
-  for (int pass = 0; pass < 8; ++pass) {
+  int pass = 0;
+  for (; pass < 8; ++pass) {
     const int shift = 56 - 8 * pass;
     unsigned int* gh = hist + (pass & 1) * 256;
     for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0;
@@ -367,15 +371,18 @@ static __device__ bool select_farthest(const float* __restrict__ mind, long long
     if (!grid_barrier(st, nblocks)) return false;
     if (threadIdx.x == 0) {
       // every block computes the same choice from the same global histogram
-      int cum = 0, digit = 0;
+      int cum = 0, digit = 0, c = 0;
       for (int dgt = 255; dgt >= 0; --dgt) {
-        const int c = (int)gh[dgt];
+        c = (int)gh[dgt];
         if (cum + c >= remaining) { digit = dgt; break; }
         cum += c;
       }
       prefix_s = prefix | ((unsigned long long)digit << shift);
       mask_s = mask | (255ull << shift);
       remaining_s = remaining - cum;
+      // the bucket is taken whole: the keys >= prefix (lower bits zero) are
+      // exactly the m largest, no further digit is needed
+      whole_s = cum + c == remaining;
     }
     block_sync();
     prefix = prefix_s;
@@ -388,8 +395,16 @@ static __device__ bool select_farthest(const float* __restrict__ mind, long long
       for (int i = threadIdx.x; i < 256; i += blockDim.x) oh[i] = 0;
     }
     if (!grid_barrier(st, nblocks)) return false;
+    if (whole_s) break;  // uniform: every block read the same histogram
   }
-  // prefix is now the m-th largest key: collect keys >= prefix (exactly m)
+  // after an early exit the last pass's histogram still holds counts; the
+  // next selection starts from both halves zero (read by nobody until then)
+  if (pass < 8 && blockIdx.x == 0) {
+    unsigned int* gh = hist + (pass & 1) * 256;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) gh[i] = 0;
+  }
+  // keys >= prefix are exactly the m largest: the m-th largest key itself
+  // after eight digits, or a whole bucket's lower bound after an early exit
   for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)nblocks * blockDim.x) {
     const unsigned long long key = reloc_key(mind[r], row_base + r);
     if (key >= prefix) {

@@ -34,11 +34,12 @@ __host__ __device__ inline size_t bulk_tile_bytes(int ld) {
   return (size_t)(ld / 4) * kBulkQuadStride + 4 * kBulkTileRows;  // quads, then labels
 }
 __host__ __device__ inline size_t bulk_tiles_bytes(int k, int ld) {
-  return 2 * bulk_tile_bytes(ld) + 16 + 4 * (4 * (size_t)k + 1 + kBulkTileRows);
+  return 2 * bulk_tile_bytes(ld) + 16 + 4 * 8 * (size_t)k;  // tiles, barriers, two mask sets
 }
 __host__ __device__ inline bool bulk_tiles_ok(int k, int ld, int threads, size_t avail) {
   const long long pairs = (long long)k * (ld / 4);
-  return ld <= 128 && pairs <= (long long)kBulkMaxPairsPerThread * threads && bulk_tiles_bytes(k, ld) <= avail;
+  return ld <= 128 && threads >= 32 * (kBulkTileRows / 32 + 1) && pairs <= (long long)kBulkMaxPairsPerThread * threads &&
+         bulk_tiles_bytes(k, ld) <= avail;
 }
 
 // Relocation candidates of one rank (multi-GPU fits), one slot per rank after

@@ -158,14 +158,18 @@ static __device__ void bulk_pass_atomic(const float* __restrict__ X, int ld, lon
 
 
 // Tiled variant (bulk_tiles_ok): block b takes the tiles b, b + B, ... of 128
-// rows. Thread 0 copies each tile's quad blocks and labels into shared memory
-// with bulk copies (two tiles in flight, completion on one mbarrier per
-// buffer); the block counting-sorts the tile's rows by label, and thread t,
-// owner of the (cluster, column quad) pairs t, t + T, ... (pair p = cluster
-// p / nq, quad p % nq, so that a warp's lanes mostly share a cluster and read
-// consecutive quads of one row), adds the quad of every row of its cluster in
-// registers. The block adds its totals to D once at the end: no per-element
-// atomics. Waits are bounded (error 1004 in *err; the pass then stops).
+// rows. Warp 0 copies each tile's quad blocks and labels into shared memory
+// with bulk copies, one per lane (two tiles in flight, completion on one
+// mbarrier per buffer). Warps 1-4 turn the tile's labels into row masks, one
+// 32-bit word per (cluster, 32-row group) (__match_any_sync: the lowest lane
+// of each label writes its group's mask), and thread t, owner of the
+// (cluster, column quad) pairs t, t + T, ... (pair p = cluster p / nq, quad
+// p % nq, so that a warp's lanes mostly share a cluster and read consecutive
+// quads of one row), adds the quad of every row in its cluster's masks in
+// registers. Two block barriers per tile; the masks alternate between two
+// sets, the one not in use cleared by the other warps. The block adds its
+// totals to D once at the end: no per-element atomics. Waits are bounded
+// (error 1004 in *err; the pass then stops).
 static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long long n,
                                        const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
                                        double scale, unsigned char* ws, int* err) {
@@ -176,15 +180,11 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
   const int* lab_s[2] = {reinterpret_cast<const int*>(ws + (size_t)nq * kBulkQuadStride),
                          reinterpret_cast<const int*>(ws + tb + (size_t)nq * kBulkQuadStride)};
   uint64_t* bars = reinterpret_cast<uint64_t*>(ws + 2 * tb);
-  int* hist2 = reinterpret_cast<int*>(bars + 2);  // 2 x k
-  int* offs = hist2 + 2 * k;                      // k + 1
-  int* cur = offs + k + 1;                        // k
-  int* rows = cur + k;                            // 128
+  unsigned int* masks = reinterpret_cast<unsigned int*>(bars + 2);  // 2 sets x k clusters x 4 groups
   __shared__ int stop_sh;
   volatile int& stop_s = stop_sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = blockDim.x;
-  const long long ks = (long long)k * ld;
   const int pairs = k * nq;
   const long long n_tiles = (n + TR - 1) / TR;
   const uint32_t tx = (uint32_t)nq * 2048u + 4u * TR;
@@ -196,14 +196,18 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
 #pragma unroll
     for (int u = 0; u < 4; ++u) acc[m][u] = 0;
   }
-  // thread 0: copy tile t into buffer b
+  // warp 0: copy tile t into buffer b (lane q < nq the quad block q, lane nq
+  // the labels; lane 0 announces the bytes first)
   auto issue = [&](long long t, int b) {
     const uint32_t bar = smem_u32(bars + b);
-    mbar_expect_tx(bar, tx);
+    if (lane == 0) mbar_expect_tx(bar, tx);
+    __syncwarp();
     const char* src = reinterpret_cast<const char*>(X + t * TR * ld);
     const uint32_t dst = smem_u32(tile_s[b]);
-    for (int q = 0; q < nq; ++q) bulk_load(dst + (uint32_t)q * kBulkQuadStride, src + (size_t)q * 2048, 2048u, bar);
-    bulk_load(smem_u32(lab_s[b]), labels + t * TR, 4u * TR, bar);
+    for (int q = lane; q <= nq; q += 32) {
+      if (q < nq) bulk_load(dst + (uint32_t)q * kBulkQuadStride, src + (size_t)q * 2048, 2048u, bar);
+      else bulk_load(smem_u32(lab_s[b]), labels + t * TR, 4u * TR, bar);
+    }
   };
   if (tid == 0) {
     mbar_init(smem_u32(bars), 1);
@@ -212,19 +216,18 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the buffers held other data
   }
-  for (int c = tid; c < 2 * k; c += T) hist2[c] = 0;
+  for (int i = tid; i < 8 * k; i += T) masks[i] = 0;
   block_sync();
   const long long t0 = blockIdx.x;
-  if (tid == 0) {
+  if (warp == 0) {
     if (t0 < n_tiles) issue(t0, 0);
     if (t0 + gridDim.x < n_tiles) issue(t0 + gridDim.x, 1);
   }
   int i = 0;
   for (long long t = t0; t < n_tiles; t += gridDim.x, ++i) {
     const int b = i & 1;
-    int* hist = hist2 + b * k;
+    unsigned int* mk = masks + b * 4 * k;
     const unsigned char* cb = tile_s[b];
-    const int* lab = lab_s[b];
     // wait for the tile (bounded)
     {
       const uint32_t bar = smem_u32(bars + b);
@@ -240,59 +243,44 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
         }
       }
     }
-    if (tid < TR) {
-      const int c = lab[tid];  // in [0, k) (E-step output, -1 past n); anything else is left out
-      if ((unsigned)c < (unsigned)k) atomicAdd(&hist[c], 1);
+    if (warp >= 1 && warp <= TR / 32) {  // masks of this tile: labels in [0, k), -1 past n
+      const int g = warp - 1;
+      const int c = lab_s[b][g * 32 + lane];
+      const unsigned int same = __match_any_sync(0xffffffffu, c);
+      if ((unsigned)c < (unsigned)k && (__ffs(same) - 1) == lane) mk[c * 4 + g] = same;
+    } else {  // the other set: read by the previous tile only (before its last barrier)
+      unsigned int* other = masks + (b ^ 1) * 4 * k;
+      const int w = warp == 0 ? 0 : warp - TR / 32;
+      const int nw_clear = (T >> 5) - TR / 32;
+      for (int j = w * 32 + lane; j < 4 * k; j += nw_clear * 32) other[j] = 0;
     }
     block_sync();
     if (stop_s) break;
-    if (warp == 0) {  // exclusive scan of the histogram
-      int carry = 0;
-      for (int b0 = 0; b0 < k; b0 += 32) {
-        const int c = b0 + lane;
-        const int h = c < k ? hist[c] : 0;
-        int x = h;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, x, o);
-          if (lane >= o) x += y;
-        }
-        if (c < k) {
-          offs[c] = carry + x - h;
-          cur[c] = carry + x - h;
-        }
-        carry += __shfl_sync(0xffffffffu, x, 31);
-      }
-      if (lane == 0) offs[k] = carry;
-    }
-#pragma unroll
-    for (int m = 0; m < kBulkMaxPairsPerThread; ++m)
-      if (tid + m * T < k) cnt_acc[m] += hist[tid + m * T];
-    block_sync();
-    if (tid < TR) {
-      const int c = lab[tid];
-      if ((unsigned)c < (unsigned)k) rows[atomicAdd(&cur[c], 1)] = tid;
-    }
-    for (int c = tid; c < k; c += T) hist[c] = 0;  // for the tile after next (this buffer's)
-    block_sync();
 #pragma unroll
     for (int m = 0; m < kBulkMaxPairsPerThread; ++m) {
       const int p = tid + m * T;
       if (p >= pairs) break;
       const int c = p / nq, q = p - c * nq;
       const unsigned char* qb = cb + (size_t)q * kBulkQuadStride;
-      for (int j = offs[c]; j < offs[c + 1]; ++j) {
-        const float4 v = *reinterpret_cast<const float4*>(qb + rows[j] * 16);
-        acc[m][0] += to_fixed(v.x, scale);
-        acc[m][1] += to_fixed(v.y, scale);
-        acc[m][2] += to_fixed(v.z, scale);
-        acc[m][3] += to_fixed(v.w, scale);
+      const uint4 w4 = *reinterpret_cast<const uint4*>(mk + c * 4);
+      const unsigned int wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      if (q == 0) cnt_acc[m] += __popc(wv[0]) + __popc(wv[1]) + __popc(wv[2]) + __popc(wv[3]);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        for (unsigned int bits = wv[g]; bits; bits &= bits - 1) {
+          const int r = g * 32 + __ffs(bits) - 1;
+          const float4 v = *reinterpret_cast<const float4*>(qb + r * 16);
+          acc[m][0] += to_fixed(v.x, scale);
+          acc[m][1] += to_fixed(v.y, scale);
+          acc[m][2] += to_fixed(v.z, scale);
+          acc[m][3] += to_fixed(v.w, scale);
+        }
       }
     }
     // the buffer is read; the next copy into it goes through the async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     block_sync();
-    if (tid == 0 && t + 2 * (long long)gridDim.x < n_tiles) issue(t + 2 * (long long)gridDim.x, b);
+    if (warp == 0 && t + 2 * (long long)gridDim.x < n_tiles) issue(t + 2 * (long long)gridDim.x, b);
   }
   // a stopped pass (at tile index i) lets its copies land before the
   // workspace is reused: tile i in buffer i & 1 and, if it exists, tile i + 1
@@ -306,6 +294,7 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
       }
     }
   }
+  const long long ks = (long long)k * ld;
 #pragma unroll
   for (int m = 0; m < kBulkMaxPairsPerThread; ++m) {
     const int p = tid + m * T;
@@ -314,8 +303,8 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         if (acc[m][u] != 0) red_add_s64(D + (long long)c * ld + 4 * q + u, acc[m][u]);
+      if (q == 0 && cnt_acc[m] != 0) red_add_s64(D + ks + c, cnt_acc[m]);
     }
-    if (tid + m * T < k && cnt_acc[m] != 0) red_add_s64(D + ks + tid + m * T, cnt_acc[m]);
   }
   block_sync();  // the workspace (and its barriers) may be reused after this
 }

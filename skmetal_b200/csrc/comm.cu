@@ -19,6 +19,7 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "comm.h"
 #include "driver.h"
@@ -45,6 +46,11 @@ struct Comm {
   int rank = 0;
   int device = 0;
   bool aborted = false;
+  // peer region (comm_peer_region): this rank's buffer and its mappings of
+  // every rank's buffer (own entry = own buffer)
+  void* region = nullptr;
+  std::vector<void*> region_ptrs;
+  int region_state = 0;  // 0 not tried, 1 ready, -1 unavailable on some rank
 };
 
 static NcclApi g_nccl;
@@ -120,6 +126,103 @@ int comm_allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes_per
   }
   SKM_NCCL(g_nccl.AllGather(send, recv, bytes_per_rank, ncclUint8, c->comm, s));
   return OK;
+}
+
+static int agree_any(Comm* c, unsigned int* dev_word, unsigned int* v, cudaStream_t s) {
+  SKM_CUDA(cudaMemcpyAsync(dev_word, v, sizeof(*v), cudaMemcpyHostToDevice, s));
+  SKM_TRY(comm_allreduce_max_u32(c, dev_word, 1, s));
+  SKM_CUDA(cudaMemcpyAsync(v, dev_word, sizeof(*v), cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  return OK;
+}
+
+static int peer_region_exchange(Comm* c, unsigned char* dev, cudaStream_t s) {
+  constexpr size_t hb = sizeof(cudaIpcMemHandle_t);
+  static_assert(hb == 64, "IPC handle size");
+  unsigned int* word = reinterpret_cast<unsigned int*>(dev + hb * (c->nranks + 1));
+  unsigned int bad = c->nranks > kMaxPeerRanks ? 1u : 0u;
+  for (int r = 0; r < c->nranks && !bad; ++r) {
+    int can = 0;
+    if (r != c->rank && (cudaDeviceCanAccessPeer(&can, c->device, r) != cudaSuccess || !can)) bad = 1;
+  }
+  cudaIpcMemHandle_t h{};
+  if (!bad && cudaMalloc(&c->region, kPeerRegionBytes) != cudaSuccess) bad = 1;
+  if (!bad && cudaIpcGetMemHandle(&h, c->region) != cudaSuccess) bad = 1;
+  cudaGetLastError();
+  SKM_TRY(agree_any(c, word, &bad, s));  // nobody opens a handle that does not exist
+  if (bad) return OK;
+  SKM_CUDA(cudaMemcpyAsync(dev + hb * c->nranks, &h, hb, cudaMemcpyHostToDevice, s));
+  SKM_TRY(comm_allgather_bytes(c, dev + hb * c->nranks, dev, hb, s));
+  std::vector<unsigned char> all(hb * c->nranks);
+  SKM_CUDA(cudaMemcpyAsync(all.data(), dev, hb * c->nranks, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  c->region_ptrs.assign(c->nranks, nullptr);
+  c->region_ptrs[c->rank] = c->region;
+  for (int r = 0; r < c->nranks && !bad; ++r) {
+    if (r == c->rank) continue;
+    cudaIpcMemHandle_t hr;
+    memcpy(&hr, all.data() + hb * r, hb);
+    if (cudaIpcOpenMemHandle(&c->region_ptrs[r], hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      c->region_ptrs[r] = nullptr;
+      bad = 1;
+    }
+  }
+  cudaGetLastError();
+  SKM_TRY(agree_any(c, word, &bad, s));
+  if (!bad) c->region_state = 1;
+  return OK;
+}
+
+// The peer region: kPeerRegionBytes of device memory per rank, mapped into
+// every other rank's address space with CUDA IPC (handles exchanged with an
+// NCCL all-gather). Kernels of one fit read their peers' buffers over
+// NVLink and write into their arrival words. Collective: every rank calls
+// it; a failure on any rank (no peer access, IPC refused) is agreed on with
+// max all-reduces, so all ranks get the same answer, and it is remembered.
+static int peer_region_setup(Comm* c, cudaStream_t s) {
+  unsigned char* dev = nullptr;
+  SKM_CUDA(cudaMalloc(reinterpret_cast<void**>(&dev), sizeof(cudaIpcMemHandle_t) * (c->nranks + 1) + 16));
+  c->region_state = -1;
+  const int rc = peer_region_exchange(c, dev, s);
+  cudaFree(dev);
+  return rc;
+}
+
+int comm_peer_region(Comm* c, cudaStream_t s, void* const** ptrs) {
+  *ptrs = nullptr;
+  if (!c || c->nranks < 2 || c->aborted) return OK;
+  if (c->region_state == 0) SKM_TRY(peer_region_setup(c, s));
+  if (c->region_state == 1) *ptrs = c->region_ptrs.data();
+  return OK;
+}
+
+// Unmaps the peers' regions, waits (all-reduce, under the watchdog) for every
+// rank to have done the same, then frees this rank's. Collective whenever the
+// region was set up (region_state is the same on every rank); the wait is
+// skipped after an abort.
+static void peer_region_release(Comm* c) {
+  for (int r = 0; r < (int)c->region_ptrs.size(); ++r)
+    if (r != c->rank && c->region_ptrs[r]) cudaIpcCloseMemHandle(c->region_ptrs[r]);
+  c->region_ptrs.clear();
+  if (c->region_state != 0 && !c->aborted && c->comm) {
+    cudaStream_t s = nullptr;
+    cudaEvent_t e = nullptr;
+    unsigned int* w = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
+        cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess &&
+        cudaMalloc(reinterpret_cast<void**>(&w), sizeof(unsigned int)) == cudaSuccess &&
+        cudaMemsetAsync(w, 0, sizeof(unsigned int), s) == cudaSuccess &&
+        g_nccl.AllReduce(w, w, 1, ncclUint32, ncclMax, c->comm, s) == ncclSuccess &&
+        cudaEventRecord(e, s) == cudaSuccess)
+      comm_wait_event(c, e);
+    if (w) cudaFree(w);
+    if (e) cudaEventDestroy(e);
+    if (s) cudaStreamDestroy(s);
+  }
+  if (c->region) cudaFree(c->region);
+  c->region = nullptr;
+  c->region_state = 0;
+  cudaGetLastError();
 }
 
 static double timeout_s() {
@@ -213,6 +316,7 @@ int skmetal_comm_init(const uint8_t* id128, int nranks, int rank) {
 int skmetal_comm_destroy(void) {
   std::lock_guard<std::mutex> lk(g_comm_mu);
   if (!g_comm) return OK;
+  if (g_comm->region_state != 0 || g_comm->region) peer_region_release(g_comm);
   if (g_comm->comm) {
     if (g_comm->aborted) {
       // already torn down by the watchdog

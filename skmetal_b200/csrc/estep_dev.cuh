@@ -192,6 +192,7 @@ __host__ __device__ constexpr int B_DONE(int t) { return B_C_FULL + 1 + t; }  //
 constexpr int NUM_BARS = B_C_FULL + 3;
 
 constexpr int MMA_W0 = 1, MMA_W1 = 2;
+constexpr int IDLE_W = 3;  // no role in the pipeline (callers give it side work)
 constexpr int EPI_W0 = 4;
 constexpr int EPI_GROUPS = 4;  // one warp per TMEM lane quarter each
 static_assert((EPI_W0 + 4 * EPI_GROUPS) * 32 == THREADS, "warp roles must fill the block");

@@ -240,6 +240,21 @@ static int run_fit(const FitParams& p) {
   double* partials = dscr + 2;
   double* shift_partial = dscr + 2 + n_part;
 
+  // Multi-GPU fits may run the persistent loop, which exchanges the deltas
+  // through the ranks' peer regions: set up once per communicator
+  // (collective) and zeroed here, before this fit's first collective, so no
+  // peer can write into it before the zeroing (peers only write from their
+  // loop kernels, which start after this fit's collectives).
+  const char* loop_env = getenv("SKMETAL_LOOP");
+  const bool launches_loop = loop_env && strcmp(loop_env, "launches") == 0;
+  void* const* regions = nullptr;
+  const size_t d_stride = round_up(d_len, 4);
+  if (comm && !p.single_step && !launches_loop) {
+    SKM_TRY(comm_peer_region(comm, s, &regions));
+    if (regions && region_bytes(d_stride, ld) > kPeerRegionBytes) regions = nullptr;  // same on every rank
+    if (regions) SKM_CUDA(cudaMemsetAsync(regions[comm_rank(comm)], 0, region_bytes(d_stride, ld), s));
+  }
+
   SKM_CUDA(cudaEventRecord(ev0, s));
   // ---- data in: row-major X (host rows are staged, a dataset is used in place)
   const float* raw = p.X_dev;
@@ -402,14 +417,24 @@ static int run_fit(const FitParams& p) {
   // One GPU with the tensor-core E-step: the persistent loop kernel runs
   // every iteration in one launch (SKMETAL_LOOP=launches selects the
   // multi-launch loop instead; both give bit-identical fits).
-  const char* loop_env = getenv("SKMETAL_LOOP");
-  const bool launches_loop = loop_env && strcmp(loop_env, "launches") == 0;
-  const bool persistent = plan.tc && !comm && !p.single_step && !launches_loop && tc_loop_supported(plan.tcp);
+  const bool multi = comm && comm_nranks(comm) > 1;
+  static_assert(kLoopMaxRanks == kMaxPeerRanks, "rank limits of the loop and the peer region");
+  bool persistent = plan.tc && (!multi || regions) && !p.single_step && !launches_loop && tc_loop_supported(plan.tcp);
+  if (multi && regions) {
+    // every rank must take the same loop (a rank with an empty shard, for
+    // one, has no tensor-core plan): agree with a max all-reduce
+    unsigned int* w = &u32s[1];  // the centred maxabs word is no longer needed
+    unsigned int not_ok = persistent ? 0u : 1u;
+    SKM_CUDA(cudaMemcpyAsync(w, &not_ok, sizeof(not_ok), cudaMemcpyHostToDevice, s));
+    SKM_TRY(comm_allreduce_max_u32(comm, w, 1, s));
+    SKM_CUDA(cudaMemcpyAsync(&not_ok, w, sizeof(not_ok), cudaMemcpyDeviceToHost, s));
+    SKM_CUDA(cudaStreamSynchronize(s));
+    persistent = not_ok == 0;
+  }
   std::vector<unsigned long long> prof_stamps;
   if (persistent) {
     // second and third delta buffers, second sums + counts (the loop rotates them)
     // (16-byte aligned: the loop reads and writes them as column quads)
-    const size_t d_stride = round_up(d_len, 4);
     long long *D23 = nullptr, *S2 = nullptr;
     SKM_TRY(buf.alloc_n(&D23, 2 * d_stride));
     SKM_TRY(buf.alloc_n(&S2, (size_t)k * ld + k));
@@ -436,6 +461,15 @@ static int run_fit(const FitParams& p) {
     li.C[1] = Cb1;
     li.m = ma;
     li.prof = prof_d;
+    if (multi) {
+      // the delta buffers are this rank's region's (see tc_lloyd_loop)
+      li.nranks = comm_nranks(comm);
+      li.rank = comm_rank(comm);
+      for (int r = 0; r < li.nranks; ++r) li.region[r] = static_cast<unsigned char*>(regions[r]);
+      li.d_stride = d_stride;
+      SKM_TRY(buf.alloc_n(&li.G, d_len));
+      SKM_TRY(buf.alloc(reinterpret_cast<void**>(&li.cand_all), cand_block_bytes(kCandCap, ld) * li.nranks));
+    }
     SKM_TRY(buf.alloc_n(&li.part, 3 * (size_t)k));
     SKM_TRY(buf.alloc_n(&li.bar, 1));
     SKM_CUDA(cudaMemsetAsync(li.bar, 0, sizeof(unsigned int), s));

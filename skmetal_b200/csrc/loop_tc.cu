@@ -1,22 +1,28 @@
-// Persistent Lloyd loop for one GPU: a single cooperative launch of one CTA
-// per SM runs all iterations of a fit. Iteration t:
+// Persistent Lloyd loop: a single cooperative launch of one CTA per SM runs
+// all iterations of a fit, on one GPU or on each rank of a sharded fit.
+// Iteration t:
 //
 //   E-step   the tensor-core pipeline of estep_dev.cuh over the CTA's tiles
 //            (labels, changed count, fixed-point deltas of changed rows); at
 //            its end the producer already issues the copies of the next
 //            iteration's first tiles (X does not change)
+//            and, meanwhile, the idle warp clears the delta buffer that
+//            E-step t + 1 adds into
 //   grid barrier
 //   M-step   [bulk iterations: fixed-point sums of all rows, grid barrier]
-//            the CTA owning cluster c (c mod CTAs) folds c's sums and count,
-//            writes its centre, centre image entries, squared shift and
-//            squared norm, or flags it empty, and clears c's deltas of
-//            iteration t - 1
+//            [several ranks: cross-rank barrier (rank_barrier)]
+//            the CTA owning cluster c (c mod CTAs) folds c's sums (and, with
+//            several ranks, every rank's deltas, read over NVLink from the
+//            ranks' peer regions) and count, writes its centre, centre image
+//            entries, squared shift and squared norm, or flags it empty
 //   grid barrier
 //            every CTA reads the k shifts, norms and flags: ||c||^2 for its
 //            epilogue and, totalled in the canonical order, the same stop
 //            decision as every other CTA; the next E-step copies the centre
 //            image from global memory. With an empty cluster instead: the
-//            cooperative relocation path of mstep_dev.cuh and a grid barrier.
+//            cooperative relocation path of mstep_dev.cuh and a grid barrier
+//            (several ranks: on the global sums, with candidate rows
+//            gathered from every rank, relocate_ranks).
 //
 // No kernel launches and no host round trips between iterations. The
 // arithmetic is that of the multi-launch loop (E-step and M-step kernels) in
@@ -24,10 +30,10 @@
 //
 // Buffers whose readers and writers overlap across iterations are rotated
 // (each 16-byte aligned, rows of ld entries): the delta buffers D by t mod 3
-// (written by E-step t, read by the owners in M-step t, cleared by them in
-// M-step t + 1, written again by E-step t + 3), the sums, counts and centres
-// by t mod 2 (the owners write the next ones while the relocation path may
-// still need the current ones).
+// (written by E-step t, read by the owners of every rank in M-step t,
+// cleared during E-step t + 2, written again by E-step t + 3), the sums,
+// counts and centres by t mod 2 (the owners write the next ones while the
+// relocation path may still need the current ones).
 //
 // Every wait is bounded: mbarrier waits (estep_dev.cuh) and grid barriers
 // record an error code in the fit state and the CTAs leave the loop together
@@ -55,6 +61,20 @@ struct LoopArgs {
   double* part;  // per cluster: squared shift [0, k), squared norm [k, 2k), empty flag [2k, 3k)
   unsigned int* bar;  // the loop's grid-barrier counter, zero at launch
   unsigned long long* prof;
+  size_t d_clear;  // entries of a delta buffer to clear (k * ld + k + 1, rounded up to even)
+  // multi-GPU (W > 1): every rank's delta buffers, arrival words and
+  // candidate block (peer mappings; index = rank), this rank's own arrival
+  // words and candidate block, local scratch for the global deltas and the
+  // gathered candidate blocks
+  int W, rank;
+  long long* pD[kLoopMaxRanks][3];
+  unsigned int* pflag[kLoopMaxRanks];
+  const unsigned char* pcand[kLoopMaxRanks];
+  unsigned int* flags;
+  unsigned char* cand_own;
+  long long* G;
+  unsigned char* cand_all;
+  size_t cand_block;
 };
 
 // Grid barrier of the loop: every CTA adds 1 to a counter that only grows
@@ -89,6 +109,79 @@ __device__ __forceinline__ bool loop_barrier(FitState* st, unsigned int* counter
   return ok_s != 0;
 }
 
+// Cross-rank barrier of the multi-GPU loop (every thread of every CTA; the
+// CTAs have just passed a local grid barrier). Block 0 writes `epoch` into
+// this rank's arrival word in every rank's region with a system-scope
+// release (the writes that the local barrier gathered become visible to any
+// rank that sees the word); thread 0 of every CTA then polls its own
+// region's words with system-scope acquires until every rank's word reaches
+// `epoch`. Epochs count the fit's cross-rank barriers from 1 (the words are
+// zeroed before the fit's first collective). Bounded: after 5 s the CTA
+// records error 1005 and returns false.
+__device__ __forceinline__ bool rank_barrier(const LoopArgs& la, FitState* st, unsigned int epoch) {
+  __shared__ int ok_s;
+  block_sync();
+  if (blockIdx.x == 0 && threadIdx.x < la.W) {
+    unsigned int* f = la.pflag[threadIdx.x] + la.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+  }
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned long long t0 = globaltimer();
+    for (int r = 0; r < la.W && ok; ++r) {
+      for (unsigned int i = 1;; ++i) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(la.flags + r) : "memory");
+        if (v >= epoch) break;
+        if ((i & 255) == 0 && globaltimer() - t0 > 5000000000ull) {
+          atomicExch(&st->error, 1005);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    ok_s = ok;
+  }
+  block_sync();
+  return ok_s != 0;
+}
+
+// Column quad i .. i + 3 of one cluster summed over every rank's deltas of
+// buffer b (the global deltas), plus S_in unless bulk; as quad_load.
+__device__ __forceinline__ QuadSums quad_load_ranks(const long long* S_in, const LoopArgs& la, int b,
+                                                    const float* C_old, long long i, int bulk) {
+  QuadSums r;
+  longlong2 s01 = make_longlong2(0, 0), s23 = make_longlong2(0, 0);
+  if (!bulk) {
+    s01 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i));
+    s23 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i + 2));
+  }
+  r.old = __ldcg(reinterpret_cast<const float4*>(C_old + i));
+#pragma unroll
+  for (int q = 0; q < kLoopMaxRanks; ++q)
+    if (q < la.W) {
+      const longlong2 d01 = __ldcv(reinterpret_cast<const longlong2*>(la.pD[q][b] + i));
+      const longlong2 d23 = __ldcv(reinterpret_cast<const longlong2*>(la.pD[q][b] + i + 2));
+      s01.x += d01.x;
+      s01.y += d01.y;
+      s23.x += d23.x;
+      s23.y += d23.y;
+    }
+  r.s[0] = s01.x;
+  r.s[1] = s01.y;
+  r.s[2] = s23.x;
+  r.s[3] = s23.y;
+  r.dnz = true;
+  return r;
+}
+
+// Entry i of delta buffer b summed over every rank.
+__device__ __forceinline__ long long ranks_sum(const LoopArgs& la, int b, long long i) {
+  long long v = 0;
+  for (int q = 0; q < la.W; ++q) v += __ldcv(la.pD[q][b] + i);
+  return v;
+}
+
 __device__ __forceinline__ void proxy_fence_all() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -101,6 +194,61 @@ __device__ __forceinline__ void stamp(unsigned long long* prof, int i) {
   if (prof && blockIdx.x == 0 && threadIdx.x == 0) prof[i] = globaltimer();
 }
 
+// Multi-GPU relocation (some cluster is empty after summing every rank's
+// counts): the global deltas into G; this rank's min(empties, cap, rows)
+// rows farthest from their centre into its candidate block; a cross-rank
+// barrier; every rank's block gathered into cand_all; then the relocation
+// path on the global sums with those candidates, as the multi-launch loop
+// runs it after its all-reduce. Every thread of every CTA.
+__device__ bool relocate_ranks(const LoopArgs& la, MStepArgs a, int b, int bulk, unsigned long long changed_now,
+                               unsigned int& n_bar, unsigned int& epoch) {
+  FitState* st = a.st;
+  const unsigned int nb = gridDim.x;
+  const long long ks = (long long)a.k * a.ld;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + a.k + 1;
+       i += (long long)nb * blockDim.x)
+    la.G[i] = ranks_sum(la, b, i);
+  a.D = la.G;
+  a.changed = reinterpret_cast<const unsigned long long*>(la.G + ks + a.k);
+  if (blockIdx.x == 0 && threadIdx.x == 0) st->sel_count = 0;
+  if (!loop_barrier(st, la.bar, nb * ++n_bar)) return false;
+  const int ne = find_empty_clusters(a, bulk);
+  const int m = (int)min((long long)min(ne, kCandCap), a.n);
+  if (m > 0) {
+    rows_dist_to_old_centres(a, nb);
+    if (!loop_barrier(st, la.bar, nb * ++n_bar)) return false;
+    if (!select_farthest(a.mind, a.n, a.row_base, m, st, a.hist, a.sel, nb)) return false;
+  }
+  if (blockIdx.x == 0) {  // this rank's candidate block (the layout of shard_prep_kernel)
+    unsigned char* mine = la.cand_own;
+    float* dist = reinterpret_cast<float*>(mine + cand_dist_off(kCandCap));
+    long long* row = reinterpret_cast<long long*>(mine + cand_row_off(kCandCap));
+    int* label = reinterpret_cast<int*>(mine + cand_label_off(kCandCap));
+    float* x = reinterpret_cast<float*>(mine + cand_x_off(kCandCap));
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+      const long long r = a.sel[i];
+      dist[i] = a.mind[r];
+      row[i] = a.row_base + r;
+      label[i] = a.labels[r];
+      for (int j = 0; j < a.ld; ++j) x[(long long)i * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
+    }
+    if (threadIdx.x == 0) *reinterpret_cast<int*>(mine) = m;
+  }
+  if (!rank_barrier(la, st, ++epoch)) return false;
+  const size_t words = la.cand_block / 16;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < words * la.W; i += (size_t)nb * blockDim.x) {
+    const int r = (int)(i / words);
+    const size_t w = i - (size_t)r * words;
+    reinterpret_cast<int4*>(la.cand_all + (size_t)r * la.cand_block)[w] =
+        __ldcv(reinterpret_cast<const int4*>(la.pcand[r]) + w);
+  }
+  if (!loop_barrier(st, la.bar, nb * ++n_bar)) return false;
+  a.cand = la.cand_all;
+  a.cand_ranks = la.W;
+  a.cand_cap = kCandCap;
+  return relocation_path(a, ne, bulk, changed_now);
+}
+
 __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la) {
   using namespace tc;
   const Params& p = la.p;
@@ -108,6 +256,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ int flags_s[2];
   __shared__ double dsq_s[MAX_KPAD];
+  __shared__ unsigned long long chg_s;
   Cta c;
   cta_setup(p, smem_raw, p.bias, c);
 
@@ -126,11 +275,12 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
   int done = st->done;
   int img_loads = 0, pre = 0, image_issued = 0;
   unsigned int n_bar = 0;  // loop barriers passed
+  unsigned int epoch = 0;  // cross-rank barriers passed
   int t = 0;
   for (; !done; ++t) {
     const int par = t & 1;
     long long* Dp = la.D[t % 3];
-    long long* D_prev = la.D[(t + 2) % 3];
+    long long* D_next = la.D[(t + 1) % 3];
     long long* dcnt = Dp + ks;
     unsigned long long* chg = reinterpret_cast<unsigned long long*>(Dp + ks + k);
     long long* S_in = la.S[par];
@@ -159,6 +309,14 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     P.negscale = negscale;
     P.deltas = bulk ? nullptr : Dp;
     P.changed = chg;
+    if (warp == IDLE_W) {
+      // the deltas E-step t + 1 adds into, idle since M-step t - 2 (every
+      // rank's reads of them ended before this iteration's first barrier):
+      // cleared off the M-step's path; the barrier after this pass orders it
+      // before E-step t + 1
+      for (size_t i = 2 * ((size_t)blockIdx.x * 32 + lane); i < la.d_clear; i += 64 * (size_t)nb)
+        *reinterpret_cast<longlong2*>(D_next + i) = make_longlong2(0, 0);
+    }
     estep_pass(p, c, P);
     ++img_loads;
     pre = P.pre_next;
@@ -166,7 +324,6 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
     if (__ldcg(&st->error)) break;  // uniform: read after the barrier
     stamp(la.prof, 4 * t + 1);
-    const unsigned long long changed_now = __ldcg(chg);
 
     // ---------------------------------------------------------------- M-step
     MStepArgs a = la.m;
@@ -183,6 +340,16 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       proxy_fence_all();
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
     }
+    // every rank's deltas of this iteration are complete
+    unsigned long long changed_now;
+    if (la.W > 1) {
+      if (!rank_barrier(la, st, ++epoch)) break;
+      if (threadIdx.x == 0) chg_s = (unsigned long long)ranks_sum(la, t % 3, ks + k);
+      block_sync();
+      changed_now = chg_s;
+    } else {
+      changed_now = __ldcg(chg);
+    }
     // (no block touches S_in, D or the counts before the barrier above)
     // owners: cluster cl is CTA cl mod nb's, one warp per owned cluster
     {
@@ -195,22 +362,17 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
         const long long i0 = (long long)cl * ld + 4 * lane;
         // the quad and the count loads go out together (one round trip)
         QuadSums r{};
-        if (lane < nq) r = quad_load(S_in, Dp, C_old, i0, bulk);
-        const long long cnew = (bulk ? 0 : __ldcg(cnt_in + cl)) + __ldcg(dcnt + cl);
+        if (lane < nq)
+          r = la.W > 1 ? quad_load_ranks(S_in, la, t % 3, C_old, i0, bulk) : quad_load(S_in, Dp, C_old, i0, bulk);
+        const long long cnew =
+            (bulk ? 0 : __ldcg(cnt_in + cl)) + (la.W > 1 ? ranks_sum(la, t % 3, ks + cl) : __ldcg(dcnt + cl));
         double dsq = 0.0, nrm = 0.0;
         if (cnew > 0 && lane < nq)  // the canonical order of warp_centre_from_sums
           quad_finish(r, cl, lane, i0, d, centre_factor(inv_scale, cnew), cs, la.m.cimg, CentreImage{}, S_out, C_new,
                       nullptr, dsq, nrm);
         dsq = warp_sum(dsq);
         nrm = warp_sum(nrm);
-        // cl's deltas of iteration t - 1: their readers finished before this
-        // iteration's first barrier; E-step t + 2 adds into them again
-        for (int j = 4 * lane; j < ld; j += 128) {
-          *reinterpret_cast<longlong2*>(D_prev + (long long)cl * ld + j) = make_longlong2(0, 0);
-          *reinterpret_cast<longlong2*>(D_prev + (long long)cl * ld + j + 2) = make_longlong2(0, 0);
-        }
         if (lane == 0) {
-          D_prev[ks + cl] = 0;
           cnt_out[cl] = cnew;
           dsq_c[cl] = dsq;
           nrm_c[cl] = nrm;
@@ -218,7 +380,6 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
           la.m.bias[cl] = (float)nrm;  // for the final E-step after the loop
         }
       }
-      if (blockIdx.x == 0 && threadIdx.x == 0) D_prev[ks + k] = 0;  // its changed counter
       proxy_fence_all();
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
       stamp(la.prof, 4 * t + 2);
@@ -257,7 +418,9 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
             st->relocated = 0;
             if (strict) st->strict = 1;
             st->done = dn;
-            *chg = 0;
+            // (with several ranks the peers may still read it: it is
+            // cleared with the other deltas of its buffer, in E-step t + 2)
+            if (la.W == 1) *chg = 0;
           }
         }
       }
@@ -269,8 +432,12 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
         // relocation: the empty clusters again with their ids, then the
         // cooperative path, which folds this iteration's sums and counts into
         // S_in and cnt_in and writes every centre, image entry and norm
-        const int ne = find_empty_clusters(a, bulk);
-        if (!relocation_path(a, ne, bulk, changed_now)) break;
+        if (la.W > 1) {
+          if (!relocate_ranks(la, a, t % 3, bulk, changed_now, n_bar, epoch)) break;
+        } else {
+          const int ne = find_empty_clusters(a, bulk);
+          if (!relocation_path(a, ne, bulk, changed_now)) break;
+        }
         for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + k;
              i += (long long)nb * blockDim.x) {
           if (i < ks) S_out[i] = __ldcg(S_in + i);
@@ -329,6 +496,32 @@ int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
   la.part = in.part;
   la.bar = in.bar;
   la.prof = in.prof;
+  la.d_clear = ((size_t)plan.k * plan.ld + plan.k + 2) & ~(size_t)1;
+  la.W = in.nranks;
+  la.rank = in.rank;
+  if (la.W > 1) {
+    if (la.W > kLoopMaxRanks || in.rank < 0 || in.rank >= la.W || !in.G || !in.cand_all) {
+      set_error(ERR_INVALID, "multi-GPU loop: bad rank layout");
+      return ERR_INVALID;
+    }
+    const size_t coff = region_cand_off(in.d_stride);
+    for (int r = 0; r < la.W; ++r) {
+      unsigned char* rg = in.region[r];
+      if (!rg) {
+        set_error(ERR_INVALID, "multi-GPU loop: no peer region for rank %d", r);
+        return ERR_INVALID;
+      }
+      for (int i = 0; i < 3; ++i) la.pD[r][i] = reinterpret_cast<long long*>(rg + kRegionD) + i * in.d_stride;
+      la.pflag[r] = reinterpret_cast<unsigned int*>(rg);
+      la.pcand[r] = rg + coff;
+    }
+    la.flags = la.pflag[in.rank];
+    la.cand_own = in.region[in.rank] + coff;
+    la.G = in.G;
+    la.cand_all = in.cand_all;
+    la.cand_block = cand_block_bytes(kCandCap, plan.ld);
+    for (int i = 0; i < 3; ++i) la.D[i] = la.pD[in.rank][i];
+  }
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -1,11 +1,15 @@
 """Sharded fits on two GPUs against the single-GPU fit (skipped with fewer GPUs).
 
 Two processes, one per GPU, each fit their row shard through
-``skmetal_kmeans_fit_shard``; the library all-reduces the fixed-point sums
-over its own NCCL communicator and exchanges relocation candidates when a
-cluster is empty. The sums are exact integers, so both ranks must return the
-single-GPU fit's centres and n_iter bit for bit, and the single-GPU labels on
-their rows; inertia is a float64 sum in another order (rtol 1e-12).
+``skmetal_kmeans_fit_shard``, with either loop:
+- persistent: one loop kernel per rank; the ranks read each other's
+  fixed-point deltas and relocation candidates over NVLink from their peer
+  regions, synchronised by cross-rank arrival words;
+- launches: kernels per iteration and an NCCL all-reduce of the sums and
+  candidates.
+The sums are exact integers, so both ranks must return the single-GPU fit's
+centres and n_iter bit for bit, and the single-GPU labels on their rows;
+inertia is a float64 sum in another order (rtol 1e-12).
 
 Rendezvous (the NCCL unique id) goes over a gloo group on 127.0.0.1 with a
 short timeout; NVLS is off.
@@ -54,14 +58,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, case, out):
+def _rank_main(rank, world, port, case, loop, out):
     import datetime
 
     import torch
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
-                      SKMETAL_COMM_TIMEOUT_S="60")
+                      SKMETAL_COMM_TIMEOUT_S="60", SKMETAL_LOOP=loop)
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     from skmetal_b200 import _bridge
@@ -74,9 +78,10 @@ def _rank_main(rank, world, port, case, out):
         lo, hi = shard_range(X.shape[0], rank, world)
         c, lab, inertia, n_iter = _bridge.kmeans_fit_shard(X[lo:hi], init, case["max_iter"], case["tol"], lo,
                                                            X.shape[0])
-        out.put((rank, "ok", c, lab, inertia, n_iter, lo, hi))
+        launches = _bridge.last_fit_stats()["launches"]
+        out.put((rank, "ok", c, lab, inertia, n_iter, lo, hi, launches))
     except Exception as e:  # noqa: BLE001
-        out.put((rank, f"error: {e}", None, None, None, None, None, None))
+        out.put((rank, f"error: {e}", None, None, None, None, None, None, None))
     finally:
         _bridge.comm_destroy()
         dist.destroy_process_group()
@@ -84,7 +89,8 @@ def _rank_main(rank, world, port, case, out):
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_two_gpu_shards_match_one_gpu(name):
+@pytest.mark.parametrize("loop", ["persistent", "launches"])
+def test_two_gpu_shards_match_one_gpu(name, loop):
     import torch.multiprocessing as mp
 
     from skmetal_b200 import _bridge
@@ -95,14 +101,16 @@ def test_two_gpu_shards_match_one_gpu(name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, case, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, case, loop, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=240) for _ in range(2))
     for p in procs:
         p.join(timeout=120)
-    for rank, status, c, lab, inertia, n_iter, lo, hi in res:
+    for rank, status, c, lab, inertia, n_iter, lo, hi, launches in res:
         assert status == "ok", f"rank {rank}: {status}"
+        # the loop asked for ran: one loop kernel, or kernels per iteration
+        assert (launches < 20) if loop == "persistent" else (launches >= 2 * n_iter), (loop, launches)
         assert n_iter == n1
         np.testing.assert_array_equal(c, c1)
         np.testing.assert_array_equal(lab, l1[lo:hi])

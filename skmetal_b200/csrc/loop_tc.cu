@@ -341,15 +341,12 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
     }
     // every rank's deltas of this iteration are complete
-    unsigned long long changed_now;
-    if (la.W > 1) {
-      if (!rank_barrier(la, st, ++epoch)) break;
-      if (threadIdx.x == 0) chg_s = (unsigned long long)ranks_sum(la, t % 3, ks + k);
-      block_sync();
-      changed_now = chg_s;
-    } else {
-      changed_now = __ldcg(chg);
-    }
+    if (la.W > 1 && !rank_barrier(la, st, ++epoch)) break;
+    // the change count over every rank (a round trip over NVLink): taken by
+    // the last warp, which owns no cluster, while the owners work; read after
+    // the next block barrier
+    if (threadIdx.x == blockDim.x - 32)
+      chg_s = la.W > 1 ? (unsigned long long)ranks_sum(la, t % 3, ks + k) : __ldcg(chg);
     // (no block touches S_in, D or the counts before the barrier above)
     // owners: cluster cl is CTA cl mod nb's, one warp per owned cluster
     {
@@ -393,6 +390,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       if (cl_t < p.k_pad) c.bias_s[cl_t] = cl_t < k ? (float)nrm_t : INFINITY;
       __syncwarp();
       const int n_empty = __syncthreads_count(emp_t != 0.0) ? 1 : 0;  // any empty cluster
+      const unsigned long long changed_now = chg_s;
       // the owners' image is complete: its copy overlaps the decision
       image_issued = n_empty == 0;
       if (image_issued && threadIdx.x == MMA_W0 * 32) {  // an otherwise idle lane

@@ -24,7 +24,7 @@ int comm_nranks(Comm* c);
 // no peer region (one rank, more than kMaxPeerRanks, or no peer access on
 // some rank).
 constexpr int kMaxPeerRanks = 8;
-constexpr size_t kPeerRegionBytes = 1u << 20;
+constexpr size_t kPeerRegionBytes = 16u << 20;
 int comm_peer_region(Comm* c, cudaStream_t s, void* const** ptrs);
 int comm_rank(Comm* c);
 // Wait for `e` while polling the communicator for asynchronous errors; aborts

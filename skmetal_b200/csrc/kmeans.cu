@@ -244,15 +244,16 @@ static int run_fit(const FitParams& p) {
   // through the ranks' peer regions: set up once per communicator
   // (collective) and zeroed here, before this fit's first collective, so no
   // peer can write into it before the zeroing (peers only write from their
-  // loop kernels, which start after this fit's collectives).
+  // loop kernels, which start after this fit's collectives, and the previous
+  // fit's kernels ended before its last collective).
   const char* loop_env = getenv("SKMETAL_LOOP");
   const bool launches_loop = loop_env && strcmp(loop_env, "launches") == 0;
   void* const* regions = nullptr;
-  const size_t d_stride = round_up(d_len, 4);
   if (comm && !p.single_step && !launches_loop) {
     SKM_TRY(comm_peer_region(comm, s, &regions));
-    if (regions && region_bytes(d_stride, ld) > kPeerRegionBytes) regions = nullptr;  // same on every rank
-    if (regions) SKM_CUDA(cudaMemsetAsync(regions[comm_rank(comm)], 0, region_bytes(d_stride, ld), s));
+    const size_t rb = region_bytes(comm_nranks(comm), k, ld);
+    if (regions && rb > kPeerRegionBytes) regions = nullptr;  // the same on every rank
+    if (regions) SKM_CUDA(cudaMemsetAsync(regions[comm_rank(comm)], 0, rb, s));
   }
 
   SKM_CUDA(cudaEventRecord(ev0, s));
@@ -435,6 +436,7 @@ static int run_fit(const FitParams& p) {
   if (persistent) {
     // second and third delta buffers, second sums + counts (the loop rotates them)
     // (16-byte aligned: the loop reads and writes them as column quads)
+    const size_t d_stride = round_up(d_len, 4);
     long long *D23 = nullptr, *S2 = nullptr;
     SKM_TRY(buf.alloc_n(&D23, 2 * d_stride));
     SKM_TRY(buf.alloc_n(&S2, (size_t)k * ld + k));
@@ -462,11 +464,9 @@ static int run_fit(const FitParams& p) {
     li.m = ma;
     li.prof = prof_d;
     if (multi) {
-      // the delta buffers are this rank's region's (see tc_lloyd_loop)
       li.nranks = comm_nranks(comm);
       li.rank = comm_rank(comm);
       for (int r = 0; r < li.nranks; ++r) li.region[r] = static_cast<unsigned char*>(regions[r]);
-      li.d_stride = d_stride;
       SKM_TRY(buf.alloc_n(&li.G, d_len));
       SKM_TRY(buf.alloc(reinterpret_cast<void**>(&li.cand_all), cand_block_bytes(kCandCap, ld) * li.nranks));
     }

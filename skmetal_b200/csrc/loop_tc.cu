@@ -10,11 +10,11 @@
 //            E-step t + 1 adds into
 //   grid barrier
 //   M-step   [bulk iterations: fixed-point sums of all rows, grid barrier]
-//            [several ranks: cross-rank barrier (rank_barrier)]
-//            the CTA owning cluster c (c mod CTAs) folds c's sums (and, with
-//            several ranks, every rank's deltas, read over NVLink from the
-//            ranks' peer regions) and count, writes its centre, centre image
-//            entries, squared shift and squared norm, or flags it empty
+//            the CTA owning cluster c (c mod CTAs) folds c's sums and count
+//            (several ranks: first pushes this rank's deltas of c into every
+//            peer's inbox over NVLink and waits for every peer's push of c,
+//            owner_exchange), writes its centre, centre image entries,
+//            squared shift and squared norm, or flags it empty
 //   grid barrier
 //            every CTA reads the k shifts, norms and flags: ||c||^2 for its
 //            epilogue and, totalled in the canonical order, the same stop
@@ -30,8 +30,10 @@
 //
 // Buffers whose readers and writers overlap across iterations are rotated
 // (each 16-byte aligned, rows of ld entries): the delta buffers D by t mod 3
-// (written by E-step t, read by the owners of every rank in M-step t,
-// cleared during E-step t + 2, written again by E-step t + 3), the sums,
+// (written by E-step t, read by the owners in M-step t, cleared during
+// E-step t + 2, written again by E-step t + 3), the peers' inbox rows by
+// t mod 2 (a rank pushes iteration t + 2 only after every peer finished
+// M-step t), the sums,
 // counts and centres by t mod 2 (the owners write the next ones while the
 // relocation path may still need the current ones).
 //
@@ -62,16 +64,14 @@ struct LoopArgs {
   unsigned int* bar;  // the loop's grid-barrier counter, zero at launch
   unsigned long long* prof;
   size_t d_clear;  // entries of a delta buffer to clear (k * ld + k + 1, rounded up to even)
-  // multi-GPU (W > 1): every rank's delta buffers, arrival words and
-  // candidate block (peer mappings; index = rank), this rank's own arrival
-  // words and candidate block, local scratch for the global deltas and the
-  // gathered candidate blocks
+  // multi-GPU (W > 1): every rank's arrival words, inbox flags, inbox rows
+  // and candidate block (peer mappings; index = rank; own included), local
+  // scratch for the global deltas and the gathered candidate blocks
   int W, rank;
-  long long* pD[kLoopMaxRanks][3];
   unsigned int* pflag[kLoopMaxRanks];
+  unsigned long long* pin[kLoopMaxRanks];
   const unsigned char* pcand[kLoopMaxRanks];
-  unsigned int* flags;
-  unsigned char* cand_own;
+  int row;  // 8-byte words of an inbox row
   long long* G;
   unsigned char* cand_all;
   size_t cand_block;
@@ -131,7 +131,7 @@ __device__ __forceinline__ bool rank_barrier(const LoopArgs& la, FitState* st, u
     for (int r = 0; r < la.W && ok; ++r) {
       for (unsigned int i = 1;; ++i) {
         unsigned int v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(la.flags + r) : "memory");
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(la.pflag[la.rank] + r) : "memory");
         if (v >= epoch) break;
         if ((i & 255) == 0 && globaltimer() - t0 > 5000000000ull) {
           atomicExch(&st->error, 1005);
@@ -146,40 +146,122 @@ __device__ __forceinline__ bool rank_barrier(const LoopArgs& la, FitState* st, u
   return ok_s != 0;
 }
 
-// Column quad i .. i + 3 of one cluster summed over every rank's deltas of
-// buffer b (the global deltas), plus S_in unless bulk; as quad_load.
-__device__ __forceinline__ QuadSums quad_load_ranks(const long long* S_in, const LoopArgs& la, int b,
-                                                    const float* C_old, long long i, int bulk) {
-  QuadSums r;
-  longlong2 s01 = make_longlong2(0, 0), s23 = make_longlong2(0, 0);
-  if (!bulk) {
-    s01 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i));
-    s23 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i + 2));
-  }
-  r.old = __ldcg(reinterpret_cast<const float4*>(C_old + i));
-#pragma unroll
-  for (int q = 0; q < kLoopMaxRanks; ++q)
-    if (q < la.W) {
-      const longlong2 d01 = __ldcv(reinterpret_cast<const longlong2*>(la.pD[q][b] + i));
-      const longlong2 d23 = __ldcv(reinterpret_cast<const longlong2*>(la.pD[q][b] + i + 2));
-      s01.x += d01.x;
-      s01.y += d01.y;
-      s23.x += d23.x;
-      s23.y += d23.y;
-    }
-  r.s[0] = s01.x;
-  r.s[1] = s01.y;
-  r.s[2] = s23.x;
-  r.s[3] = s23.y;
-  r.dnz = true;
-  return r;
+// Inbox row of rank q's deltas of cluster c (iteration parity par) in the
+// region of rank `dst`: 8-byte words, value j in words 2j (low half) and
+// 2j + 1 (high half), each word {32 bits of the value, epoch}. A word is
+// written by one 8-byte store, so a reader that sees the epoch in it sees
+// its half of the value: no fence and no separate flag.
+__device__ __forceinline__ unsigned long long* inbox_row(const LoopArgs& la, int dst, int par, int q, int c, int k) {
+  return la.pin[dst] + (((long long)par * la.W + q) * k + c) * la.row;
+}
+__device__ __forceinline__ ulonglong2 ll_pack(long long v, unsigned int epoch) {
+  const unsigned long long e = (unsigned long long)epoch << 32;
+  return make_ulonglong2(e | (unsigned int)(unsigned long long)v, e | (unsigned int)((unsigned long long)v >> 32));
+}
+__device__ __forceinline__ long long ll_value(ulonglong2 w) {
+  return (long long)(((w.y & 0xffffffffull) << 32) | (w.x & 0xffffffffull));
+}
+__device__ __forceinline__ bool ll_ready(ulonglong2 w, unsigned int epoch) {
+  return (unsigned int)(w.x >> 32) == epoch && (unsigned int)(w.y >> 32) == epoch;
+}
+__device__ __forceinline__ void ll_store(unsigned long long* p, ulonglong2 w) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w.x), "l"(w.y) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ll_load(const unsigned long long* p) {
+  ulonglong2 w;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+  return w;
+}
+// Value j of an inbox row whose epoch was already seen.
+__device__ __forceinline__ long long ll_get(const unsigned long long* row, int j) {
+  return ll_value(make_ulonglong2(__ldcg(row + 2 * j), __ldcg(row + 2 * j + 1)));
 }
 
-// Entry i of delta buffer b summed over every rank.
-__device__ __forceinline__ long long ranks_sum(const LoopArgs& la, int b, long long i) {
-  long long v = 0;
-  for (int q = 0; q < la.W; ++q) v += __ldcv(la.pD[q][b] + i);
-  return v;
+// One owner warp of the multi-GPU loop, cluster c, iteration parity par,
+// after the local barrier that completed this rank's deltas: pushes the
+// rank's deltas of c (lane l: column quad l), count delta and, for c = 0,
+// change count into every peer's inbox row (8-byte stores over NVLink),
+// then waits (each lane for its own words; bounded: 5 s, then error 1005)
+// until every peer's row of c carries this iteration's epoch, and returns
+// c's sums over every rank (S_in added unless bulk; as quad_load) and c's
+// count delta over every rank.
+__device__ __forceinline__ QuadSums owner_exchange(const LoopArgs& la, FitState* st, const long long* S_in,
+                                                   const long long* Dp, const unsigned long long* chg,
+                                                   const float* C_old, int c, int par, unsigned int epoch, int bulk,
+                                                   long long* cnt_delta) {
+  const int lane = threadIdx.x & 31;
+  const int k = la.p.k, ld = la.p.ld, nq = ld >> 2;
+  const long long i = (long long)c * ld + 4 * lane;
+  const long long* dcnt = Dp + (long long)k * ld;
+  long long o[4] = {0, 0, 0, 0};
+  if (lane < nq) {
+    const longlong2 o01 = __ldcg(reinterpret_cast<const longlong2*>(Dp + i));
+    const longlong2 o23 = __ldcg(reinterpret_cast<const longlong2*>(Dp + i + 2));
+    o[0] = o01.x;
+    o[1] = o01.y;
+    o[2] = o23.x;
+    o[3] = o23.y;
+  }
+  const long long ocnt = __ldcg(dcnt + c);
+  const long long ochg = c == 0 ? (long long)__ldcg(chg) : 0;
+  for (int q = 0; q < la.W; ++q) {
+    if (q == la.rank) continue;
+    unsigned long long* dst = inbox_row(la, q, par, la.rank, c, k);
+    if (lane < nq)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ll_store(dst + 2 * (4 * lane + u), ll_pack(o[u], epoch));
+    if (lane == 0) {
+      ll_store(dst + 2 * ld, ll_pack(ocnt, epoch));
+      ll_store(dst + 2 * (ld + 1), ll_pack(ochg, epoch));
+    }
+  }
+  long long s[4] = {o[0], o[1], o[2], o[3]};
+  if (!bulk && lane < nq) {
+    const longlong2 a01 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i));
+    const longlong2 a23 = __ldcg(reinterpret_cast<const longlong2*>(S_in + i + 2));
+    s[0] += a01.x;
+    s[1] += a01.y;
+    s[2] += a23.x;
+    s[3] += a23.y;
+  }
+  long long cnt = ocnt;
+  const unsigned long long t0 = globaltimer();
+  for (int q = 0; q < la.W; ++q) {
+    if (q == la.rank) continue;
+    const unsigned long long* src = inbox_row(la, la.rank, par, q, c, k);
+    ulonglong2 w[4], wc = make_ulonglong2(0, 0);
+    for (unsigned int it = 1;; ++it) {
+      bool ready = true;
+      if (lane < nq)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          w[u] = ll_load(src + 2 * (4 * lane + u));
+          ready = ready && ll_ready(w[u], epoch);
+        }
+      wc = ll_load(src + 2 * ld);  // every lane: the count delta
+      ready = ready && ll_ready(wc, epoch);
+      if (c == 0 && lane == 0) ready = ready && ll_ready(ll_load(src + 2 * (ld + 1)), epoch);  // change count
+      if (__all_sync(0xffffffffu, ready)) break;
+      if ((it & 63) == 0) {  // the same iterations on every lane; lane 0's clock decides
+        const bool late = __shfl_sync(0xffffffffu, globaltimer() - t0 > 5000000000ull, 0);
+        if (late) {
+          if (lane == 0) atomicExch(&st->error, 1005);
+          break;
+        }
+      }
+    }
+    if (lane < nq)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s[u] += ll_value(w[u]);
+    cnt += ll_value(wc);
+  }
+  QuadSums r;
+  r.old = lane < nq ? __ldcg(reinterpret_cast<const float4*>(C_old + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) r.s[u] = s[u];
+  r.dnz = true;
+  *cnt_delta = cnt;
+  return r;
 }
 
 __device__ __forceinline__ void proxy_fence_all() {
@@ -200,14 +282,25 @@ __device__ __forceinline__ void stamp(unsigned long long* prof, int i) {
 // barrier; every rank's block gathered into cand_all; then the relocation
 // path on the global sums with those candidates, as the multi-launch loop
 // runs it after its all-reduce. Every thread of every CTA.
-__device__ bool relocate_ranks(const LoopArgs& la, MStepArgs a, int b, int bulk, unsigned long long changed_now,
-                               unsigned int& n_bar, unsigned int& epoch) {
+__device__ bool relocate_ranks(const LoopArgs& la, MStepArgs a, const long long* Dp, int par, int bulk,
+                               unsigned long long changed_now, unsigned int& n_bar, unsigned int& epoch) {
   FitState* st = a.st;
   const unsigned int nb = gridDim.x;
   const long long ks = (long long)a.k * a.ld;
+  // every owner has seen every peer's push (before the last grid barrier)
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < ks + a.k + 1;
-       i += (long long)nb * blockDim.x)
-    la.G[i] = ranks_sum(la, b, i);
+       i += (long long)nb * blockDim.x) {
+    long long v = __ldcg(Dp + i);
+    if (i < ks + a.k) {
+      const int c = i < ks ? (int)(i / a.ld) : (int)(i - ks);
+      const int j = i < ks ? (int)(i - (long long)c * a.ld) : a.ld;
+      for (int q = 0; q < la.W; ++q)
+        if (q != la.rank) v += ll_get(inbox_row(la, la.rank, par, q, c, a.k), j);
+    } else {
+      v = (long long)changed_now;
+    }
+    la.G[i] = v;
+  }
   a.D = la.G;
   a.changed = reinterpret_cast<const unsigned long long*>(la.G + ks + a.k);
   if (blockIdx.x == 0 && threadIdx.x == 0) st->sel_count = 0;
@@ -220,7 +313,7 @@ __device__ bool relocate_ranks(const LoopArgs& la, MStepArgs a, int b, int bulk,
     if (!select_farthest(a.mind, a.n, a.row_base, m, st, a.hist, a.sel, nb)) return false;
   }
   if (blockIdx.x == 0) {  // this rank's candidate block (the layout of shard_prep_kernel)
-    unsigned char* mine = la.cand_own;
+    unsigned char* mine = const_cast<unsigned char*>(la.pcand[la.rank]);
     float* dist = reinterpret_cast<float*>(mine + cand_dist_off(kCandCap));
     long long* row = reinterpret_cast<long long*>(mine + cand_row_off(kCandCap));
     int* label = reinterpret_cast<int*>(mine + cand_label_off(kCandCap));
@@ -310,10 +403,10 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     P.deltas = bulk ? nullptr : Dp;
     P.changed = chg;
     if (warp == IDLE_W) {
-      // the deltas E-step t + 1 adds into, idle since M-step t - 2 (every
-      // rank's reads of them ended before this iteration's first barrier):
-      // cleared off the M-step's path; the barrier after this pass orders it
-      // before E-step t + 1
+      // the deltas E-step t + 1 adds into, idle since M-step t - 2 (their
+      // readers finished before this iteration's first barrier): cleared off
+      // the M-step's path; the barrier after this pass orders it before
+      // E-step t + 1
       for (size_t i = 2 * ((size_t)blockIdx.x * 32 + lane); i < la.d_clear; i += 64 * (size_t)nb)
         *reinterpret_cast<longlong2*>(D_next + i) = make_longlong2(0, 0);
     }
@@ -341,12 +434,10 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
     }
     // every rank's deltas of this iteration are complete
-    if (la.W > 1 && !rank_barrier(la, st, ++epoch)) break;
-    // the change count over every rank (a round trip over NVLink): taken by
-    // the last warp, which owns no cluster, while the owners work; read after
-    // the next block barrier
-    if (threadIdx.x == blockDim.x - 32)
-      chg_s = la.W > 1 ? (unsigned long long)ranks_sum(la, t % 3, ks + k) : __ldcg(chg);
+    // one GPU: the change count, taken by the last warp (which owns no
+    // cluster) while the owners work, read after the next block barrier.
+    // Several ranks: it comes with the pushes of cluster 0 (below).
+    if (la.W == 1 && threadIdx.x == blockDim.x - 32) chg_s = __ldcg(chg);
     // (no block touches S_in, D or the counts before the barrier above)
     // owners: cluster cl is CTA cl mod nb's, one warp per owned cluster
     {
@@ -359,10 +450,15 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
         const long long i0 = (long long)cl * ld + 4 * lane;
         // the quad and the count loads go out together (one round trip)
         QuadSums r{};
-        if (lane < nq)
-          r = la.W > 1 ? quad_load_ranks(S_in, la, t % 3, C_old, i0, bulk) : quad_load(S_in, Dp, C_old, i0, bulk);
-        const long long cnew =
-            (bulk ? 0 : __ldcg(cnt_in + cl)) + (la.W > 1 ? ranks_sum(la, t % 3, ks + cl) : __ldcg(dcnt + cl));
+        long long cnew;
+        if (la.W > 1) {  // the exchange of cl's deltas with every peer
+          long long cd = 0;
+          r = owner_exchange(la, st, S_in, Dp, chg, C_old, cl, par, (unsigned int)t + 1, bulk, &cd);
+          cnew = (bulk ? 0 : __ldcg(cnt_in + cl)) + cd;
+        } else {
+          if (lane < nq) r = quad_load(S_in, Dp, C_old, i0, bulk);
+          cnew = (bulk ? 0 : __ldcg(cnt_in + cl)) + __ldcg(dcnt + cl);
+        }
         double dsq = 0.0, nrm = 0.0;
         if (cnew > 0 && lane < nq)  // the canonical order of warp_centre_from_sums
           quad_finish(r, cl, lane, i0, d, centre_factor(inv_scale, cnew), cs, la.m.cimg, CentreImage{}, S_out, C_new,
@@ -380,6 +476,17 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
       proxy_fence_all();
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
       stamp(la.prof, 4 * t + 2);
+      if (la.W > 1) {
+        if (__ldcg(&st->error)) break;  // uniform: a peer's push did not arrive
+        // the change count over every rank: own plus the peers' rows of
+        // cluster 0 (their owner saw them arrive before the barrier)
+        if (threadIdx.x == blockDim.x - 32) {
+          unsigned long long v = __ldcg(chg);
+          for (int q = 0; q < la.W; ++q)
+            if (q != la.rank) v += (unsigned long long)ll_get(inbox_row(la, la.rank, par, q, 0, k), ld + 1);
+          chg_s = v;
+        }
+      }
       // every CTA: flags, ||c||^2, and the total shift in the canonical
       // order (warp_ordered_sum); one load round (k <= 256 < threads)
       const int cl_t = threadIdx.x;
@@ -416,8 +523,8 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
             st->relocated = 0;
             if (strict) st->strict = 1;
             st->done = dn;
-            // (with several ranks the peers may still read it: it is
-            // cleared with the other deltas of its buffer, in E-step t + 2)
+            // (with several ranks other CTAs may still read it after the
+            // barrier: it is cleared with its buffer, in E-step t + 2)
             if (la.W == 1) *chg = 0;
           }
         }
@@ -431,7 +538,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
         // cooperative path, which folds this iteration's sums and counts into
         // S_in and cnt_in and writes every centre, image entry and norm
         if (la.W > 1) {
-          if (!relocate_ranks(la, a, t % 3, bulk, changed_now, n_bar, epoch)) break;
+          if (!relocate_ranks(la, a, Dp, par, bulk, changed_now, n_bar, epoch)) break;
         } else {
           const int ne = find_empty_clusters(a, bulk);
           if (!relocation_path(a, ne, bulk, changed_now)) break;
@@ -502,23 +609,21 @@ int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
       set_error(ERR_INVALID, "multi-GPU loop: bad rank layout");
       return ERR_INVALID;
     }
-    const size_t coff = region_cand_off(in.d_stride);
+    const size_t ioff = region_inbox_off(la.W, plan.k), coff = region_cand_off(la.W, plan.k, plan.ld);
     for (int r = 0; r < la.W; ++r) {
       unsigned char* rg = in.region[r];
       if (!rg) {
         set_error(ERR_INVALID, "multi-GPU loop: no peer region for rank %d", r);
         return ERR_INVALID;
       }
-      for (int i = 0; i < 3; ++i) la.pD[r][i] = reinterpret_cast<long long*>(rg + kRegionD) + i * in.d_stride;
       la.pflag[r] = reinterpret_cast<unsigned int*>(rg);
+      la.pin[r] = reinterpret_cast<unsigned long long*>(rg + ioff);
       la.pcand[r] = rg + coff;
     }
-    la.flags = la.pflag[in.rank];
-    la.cand_own = in.region[in.rank] + coff;
+    la.row = (int)region_row(plan.ld);
     la.G = in.G;
     la.cand_all = in.cand_all;
     la.cand_block = cand_block_bytes(kCandCap, plan.ld);
-    for (int i = 0; i < 3; ++i) la.D[i] = la.pD[in.rank][i];
   }
   static int attr_dev = -1;
   int dev = 0;

@@ -14,14 +14,22 @@ namespace skm {
 
 // Multi-GPU loop (one rank per GPU, rows sharded): each rank's peer region
 // (mapped into every rank) holds, at these byte offsets,
-//   [0, 64)                 one arrival word per rank, written by that rank
-//   [kRegionD, + 3 d_stride int64)   the rank's delta buffers D[0..2]
-//   region_cand_off(..)     the rank's relocation-candidate block
-//                           (cand_block_bytes(kCandCap, ld) bytes)
+//   [0, 256)              one arrival word per rank (rank_barrier)
+//   region_inbox_off      inbox rows: 2 parities x W ranks x k clusters x
+//                         2 (ld + 4) words: the sender's deltas of the
+//                         cluster, its count delta and (cluster 0) its change
+//                         count, each int64 as two 8-byte words {32 bits of
+//                         the value, the iteration's epoch}
+//   region_cand_off       the rank's relocation-candidate block
+//                         (cand_block_bytes(kCandCap, ld) bytes)
 constexpr int kLoopMaxRanks = 8;
-constexpr size_t kRegionD = 256;
-inline size_t region_cand_off(size_t d_stride) { return kRegionD + 3 * d_stride * sizeof(long long); }
-inline size_t region_bytes(size_t d_stride, int ld) { return region_cand_off(d_stride) + cand_block_bytes(kCandCap, ld); }
+constexpr size_t kRegionFlags = 256;
+inline size_t region_row(int ld) { return 2 * ((size_t)ld + 4); }  // 8-byte words per inbox row
+inline size_t region_inbox_off(int, int) { return kRegionFlags; }
+inline size_t region_cand_off(int W, int k, int ld) {
+  return region_inbox_off(W, k) + 2 * (size_t)W * k * region_row(ld) * sizeof(long long);
+}
+inline size_t region_bytes(int W, int k, int ld) { return region_cand_off(W, k, ld) + cand_block_bytes(kCandCap, ld); }
 
 struct LoopInputs {
   const uint16_t* img;       // centre image of the start centres (B operand)
@@ -35,13 +43,11 @@ struct LoopInputs {
   double* part;              // 3 k doubles of per-cluster results of the owners
   unsigned int* bar;         // grid-barrier counter of the loop, zero at launch
   unsigned long long* prof;  // nullable: 4 * max_iter + 1 globaltimer stamps (see lloyd_loop_kernel)
-  // multi-GPU (nranks > 1): every rank's peer region (own at [rank]; the
-  // delta buffers are then this rank's region buffers, D above is ignored),
-  // d_stride, and local scratch for the global deltas (k * ld + k + 1) and
-  // the gathered candidate blocks
+  // multi-GPU (nranks > 1): every rank's peer region (own at [rank]), and
+  // local scratch for the global deltas (k * ld + k + 1) and the gathered
+  // candidate blocks
   int nranks = 1, rank = 0;
   unsigned char* region[kLoopMaxRanks] = {};
-  size_t d_stride = 0;
   long long* G = nullptr;
   unsigned char* cand_all = nullptr;
 };

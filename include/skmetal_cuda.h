@@ -31,7 +31,7 @@ extern "C" {
 #define SKMETAL_FIT_CENTER      0x1u  /* centre X and init by the column mean (KMeans.fit semantics) */
 #define SKMETAL_FIT_SIMT        0x2u  /* force the SIMT E-step instead of the tensor-core one */
 #define SKMETAL_FIT_PROFILE     0x4u  /* time the E-step launches of every 10th iteration with CUDA events (see fit stats) */
-#define SKMETAL_FIT_DISTRIBUTED 0x8u  /* X is this rank's shard; sums are all-reduced over the communicator */
+#define SKMETAL_FIT_DISTRIBUTED 0x8u  /* X is this rank's shard; sums are summed over the communicator's ranks */
 #define SKMETAL_FIT_TOL_ABS     0x10u /* tol is the absolute threshold on the sum of squared centre shifts */
 #define SKMETAL_FIT_BULK_SUMS   0x20u /* recompute the centroid sums from all rows every iteration (diagnostic) */
 

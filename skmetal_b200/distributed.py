@@ -1,9 +1,10 @@
 """Host-side plumbing of multi-GPU fits (one process per GPU).
 
 The data path is sharded by rows: rank ``r`` of ``W`` holds rows
-``[n r / W, n (r + 1) / W)`` of the dataset and the library all-reduces the
-per-iteration ``k x d`` fixed-point sums and ``k`` counts over NCCL itself
-(``skmetal_kmeans_fit_shard``). Python only has to give every rank its shard,
+``[n r / W, n (r + 1) / W)`` of the dataset and the library sums the
+per-iteration ``k x d`` fixed-point sums and ``k`` counts over the ranks itself
+(``skmetal_kmeans_fit_shard``: inside its loop kernel over NVLink, or with an
+NCCL all-reduce per iteration when the GPUs cannot map each other's memory). Python only has to give every rank its shard,
 create the library's communicator from one NCCL unique id, and reduce timings
 over ranks. These helpers take the ``torch.distributed`` module (any backend)
 and the bridge as arguments, so the same code runs under NCCL on GPUs and

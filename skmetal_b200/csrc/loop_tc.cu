@@ -411,7 +411,8 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
         *reinterpret_cast<longlong2*>(D_next + i) = make_longlong2(0, 0);
     }
     estep_pass(p, c, P);
-    ++img_loads;
+    ++img_loads;        // the pass waited for its image copy
+    image_issued = 0;
     pre = P.pre_next;
     proxy_fence_all();
     if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;
@@ -561,6 +562,12 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
   }
   stamp(la.prof, 4 * t);
   if (t > 0 && blockIdx.x == 0 && threadIdx.x == 0) st->cexp = xexp;  // scale of the final image
+  // the image copy issued by the last M-step (the loop stopped after it)
+  // lands before the CTA exits
+  if (image_issued && threadIdx.x == MMA_W0 * 32) {
+    volatile int no_abort = 0;
+    mbar_wait(c.bar(B_C_FULL), img_loads & 1, &no_abort, p.err, 2106);
+  }
   cta_teardown(p, c);
 }
 

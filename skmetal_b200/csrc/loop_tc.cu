@@ -181,8 +181,9 @@ __device__ __forceinline__ long long ll_get(const unsigned long long* row, int j
 // after the local barrier that completed this rank's deltas: pushes the
 // rank's deltas of c (lane l: column quad l), count delta and, for c = 0,
 // change count into every peer's inbox row (8-byte stores over NVLink),
-// then waits (each lane for its own words; bounded: 5 s, then error 1005)
-// until every peer's row of c carries this iteration's epoch, and returns
+// then reads every peer's row of c (all peers' loads in flight together) and
+// re-polls the words that did not carry this iteration's epoch yet (each lane
+// its own; bounded: 5 s, then error 1005), and returns
 // c's sums over every rank (S_in added unless bulk; as quad_load) and c's
 // count delta over every rank.
 __device__ __forceinline__ QuadSums owner_exchange(const LoopArgs& la, FitState* st, const long long* S_in,
@@ -225,12 +226,38 @@ __device__ __forceinline__ QuadSums owner_exchange(const LoopArgs& la, FitState*
     s[3] += a23.y;
   }
   long long cnt = ocnt;
-  const unsigned long long t0 = globaltimer();
-  for (int q = 0; q < la.W; ++q) {
-    if (q == la.rank) continue;
+  // every peer's words go out together; a peer whose words (this lane's) do
+  // not carry the epoch yet is polled again below
+  unsigned int pending = 0;
+#pragma unroll
+  for (int q = 0; q < kLoopMaxRanks; ++q) {
+    if (q >= la.W || q == la.rank) continue;
     const unsigned long long* src = inbox_row(la, la.rank, par, q, c, k);
-    ulonglong2 w[4], wc = make_ulonglong2(0, 0);
-    for (unsigned int it = 1;; ++it) {
+    ulonglong2 w[4] = {};
+    bool ready = true;
+    if (lane < nq)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        w[u] = ll_load(src + 2 * (4 * lane + u));
+        ready = ready && ll_ready(w[u], epoch);
+      }
+    const ulonglong2 wc = ll_load(src + 2 * ld);  // every lane: the count delta
+    ready = ready && ll_ready(wc, epoch);
+    if (c == 0 && lane == 0) ready = ready && ll_ready(ll_load(src + 2 * (ld + 1)), epoch);  // change count
+    if (ready) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s[u] += ll_value(w[u]);
+      cnt += ll_value(wc);
+    } else {
+      pending |= 1u << q;
+    }
+  }
+  const unsigned long long t0 = globaltimer();
+  for (unsigned int it = 1; __any_sync(0xffffffffu, pending != 0); ++it) {
+    if (pending) {
+      const int q = __ffs(pending) - 1;
+      const unsigned long long* src = inbox_row(la, la.rank, par, q, c, k);
+      ulonglong2 w[4] = {};
       bool ready = true;
       if (lane < nq)
 #pragma unroll
@@ -238,22 +265,23 @@ __device__ __forceinline__ QuadSums owner_exchange(const LoopArgs& la, FitState*
           w[u] = ll_load(src + 2 * (4 * lane + u));
           ready = ready && ll_ready(w[u], epoch);
         }
-      wc = ll_load(src + 2 * ld);  // every lane: the count delta
+      const ulonglong2 wc = ll_load(src + 2 * ld);
       ready = ready && ll_ready(wc, epoch);
-      if (c == 0 && lane == 0) ready = ready && ll_ready(ll_load(src + 2 * (ld + 1)), epoch);  // change count
-      if (__all_sync(0xffffffffu, ready)) break;
-      if ((it & 63) == 0) {  // the same iterations on every lane; lane 0's clock decides
-        const bool late = __shfl_sync(0xffffffffu, globaltimer() - t0 > 5000000000ull, 0);
-        if (late) {
-          if (lane == 0) atomicExch(&st->error, 1005);
-          break;
-        }
+      if (c == 0 && lane == 0) ready = ready && ll_ready(ll_load(src + 2 * (ld + 1)), epoch);
+      if (ready) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) s[u] += ll_value(w[u]);
+        cnt += ll_value(wc);
+        pending &= ~(1u << q);
       }
     }
-    if (lane < nq)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) s[u] += ll_value(w[u]);
-    cnt += ll_value(wc);
+    if ((it & 63) == 0) {  // the same iterations on every lane; lane 0's clock decides
+      const bool late = __shfl_sync(0xffffffffu, globaltimer() - t0 > 5000000000ull, 0);
+      if (late) {
+        if (lane == 0) atomicExch(&st->error, 1005);
+        break;
+      }
+    }
   }
   QuadSums r;
   r.old = lane < nq ? __ldcg(reinterpret_cast<const float4*>(C_old + i)) : make_float4(0.f, 0.f, 0.f, 0.f);

@@ -334,11 +334,42 @@ static __device__ __forceinline__ unsigned long long reloc_key(float dist, long 
 }
 
 // Selection of the m rows farthest from their assigned centre (largest
-// (distance, -row) keys) by an exact 8-pass radix select over 64-bit keys.
-// Keys are unique, so exactly m rows are collected. Runs inside the
-// cooperative M-step; `hist` holds 2 x 256 counters.
+// (distance, -row) keys) by an exact 8-pass radix select over 64-bit keys
+// (one maximum pass when m = 1). Keys are unique, so exactly m rows are
+// collected. Runs inside the cooperative M-step; `hist` holds 2 x 256
+// counters (8-byte aligned), zero on entry and on return.
 static __device__ bool select_farthest(const float* __restrict__ mind, long long n, long long row_base, int m,
                                 FitState* st, unsigned int* hist, long long* sel, unsigned int nblocks) {
+  if (m == 1) {
+    // one row: the largest key (keys are unique), by a block maximum and a
+    // 64-bit atomicMax on the first two histogram words (zero on entry; the
+    // same row as the radix select)
+    __shared__ unsigned long long wmax_s[32];
+    unsigned long long* top = reinterpret_cast<unsigned long long*>(hist);
+    unsigned long long best = 0;
+    for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)nblocks * blockDim.x)
+      best = max(best, reloc_key(mind[r], row_base + r));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) wmax_s[threadIdx.x >> 5] = best;
+    block_sync();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = max(best, wmax_s[w]);
+      if (best) atomicMax(top, best);
+    }
+    if (!grid_barrier(st, nblocks)) return false;
+    const unsigned long long k1 = *reinterpret_cast<volatile unsigned long long*>(top);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      // low 32 bits: 0xffffffff - global row (reloc_key)
+      const long long g = (long long)(0xffffffffu - (unsigned int)(k1 & 0xffffffffull));
+      sel[0] = g - row_base;
+      st->sel_count = 1;
+    }
+    if (!grid_barrier(st, nblocks)) return false;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *top = 0;  // read by nobody until the next selection
+    return true;
+  }
+
   __shared__ unsigned int h[256];
   __shared__ unsigned long long prefix_s, mask_s;
   __shared__ int remaining_s, whole_s;

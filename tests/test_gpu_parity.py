@@ -191,6 +191,22 @@ def test_lloyd_step_relocation_lockstep():
     _lockstep(X, init, 5)
 
 
+def test_fit_single_empty_cluster_matches_oracle():
+    """A duplicated initial centre leaves exactly one cluster empty in the
+    first iteration (ties go to the lower index), so the relocation picks one
+    farthest row, through the selection's one-row path: the fit must match the
+    oracle's (_k_means_common.pyx:160-196); the oracle relocates one row in
+    each of the first two iterations."""
+    X, _ = gaussian_mixture(20000, 16, 6, seed=23)
+    init = np.ascontiguousarray(np.concatenate([X[:6], X[:1]]))  # centre 6 duplicates centre 0
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 30, 0.0)
+    res = ora.kmeans_lloyd(X, init, 30, 0.0, relocation_order="sorted")
+    assert n_iter == res.n_iter
+    assert np.mean(lab == res.labels) >= 0.9999
+    np.testing.assert_allclose(c, res.centers, rtol=CENTER_RTOL, atol=1e-5)
+    assert inertia == pytest.approx(res.inertia, rel=INERTIA_RTOL)
+
+
 @pytest.mark.parametrize("n,d,k", [(300_000, 36, 24), (200_000, 100, 50), (150_000, 64, 256)])
 def test_estep_many_tiles_per_cta(n, d, k):
     """Sizes at which every CTA of the persistent tensor-core E-step runs many

@@ -48,6 +48,12 @@ def case_inputs(gen: str):
         X, _ = gaussian_mixture(4000, 10, 5, seed=11)
         init = np.ascontiguousarray(np.repeat(X[:4], 5, axis=0))
         return X, init
+    if gen == "reloc1":
+        # 6 blobs, 7 initial centres of which the last duplicates the first:
+        # exactly one cluster is empty in each of the first two iterations
+        X, _ = gaussian_mixture(20000, 16, 6, seed=23)
+        init = np.ascontiguousarray(np.concatenate([X[:6], X[:1]]))
+        return X, init
     if gen == "odd":
         rng = np.random.default_rng(257)
         X = (rng.standard_normal((257, 9)) * 3).astype(np.float32)

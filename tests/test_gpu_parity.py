@@ -197,8 +197,7 @@ def test_fit_single_empty_cluster_matches_oracle():
     farthest row, through the selection's one-row path: the fit must match the
     oracle's (_k_means_common.pyx:160-196); the oracle relocates one row in
     each of the first two iterations."""
-    X, _ = gaussian_mixture(20000, 16, 6, seed=23)
-    init = np.ascontiguousarray(np.concatenate([X[:6], X[:1]]))  # centre 6 duplicates centre 0
+    X, init = _golden_gen("reloc1")  # centre 6 duplicates centre 0
     c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 30, 0.0)
     res = ora.kmeans_lloyd(X, init, 30, 0.0, relocation_order="sorted")
     assert n_iter == res.n_iter

@@ -30,6 +30,8 @@ CASES = {
     "c2_60k": dict(gen="mixture:60000:100:50:1", max_iter=30, tol=0.0),
     # relative tolerance: the stop decision must agree on both ranks
     "tol": dict(gen="mixture:40000:32:8:0", max_iter=100, tol=1e-4),
+    # one empty cluster: each rank offers its single farthest row
+    "one_empty": dict(gen="reloc1", max_iter=30, tol=0.0),
 }
 
 

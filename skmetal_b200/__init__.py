@@ -16,7 +16,6 @@ Drop-in for the reference's public surface for this path::
 """
 
 from ._about import __version__, __version_info__
-from ._bridge import CUDA_AVAILABLE, GPU_AVAILABLE, METAL_AVAILABLE
 from ._config import (
     get_config,
     reset_thresholds,
@@ -31,13 +30,23 @@ from ._config import (
 from .accelerate import accelerate, accelerate_context
 
 
+def __getattr__(name: str):
+    # CUDA_AVAILABLE / GPU_AVAILABLE / METAL_AVAILABLE load the native library
+    # on first access (importing the package maps no native code)
+    if name in ("CUDA_AVAILABLE", "GPU_AVAILABLE", "METAL_AVAILABLE"):
+        from . import _bridge
+
+        return getattr(_bridge, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
+
+
 def device_info() -> dict:
     """Name and memory of the current CUDA device (raises without a GPU)."""
-    from ._bridge import device_info as _di
+    from . import _bridge
 
-    if not GPU_AVAILABLE:
+    if not _bridge.GPU_AVAILABLE:
         raise RuntimeError("skmetal_b200: device_info() requires a CUDA GPU; none is visible.")
-    return _di()
+    return _bridge.device_info()
 
 
 __all__ = [

@@ -1,8 +1,8 @@
 """ctypes bridge to ``libskmetal_cuda.so`` (the CUDA replacement of the
 reference's ``libSkMetalBridge.dylib``).
 
-Mirrors ``skmetal/_bridge.py``: the library is loaded once at import,
-``_bridge_call`` converts numpy arrays / ints / floats / bools the same way
+Mirrors ``skmetal/_bridge.py``: the library is loaded once per process (on
+first use rather than at import), ``_bridge_call`` converts numpy arrays / ints / floats / bools the same way
 (``skmetal/_bridge.py:78-103``) and raises ``RuntimeError`` on a nonzero
 status. Unlike the reference, symbols are bound tolerantly (a missing symbol
 disables only its wrapper) and the error text comes from the library.
@@ -24,7 +24,7 @@ __all__ = [
     "CUDA_AVAILABLE", "GPU_AVAILABLE", "METAL_AVAILABLE", "LIB_PATH",
     "ensure_warmed_up", "kmeans_assign", "kmeans_batch_fused", "compute_mindists", "kmeans_inertia",
     "row_norm_sq", "kmeans_fit", "kmeans_lloyd_iter", "kmeans_transform", "Dataset", "last_fit_stats",
-    "launch_count", "device_info", "device_count", "set_device", "comm_unique_id", "comm_init",
+    "launch_count", "device_info", "device_count", "is_loaded", "set_device", "comm_unique_id", "comm_init",
     "comm_destroy", "kmeans_fit_shard", "debug_inject_failure", "debug_loop_stamps", "FIT_CENTER", "FIT_SIMT", "FIT_PROFILE",
     "FIT_DISTRIBUTED", "FIT_TOL_ABS", "EXPORTED_SYMBOLS",
 ]
@@ -102,52 +102,80 @@ def _find_library() -> Path:
         "(or __graft_entry__.build())")
 
 
-LIB_PATH: Path | None = None
+# The library is loaded on first use (any wrapper call, or reading
+# CUDA_AVAILABLE / GPU_AVAILABLE / METAL_AVAILABLE / LIB_PATH), not at import:
+# importing the package, e.g. only for its workload generators, maps no
+# native code and touches no GPU.
 _lib = None
 _load_error = None
-try:
-    LIB_PATH = _find_library()
-    _lib = ctypes.CDLL(str(LIB_PATH))
-except Exception as _e:  # noqa: BLE001
-    _load_error = str(_e)
-    _lib = None
-
+_loaded = False
 _funcs: dict = {}
-if _lib is not None:
-    for _name, _res, _args in _SIGNATURES:
-        try:
-            _f = getattr(_lib, _name)
-        except AttributeError:
-            continue
-        _f.restype = _res
-        _f.argtypes = _args
-        _funcs[_name] = _f
-
-CUDA_AVAILABLE = _lib is not None
+_state: dict = {}
 
 
-def device_count() -> int:
-    if not CUDA_AVAILABLE:
-        return 0
+def _load() -> None:
+    """Load ``libskmetal_cuda.so`` and bind its symbols (once per process)."""
+    global _lib, _load_error, _loaded
+    if _loaded:
+        return
+    _loaded = True
+    path = None
+    try:
+        path = _find_library()
+        _lib = ctypes.CDLL(str(path))
+    except Exception as e:  # noqa: BLE001
+        _load_error = str(e)
+        _lib = None
+    if _lib is not None:
+        for name, res, args in _SIGNATURES:
+            try:
+                f = getattr(_lib, name)
+            except AttributeError:
+                continue
+            f.restype = res
+            f.argtypes = args
+            _funcs[name] = f
+    cuda = _lib is not None
+    gpu = cuda and _device_count_loaded() > 0
+    _state.update(LIB_PATH=path, CUDA_AVAILABLE=cuda, GPU_AVAILABLE=gpu,
+                  # the reference's public flag name, meaning "GPU path available" here
+                  METAL_AVAILABLE=gpu)
+    if not cuda:
+        warnings.warn(f"skmetal_b200: CUDA library not loaded ({_load_error}); GPU estimators will raise.",
+                      stacklevel=3)
+
+
+def _device_count_loaded() -> int:
     n = _c_int(0)
     if _funcs["skmetal_device_count"](ctypes.byref(n)) != 0:
         return 0
     return int(n.value)
 
 
-GPU_AVAILABLE = CUDA_AVAILABLE and device_count() > 0
-# the reference's public flag name, meaning "GPU path available" here
-METAL_AVAILABLE = GPU_AVAILABLE
+def __getattr__(name: str):
+    if name in ("LIB_PATH", "CUDA_AVAILABLE", "GPU_AVAILABLE", "METAL_AVAILABLE"):
+        _load()
+        return _state[name]
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
 
-if not CUDA_AVAILABLE:
-    warnings.warn(f"skmetal_b200: CUDA library not loaded ({_load_error}); GPU estimators will raise.",
-                  stacklevel=2)
+
+def is_loaded() -> bool:
+    """True once this process has mapped the native library."""
+    return _lib is not None
+
+
+def device_count() -> int:
+    _load()
+    if _lib is None:
+        return 0
+    return _device_count_loaded()
 
 
 def _require():
-    if not CUDA_AVAILABLE:
+    _load()
+    if not _state["CUDA_AVAILABLE"]:
         raise RuntimeError(f"skmetal_b200: CUDA library not available ({_load_error})")
-    if not GPU_AVAILABLE:
+    if not _state["GPU_AVAILABLE"]:
         raise RuntimeError("skmetal_b200: no CUDA device visible; the KMeans path has no CPU fallback")
 
 
@@ -155,11 +183,14 @@ def _fn(name: str):
     _require()
     f = _funcs.get(name)
     if f is None:
-        raise RuntimeError(f"skmetal_b200: symbol {name} missing from {LIB_PATH}")
+        raise RuntimeError(f"skmetal_b200: symbol {name} missing from {_state['LIB_PATH']}")
     return f
 
 
 def _last_error() -> str:
+    _load()
+    if "skmetal_last_error" not in _funcs:
+        return str(_load_error)
     buf = ctypes.create_string_buffer(1024)
     _funcs["skmetal_last_error"](buf, 1024)
     return buf.value.decode("utf-8", "replace")
@@ -463,7 +494,7 @@ def comm_init(uid: bytes, nranks: int, rank: int) -> None:
 
 
 def comm_destroy() -> None:
-    if CUDA_AVAILABLE:
+    if is_loaded() and "skmetal_comm_destroy" in _funcs:
         _funcs["skmetal_comm_destroy"]()
 
 

@@ -16,7 +16,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-__all__ = ["Workload", "WORKLOADS", "make_workload", "gaussian_mixture", "scaled"]
+__all__ = ["Workload", "WORKLOADS", "make_workload", "make_rows", "gaussian_mixture", "scaled"]
 
 
 @dataclass(frozen=True)
@@ -69,7 +69,9 @@ def _unit_rows(n: int, d: int, k: int, seed: int) -> tuple[np.ndarray, np.ndarra
     return X, init
 
 
-def _dirichlet_mixture(n: int, d: int, k: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
+def _dirichlet_plan(n: int, d: int, k: int, seed: int):
+    """Mixture parameters, every row's component and the init row indices of
+    the C4 recipe (the main stream of ``default_rng(seed)``)."""
     rng = np.random.default_rng(seed)
     centres = rng.uniform(-5.0, 5.0, (k, d)).astype(np.float32)
     sigma = rng.uniform(0.5, 2.0, k).astype(np.float32)
@@ -77,21 +79,50 @@ def _dirichlet_mixture(n: int, d: int, k: int, seed: int) -> tuple[np.ndarray, n
     sizes = rng.multinomial(n, p)
     labels = np.repeat(np.arange(k, dtype=np.int32), sizes)
     rng.shuffle(labels)
-    X = np.empty((n, d), dtype=np.float32)
-    for s in range(0, n, _CHUNK):
-        e = min(n, s + _CHUNK)
-        lab = labels[s:e]
-        X[s:e] = centres[lab] + sigma[lab, None] * rng.standard_normal((e - s, d), dtype=np.float32)
-    init = np.ascontiguousarray(X[rng.choice(n, k, replace=False)])
+    # k seed-chosen rows of the first chunk (an unbiased sample: the rows'
+    # components are shuffled), so that the init needs no other chunk
+    init_idx = rng.choice(min(n, _CHUNK), k, replace=False)
+    return centres, sigma, labels, init_idx
+
+
+def _dirichlet_rows(plan, d: int, lo: int, hi: int) -> np.ndarray:
+    """Rows [lo, hi) of the C4 recipe: chunk c (rows [c * _CHUNK, ...)) draws
+    its noise from its own stream default_rng([seed, c + 1]), so any row range
+    is generated without the rows before it."""
+    centres, sigma, labels, _, seed = plan
+    X = np.empty((hi - lo, d), dtype=np.float32)
+    for c in range(lo // _CHUNK, -(-hi // _CHUNK)):
+        s0, e0 = c * _CHUNK, min(labels.shape[0], (c + 1) * _CHUNK)
+        a, b = max(lo, s0), min(hi, e0)
+        if a >= b:
+            continue
+        noise = np.random.default_rng([seed, c + 1]).standard_normal((b - s0, d), dtype=np.float32)[a - s0:]
+        lab = labels[a:b]
+        X[a - lo:b - lo] = centres[lab] + sigma[lab, None] * noise
+    return X
+
+
+def _dirichlet_mixture(n: int, d: int, k: int, seed: int, lo: int = 0, hi: int | None = None):
+    hi = n if hi is None else hi
+    centres, sigma, labels, init_idx = _dirichlet_plan(n, d, k, seed)
+    plan = (centres, sigma, labels, init_idx, seed)
+    X = _dirichlet_rows(plan, d, lo, hi)
+    head = X if lo == 0 and hi >= min(n, _CHUNK) else _dirichlet_rows(plan, d, 0, min(n, _CHUNK))
+    init = np.ascontiguousarray(head[init_idx])
     return X, init
 
 
-def _uniform_predict(n: int, d: int, k: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
-    rng = np.random.default_rng(seed)
-    X = np.empty((n, d), dtype=np.float32)
-    for s in range(0, n, _CHUNK):
-        e = min(n, s + _CHUNK)
-        X[s:e] = rng.random((e - s, d), dtype=np.float32)
+def _uniform_predict(n: int, d: int, k: int, seed: int, lo: int = 0, hi: int | None = None):
+    """Rows [lo, hi) of U[0,1)^d (chunk c from default_rng([seed, c + 1])) and
+    the k centres U[0,1)^d from default_rng(seed + 1)."""
+    hi = n if hi is None else hi
+    X = np.empty((hi - lo, d), dtype=np.float32)
+    for c in range(lo // _CHUNK, -(-hi // _CHUNK)):
+        s0, e0 = c * _CHUNK, min(n, (c + 1) * _CHUNK)
+        a, b = max(lo, s0), min(hi, e0)
+        if a >= b:
+            continue
+        X[a - lo:b - lo] = np.random.default_rng([seed, c + 1]).random((b - s0, d), dtype=np.float32)[a - s0:]
     centers = np.random.default_rng(seed + 1).random((k, d), dtype=np.float32)
     return X, centers
 
@@ -106,12 +137,21 @@ def make_workload(w: Workload | str) -> tuple[np.ndarray, np.ndarray]:
     """Generate ``(X, init)`` (fit workloads) or ``(X, centers)`` (predict)."""
     if isinstance(w, str):
         w = WORKLOADS[w]
-    if w.name in ("c1", "c2"):
-        return gaussian_mixture(w.n, w.d, w.k, w.seed)
-    if w.name == "c3":
-        return _unit_rows(w.n, w.d, w.k, w.seed)
+    return make_rows(w, 0, w.n)
+
+
+def make_rows(w: Workload | str, lo: int, hi: int) -> tuple[np.ndarray, np.ndarray]:
+    """Rows ``[lo, hi)`` of the workload's X and its init (or centres): the
+    same values as ``make_workload(w)[0][lo:hi]``. The C4 and C5 recipes
+    generate only the requested rows (plus the init's chunk), so every rank of
+    a sharded run holds just its shard."""
+    if isinstance(w, str):
+        w = WORKLOADS[w]
+    if w.name in ("c1", "c2", "c3"):
+        X, init = (gaussian_mixture(w.n, w.d, w.k, w.seed) if w.name != "c3" else _unit_rows(w.n, w.d, w.k, w.seed))
+        return (X if (lo, hi) == (0, w.n) else np.ascontiguousarray(X[lo:hi])), init
     if w.name == "c4":
-        return _dirichlet_mixture(w.n, w.d, w.k, w.seed)
+        return _dirichlet_mixture(w.n, w.d, w.k, w.seed, lo, hi)
     if w.name == "c5":
-        return _uniform_predict(w.n, w.d, w.k, w.seed)
+        return _uniform_predict(w.n, w.d, w.k, w.seed, lo, hi)
     raise KeyError(w.name)

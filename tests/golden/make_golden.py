@@ -34,6 +34,11 @@ CASES = {
     "c1_small": ("mixture:4000:32:8:0", 8, 50, 0.0),
     "c2_small": ("mixture:6000:100:50:1", 50, 30, 0.0),
     "c3_small": ("unit:3000:128:64:2", 64, 10, 0.0),
+    # the C3 codebook shape: k = 1024 (several 256-cluster blocks of the
+    # tensor-core E-step), d = 128
+    "c3_k1024": ("unit:20000:128:1024:2", 1024, 4, 0.0),
+    # k = 300: two uneven cluster blocks, d not a multiple of 8
+    "k300_odd": ("mixture:9000:37:300:4", 300, 6, 0.0),
     "c4_small": ("dirichlet:5000:64:256:3", 256, 8, 0.0),
     "tol_rel": ("mixture:3000:32:8:0", 8, 100, 1e-4),
     "relocation": ("reloc", 20, 10, 0.0),

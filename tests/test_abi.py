@@ -39,7 +39,24 @@ def test_bridge_binds_every_declared_symbol():
 
     declared = set(_declared())
     assert set(_bridge.EXPORTED_SYMBOLS) == declared
+    _bridge._load()
     assert set(_bridge._funcs) == declared
+
+
+def test_package_import_maps_no_native_code():
+    """Importing the package (e.g. for its workload generators, as the bench's
+    reference arm does) must not load libskmetal_cuda.so; first use does."""
+    import sys
+
+    code = ("import skmetal_b200, skmetal_b200._synthetic, skmetal_b200.estimators; "
+            "from skmetal_b200 import _bridge; "
+            "maps = open('/proc/self/maps').read(); "
+            "assert 'libskmetal_cuda' not in maps, 'mapped at import'; "
+            "assert not _bridge.is_loaded(); "
+            "_bridge.CUDA_AVAILABLE; "
+            "assert 'libskmetal_cuda' in open('/proc/self/maps').read(), 'not mapped on first use'")
+    r = subprocess.run([sys.executable, "-c", code], cwd=str(ROOT), capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
 
 
 def test_dynamic_symbol_table_has_only_the_c_abi():

@@ -71,6 +71,12 @@ int skmetal_debug_inject_failure(int code, int after_calls);
  * two-segment layout. */
 int skmetal_debug_tc_probe(int* mode, uint32_t* raw4096);
 
+/* The same self-check for the E-step of more than 256 clusters (no reference
+ * counterpart): 32 centres in two blocks of 16 (the blocked centre image) and
+ * its three-MMA sequence per block. raw4096 receives the 128 x 32 products
+ * (float bits). */
+int skmetal_debug_tc_probe_wide(int* mode, uint32_t* raw4096);
+
 /* ---- KMeans path: reference entry points -------------------------------- */
 
 /* Replaces skmetal_kmeans_assign (KMeansBridge.swift:138-181; bound at

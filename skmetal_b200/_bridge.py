@@ -52,6 +52,7 @@ _SIGNATURES = [
     ("skmetal_launch_count", ctypes.c_ulonglong, []),
     ("skmetal_debug_inject_failure", _c_int, [_c_int, _c_int]),
     ("skmetal_debug_tc_probe", _c_int, [ctypes.POINTER(_c_int), _c_void_p]),
+    ("skmetal_debug_tc_probe_wide", _c_int, [ctypes.POINTER(_c_int), _c_void_p]),
     ("skmetal_debug_loop_stamps", _c_int, [_c_void_p, _c_int]),
     ("skmetal_kmeans_assign", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t]),
     ("skmetal_kmeans_batch_fused", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t,
@@ -439,6 +440,18 @@ def debug_tc_probe(raw: bool = False):
     rc = _fn("skmetal_debug_tc_probe")(ctypes.byref(mode), out.ctypes.data if raw else None)
     if rc != 0:
         raise RuntimeError(f"skmetal_debug_tc_probe failed with code {rc}: {_last_error()}")
+    return int(mode.value), out
+
+
+def debug_tc_probe_wide():
+    """Self-check of the k > 256 E-step's blocked centre image and MMA
+    sequence: (mode, raw) with raw the 128 x 32 products (uint32 bit patterns
+    of float32); mode 0 exact, -1 unusable (SIMT E-step for k > 256)."""
+    mode = _c_int(-3)
+    out = np.zeros(4096, dtype=np.uint32)
+    rc = _fn("skmetal_debug_tc_probe_wide")(ctypes.byref(mode), out.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"skmetal_debug_tc_probe_wide failed with code {rc}: {_last_error()}")
     return int(mode.value), out
 
 

@@ -100,6 +100,15 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return pol;
 }
 
+// L2 policy for small data every CTA re-reads many times in a pass (the
+// centre units of the k > 256 E-step): kept in L2 in preference to the
+// streamed tiles.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
                                                uint64_t pol) {
   asm volatile(
@@ -250,16 +259,34 @@ __device__ __forceinline__ int split_exp(unsigned int maxabs_bits) {
 //  otherwise: N = k_pad; segment 1 holds (c_hi | c_hi) per chunk, segment 2
 //    (after nk chunks) holds c_lo of chunk pairs (2m | 2m + 1), multiplied by
 //    x_hi of the same pair; both accumulate into one accumulator.
+//  blocked (kCimgBlocked, k > 256): the clusters in blocks of nbs (<= 256, a
+//    multiple of 16); for block b and column pair m (columns 16m .. 16m + 15)
+//    one unit of nbs * 64 bytes at ((b * npairs + m) * nbs * 32) halves, with
+//    npairs = (nk + 1) / 2: c_hi of the pair (nbs rows x 16 halves, K-major,
+//    K halves nbs * 16 bytes apart) then c_lo of the pair (same layout). One
+//    unit is the B operand of three MMAs of N = nbs, K = 16: x_hi.c_hi,
+//    x_lo.c_hi and x_hi.c_lo of the pair.
 // Entries of padding rows and columns are zero.
+constexpr int kCimgTwoSegment = 0, kCimgStacked = 1, kCimgBlocked = 2;
 struct CentreImage {
   uint16_t* img;  // fp16 bit patterns; null when the tensor-core path is off
-  int k_pad;      // clusters padded to 16
+  int k_pad;      // clusters padded to 16 (blocked: nbs * blocks)
   int nk;         // K chunks of 8 columns
-  int stacked;
+  int stacked;    // layout: kCimgTwoSegment, kCimgStacked or kCimgBlocked
+  int nbs;        // blocked: clusters per block
 };
 
 __host__ __device__ inline size_t cimg_halves(int k_pad, int nk, int stacked) {
+  if (stacked == kCimgBlocked) return (size_t)k_pad * ((nk + 1) / 2) * 32;
   return stacked ? (size_t)nk * 2 * k_pad * 16 : (size_t)nk * k_pad * 16 + (size_t)((nk + 1) / 2) * k_pad * 16;
+}
+
+// Offset (halves) of centre c, column e of pair m in the blocked layout, and
+// that of its c_lo entry (one c_hi slice further).
+__host__ __device__ __forceinline__ size_t cimg_blocked_off(const CentreImage& ci, int c, int m, int e) {
+  const int b = c / ci.nbs, cl = c - b * ci.nbs;
+  const size_t unit = ((size_t)b * ((ci.nk + 1) >> 1) + m) * (size_t)ci.nbs * 32;
+  return unit + (size_t)(e >> 3) * ci.nbs * 8 + (size_t)(cl >> 3) * 64 + (size_t)(cl & 7) * 8 + (e & 7);
 }
 
 // Writes centre c, columns 4q .. 4q + 3 (values v[0..3], scale s = 2^e) into
@@ -276,6 +303,12 @@ __device__ __forceinline__ void cimg_put4(const CentreImage& ci, int c, int q, c
     l[p] = *reinterpret_cast<const uint32_t*>(&ll);
   }
   const uint2 hv = make_uint2(h[0], h[1]), lv = make_uint2(l[0], l[1]);
+  if (ci.stacked == kCimgBlocked) {  // quad q = columns 4 (q & 3) .. + 3 of pair q / 4
+    const size_t o = cimg_blocked_off(ci, c, q >> 2, (q & 3) * 4);
+    *reinterpret_cast<uint2*>(ci.img + o) = hv;
+    *reinterpret_cast<uint2*>(ci.img + o + (size_t)ci.nbs * 16) = lv;
+    return;
+  }
   const int chunk = q >> 1, e = (q & 1) * 4;
   const int N = ci.stacked ? 2 * ci.k_pad : ci.k_pad;
   const size_t base = (size_t)chunk * N * 16;
@@ -298,6 +331,12 @@ __device__ __forceinline__ void cimg_put(const CentreImage& ci, int c, int j, fl
   const __half hi = __float2half_rn(vs);
   const __half lo = __float2half_rn(vs - __half2float(hi));
   const uint16_t hb = __half_as_ushort(hi), lb = __half_as_ushort(lo);
+  if (ci.stacked == kCimgBlocked) {
+    const size_t o = cimg_blocked_off(ci, c, j >> 4, j & 15);
+    ci.img[o] = hb;
+    ci.img[o + (size_t)ci.nbs * 16] = lb;
+    return;
+  }
   const int chunk = j >> 3, e = j & 7;
   const int N = ci.stacked ? 2 * ci.k_pad : ci.k_pad;
   const size_t base = (size_t)chunk * N * 16;

@@ -492,6 +492,22 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
 }
 
 
+// Operands of the tensor-core probes (estep_tc.cu, estep_wide.cu): x and c
+// values whose fp16 splits are exact (x = p + q 2^-12, c = r + s 2^-12 with
+// |p|, |r| in [8, 16), |q|, |s| <= 8), so that x_hi.c_hi + x_lo.c_hi +
+// x_hi.c_lo is exact in fp32 for 16 columns.
+__host__ __device__ inline float probe_x(int m, int j) {
+  const int p = 8 + ((m * 7 + j * 3) % 8);
+  const int q = ((m * 5 + j * 11) % 17) - 8;
+  return (float)(((m + j) & 1) ? -p : p) + (float)q * (1.0f / 4096.0f);
+}
+
+__host__ __device__ inline float probe_c(int c, int j) {
+  const int r = 8 + ((c * 3 + j * 5) % 8);
+  const int s = ((c * 13 + j * 7) % 17) - 8;
+  return (float)(((c + 2 * j) % 3 == 0) ? -r : r) + (float)s * (1.0f / 4096.0f);
+}
+
 // Launch parameters of a plan; the per-launch operands (image, scales, bias,
 // labels, changed, D, fit state, error word) are filled in by the caller.
 inline Params make_params(const TcPlan& plan) {

@@ -117,18 +117,6 @@ __global__ void split_x_kernel(const float* __restrict__ X, int ld, int nk, long
 // two-segment x.c, row-major 128 x 16; [4096] error code.
 constexpr int PROBE_K = 16, PROBE_NK = 2;
 
-__host__ __device__ inline float probe_x(int m, int j) {
-  const int p = 8 + ((m * 7 + j * 3) % 8);
-  const int q = ((m * 5 + j * 11) % 17) - 8;
-  return (float)(((m + j) & 1) ? -p : p) + (float)q * (1.0f / 4096.0f);
-}
-
-__host__ __device__ inline float probe_c(int c, int j) {
-  const int r = 8 + ((c * 3 + j * 5) % 8);
-  const int s = ((c * 13 + j * 7) % 17) - 8;
-  return (float)(((c + 2 * j) % 3 == 0) ? -r : r) + (float)s * (1.0f / 4096.0f);
-}
-
 __global__ void __launch_bounds__(128, 1) tc_probe_kernel(uint16_t* img_st, uint16_t* img_2s, uint32_t* out) {
   constexpr uint32_t TILE = PROBE_NK * CHUNK_BYTES;                 // 8 KB
   constexpr uint32_t IMG_ST = PROBE_NK * 2 * PROBE_K * 32;          // 2 KB
@@ -288,13 +276,14 @@ int tc_probe(int* mode_out, uint32_t* raw_out) {
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->supported = false;
   if (getenv("SKMETAL_DISABLE_TC")) return OK;
-  if (d > tc::MAX_NK * tc::KC || k > tc::MAX_KPAD || n < 1) return OK;
+  if (d > tc::MAX_NK * tc::KC || n < 1) return OK;
   if ((reinterpret_cast<uintptr_t>(X) & 15) || ((ld * 4) & 15)) return OK;
   int dev = 0, optin = 0, major = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   if (major != 10) return OK;
+  if (k > tc::MAX_KPAD) return tc_plan_wide(X, ld, n, d, k, optin, plan);
   int mode = -1;
   SKM_TRY(tc_probe(&mode, nullptr));
   if (mode < 0) return OK;  // unexpected tensor-core behaviour: use the SIMT E-step
@@ -359,11 +348,12 @@ int tc_split_x(TcPlan* plan, void* Xs, const int* sexp, cudaStream_t s) {
 }
 
 CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img) {
-  return CentreImage{img, plan.k_pad, plan.k_steps, plan.stacked};
+  return CentreImage{img, plan.k_pad, plan.k_steps, plan.stacked, plan.nbs};
 }
 
 int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,
              unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s, bool pdl) {
+  if (plan.wide) return tc_estep_wide(plan, img, sexp, bias, labels, changed, D, st, err, s, pdl);
   tc::Params p = tc::make_params(plan);
   p.img = img;
   p.sexp = sexp;

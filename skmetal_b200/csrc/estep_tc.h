@@ -32,6 +32,13 @@ struct TcPlan {
   uint32_t img_bytes = 0;
   int grid = 0;
   size_t smem = 0;
+  // k > 256 (estep_wide.cu): the clusters in nblk blocks of nbs, centre units
+  // of unit_bytes streamed through `ring` shared-memory stages
+  int wide = 0;
+  int nblk = 0;
+  int nbs = 0;
+  int ring = 0;
+  uint32_t unit_bytes = 0;
 };
 
 // Runs (once per device) a tiny kernel that pushes exactly representable
@@ -41,8 +48,15 @@ struct TcPlan {
 // probe reruns and returns its raw output.
 int tc_probe(int* mode, uint32_t* raw4096);
 
+// The same check for the k > 256 E-step's blocked centre image and MMA
+// sequence (estep_wide.cu).
+int tc_probe_wide(int* mode, uint32_t* raw4096);
+
 // X: the fit's blocked working copy (xblk_index), round_up(n, 128) rows.
+// k <= 256: the pipeline of estep_dev.cuh; 256 < k <= 4096: the blocked one
+// of estep_wide.cu (plan.wide); d <= 128 either way.
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan);
+int tc_plan_wide(const float* X, int ld, long long n, int d, int k, int optin, TcPlan* plan);
 
 // Bytes of the split working copy of X for this plan, and the launch that
 // builds it from the fp32 blocked copy with the scale 2^sexp[0] (device int);
@@ -66,5 +80,7 @@ CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img);
 int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,
              unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s,
              bool pdl = false);
+int tc_estep_wide(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,
+                  unsigned long long* changed, long long* D, const FitState* st, int* err, cudaStream_t s, bool pdl);
 
 }  // namespace skm

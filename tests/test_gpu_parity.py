@@ -18,7 +18,7 @@ from oracle import lloyd as ora
 from skmetal_b200 import _bridge
 from skmetal_b200._synthetic import gaussian_mixture, make_workload, scaled
 
-from parity import CENTER_RTOL, INERTIA_RTOL, check_counts, check_labels
+from parity import CENTER_RTOL, INERTIA_RTOL, check_counts, check_labels, lockstep, probe_c as _probe_c, probe_x as _probe_x
 
 pytestmark = pytest.mark.gpu
 
@@ -53,18 +53,6 @@ def test_compute_mindists_and_inertia_golden():
     np.testing.assert_allclose(dists, [0.0, 2.0, 0.0, 2.0], rtol=1e-6)
     assert _bridge.kmeans_inertia(X, C, lab, 4, 2, 2) == pytest.approx(4.0, rel=1e-6)
     np.testing.assert_allclose(_bridge.row_norm_sq(X), [0, 2, 200, 162], rtol=1e-6)
-
-
-def _probe_x(m, j):
-    p = 8 + (m * 7 + j * 3) % 8
-    q = (m * 5 + j * 11) % 17 - 8
-    return np.where((m + j) & 1, -p, p) + q / 4096.0
-
-
-def _probe_c(c, j):
-    r = 8 + (c * 3 + j * 5) % 8
-    s = (c * 13 + j * 7) % 17 - 8
-    return np.where((c + 2 * j) % 3 == 0, -r, r) + s / 4096.0
 
 
 def test_tensor_core_probe():
@@ -126,14 +114,16 @@ def _golden_case(name):
     return X, init, c, z
 
 
-@pytest.mark.parametrize("name", ["c1_small", "c2_small", "c3_small", "c4_small", "tol_rel", "relocation",
-                                  "odd_shape"])
+@pytest.mark.parametrize("name", ["c1_small", "c2_small", "c3_small", "c3_k1024", "c4_small", "k300_odd",
+                                  "tol_rel", "relocation", "odd_shape"])
 def test_fit_matches_reference_golden(name):
-    """Full fits against the reference's outputs on the same inputs."""
+    """Full fits against the reference's outputs on the same inputs (the
+    BASELINE recipes with near-ties by the relative-gap rule only)."""
     X, init, c, z = _golden_case(name)
     centers, labels, inertia, n_iter = _bridge.kmeans_fit(X, init, c["max_iter"], c["tol"])
     mean, Xc, _ = ora.center_data(X)
-    check_labels(Xc, centers - mean, labels, z[f"{name}/full/labels"], f"{name} labels")
+    check_labels(Xc, centers - mean, labels, z[f"{name}/full/labels"], f"{name} labels",
+                 strict=name.startswith(("c1", "c2", "c3", "c4")))
     scale = float(np.abs(X).max())
     np.testing.assert_allclose(centers, z[f"{name}/full/centers"], rtol=CENTER_RTOL, atol=1e-5 * scale)
     assert inertia == pytest.approx(float(z[f"{name}/full/inertia"]), rel=INERTIA_RTOL)
@@ -144,42 +134,15 @@ def test_fit_matches_reference_golden(name):
 # lockstep Lloyd steps
 # ---------------------------------------------------------------------------
 
-def _lockstep(X, init, iters):
-    mean, Xc, C = ora.center_data(X, init)
-    reports = []
-    for _ in range(iters):
-        step = ora.lloyd_iter(Xc, C, "fp32", relocation_order="sorted")
-        lab, cnew, weight, shift = _bridge.kmeans_lloyd_iter(Xc, C)
-        rep = check_labels(Xc, C, lab, step.labels, "lloyd step labels")
-        check_counts(weight, step.weight, lab, step.labels, C.shape[0])
-        # centres: exact float64 means of the GPU's own assignment (+ relocation)
-        ref, cnt = _fp64_centres(Xc, lab, C.shape[0], C)
-        same = np.ones(C.shape[0], bool)
-        mism = lab != step.labels
-        same[np.unique(np.concatenate([lab[mism], step.labels[mism]]))] = False
-        moved = np.zeros(C.shape[0], bool)
-        if step.far.size:
-            moved[step.empty] = True
-            moved[step.labels[step.far]] = True
-        keep = (cnt > 0) & ~moved
-        scale = float(np.abs(Xc).max())
-        np.testing.assert_allclose(cnew[keep], ref[keep], rtol=CENTER_RTOL, atol=1e-6 * scale)
-        # against the oracle's own centres where nothing differs
-        ok = keep & same
-        np.testing.assert_allclose(cnew[ok], step.centers_new[ok], rtol=CENTER_RTOL, atol=1e-6 * scale)
-        if not mism.any():
-            np.testing.assert_allclose(cnew, step.centers_new, rtol=CENTER_RTOL, atol=1e-6 * scale)
-            np.testing.assert_allclose(shift, step.center_shift, rtol=1e-3, atol=1e-5 * scale)
-        reports.append(rep)
-        C = step.centers_new
-    return reports
+def _lockstep(X, init, iters, strict=False):
+    return lockstep(X, init, iters, strict=strict)
 
 
 @pytest.mark.parametrize("name,n", [("c1", 20000), ("c2", 25000)])
 def test_lloyd_step_lockstep(name, n):
     w = scaled(name, n)
     X, init = make_workload(w)
-    reps = _lockstep(X, init, 8)
+    reps = _lockstep(X, init, 8, strict=True)  # BASELINE recipes: relative-gap near-ties only
     assert sum(r["mismatches"] for r in reps) <= 8 * max(1, n // 10000)
 
 
@@ -307,17 +270,40 @@ def test_batch_fused_reference_abi():
 @pytest.mark.parametrize("n,d,k", [(5, 3, 2), (130, 1, 1), (257, 9, 7), (1000, 33, 32), (64, 4, 64),
                                    (300, 129, 5), (2000, 16, 257)])
 def test_fit_odd_shapes(n, d, k):
+    """Every E-step variant by shape (tensor core k <= 256, blocked tensor
+    core k > 256, SIMT d > 128) against the oracle: lockstep steps, the final
+    labels as the assignment of the returned centres, and the end-to-end fit.
+    End to end the fit must equal the oracle's wherever the oracle's float32
+    and float64 runs reach the same clustering; where they do not (the k = 257
+    case is chaotic), it must reproduce one of those two runs."""
     rng = np.random.default_rng(n * 7 + d + k)
     X = (rng.standard_normal((n, d)) * 2 + 5).astype(np.float32)
     init = np.ascontiguousarray(X[rng.choice(n, k, replace=False)])
+    lockstep(X, init, 2)
     c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 20, 0.0)
     res = ora.kmeans_lloyd(X, init, 20, 0.0, relocation_order="sorted")
+    res64 = ora.kmeans_lloyd(X, init, 20, 0.0, mode="fp64", relocation_order="sorted")
     assert c.shape == (k, d) and lab.shape == (n,)
     assert lab.min() >= 0 and lab.max() < k
+    # the returned labels are the final E-step's assignment of the returned centres
+    mean, Xc, _ = ora.center_data(X)
+    want, _ = ora.assign(Xc, c - mean, "fp64")
+    check_labels(Xc, c - mean, lab, want, "final labels vs returned centres")
     # inertia is consistent with the returned labels and centres
-    ref_in = ora.inertia(X, c, lab)
-    assert inertia == pytest.approx(ref_in, rel=1e-5, abs=1e-6)
-    assert inertia <= res.inertia * (1 + 1e-3) + 1e-6 or np.mean(lab == res.labels) < 1.0
+    assert inertia == pytest.approx(ora.inertia(X, c, lab), rel=1e-5, abs=1e-6)
+    floor = float(np.mean(res64.labels == res.labels))
+    if floor == 1.0 and res64.n_iter == res.n_iter:
+        np.testing.assert_array_equal(lab, res.labels)
+        assert n_iter == res.n_iter
+        np.testing.assert_allclose(c, res.centers, rtol=CENTER_RTOL, atol=1e-5 * float(np.abs(X).max()))
+        assert inertia == pytest.approx(res.inertia, rel=INERTIA_RTOL)
+    else:
+        # chaotic: the oracle's float32 and float64 runs end in different
+        # clusterings; the fit must reproduce one of the two trajectories
+        ref = max((res, res64), key=lambda r: float(np.mean(lab == r.labels)))
+        assert np.mean(lab == ref.labels) >= 0.9999, (np.mean(lab == res.labels), np.mean(lab == res64.labels))
+        assert n_iter == ref.n_iter
+        assert inertia == pytest.approx(ref.inertia, rel=INERTIA_RTOL)
 
 
 def test_fit_all_rows_identical():

@@ -151,22 +151,6 @@ int check_launch(const char* what) {
   return OK;
 }
 
-// ---------------------------------------------------------------------------
-// host <-> device staging of row-major matrices into the padded layout
-// ---------------------------------------------------------------------------
-
-int upload_rows(float* dst, int ld, const float* src, long long n, int d, cudaStream_t s) {
-  if (n == 0) return OK;
-  if (ld == d) {
-    SKM_CUDA(cudaMemcpyAsync(dst, src, sizeof(float) * (size_t)n * d, cudaMemcpyDefault, s));
-  } else {
-    SKM_CUDA(cudaMemcpy2DAsync(dst, sizeof(float) * ld, src, sizeof(float) * d, sizeof(float) * d, n,
-                               cudaMemcpyDefault, s));
-    SKM_CUDA(cudaMemset2DAsync(dst + d, sizeof(float) * ld, 0, sizeof(float) * (ld - d), n, s));
-  }
-  return OK;
-}
-
 }  // namespace skm
 
 using namespace skm;

@@ -672,6 +672,7 @@ struct Staged {
   float* X = nullptr;
   float* C = nullptr;
   int32_t* labels = nullptr;
+  unsigned int* maxabs = nullptr;  // [0] max |x| bits of X, [1] of C (NaN above +inf)
   int ld = 0;
 };
 
@@ -680,12 +681,30 @@ static int stage_xc(DevBuffers& buf, const float* X, const float* C, long long n
   out->ld = ld_of(d);
   SKM_TRY(buf.alloc_n(&out->X, (size_t)n * out->ld));
   SKM_TRY(buf.alloc_n(&out->C, (size_t)k * out->ld));
+  SKM_TRY(buf.alloc_n(&out->maxabs, 2));
   SKM_TRY(upload_rows(out->X, out->ld, X, n, d, s));
   SKM_TRY(upload_rows(out->C, out->ld, C, k, d, s));
+  // non-finite inputs are detected on the device (callers need not scan X on the host)
+  SKM_CUDA(cudaMemsetAsync(out->maxabs, 0, 2 * sizeof(unsigned int), s));
+  maxabs_kernel<<<blocks_for(n * out->ld / 4, 256, 8), 256, 0, s>>>(out->X, out->ld, n, d, out->maxabs);
+  SKM_TRY(check_launch("maxabs_kernel"));
+  maxabs_kernel<<<1, 256, 0, s>>>(out->C, out->ld, k, d, out->maxabs + 1);
+  SKM_TRY(check_launch("maxabs_kernel"));
   if (want_labels || labels_in) {
     SKM_TRY(buf.alloc_n(&out->labels, (size_t)n));
     if (labels_in)
       SKM_CUDA(cudaMemcpyAsync(out->labels, labels_in, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s));
+  }
+  return OK;
+}
+
+// After the stream has been synchronised: ERR_INVALID when X or C held NaN
+// or infinity (their max |x| words, copied back into mx).
+static int check_finite(const unsigned int* mx, const char* what) {
+  if ((mx[0] & 0x7fffffffu) >= 0x7f800000u || (mx[1] & 0x7fffffffu) >= 0x7f800000u) {
+    set_error(ERR_INVALID, "%s: %s contains NaN or infinity", what,
+              (mx[0] & 0x7fffffffu) >= 0x7f800000u ? "X" : "the centres");
+    return ERR_INVALID;
   }
   return OK;
 }
@@ -705,9 +724,11 @@ int skmetal_kmeans_assign(const float* X, const float* centroids, uint32_t* labe
   Staged g;
   SKM_TRY(stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, true, nullptr, &g, s));
   SKM_TRY(launch_assign_any(g.X, g.ld, (long long)n, (int)d, g.C, (int)k, g.labels, nullptr, s));
+  unsigned int mx[2];
+  SKM_CUDA(cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaMemcpyAsync(labels, g.labels, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaStreamSynchronize(s));
-  return OK;
+  return check_finite(mx, "kmeans_assign");
 }
 
 int skmetal_compute_mindists(const float* X, const float* centroids, const uint32_t* labels, float* dists, size_t n,
@@ -723,9 +744,11 @@ int skmetal_compute_mindists(const float* X, const float* centroids, const uint3
   SKM_TRY(buf.alloc_n(&out, n));
   mindist_kernel<<<blocks_for((long long)n, 256), 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, out);
   SKM_TRY(check_launch("mindist_kernel"));
+  unsigned int mx[2];
+  SKM_CUDA(cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaMemcpyAsync(dists, out, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaStreamSynchronize(s));
-  return OK;
+  return check_finite(mx, "compute_mindists");
 }
 
 float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint32_t* labels, size_t n, size_t d,
@@ -745,11 +768,14 @@ float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint3
   ordered_sum_kernel<<<1, 32, 0, s>>>(part, n_part, part + n_part);
   if (check_launch("ordered_sum_kernel")) return -1.0f;
   double v = 0;
+  unsigned int mx[2];
+  if (cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
   if (cudaMemcpyAsync(&v, part + n_part, sizeof(double), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
   if (cudaStreamSynchronize(s) != cudaSuccess) {
     set_error(ERR_CUDA, "kmeans_inertia: %s", cudaGetErrorString(cudaGetLastError()));
     return -1.0f;
   }
+  if (check_finite(mx, "kmeans_inertia")) return -1.0f;
   return (float)v;
 }
 
@@ -789,9 +815,11 @@ int skmetal_kmeans_transform(const float* X, const float* centroids, float* D, s
   transform_kernel<<<blocks_for((long long)n * k, 256), 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, (int)k,
                                                                    out);
   SKM_TRY(check_launch("transform_kernel"));
+  unsigned int mx[2];
+  SKM_CUDA(cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaMemcpyAsync(D, out, sizeof(float) * n * k, cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaStreamSynchronize(s));
-  return OK;
+  return check_finite(mx, "kmeans_transform");
 }
 
 int skmetal_kmeans_batch_fused(const float* X, float* centroids, uint32_t* labels, size_t n, size_t d, size_t k,

@@ -20,7 +20,9 @@ class BaseGPUEstimator(BaseEstimator):
         self._fitted = False
 
     def _validate_data(self, X, y=None):
-        X = check_array(X, dtype=np.float32, order="C", ensure_min_samples=2)
+        # NaN / infinity are detected by the library on the device (a fit, an
+        # assignment or a transform raises), so X is not scanned on the host
+        X = check_array(X, dtype=np.float32, order="C", ensure_min_samples=2, ensure_all_finite=False)
         if y is not None:
             y = check_array(y, dtype=np.float32, order="C", ensure_2d=False)
         return X, y

@@ -36,6 +36,17 @@ except Exception:  # noqa: BLE001
     _is_same_clustering = None
 
 
+def _gpu_call(fn, *args, **kwargs):
+    """A library call; its report of NaN or infinity in the input becomes
+    scikit-learn's ValueError."""
+    try:
+        return fn(*args, **kwargs)
+    except RuntimeError as e:
+        if "NaN or infinity" in str(e):
+            raise ValueError(f"Input X contains NaN or infinity ({e}).") from None
+        raise
+
+
 def _same_clustering(a: np.ndarray, b: np.ndarray, k: int) -> bool:
     if _is_same_clustering is not None:
         return bool(_is_same_clustering(a.astype(np.int32), b.astype(np.int32), k))
@@ -116,14 +127,15 @@ class MetalKMeans(BaseGPUEstimator):
                 centers_init = est._init_centroids(Xc, x_squared_norms=x_sq, init=init,
                                                    random_state=random_state, sample_weight=ones)
                 centers_init = np.ascontiguousarray((centers_init + mean).astype(np.float32))
-            centers, labels, inertia, n_iter = _bridge.kmeans_fit(
-                X, centers_init, int(est.max_iter), float(est.tol), center=True)
+            centers, labels, inertia, n_iter = _gpu_call(
+                _bridge.kmeans_fit, X, centers_init, int(est.max_iter), float(est.tol), center=True)
             if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
                 best = (centers, labels, inertia, n_iter)
         centers, labels, inertia, n_iter = best
 
-        if len(np.unique(labels)) < k:
-            warnings.warn(f"Number of distinct clusters ({len(np.unique(labels))}) found smaller than "
+        distinct = int(np.count_nonzero(np.bincount(labels, minlength=k)))
+        if distinct < k:
+            warnings.warn(f"Number of distinct clusters ({distinct}) found smaller than "
                           f"n_clusters ({k}). Possibly due to duplicate points in X.", ConvergenceWarning,
                           stacklevel=2)
         est.cluster_centers_ = centers
@@ -150,7 +162,8 @@ class MetalKMeans(BaseGPUEstimator):
         return np.ascontiguousarray(self._estimator.cluster_centers_, dtype=np.float32)
 
     def _check_test(self, X):
-        X = check_array(X, dtype=np.float32, order="C")
+        # non-finite values are detected on the device (the library raises)
+        X = check_array(X, dtype=np.float32, order="C", ensure_all_finite=False)
         if X.shape[1] != self._estimator.n_features_in_:
             raise ValueError(f"X has {X.shape[1]} features, but KMeans is expecting "
                              f"{self._estimator.n_features_in_} features as input.")
@@ -161,13 +174,13 @@ class MetalKMeans(BaseGPUEstimator):
         C = self._centers()
         X = self._check_test(X)
         labels = np.empty(X.shape[0], dtype=np.int32)
-        _bridge.kmeans_assign(X, C, labels, X.shape[0], X.shape[1], C.shape[0])
+        _gpu_call(_bridge.kmeans_assign, X, C, labels, X.shape[0], X.shape[1], C.shape[0])
         return labels
 
     def transform(self, X):
         C = self._centers()
         X = self._check_test(X)
-        return _bridge.kmeans_transform(X, C)
+        return _gpu_call(_bridge.kmeans_transform, X, C)
 
     def fit_predict(self, X, y=None, sample_weight=None):
         return self.fit(X, sample_weight=sample_weight)._estimator.labels_
@@ -180,4 +193,4 @@ class MetalKMeans(BaseGPUEstimator):
         X = self._check_test(X)
         self._check_weights(sample_weight, X.shape[0])
         labels = self.predict(X)
-        return -_bridge.kmeans_inertia(X, C, labels, X.shape[0], X.shape[1], C.shape[0])
+        return -_gpu_call(_bridge.kmeans_inertia, X, C, labels, X.shape[0], X.shape[1], C.shape[0])

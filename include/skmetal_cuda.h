@@ -218,12 +218,14 @@ int skmetal_dataset_fit_shard(void* handle, const float* init, size_t k, int32_t
  * return 1 (invalid argument) with a message; so do labels outside [0, k) and
  * non-finite X, which leave centers and weight untouched.
  *
- * The first call on each device looks up the scratch's device address
- * (cudaGetSymbolAddress, with that device current), which can load the
- * library's device code there; make that first call before any stream capture
- * begins. All callers on a device share the one scratch array: calls on the
- * same device that overlap in time (from several threads, or on several
- * streams) race on it and corrupt each other's results, so serialise them. */
+ * Every call looks up the scratch's device address (cudaGetSymbolAddress, with
+ * the current device), so it stays valid across a cudaDeviceReset; the first
+ * call on a device also loads the library's device code there, so make that
+ * first call before any stream capture begins. Each call synchronises `stream`
+ * before it returns. All callers on a device share the one scratch array:
+ * calls on the same device that overlap in time (from several threads, or on
+ * several streams) race on it and corrupt each other's results, so serialise
+ * them. */
 int skmetal_kmeans_update_centers_noalloc(const float* X, const int32_t* labels, size_t n, size_t d, size_t k,
                                           float* centers, float* weight, void* stream);
 

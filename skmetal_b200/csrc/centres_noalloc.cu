@@ -15,15 +15,15 @@
 // Its scratch (max |x| bits, a bad-label counter, per-cluster row counts and
 // fixed-point column sums) lives in one static device array of
 // SKMETAL_NOALLOC_SCRATCH_BYTES, which every device that loads this library
-// holds until the process exits. The first call on a device looks up that
-// array's device address with cudaGetSymbolAddress, which can load this
-// library's device code onto the device. There is one array per device, shared
-// by every caller, so calls on the same device that overlap in time race on it.
+// holds until the process exits. Every call looks up that array's device
+// address with cudaGetSymbolAddress (the first call on a device can load this
+// library's device code there) and waits for its work on the caller's stream
+// before it returns. There is one array per device, shared by every caller,
+// so calls on the same device that overlap in time race on it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdint>
-#include <mutex>
 
 #include "device_util.cuh"
 #include "driver.h"
@@ -40,9 +40,6 @@ namespace {
 
 constexpr size_t kScratchWords = kNoallocScratchWords;
 constexpr int kMaxDevices = 64;
-
-std::mutex g_setup_mutex;
-long long* g_scratch_ptr[kMaxDevices] = {};
 
 // Same formula as the fit's fixed-point scale: 2^F with F = 62 - E - L, where
 // max |x| < 2^E and n <= 2^L, so no sum of up to n values can reach 2^62.
@@ -115,22 +112,22 @@ __global__ void noalloc_centres_kernel(const long long* __restrict__ S, const lo
       weight[c] = (float)counts[c];
 }
 
-// Device address of the static scratch on the current device `dev`, looked up
-// once per device (with that device current) and remembered.
+// Device address of the static scratch on the current device `dev`. Looked
+// up on every call (with that device current): the lookup allocates nothing,
+// costs little once the library's device code is loaded, and stays right
+// after a cudaDeviceReset, which gives the scratch a new address in the new
+// context. The first lookup on a device can load the library's device code
+// there.
 int scratch_for_device(int dev, long long** out) {
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
-    long long* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || ptr == nullptr) {
-      cudaGetLastError();
-      set_error(ERR_CUDA, "kmeans_update_centers_noalloc: cudaGetSymbolAddress of the static scratch failed on device %d: %s",
-                dev, cudaGetErrorString(e));
-      return ERR_CUDA;
-    }
-    g_scratch_ptr[dev] = ptr;
+  long long* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || ptr == nullptr) {
+    cudaGetLastError();
+    set_error(ERR_CUDA, "kmeans_update_centers_noalloc: cudaGetSymbolAddress of the static scratch failed on device %d: %s",
+              dev, cudaGetErrorString(e));
+    return ERR_CUDA;
   }
-  *out = g_scratch_ptr[dev];
+  *out = ptr;
   return OK;
 }
 

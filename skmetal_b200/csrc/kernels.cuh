@@ -131,6 +131,13 @@ __global__ void counts_to_float_kernel(const long long* c, int k, float* out);
 bool launch_assign_small(int d, int blocks, int threads, size_t smem, cudaStream_t s, const float* X, int ld,
                          long long n, const float* C, int k, int32_t* labels, float* mind);
 
+// Small-d, small-k assignment with the centres in the kernel's parameter
+// block (predict.cu): d in {4, 8, 16}, k <= 32 (16 for d = 16), ld == d.
+// C_host: the k x d centres on the host; C_dev: the same on the device (k x
+// ldc). *used = false when the shape has no specialisation (nothing launched).
+int launch_assign_const(const float* X, int ld, long long n, int d, const float* C_host, const float* C_dev, int ldc,
+                        int k, int32_t* labels, cudaStream_t s, bool* used);
+
 __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a);
 // Multi-GPU, before the all-reduce (cooperative): bulk pass, the rank's
 // local counts and its relocation-candidate slot (see kernels.cu).

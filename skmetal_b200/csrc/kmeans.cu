@@ -248,6 +248,13 @@ static int run_fit(const FitParams& p) {
   // fit's kernels ended before its last collective).
   const char* loop_env = getenv("SKMETAL_LOOP");
   const bool launches_loop = loop_env && strcmp(loop_env, "launches") == 0;
+  // SKMETAL_PEER_WAIT_MS: limit of the persistent loop's waits on other ranks
+  // (default 5 s); SKMETAL_DEBUG_ORPHAN_PEER=1 (tests only): a one-GPU fit
+  // runs its loop as rank 0 of two ranks of which the second never starts
+  const char* wait_env = getenv("SKMETAL_PEER_WAIT_MS");
+  const unsigned long long peer_wait_ns = wait_env ? (unsigned long long)(atof(wait_env) * 1e6) : 0ull;
+  const char* orphan_env = getenv("SKMETAL_DEBUG_ORPHAN_PEER");
+  const bool orphan_peer = !comm && orphan_env && atoi(orphan_env) == 1;
   void* const* regions = nullptr;
   if (comm && !p.single_step && !launches_loop) {
     SKM_TRY(comm_peer_region(comm, s, &regions));
@@ -469,7 +476,22 @@ static int run_fit(const FitParams& p) {
       for (int r = 0; r < li.nranks; ++r) li.region[r] = static_cast<unsigned char*>(regions[r]);
       SKM_TRY(buf.alloc_n(&li.G, d_len));
       SKM_TRY(buf.alloc(reinterpret_cast<void**>(&li.cand_all), cand_block_bytes(kCandCap, ld) * li.nranks));
+    } else if (orphan_peer) {
+      // failure-path test: the loop runs as rank 0 of two whose rank 1 never
+      // starts. Both regions are local, zeroed, and only this kernel touches
+      // them: its pushes land in region 1, and its polls for rank 1's pushes
+      // into region 0 run out after the peer-wait limit (error 1005)
+      li.nranks = 2;
+      li.rank = 0;
+      const size_t rb = region_bytes(2, k, ld);
+      for (int r = 0; r < 2; ++r) {
+        SKM_TRY(buf.alloc(reinterpret_cast<void**>(&li.region[r]), rb));
+        SKM_CUDA(cudaMemsetAsync(li.region[r], 0, rb, s));
+      }
+      SKM_TRY(buf.alloc_n(&li.G, d_len));
+      SKM_TRY(buf.alloc(reinterpret_cast<void**>(&li.cand_all), cand_block_bytes(kCandCap, ld) * 2));
     }
+    li.peer_wait_ns = peer_wait_ns;
     SKM_TRY(buf.alloc_n(&li.part, 3 * (size_t)k));
     SKM_TRY(buf.alloc_n(&li.bar, 1));
     SKM_CUDA(cudaMemsetAsync(li.bar, 0, sizeof(unsigned int), s));
@@ -723,7 +745,9 @@ int skmetal_kmeans_assign(const float* X, const float* centroids, uint32_t* labe
   DevBuffers buf(s);
   Staged g;
   SKM_TRY(stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, true, nullptr, &g, s));
-  SKM_TRY(launch_assign_any(g.X, g.ld, (long long)n, (int)d, g.C, (int)k, g.labels, nullptr, s));
+  bool done = false;
+  SKM_TRY(launch_assign_const(g.X, g.ld, (long long)n, (int)d, centroids, g.C, g.ld, (int)k, g.labels, s, &done));
+  if (!done) SKM_TRY(launch_assign_any(g.X, g.ld, (long long)n, (int)d, g.C, (int)k, g.labels, nullptr, s));
   unsigned int mx[2];
   SKM_CUDA(cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaMemcpyAsync(labels, g.labels, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, s));
@@ -1019,7 +1043,9 @@ int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t 
   SKM_TRY(buf.alloc_n(&lab, (size_t)ds->n));
   SKM_TRY(upload_rows(C, ds->ld, centroids, (long long)k, ds->d, s));
   SKM_CUDA(cudaEventRecord(e0, s));
-  SKM_TRY(launch_assign_any(ds->X, ds->ld, ds->n, ds->d, C, (int)k, lab, nullptr, s));
+  bool done = false;
+  SKM_TRY(launch_assign_const(ds->X, ds->ld, ds->n, ds->d, centroids, C, ds->ld, (int)k, lab, s, &done));
+  if (!done) SKM_TRY(launch_assign_any(ds->X, ds->ld, ds->n, ds->d, C, (int)k, lab, nullptr, s));
   SKM_CUDA(cudaEventRecord(e1, s));
   if (labels_out) SKM_CUDA(cudaMemcpyAsync(labels_out, lab, sizeof(int32_t) * ds->n, cudaMemcpyDeviceToHost, s));
   SKM_CUDA(cudaStreamSynchronize(s));

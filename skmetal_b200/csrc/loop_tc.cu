@@ -75,6 +75,7 @@ struct LoopArgs {
   long long* G;
   unsigned char* cand_all;
   size_t cand_block;
+  unsigned long long peer_wait_ns;  // limit of every wait on another rank (inbox polls, rank barrier)
 };
 
 // Grid barrier of the loop: every CTA adds 1 to a counter that only grows
@@ -116,8 +117,8 @@ __device__ __forceinline__ bool loop_barrier(FitState* st, unsigned int* counter
 // rank that sees the word); thread 0 of every CTA then polls its own
 // region's words with system-scope acquires until every rank's word reaches
 // `epoch`. Epochs count the fit's cross-rank barriers from 1 (the words are
-// zeroed before the fit's first collective). Bounded: after 5 s the CTA
-// records error 1005 and returns false.
+// zeroed before the fit's first collective). Bounded: after la.peer_wait_ns
+// (5 s by default) the CTA records error 1005 and returns false.
 __device__ __forceinline__ bool rank_barrier(const LoopArgs& la, FitState* st, unsigned int epoch) {
   __shared__ int ok_s;
   block_sync();
@@ -133,7 +134,7 @@ __device__ __forceinline__ bool rank_barrier(const LoopArgs& la, FitState* st, u
         unsigned int v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(la.pflag[la.rank] + r) : "memory");
         if (v >= epoch) break;
-        if ((i & 255) == 0 && globaltimer() - t0 > 5000000000ull) {
+        if ((i & 255) == 0 && globaltimer() - t0 > la.peer_wait_ns) {
           atomicExch(&st->error, 1005);
           ok = 0;
           break;
@@ -183,7 +184,7 @@ __device__ __forceinline__ long long ll_get(const unsigned long long* row, int j
 // change count into every peer's inbox row (8-byte stores over NVLink),
 // then reads every peer's row of c (all peers' loads in flight together) and
 // re-polls the words that did not carry this iteration's epoch yet (each lane
-// its own; bounded: 5 s, then error 1005), and returns
+// its own; bounded: la.peer_wait_ns, then error 1005), and returns
 // c's sums over every rank (S_in added unless bulk; as quad_load) and c's
 // count delta over every rank.
 __device__ __forceinline__ QuadSums owner_exchange(const LoopArgs& la, FitState* st, const long long* S_in,
@@ -276,7 +277,7 @@ __device__ __forceinline__ QuadSums owner_exchange(const LoopArgs& la, FitState*
       }
     }
     if ((it & 63) == 0) {  // the same iterations on every lane; lane 0's clock decides
-      const bool late = __shfl_sync(0xffffffffu, globaltimer() - t0 > 5000000000ull, 0);
+      const bool late = __shfl_sync(0xffffffffu, globaltimer() - t0 > la.peer_wait_ns, 0);
       if (late) {
         if (lane == 0) atomicExch(&st->error, 1005);
         break;
@@ -639,6 +640,7 @@ int tc_lloyd_loop(const TcPlan& plan, const LoopInputs& in, cudaStream_t s) {
   la.d_clear = ((size_t)plan.k * plan.ld + plan.k + 2) & ~(size_t)1;
   la.W = in.nranks;
   la.rank = in.rank;
+  la.peer_wait_ns = in.peer_wait_ns ? in.peer_wait_ns : 5000000000ull;
   if (la.W > 1) {
     if (la.W > kLoopMaxRanks || in.rank < 0 || in.rank >= la.W || !in.G || !in.cand_all) {
       set_error(ERR_INVALID, "multi-GPU loop: bad rank layout");

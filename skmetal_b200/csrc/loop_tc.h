@@ -50,6 +50,9 @@ struct LoopInputs {
   unsigned char* region[kLoopMaxRanks] = {};
   long long* G = nullptr;
   unsigned char* cand_all = nullptr;
+  // limit of every wait on another rank, in ns (0: 5 s); a rank that stops
+  // leaves its peers to run out of it and report error 1005
+  unsigned long long peer_wait_ns = 0;
 };
 
 // True when the plan's shared memory leaves room for the loop kernel's own.

@@ -427,3 +427,71 @@ def test_injected_failure_raises():
     # the next call works again
     c, lab, inertia, n_iter = _bridge.kmeans_fit(X, X[:2].copy(), 5, 0.0)
     assert c.shape == (2, 3)
+
+
+# ---------------------------------------------------------------------------
+# predict: the small-d kernel with the centres in its parameter block
+# ---------------------------------------------------------------------------
+
+def test_predict_c5_recipe():
+    """The C5 recipe (U[0,1)^8, 16 fixed centres) at 4M rows through the
+    reference's assign entry point: labels against the float64 argmin,
+    near-ties by the relative-gap rule only; a resident dataset's predict
+    gives the same labels."""
+    X, C = make_workload(scaled("c5", 4_000_000))
+    lab = np.empty(X.shape[0], dtype=np.int32)
+    _bridge.kmeans_assign(X, C, lab, X.shape[0], X.shape[1], C.shape[0])
+    want, _ = ora.assign(X, C, "fp64")
+    check_labels(X, C, lab, want, "predict c5", strict=True)
+    ds = _bridge.Dataset(X)
+    p = np.empty_like(lab)
+    ds.predict(C, p)
+    np.testing.assert_array_equal(p, lab)
+    ds.close()
+
+
+@pytest.mark.parametrize("d,k", [(8, 16), (8, 27), (4, 9), (16, 16)])
+def test_predict_exact_ties_take_lowest_index(d, k):
+    """Rows exactly halfway between two centres (dyadic values: every sum,
+    difference and square is exact) tie in any arithmetic; the kernel must
+    see that its expansion cannot decide them and fall back to direct
+    differences with strict '<', i.e. the lower index (np.argmin's rule)."""
+    rng = np.random.default_rng(d * 100 + k)
+    C = (rng.integers(0, 64, (k, d)) / 64.0).astype(np.float32)
+    pairs = [(a, b) for a in range(k) for b in range(a + 1, k)]
+    X = np.concatenate([(C[[a for a, _ in pairs]] + C[[b for _, b in pairs]]) / 2,
+                        (rng.integers(0, 64, (5000, d)) / 64.0)]).astype(np.float32)
+    lab = np.empty(X.shape[0], dtype=np.int32)
+    _bridge.kmeans_assign(X, C, lab, X.shape[0], d, k)
+    D = ((X[:, None, :].astype(np.float64) - C[None].astype(np.float64)) ** 2).sum(-1)
+    np.testing.assert_array_equal(lab, np.argmin(D, axis=1))
+
+
+# ---------------------------------------------------------------------------
+# full-size BASELINE workloads, one step each
+# ---------------------------------------------------------------------------
+
+def test_lloyd_step_full_size_c2():
+    """The metric workload itself (C2: 500k x 100, k = 50): one Lloyd step
+    from its explicit init in lockstep with the oracle."""
+    X, init = make_workload("c2")
+    reps = lockstep(X, init, 1, strict=True)
+    assert reps[0]["agreement"] >= 0.9999
+
+
+def test_estep_full_size_c3():
+    """C3 at full size (2M x 128, k = 1024, the k > 256 tensor-core E-step):
+    one step's labels against the oracle's float32 E-step, counts exact."""
+    X, init = make_workload("c3")
+    lab, cnew, weight, shift = _bridge.kmeans_lloyd_iter(X, init)
+    want, _ = ora.assign(X, init, "fp32")
+    check_labels(X, init, lab, want, "C3 full-size E-step", strict=True)
+    np.testing.assert_array_equal(weight.astype(np.int64), np.bincount(lab, minlength=init.shape[0]))
+
+
+def test_lloyd_step_c4_5m_rows():
+    """The C4 recipe (Dirichlet-sized mixture, k = 256) at 5M rows: one Lloyd
+    step in lockstep with the oracle."""
+    X, init = make_workload(scaled("c4", 5_000_000))
+    reps = lockstep(X, init, 1, strict=True)
+    assert reps[0]["agreement"] >= 0.9999

@@ -413,7 +413,20 @@ def main():
         est_n += st["estep_launches"]
     wall = time.perf_counter() - t0
     launches = _bridge.launch_count() - l0
-    persistent = fit and len(_bridge.debug_loop_stamps()) > 0  # the profiled fits ran the loop kernel
+    stamps = _bridge.debug_loop_stamps() if fit else []
+    persistent = len(stamps) > 0  # the profiled fits ran the loop kernel
+    phases = None
+    if persistent:
+        # device timestamps of the last fit: per iteration [start, E-step done,
+        # owners done, M-step done]; bulk / relocation iterations show a long M-step
+        T = (len(stamps) - 1) // 4
+        st4 = np.asarray(stamps[:4 * T], dtype=np.float64).reshape(T, 4) / 1e3  # us
+        e_us = st4[:, 1] - st4[:, 0]
+        m_us = np.concatenate([st4[1:, 0] - st4[:-1, 1], [stamps[4 * T] / 1e3 - st4[-1, 1]]])
+        phases = {"iterations": int(T), "estep_us_median": float(np.median(e_us)), "estep_us_sum": float(e_us.sum()),
+                  "mstep_us_median": float(np.median(m_us)), "mstep_us_sum": float(m_us.sum()),
+                  "mstep_over_2x_median": int((m_us > 2 * np.median(m_us)).sum()),
+                  "timing": "globaltimer stamps of the loop kernel (last timed fit)"}
     barrier()
     clk = clocks.stop()
     t_dev = ms_total / 1e3
@@ -531,6 +544,7 @@ def main():
         "e2e_pinned": {"value": e2e_pinned, "unit": unit, "host_memory": "page-locked"},
         "gpu_launches": int(launches),
         "roofline": roofline,
+        "phases": phases,
         "clocks": clk,
         "wall_s": wall,
     }

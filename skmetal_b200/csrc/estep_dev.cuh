@@ -114,6 +114,32 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, SmemDesc a, SmemDesc b,
       : "memory");
 }
 
+// The same MMA issued by one elected lane of a converged warp. The whole warp
+// runs the issuing loop with warp-uniform operands (descriptors, addresses,
+// predicates), so they stay uniform values; elect.sync picks the one lane
+// that issues, as tcgen05.mma is issued by a single thread.
+__device__ __forceinline__ void mma_f16_elect(uint32_t tmem_d, SmemDesc a, SmemDesc b, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 ad, bd;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}"
+      ::"r"(tmem_d), "r"(a.lo), "r"(a.hi), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// tcgen05.commit by one elected lane of a converged warp.
+__device__ __forceinline__ void tc_commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -441,24 +467,35 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
       // four independent running minima (columns j = 4m + u), merged in index order
       float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
       int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
-      for (int jb = 0; jb < p.k_pad; jb += 16) {
-        uint32_t v[16], w[16];
+      // two 16-column loads per wait (wait::ld waits for every load of the
+      // thread, so loads are batched): 32 columns, or 16 stacked (with their
+      // c_lo half); more would spill in the 640-thread loop kernel
+      const int step = p.stacked ? 16 : 32;
+      for (int jb = 0; jb < p.k_pad; jb += step) {
+        uint32_t v[2][16];
+        const bool two = !p.stacked && jb + 16 < p.k_pad;  // warp-uniform
         // tcgen05.ld / wait::ld are .sync.aligned: the running minima below
-        // branch per lane, so the warp reconverges before each load
+        // branch per lane, so the warp reconverges before the loads
         __syncwarp();
-        tmem_ld16(taddr + (uint32_t)jb, v);
-        if (p.stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + jb), w);
-        tmem_ld_wait16(v);
-        if (p.stacked) reg_pin16(w);
+        tmem_ld16(taddr + (uint32_t)jb, v[0]);
+        if (p.stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + jb), v[1]);
+        else if (two) tmem_ld16(taddr + (uint32_t)(jb + 16), v[1]);
+        tmem_ld_wait16(v[0]);
+        reg_pin16(v[1]);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = jb + jj;
-          float dot = __uint_as_float(v[jj]);
-          if (p.stacked) dot += __uint_as_float(w[jj]);
-          const float dist = fmaf(dot, negscale, c.bias_s[j]);
-          if (dist < bd[jj & 3]) {
-            bd[jj & 3] = dist;
-            bi[jj & 3] = j;
+        for (int t = 0; t < 2; ++t) {
+          if (t == 1 && !two) break;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = jb + 16 * t + jj;
+            // stacked: v[0] holds acc[j], v[1] acc[k_pad + j]
+            const float dot = p.stacked ? __uint_as_float(v[0][jj]) + __uint_as_float(v[1][jj])
+                                        : __uint_as_float(v[t][jj]);
+            const float dist = fmaf(dot, negscale, c.bias_s[j]);
+            if (dist < bd[jj & 3]) {
+              bd[jj & 3] = dist;
+              bi[jj & 3] = j;
+            }
           }
         }
       }

@@ -29,8 +29,10 @@
 // The n x k distance matrix never leaves the SM, and X is read from HBM once
 // per launch.
 //
-// Warp roles (384 threads): 0 X producer, 1 TMEM owner and MMA issuer, 2
-// centre-unit producer, 3 idle, 4-7 epilogue group 0, 8-11 epilogue group 1.
+// Warp roles (384 threads): 0 X producer, 1 TMEM owner and MMA issuer (the
+// whole warp runs the issuing loop on warp-uniform values, one elected lane
+// issues each MMA), 2 centre-unit producer, 3 idle, 4-7 epilogue group 0,
+// 8-11 epilogue group 1.
 //
 // Every wait is bounded (2 s); on a timeout the CTA records an error code,
 // sets its abort flag (every role then stops issuing work), each producer
@@ -233,54 +235,54 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
     }
   } else if (warp == MMA_W) {
     // ------------------------------------------------------------- MMAs
-    if (lane == 0) {
-      const uint32_t idesc = tc::idesc_f16(p.nbs);
-      long long v = 0;
-      bool ok = true;
-      for (int i = 0; ok && i < my_tiles; ++i) {
-        const int s = i % p.xst;
-        if (!tc::mbar_wait(bar(XF(s)), (uint32_t)(i / p.xst) & 1u, abort_flag, p.err, 2603)) break;
+    // the whole warp runs this loop (every value in it is warp-uniform); one
+    // elected lane issues each MMA and commit
+    const uint32_t idesc = tc::idesc_f16(p.nbs);
+    long long v = 0;
+    bool ok = true;
+    for (int i = 0; ok && i < my_tiles; ++i) {
+      const int s = i % p.xst;
+      if (!warp_wait(bar(XF(s)), (uint32_t)(i / p.xst) & 1u, abort_flag, p.err, 2603)) break;
+      tc::tc_fence_after();
+      const uint32_t stage = sbase + (uint32_t)s * p.stage_bytes;
+      // A: x_hi of the pair's two chunks (K halves 4096 bytes apart), x_lo 2048 bytes further
+      const tc::SmemDesc ahi0 = tc::kmajor_desc(stage, (uint32_t)CHUNK_BYTES, 128u);
+      const tc::SmemDesc alo0 = tc::kmajor_desc(stage + 2048u, (uint32_t)CHUNK_BYTES, 128u);
+      for (int b = 0; ok && b < p.nblk; ++b) {
+        const int u = i * p.nblk + b, a = u & 1;
+        if (!warp_wait(bar(AE(a)), (uint32_t)((u >> 1) & 1) ^ 1u, abort_flag, p.err, 2604)) {
+          ok = false;
+          break;
+        }
         tc::tc_fence_after();
-        const uint32_t stage = sbase + (uint32_t)s * p.stage_bytes;
-        // A: x_hi of the pair's two chunks (K halves 4096 bytes apart), x_lo 2048 bytes further
-        const tc::SmemDesc ahi0 = tc::kmajor_desc(stage, (uint32_t)CHUNK_BYTES, 128u);
-        const tc::SmemDesc alo0 = tc::kmajor_desc(stage + 2048u, (uint32_t)CHUNK_BYTES, 128u);
-        for (int b = 0; ok && b < p.nblk; ++b) {
-          const int u = i * p.nblk + b, a = u & 1;
-          if (!tc::mbar_wait(bar(AE(a)), (uint32_t)((u >> 1) & 1) ^ 1u, abort_flag, p.err, 2604)) {
+        const uint32_t tacc = tmem_base + (uint32_t)(a * p.nbs);
+        for (int m = 0; m < p.npairs; ++m, ++v) {
+          const int r = (int)(v % p.ring);
+          if (!warp_wait(bar(CF(r)), (uint32_t)((v / p.ring) & 1), abort_flag, p.err, 2605)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t tacc = tmem_base + (uint32_t)(a * p.nbs);
-          for (int m = 0; m < p.npairs; ++m, ++v) {
-            const int r = (int)(v % p.ring);
-            if (!tc::mbar_wait(bar(CF(r)), (uint32_t)((v / p.ring) & 1), abort_flag, p.err, 2605)) {
-              ok = false;
-              break;
-            }
-            tc::tc_fence_after();
-            const uint32_t unit = sbase + L.ring + (uint32_t)r * p.unit_bytes;
-            const tc::SmemDesc bhi = tc::kmajor_desc(unit, (uint32_t)(p.nbs * 16), 128u);
-            const tc::SmemDesc blo = tc::kmajor_desc(unit + (uint32_t)(p.nbs * 32), (uint32_t)(p.nbs * 16), 128u);
-            const tc::SmemDesc ahi = tc::desc_advance(ahi0, (uint32_t)(2 * m) * CHUNK_BYTES);
-            const tc::SmemDesc alo = tc::desc_advance(alo0, (uint32_t)(2 * m) * CHUNK_BYTES);
-            tc::mma_f16(tacc, ahi, bhi, idesc, m > 0 ? 1u : 0u);
-            tc::mma_f16(tacc, alo, bhi, idesc, 1u);
-            tc::mma_f16(tacc, ahi, blo, idesc, 1u);
-            tc::tc_commit(bar(CE(r)));  // the unit is no longer read by the tensor core
-          }
-          if (!ok) break;
-          tc::tc_commit(bar(AF(a)));
+          const uint32_t unit = sbase + L.ring + (uint32_t)r * p.unit_bytes;
+          const tc::SmemDesc bhi = tc::kmajor_desc(unit, (uint32_t)(p.nbs * 16), 128u);
+          const tc::SmemDesc blo = tc::kmajor_desc(unit + (uint32_t)(p.nbs * 32), (uint32_t)(p.nbs * 16), 128u);
+          const tc::SmemDesc ahi = tc::desc_advance(ahi0, (uint32_t)(2 * m) * CHUNK_BYTES);
+          const tc::SmemDesc alo = tc::desc_advance(alo0, (uint32_t)(2 * m) * CHUNK_BYTES);
+          tc::mma_f16_elect(tacc, ahi, bhi, idesc, m > 0 ? 1u : 0u);
+          tc::mma_f16_elect(tacc, alo, bhi, idesc, 1u);
+          tc::mma_f16_elect(tacc, ahi, blo, idesc, 1u);
+          tc::tc_commit_elect(bar(CE(r)));  // the unit is no longer read by the tensor core
         }
         if (!ok) break;
-        tc::tc_commit(bar(XE(s)));
+        tc::tc_commit_elect(bar(AF(a)));
       }
-      // every tcgen05 operation issued by this thread is complete once DONE fires
-      tc::tc_commit(bar(B_DONE));
-      volatile int no_abort = 0;
-      tc::mbar_wait(bar(B_DONE), 0u, &no_abort, p.err, 2606);
+      if (!ok) break;
+      tc::tc_commit_elect(bar(XE(s)));
     }
+    // every tcgen05 operation issued by this warp is complete once DONE fires
+    tc::tc_commit_elect(bar(B_DONE));
+    volatile int no_abort = 0;
+    warp_wait(bar(B_DONE), 0u, &no_abort, p.err, 2606);
   } else if (warp >= EPI_W0) {
     // -------------------------------------------------------------- epilogue
     const int g = (warp - EPI_W0) >> 2;
@@ -305,19 +307,32 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
         // four independent running minima (columns j = 4 t + w), merged in index order
         float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
         int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
-        for (int jb = 0; jb < p.nbs; jb += 16) {
-          uint32_t v[16];
+        // 64 columns per wait: four loads in flight together (wait::ld waits
+        // for every load of the thread, so loads are batched, not pipelined)
+        for (int jb = 0; jb < p.nbs; jb += 64) {
+          uint32_t v[4][16];
+          const int nv = min(4, (p.nbs - jb) >> 4);  // warp-uniform
           // tcgen05.ld / wait::ld are .sync.aligned: the minima branch per lane
           __syncwarp();
-          tc::tmem_ld16(taddr + (uint32_t)jb, v);
-          tc::tmem_ld_wait16(v);
+          tc::tmem_ld16(taddr + (uint32_t)jb, v[0]);
+          if (nv > 1) tc::tmem_ld16(taddr + (uint32_t)(jb + 16), v[1]);
+          if (nv > 2) tc::tmem_ld16(taddr + (uint32_t)(jb + 32), v[2]);
+          if (nv > 3) tc::tmem_ld16(taddr + (uint32_t)(jb + 48), v[3]);
+          tc::tmem_ld_wait16(v[0]);
+          tc::reg_pin16(v[1]);
+          tc::reg_pin16(v[2]);
+          tc::reg_pin16(v[3]);
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = jb + jj;
-            const float dist = fmaf(__uint_as_float(v[jj]), negscale, bias_b[j]);
-            if (dist < bd[jj & 3]) {
-              bd[jj & 3] = dist;
-              bi[jj & 3] = b * p.nbs + j;
+          for (int t = 0; t < 4; ++t) {
+            if (t >= nv) break;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = jb + 16 * t + jj;
+              const float dist = fmaf(__uint_as_float(v[t][jj]), negscale, bias_b[j]);
+              if (dist < bd[jj & 3]) {
+                bd[jj & 3] = dist;
+                bi[jj & 3] = b * p.nbs + j;
+              }
             }
           }
         }

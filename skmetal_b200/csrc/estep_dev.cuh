@@ -202,10 +202,10 @@ __device__ __forceinline__ void issue_tile_mmas(uint32_t tacc, uint32_t stage, u
   }
 }
 
-// stages at s * stage_bytes from 0, then the centre image, bias, barriers and
-// misc words
+// stages at s * stage_bytes from 0, then the centre image, bias, the split
+// epilogue's partial minima, barriers and misc words
 struct Smem {
-  uint32_t c, bias, bars, misc, total;
+  uint32_t c, bias, part, bars, misc, total;
 };
 
 // barrier indices
@@ -215,7 +215,11 @@ __host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + a;
 __host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + MAX_ACC + a; }
 constexpr int B_C_FULL = 2 * MAX_STAGES + 2 * MAX_ACC;
 __host__ __device__ constexpr int B_DONE(int t) { return B_C_FULL + 1 + t; }  // drain of MMA issuer t
-constexpr int NUM_BARS = B_C_FULL + 3;
+// split epilogue (two groups per accumulator): partial minima of accumulator
+// a's use slot s (use count mod 2) written / consumed
+__host__ __device__ constexpr int B_PART_FULL(int a, int s) { return B_C_FULL + 3 + 2 * a + s; }
+__host__ __device__ constexpr int B_PART_EMPTY(int a, int s) { return B_C_FULL + 7 + 2 * a + s; }
+constexpr int NUM_BARS = B_C_FULL + 11;
 
 constexpr int MMA_W0 = 1, MMA_W1 = 2;
 constexpr int IDLE_W = 3;  // no role in the pipeline (callers give it side work)
@@ -223,7 +227,18 @@ constexpr int EPI_W0 = 4;
 constexpr int EPI_GROUPS = 4;  // one warp per TMEM lane quarter each
 static_assert((EPI_W0 + 4 * EPI_GROUPS) * 32 == THREADS, "warp roles must fill the block");
 
-__host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_bytes, int k_pad, int stages) {
+// Epilogue groups share an accumulator's columns when there are fewer
+// accumulators than groups (two accumulators: each tile's columns split
+// between two groups, whose partial minima meet in shared memory).
+// (plans have two or four accumulators: tc_plan keeps an accumulator within
+// 256 columns)
+__host__ __device__ constexpr int epi_split(int nacc) { return nacc >= EPI_GROUPS ? 1 : 2; }
+__host__ __device__ constexpr uint32_t part_bytes(int nacc) {
+  return epi_split(nacc) == 2 ? (uint32_t)(2 * 2 * BM * 8) : 0u;  // 2 accumulators x 2 slots x 128 rows
+}
+
+__host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_bytes, int k_pad, int stages,
+                                            int nacc) {
   Smem s;
   uint32_t off = (uint32_t)stages * stage_bytes;
   s.c = off;
@@ -231,6 +246,8 @@ __host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_b
   s.bias = off;
   off += (uint32_t)k_pad * 4;
   off = (off + 15) & ~15u;
+  s.part = off;
+  off += part_bytes(nacc);
   s.bars = off;
   off += NUM_BARS * 8;
   s.misc = off;
@@ -240,6 +257,7 @@ __host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_b
 }
 
 __device__ __forceinline__ bool better(float d, int i, float bd, int bi) { return d < bd || (d == bd && i < bi); }
+__host__ __device__ constexpr int round_up_dev(int a, int b) { return (a + b - 1) / b * b; }
 
 // Per-CTA view of a launch's shared memory, barriers and tensor memory.
 struct Cta {
@@ -253,7 +271,7 @@ struct Cta {
   uint32_t tmem_base;
   int my_tiles;  // tiles blockIdx.x + i * gridDim.x, i < my_tiles
   int n_iss;     // MMA issuers (1 or 2)
-  int n_grp;     // epilogue groups (= accumulators)
+  int n_grp;     // epilogue group sets (= accumulators); a set is epi_split(nacc) groups
   int issued;    // producer thread: tiles of the CTA's sequence whose copies it issued
   __device__ __forceinline__ uint32_t bar(int i) const { return bar0 + 8u * (uint32_t)i; }
 };
@@ -294,7 +312,7 @@ __device__ __forceinline__ void load_bias(const Params& p, const Cta& c, const f
 // barrier after which c.tmem_base is valid.
 __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_raw, const float* bias, Cta& c) {
   c.base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  c.L = smem_layout(p.stage_bytes, p.img_bytes, p.k_pad, p.stages);
+  c.L = smem_layout(p.stage_bytes, p.img_bytes, p.k_pad, p.stages, p.nacc);
   c.sbase = smem_u32(c.base);
   c.bar0 = c.sbase + c.L.bars;
   c.misc = reinterpret_cast<uint32_t*>(c.base + c.L.misc);
@@ -315,8 +333,14 @@ __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_r
     }
     for (int a = 0; a < MAX_ACC; ++a) {
       mbar_init(c.bar(B_ACC_FULL(a)), 1);
-      mbar_init(c.bar(B_ACC_EMPTY(a)), 4);  // the four warps of one epilogue group
+      // the four warps of each epilogue group reading the accumulator
+      mbar_init(c.bar(B_ACC_EMPTY(a)), 4 * epi_split(p.nacc));
     }
+    for (int a = 0; a < 2; ++a)
+      for (int sl = 0; sl < 2; ++sl) {
+        mbar_init(c.bar(B_PART_FULL(a, sl)), BM);   // every thread of the partner group
+        mbar_init(c.bar(B_PART_EMPTY(a, sl)), BM);  // every thread of the finishing group
+      }
     mbar_init(c.bar(B_C_FULL), 1);
     mbar_init(c.bar(B_DONE(0)), 1);
     mbar_init(c.bar(B_DONE(1)), 1);
@@ -439,29 +463,42 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
   } else if (warp >= EPI_W0) {
     // ----------------------------------------------------------------- epilogue
     // groups of four warps (one per TMEM lane quarter) take the tiles of their
-    // accumulator; each warp scans all clusters of its 32 rows
+    // accumulator. With four accumulators each group scans every cluster of
+    // its 32 rows; with two, groups g and g + 2 share accumulator g, each
+    // scanning one part of the clusters (h = 0 the first), and group g + 2
+    // hands its partial minima to group g through shared memory
     const int q = warp & 3;
     const int g = (warp - EPI_W0) >> 2;
+    const int split = epi_split(p.nacc);
+    const int ga = g % c.n_grp;  // accumulator whose tiles this group takes
+    const int h = g / c.n_grp;   // part of the clusters
+    const int jsplit = (int)round_up_dev(p.k_pad / 2, 16);
+    const int jlo = split == 1 ? 0 : (h == 0 ? 0 : jsplit);
+    const int jhi = split == 1 ? p.k_pad : (h == 0 ? jsplit : p.k_pad);
+    const bool finisher = h == 0;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    float* part_d = reinterpret_cast<float*>(c.base + c.L.part);  // [a][slot][row]
+    int* part_i = reinterpret_cast<int*>(c.base + c.L.part + 2 * 2 * BM * 4);
     // dist = ||c||^2 - 2 x.c with x.c = acc * 2^-(xexp + cexp)
     const float negscale = P.negscale;
-    const int i0 = g < c.n_grp ? (g - ig0 % c.n_grp + c.n_grp) % c.n_grp : my_tiles;
+    const int i0 = (g < c.n_grp * split) ? (ga - ig0 % c.n_grp + c.n_grp) % c.n_grp : my_tiles;
     int old_next = -1;
-    if (changed && i0 < my_tiles) {
+    if (finisher && changed && i0 < my_tiles) {
       const long long g0 = (long long)((int)blockIdx.x + i0 * (int)gridDim.x) * BM + row;
       old_next = g0 < p.n ? p.labels[g0] : -1;
     }
     for (int i = i0; i < my_tiles; i += c.n_grp) {
       const int ig = ig0 + i;
       const int a = ig % p.nacc;
+      const int use = ig / p.nacc;  // uses of accumulator a so far in the launch
       const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
       const int old = old_next;
-      if (changed && i + c.n_grp < my_tiles) {  // prefetch the next tile's previous labels
+      if (finisher && changed && i + c.n_grp < my_tiles) {  // prefetch the next tile's previous labels
         const long long g1 = grow + (long long)c.n_grp * gridDim.x * BM;
         old_next = g1 < p.n ? p.labels[g1] : -1;
       }
-      if (!mbar_wait(c.bar(B_ACC_FULL(a)), (ig / p.nacc) & 1, c.abort_flag, p.err, 2401)) break;
+      if (!mbar_wait(c.bar(B_ACC_FULL(a)), use & 1, c.abort_flag, p.err, 2401)) break;
       tc_fence_after();
       const uint32_t taddr = c.tmem_base + lane_off + (uint32_t)(a * p.acc_cols);
       // four independent running minima (columns j = 4m + u), merged in index order
@@ -471,9 +508,9 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
       // thread, so loads are batched): 32 columns, or 16 stacked (with their
       // c_lo half); more would spill in the 640-thread loop kernel
       const int step = p.stacked ? 16 : 32;
-      for (int jb = 0; jb < p.k_pad; jb += step) {
+      for (int jb = jlo; jb < jhi; jb += step) {
         uint32_t v[2][16];
-        const bool two = !p.stacked && jb + 16 < p.k_pad;  // warp-uniform
+        const bool two = !p.stacked && jb + 16 < jhi;  // warp-uniform
         // tcgen05.ld / wait::ld are .sync.aligned: the running minima below
         // branch per lane, so the warp reconverges before the loads
         __syncwarp();
@@ -486,15 +523,22 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
         for (int t = 0; t < 2; ++t) {
           if (t == 1 && !two) break;
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = jb + 16 * t + jj;
-            // stacked: v[0] holds acc[j], v[1] acc[k_pad + j]
-            const float dot = p.stacked ? __uint_as_float(v[0][jj]) + __uint_as_float(v[1][jj])
-                                        : __uint_as_float(v[t][jj]);
-            const float dist = fmaf(dot, negscale, c.bias_s[j]);
-            if (dist < bd[jj & 3]) {
-              bd[jj & 3] = dist;
-              bi[jj & 3] = j;
+          for (int u4 = 0; u4 < 4; ++u4) {
+            // the bias of four columns in one 16-byte load (jb is a multiple of 16)
+            const float4 b4 = *reinterpret_cast<const float4*>(c.bias_s + jb + 16 * t + 4 * u4);
+            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const int jj = 4 * u4 + w;
+              const int j = jb + 16 * t + jj;
+              // stacked: v[0] holds acc[j], v[1] acc[k_pad + j]
+              const float dot = p.stacked ? __uint_as_float(v[0][jj]) + __uint_as_float(v[1][jj])
+                                          : __uint_as_float(v[t][jj]);
+              const float dist = fmaf(dot, negscale, bb[w]);
+              // branch-free strict '<' (a NaN distance never wins): a select
+              // per element, no divergent branch
+              bi[w] = dist < bd[w] ? j : bi[w];
+              bd[w] = fminf(dist, bd[w]);
             }
           }
         }
@@ -510,6 +554,27 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
           best = bd[u];
           bl = bi[u];
         }
+      if (split > 1) {
+        // partial minima of the two parts meet in slot use mod 2 of accumulator a
+        const int sl = use & 1;
+        const uint32_t ph = (uint32_t)(use >> 1) & 1u;
+        const int o = (a * 2 + sl) * BM + row;
+        if (!finisher) {
+          if (!mbar_wait(c.bar(B_PART_EMPTY(a, sl)), ph ^ 1u, c.abort_flag, p.err, 2402)) break;
+          part_d[o] = best;
+          part_i[o] = bl;
+          mbar_arrive(c.bar(B_PART_FULL(a, sl)));
+          continue;
+        }
+        if (!mbar_wait(c.bar(B_PART_FULL(a, sl)), ph, c.abort_flag, p.err, 2403)) break;
+        const float ob = part_d[o];
+        const int oi = part_i[o];
+        mbar_arrive(c.bar(B_PART_EMPTY(a, sl)));
+        if (better(ob, oi, best, bl)) {
+          best = ob;
+          bl = oi;
+        }
+      }
       if (bl >= p.k) bl = 0;  // only reachable when every distance is +inf or NaN
       bool ch = false;
       if (grow < p.n) {

@@ -302,8 +302,10 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
     const int nkx = stacked ? plan->k_steps : (plan->k_steps + 1) & ~1;
     const uint32_t stage_bytes = (uint32_t)nkx * tc::CHUNK_BYTES;
     const uint32_t img_bytes = (uint32_t)(cimg_halves(plan->k_pad, plan->k_steps, stacked) * 2);
+    const int acc_cols = stacked ? 2 * plan->k_pad : plan->k_pad;
+    const int nacc = 4 * acc_cols <= 512 ? 4 : (2 * acc_cols <= 512 ? 2 : 1);
     for (int st = tc::MAX_STAGES; st >= 2; --st) {
-      const tc::Smem L = tc::smem_layout(stage_bytes, img_bytes, plan->k_pad, st);
+      const tc::Smem L = tc::smem_layout(stage_bytes, img_bytes, plan->k_pad, st, nacc);
       if ((int)L.total <= avail) {
         plan->stacked = stacked;
         plan->stages = st;

@@ -329,10 +329,9 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
             for (int jj = 0; jj < 16; ++jj) {
               const int j = jb + 16 * t + jj;
               const float dist = fmaf(__uint_as_float(v[t][jj]), negscale, bias_b[j]);
-              if (dist < bd[jj & 3]) {
-                bd[jj & 3] = dist;
-                bi[jj & 3] = b * p.nbs + j;
-              }
+              // branch-free strict '<' (a NaN distance never wins)
+              bi[jj & 3] = dist < bd[jj & 3] ? b * p.nbs + j : bi[jj & 3];
+              bd[jj & 3] = fminf(dist, bd[jj & 3]);
             }
           }
         }

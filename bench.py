@@ -17,11 +17,14 @@ predict workload (400M x 8, 16 fixed centres): a step is one assignment pass.
   GPU, the sharded C-ABI fit on several -- with X in ordinary (pageable)
   host memory, its upload and the labels' / centres' download inside the
   timed region. ``e2e_pinned`` repeats it from page-locked host memory.
-* ``roofline``: the dominant kernel against ``MEASURED_PEAKS.json``. HBM-bound
-  fits (c1, c2, c4): the persistent loop kernel, algorithmic bytes = 4 n d per
-  Lloyd iteration (X read once), one launch per fit. The k > 256 codebook fit
-  (c3): the tensor-core E-step, algorithmic flops = 3 (2 n k d) per
-  iteration. Predict (c5): the assignment kernel, 4 n d + 4 n bytes per pass.
+* ``roofline``: the dominant kernel against ``MEASURED_PEAKS.json``. A Lloyd
+  iteration reads X once (4 n d bytes) and runs 3 (2 n k d) tensor flops; its
+  roofline is the slower of the two at the measured copy bandwidth and bf16
+  burst peak (the MMAs are kind::f16), so c1 and c2 are HBM-bound and c3 and
+  c4 tensor-bound. Fits with k <= 256 (c1, c2, c4): the persistent loop
+  kernel, one launch per fit; the k > 256 codebook fit (c3): the tensor-core
+  E-step launches. Predict (c5): the assignment kernel, 4 n d + 4 n bytes per
+  pass.
   ``traffic`` = DRAM bytes per launch from the committed ncu summary
   (profiles/), scaled to this run's rows and iterations.
 * ``cpu_baseline`` (rank 0, N = 1): the reference's CPU path on a bounded
@@ -484,41 +487,42 @@ def main():
 
     hbm, bf16, bf16_sus, src = _peaks()
     rows_here = Xs.shape[0]
-    if fit and w.k > 256:
-        # tensor-bound codebook fit: the E-step's 3 (2 n k d) flops per launch
+    if fit:
+        # per Lloyd iteration: X read once (4 n d bytes) and 3 (2 n k d) tensor
+        # flops (the split product); the roofline is the slower of the two at
+        # the measured peaks (the MMAs are kind::f16, the bf16 burst peak)
+        alg_bytes = 4.0 * rows_here * w.d
         flops = 6.0 * rows_here * w.k * w.d
+        t_hbm, t_tc = alg_bytes / (hbm * 1e9), flops / (bf16 * 1e12)
+        tensor = t_tc > t_hbm
+        work, peak, scale, unit_r = (flops, bf16, 1e12, "TFLOP/s") if tensor else (alg_bytes, hbm, 1e9, "GB/s")
         est_avg_s = est_ms / max(1, est_n) / 1e3
-        achieved = flops / est_avg_s / 1e12 if est_avg_s > 0 else None
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                    "frac": (achieved / bf16) if achieved else None,
-                    "frac_of_sustained": (achieved / bf16_sus) if achieved else None,
-                    "traffic": _traffic_for("estep_wide", w.name, rows_here),
-                    "kernel": "estep_wide_kernel (tcgen05 E-step, k > 256)", "peak_source": f"{src} bf16 burst",
-                    "algorithmic_flops_per_launch": flops,
-                    "timing": "CUDA events on the E-step launches of every 10th iteration"}
-    elif fit:
-        alg_bytes = 4.0 * rows_here * w.d  # X read once per Lloyd iteration
-        est_avg_s = est_ms / max(1, est_n) / 1e3
-        e_achieved = alg_bytes / est_avg_s / 1e9 if est_avg_s > 0 else None
+        e_achieved = work / est_avg_s / scale if est_avg_s > 0 else None
         if persistent:
-            per_launch = alg_bytes * iters / args.steps  # one launch per fit, all its iterations
+            per_launch = work * iters / args.steps  # one launch per fit, all its iterations
             dur_s = ms_loop / 1e3 / args.steps
-            achieved = per_launch / dur_s / 1e9 if dur_s > 0 else None
+            achieved = per_launch / dur_s / scale if dur_s > 0 else None
             traffic = _traffic_for("lloyd_loop", w.name, rows_here, iters / args.steps)
             kernel = "lloyd_loop_kernel (persistent: every Lloyd iteration of a fit in one launch)"
             e_timing = "device globaltimer stamps of every iteration (E-step through the grid barrier)"
         else:
-            per_launch = alg_bytes
+            per_launch = work
             achieved = e_achieved
-            traffic = _traffic_for("estep_tc", w.name, rows_here)
-            kernel = "E-step (estep_tc_kernel)"
+            wide = w.k > 256
+            traffic = _traffic_for("estep_wide" if wide else "estep_tc", w.name, rows_here)
+            kernel = "estep_wide_kernel (tcgen05 E-step, k > 256)" if wide else "E-step (estep_tc_kernel)"
             e_timing = "CUDA events on the E-step launches of every 10th iteration"
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                    "frac": (achieved / hbm) if achieved else None, "traffic": traffic, "kernel": kernel,
-                    "peak_source": src, "algorithmic_bytes_per_launch": per_launch,
-                    "e_phase": {"achieved": e_achieved, "frac": (e_achieved / hbm) if e_achieved else None,
-                                "timing": e_timing},
-                    "loop_frac": (alg_bytes * iters / (ms_loop / 1e3)) / 1e9 / hbm if ms_loop > 0 else None}
+        roofline = {"bound": "tensor" if tensor else "hbm", "achieved": achieved, "peak": peak, "unit": unit_r,
+                    "frac": (achieved / peak) if achieved else None, "traffic": traffic, "kernel": kernel,
+                    "peak_source": f"{src} bf16 burst" if tensor else src,
+                    ("algorithmic_flops_per_launch" if tensor else "algorithmic_bytes_per_launch"): per_launch,
+                    "iteration_roofline_us": {"hbm": t_hbm * 1e6, "tensor": t_tc * 1e6},
+                    "e_phase": {"achieved": e_achieved, "frac": (e_achieved / peak) if e_achieved else None,
+                                "timing": e_timing}}
+        if tensor:
+            roofline["frac_of_sustained"] = (achieved / bf16_sus) if achieved else None
+        if persistent and ms_loop > 0:
+            roofline["loop_frac"] = (work * iters / (ms_loop / 1e3)) / scale / peak
     else:
         per_launch = 4.0 * rows_here * (w.d + 1)  # X read once, int32 labels written
         dur_s = ms_loop / 1e3 / args.steps

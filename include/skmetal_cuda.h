@@ -110,6 +110,12 @@ float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint3
  * include/bridge.h:25), kernel row_norm_sq (DistanceKernels.metal:6-28). */
 int skmetal_row_norm_sq(const float* X, float* norms, size_t n, size_t d);
 
+/* Squared Euclidean distance matrix D[i*n + j] = max(||x_i||^2 + ||x_j||^2
+ * - 2 x_i.x_j, 0) of the n rows of X, float32 (replaces skmetal_pairwise_
+ * distance, skmetal_bridge/Sources/SkMetalBridge/KMeansBridge.swift:8-85,
+ * bound at skmetal/_bridge.py:108 and called at skmetal/_bridge.py:566-573). */
+int skmetal_pairwise_distance(const float* X, float* D, size_t n, size_t d);
+
 /* ---- KMeans path: extended entry points ---------------------------------- */
 
 /* Full KMeans.fit for one explicit initialisation (sklearn/cluster/
@@ -149,6 +155,26 @@ int skmetal_kmeans_fit_dataset(void* handle, const float* init, size_t k, int32_
 /* Predict on a resident dataset: labels_out (host, may be NULL to keep the
  * labels on the device). */
 int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t k, int32_t* labels_out);
+
+/* k-means++ seeding of the n rows of X (scikit-learn's greedy k-means++,
+ * sklearn/cluster/_kmeans.py _kmeans_plusplus, which the reference's KMeans
+ * runs on this platform; the reference's own Metal seeding is k-means||,
+ * skmetal/estimators/cluster.py:70-116). The caller draws from its random
+ * stream what scikit-learn draws, in the same order: first_index (the first
+ * centre, random_state.choice over w / sum(w)) and, for every further centre,
+ * n_local_trials (1..16) uniforms in [0, 1): uniforms[(c - 1) * T + t].
+ * sample_weight (n floats) may be NULL (unit weights). With center != 0 the
+ * rows are centred by their exact column mean first, as the fit centres them.
+ * centers_out (k x d) receives the chosen raw rows, indices_out their
+ * indices. */
+int skmetal_kmeans_plusplus(const float* X, size_t n, size_t d, size_t k, const float* sample_weight,
+                            int64_t first_index, const double* uniforms, size_t n_local_trials, int center,
+                            float* centers_out, int64_t* indices_out);
+
+/* skmetal_kmeans_plusplus on a resident dataset. */
+int skmetal_dataset_kmeans_plusplus(void* handle, size_t k, const float* sample_weight, int64_t first_index,
+                                    const double* uniforms, size_t n_local_trials, int center, float* centers_out,
+                                    int64_t* indices_out);
 
 /* Statistics of the calling thread's last fit / predict: device times in
  * milliseconds measured with CUDA events on the library's stream

@@ -23,7 +23,7 @@ import numpy as np
 __all__ = [
     "CUDA_AVAILABLE", "GPU_AVAILABLE", "METAL_AVAILABLE", "LIB_PATH",
     "ensure_warmed_up", "kmeans_assign", "kmeans_batch_fused", "compute_mindists", "kmeans_inertia",
-    "row_norm_sq", "kmeans_fit", "kmeans_lloyd_iter", "kmeans_transform", "Dataset", "last_fit_stats",
+    "row_norm_sq", "pairwise_distance", "kmeans_plusplus", "kmeans_fit", "kmeans_lloyd_iter", "kmeans_transform", "Dataset", "last_fit_stats",
     "launch_count", "device_info", "device_count", "is_loaded", "set_device", "comm_unique_id", "comm_init",
     "comm_destroy", "kmeans_fit_shard", "debug_inject_failure", "debug_loop_stamps", "FIT_CENTER", "FIT_SIMT", "FIT_PROFILE",
     "FIT_DISTRIBUTED", "FIT_TOL_ABS", "EXPORTED_SYMBOLS",
@@ -61,12 +61,17 @@ _SIGNATURES = [
                                           _c_size_t]),
     ("skmetal_kmeans_inertia", _c_float, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t]),
     ("skmetal_row_norm_sq", _c_int, [_c_void_p, _c_void_p, _c_size_t, _c_size_t]),
+    ("skmetal_pairwise_distance", _c_int, [_c_void_p, _c_void_p, _c_size_t, _c_size_t]),
     ("skmetal_kmeans_fit", _c_int, [_c_void_p, _c_size_t, _c_size_t, _c_size_t, _c_void_p, _c_i32, _c_double,
                                     _c_u32, _c_void_p, _c_void_p, ctypes.POINTER(_c_double),
                                     ctypes.POINTER(_c_i32)]),
     ("skmetal_kmeans_lloyd_iter", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                            _c_size_t, _c_size_t, _c_size_t]),
     ("skmetal_kmeans_transform", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t]),
+    ("skmetal_kmeans_plusplus", _c_int, [_c_void_p, _c_size_t, _c_size_t, _c_size_t, _c_void_p, ctypes.c_int64,
+                                         _c_void_p, _c_size_t, _c_int, _c_void_p, _c_void_p]),
+    ("skmetal_dataset_kmeans_plusplus", _c_int, [_c_void_p, _c_size_t, _c_void_p, ctypes.c_int64, _c_void_p,
+                                                 _c_size_t, _c_int, _c_void_p, _c_void_p]),
     ("skmetal_dataset_create", _c_int, [_c_void_p, _c_size_t, _c_size_t, ctypes.POINTER(_c_void_p)]),
     ("skmetal_dataset_free", _c_int, [_c_void_p]),
     ("skmetal_kmeans_fit_dataset", _c_int, [_c_void_p, _c_void_p, _c_size_t, _c_i32, _c_double, _c_u32,
@@ -295,6 +300,57 @@ def row_norm_sq(X) -> np.ndarray:
     out = np.empty(X.shape[0], dtype=np.float32)
     _bridge_call("skmetal_row_norm_sq", X, out, int(X.shape[0]), int(X.shape[1]))
     return out
+
+
+def _plusplus_draws(n: int, k: int, random_state, sample_weight, n_local_trials):
+    """What scikit-learn's _kmeans_plusplus draws from ``random_state``, in its
+    order: the first centre over w / sum(w), then n_local_trials uniforms per
+    further centre (one block of (k - 1) x T, the same stream)."""
+    w = np.ones(n, dtype=np.float32) if sample_weight is None else np.ascontiguousarray(sample_weight, np.float32)
+    if n_local_trials is None:
+        n_local_trials = 2 + int(np.log(k))
+    first = int(random_state.choice(n, p=w / w.sum()))
+    u = np.ascontiguousarray(random_state.uniform(size=(max(k - 1, 0), n_local_trials)), dtype=np.float64)
+    return (None if sample_weight is None else w), first, u, int(n_local_trials)
+
+
+def kmeans_plusplus(X, k: int, random_state, sample_weight=None, n_local_trials=None, center: bool = True):
+    """k-means++ seeding on the GPU (scikit-learn's greedy variant and random
+    stream). ``X`` is a host array or a :class:`Dataset`. Returns the centres
+    (raw rows of X, k x d float32) and their row indices (int64)."""
+    k = int(k)
+    ds = X if isinstance(X, Dataset) else None
+    if ds is None:
+        X = _f32c(X, "X")
+        n, d = X.shape
+    else:
+        n, d = ds.n, ds.d
+    if not 1 <= k <= n:
+        raise ValueError(f"n_samples={n} should be >= n_clusters={k}.")
+    w, first, u, T = _plusplus_draws(n, k, random_state, sample_weight, n_local_trials)
+    centers = np.empty((k, d), dtype=np.float32)
+    idx = np.empty(k, dtype=np.int64)
+    if ds is None:
+        _bridge_call("skmetal_kmeans_plusplus", X, n, d, k, w, ctypes.c_int64(first), u, T, _c_int(int(bool(center))),
+                     centers, idx)
+    else:
+        _bridge_call("skmetal_dataset_kmeans_plusplus", ds._h, k, w, ctypes.c_int64(first), u, T,
+                     _c_int(int(bool(center))), centers, idx)
+    return centers, idx
+
+
+def pairwise_distance(X: np.ndarray) -> np.ndarray:
+    """Squared Euclidean pairwise distance matrix (n x n float32).
+
+    Same contract as the reference's ``skmetal/_bridge.py:566-573``: X must be
+    float32 and C-contiguous; D[i, j] = max(|x_i|^2 + |x_j|^2 - 2 x_i.x_j, 0).
+    """
+    if not isinstance(X, np.ndarray) or X.dtype != np.float32 or not X.flags["C_CONTIGUOUS"] or X.ndim != 2:
+        raise TypeError("X must be float32 and C-contiguous")
+    n, d = X.shape
+    D = np.empty((n, n), dtype=np.float32, order="C")
+    _bridge_call("skmetal_pairwise_distance", X, D, n, d)
+    return D
 
 
 # ----------------------------------------------------------------------------

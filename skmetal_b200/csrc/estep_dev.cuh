@@ -215,7 +215,7 @@ __host__ __device__ constexpr int B_ACC_FULL(int a) { return 2 * MAX_STAGES + a;
 __host__ __device__ constexpr int B_ACC_EMPTY(int a) { return 2 * MAX_STAGES + MAX_ACC + a; }
 constexpr int B_C_FULL = 2 * MAX_STAGES + 2 * MAX_ACC;
 __host__ __device__ constexpr int B_DONE(int t) { return B_C_FULL + 1 + t; }  // drain of MMA issuer t
-// split epilogue (two groups per accumulator): partial minima of accumulator
+// split epilogue (groups sharing every tile): partial minima of accumulator
 // a's use slot s (use count mod 2) written / consumed
 __host__ __device__ constexpr int B_PART_FULL(int a, int s) { return B_C_FULL + 3 + 2 * a + s; }
 __host__ __device__ constexpr int B_PART_EMPTY(int a, int s) { return B_C_FULL + 7 + 2 * a + s; }
@@ -227,14 +227,17 @@ constexpr int EPI_W0 = 4;
 constexpr int EPI_GROUPS = 4;  // one warp per TMEM lane quarter each
 static_assert((EPI_W0 + 4 * EPI_GROUPS) * 32 == THREADS, "warp roles must fill the block");
 
-// Epilogue groups share an accumulator's columns when there are fewer
-// accumulators than groups (two accumulators: each tile's columns split
-// between two groups, whose partial minima meet in shared memory).
-// (plans have two or four accumulators: tc_plan keeps an accumulator within
-// 256 columns)
-__host__ __device__ constexpr int epi_split(int nacc) { return nacc >= EPI_GROUPS ? 1 : 2; }
+// With fewer accumulators than epilogue groups (two: tc_plan keeps an
+// accumulator within 256 columns), every group takes every tile and scans one
+// quarter of its clusters, and groups 1-3 hand their partial minima to group
+// 0 through shared memory. All sixteen epilogue warps then work on the tile
+// of one accumulator while the MMAs fill the other; with two groups per
+// accumulator both accumulators' epilogues ran together and the tensor core
+// waited for them.
+__host__ __device__ constexpr int epi_split(int nacc) { return nacc >= EPI_GROUPS ? 1 : EPI_GROUPS; }
 __host__ __device__ constexpr uint32_t part_bytes(int nacc) {
-  return epi_split(nacc) == 2 ? (uint32_t)(2 * 2 * BM * 8) : 0u;  // 2 accumulators x 2 slots x 128 rows
+  // 2 accumulators x 2 slots x (split - 1) parts x 128 rows x {float, int}
+  return epi_split(nacc) > 1 ? (uint32_t)(2 * 2 * (epi_split(nacc) - 1) * BM * 8) : 0u;
 }
 
 __host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_bytes, int k_pad, int stages,
@@ -258,6 +261,154 @@ __host__ __device__ inline Smem smem_layout(uint32_t stage_bytes, uint32_t img_b
 
 __device__ __forceinline__ bool better(float d, int i, float bd, int bi) { return d < bd || (d == bd && i < bi); }
 __host__ __device__ constexpr int round_up_dev(int a, int b) { return (a + b - 1) / b * b; }
+
+// ---------------------------------------------------------------------------
+// Row scan of the epilogue: the first column of smallest distance, with
+// dist = fmaf(dot, negscale, bias) in float32 and strict '<' (a NaN distance
+// never wins, ties keep the lower column). Columns are taken in pairs: one
+// fma.rn.f32x2 forms both distances (each half rounds exactly as fmaf), one
+// three-input min folds both into a running minimum, and the pair's first
+// column wins when it equals the new minimum. Four chains of pairs run
+// independently and are merged in (distance, column) order.
+// ---------------------------------------------------------------------------
+
+// {a + b} on float pairs (add.rn.f32x2)
+__device__ __forceinline__ unsigned long long add_pair(uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
+  unsigned long long a, b, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "r"(a0), "r"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "r"(b0), "r"(b1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// the distances of a column pair from the packed dot products: dot * s + bias
+__device__ __forceinline__ void dist_pair(unsigned long long dot, unsigned long long s2, float b0, float b1,
+                                          float& d0, float& d1) {
+  unsigned long long c, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(b0), "f"(b1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(dot), "l"(s2), "l"(c));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+__device__ __forceinline__ unsigned long long pack_pair(uint32_t a0, uint32_t a1) {
+  unsigned long long a;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "r"(a0), "r"(a1));
+  return a;
+}
+
+// running minimum (bd, bi) of one chain after the pair (d0 at column j, d1 at j + 1)
+__device__ __forceinline__ void pair_step(float& bd, int& bi, float d0, float d1, int j) {
+  float m;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(bd), "f"(d0), "f"(d1));
+  const int jm = d0 == m ? j : j + 1;
+  bi = m < bd ? jm : bi;
+  bd = m;
+}
+
+// Scan of NB16 x 16 columns of one TMEM accumulator row (columns local to
+// `taddr`; stacked: column j's dot product is acc[j] + acc[koff + j]); bias
+// points at the bias of local column 0 (16-byte aligned). LPW 16-column loads
+// go out before each wait (wait::ld waits for every load of the thread, so
+// loads are batched; stacked: one block and its second half). Returns the
+// local column in `bl` (INT_MAX when no distance is below +inf).
+template <int NB16, bool STACKED, int LPW = 2>
+__device__ __forceinline__ void scan_row(uint32_t taddr, uint32_t koff, const float* __restrict__ bias,
+                                         unsigned long long s2, float& best, int& bl) {
+  float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+  int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
+  constexpr int PER = STACKED ? 1 : LPW;  // 16-column blocks per wave
+  constexpr int WAVES = (NB16 + PER - 1) / PER;
+#pragma unroll
+  for (int w = 0; w < WAVES; ++w) {
+    uint32_t v[STACKED ? 2 : LPW][16];
+    // tcgen05.ld / wait::ld are .sync.aligned: the warp reconverges first
+    __syncwarp();
+    if (STACKED) {
+      tmem_ld16(taddr + (uint32_t)(16 * w), v[0]);
+      tmem_ld16(taddr + koff + (uint32_t)(16 * w), v[1]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < PER; ++t)
+        if (PER * w + t < NB16) tmem_ld16(taddr + (uint32_t)(16 * (PER * w + t)), v[t]);
+    }
+    tmem_ld_wait16(v[0]);
+#pragma unroll
+    for (int t = 1; t < (STACKED ? 2 : LPW); ++t) reg_pin16(v[t]);
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      if (PER * w + t >= NB16) break;
+      const int cb = 16 * (PER * w + t);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 b4 = *reinterpret_cast<const float4*>(bias + cb + 4 * u);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int jj = 4 * u + 2 * e;
+          const unsigned long long dot = STACKED ? add_pair(v[0][jj], v[0][jj + 1], v[1][jj], v[1][jj + 1])
+                                                 : pack_pair(v[t][jj], v[t][jj + 1]);
+          float d0, d1;
+          dist_pair(dot, s2, e ? b4.z : b4.x, e ? b4.w : b4.y, d0, d1);
+          pair_step(bd[(jj >> 1) & 3], bi[(jj >> 1) & 3], d0, d1, cb + jj);
+        }
+      }
+    }
+  }
+  best = bd[0];
+  bl = bi[0];
+#pragma unroll
+  for (int u = 1; u < 4; ++u)
+    if (better(bd[u], bi[u], best, bl)) {
+      best = bd[u];
+      bl = bi[u];
+    }
+}
+
+// scan_row of 1..16 unstacked 16-column blocks with four loads per wait
+// (kernels with registers to spare: 64 columns in flight)
+__device__ __forceinline__ void scan_row4_n(int nb16, uint32_t taddr, const float* __restrict__ bias,
+                                            unsigned long long s2, float& best, int& bl) {
+#define SKM_SCAN4_CASE(N)                                    \
+  case N:                                                    \
+    scan_row<N, false, 4>(taddr, 0u, bias, s2, best, bl);    \
+    return;
+  best = INFINITY;
+  bl = 0x7fffffff;
+  switch (nb16) {
+    SKM_SCAN4_CASE(1) SKM_SCAN4_CASE(2) SKM_SCAN4_CASE(3) SKM_SCAN4_CASE(4) SKM_SCAN4_CASE(5)
+    SKM_SCAN4_CASE(6) SKM_SCAN4_CASE(7) SKM_SCAN4_CASE(8) SKM_SCAN4_CASE(9) SKM_SCAN4_CASE(10)
+    SKM_SCAN4_CASE(11) SKM_SCAN4_CASE(12) SKM_SCAN4_CASE(13) SKM_SCAN4_CASE(14) SKM_SCAN4_CASE(15)
+    SKM_SCAN4_CASE(16)
+    default: return;
+  }
+#undef SKM_SCAN4_CASE
+}
+
+// scan_row for a run-time count of 16-column blocks (1..16; stacked 1..8)
+__device__ __forceinline__ void scan_row_n(int nb16, bool stacked, uint32_t taddr, uint32_t koff,
+                                           const float* __restrict__ bias, unsigned long long s2, float& best,
+                                           int& bl) {
+#define SKM_SCAN_CASE(N, ST)                                \
+  case N:                                                   \
+    scan_row<N, ST>(taddr, koff, bias, s2, best, bl);       \
+    return;
+  best = INFINITY;
+  bl = 0x7fffffff;
+  if (stacked) {
+    switch (nb16) {
+      SKM_SCAN_CASE(1, true) SKM_SCAN_CASE(2, true) SKM_SCAN_CASE(3, true) SKM_SCAN_CASE(4, true)
+      SKM_SCAN_CASE(5, true) SKM_SCAN_CASE(6, true) SKM_SCAN_CASE(7, true) SKM_SCAN_CASE(8, true)
+      default: return;
+    }
+  }
+  switch (nb16) {
+    SKM_SCAN_CASE(1, false) SKM_SCAN_CASE(2, false) SKM_SCAN_CASE(3, false) SKM_SCAN_CASE(4, false)
+    SKM_SCAN_CASE(5, false) SKM_SCAN_CASE(6, false) SKM_SCAN_CASE(7, false) SKM_SCAN_CASE(8, false)
+    SKM_SCAN_CASE(9, false) SKM_SCAN_CASE(10, false) SKM_SCAN_CASE(11, false) SKM_SCAN_CASE(12, false)
+    SKM_SCAN_CASE(13, false) SKM_SCAN_CASE(14, false) SKM_SCAN_CASE(15, false) SKM_SCAN_CASE(16, false)
+    default: return;
+  }
+#undef SKM_SCAN_CASE
+}
 
 // Per-CTA view of a launch's shared memory, barriers and tensor memory.
 struct Cta {
@@ -323,7 +474,7 @@ __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_r
   // with a = g mod n_grp (n_iss and n_grp divide nacc), so each accumulator
   // barrier has exactly one producer and one consumer
   c.n_iss = p.nacc >= 2 ? 2 : 1;
-  c.n_grp = p.nacc;
+  c.n_grp = EPI_GROUPS / epi_split(p.nacc);
   c.issued = 0;
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
@@ -338,7 +489,8 @@ __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_r
     }
     for (int a = 0; a < 2; ++a)
       for (int sl = 0; sl < 2; ++sl) {
-        mbar_init(c.bar(B_PART_FULL(a, sl)), BM);   // every thread of the partner group
+        // every thread of the partner groups (unused without a split)
+        mbar_init(c.bar(B_PART_FULL(a, sl)), BM * (epi_split(p.nacc) > 1 ? epi_split(p.nacc) - 1 : 1));
         mbar_init(c.bar(B_PART_EMPTY(a, sl)), BM);  // every thread of the finishing group
       }
     mbar_init(c.bar(B_C_FULL), 1);
@@ -462,26 +614,28 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
     }
   } else if (warp >= EPI_W0) {
     // ----------------------------------------------------------------- epilogue
-    // groups of four warps (one per TMEM lane quarter) take the tiles of their
-    // accumulator. With four accumulators each group scans every cluster of
-    // its 32 rows; with two, groups g and g + 2 share accumulator g, each
-    // scanning one part of the clusters (h = 0 the first), and group g + 2
-    // hands its partial minima to group g through shared memory
+    // groups of four warps (one per TMEM lane quarter). With four
+    // accumulators group g takes the tiles of accumulator g and scans every
+    // cluster of its 32 rows; with two, every group takes every tile and
+    // scans part h = g of the clusters, and groups 1-3 hand their partial
+    // minima to group 0 (the finisher) through shared memory
     const int q = warp & 3;
     const int g = (warp - EPI_W0) >> 2;
     const int split = epi_split(p.nacc);
-    const int ga = g % c.n_grp;  // accumulator whose tiles this group takes
+    const int ga = g % c.n_grp;  // accumulator set whose tiles this group takes
     const int h = g / c.n_grp;   // part of the clusters
-    const int jsplit = (int)round_up_dev(p.k_pad / 2, 16);
-    const int jlo = split == 1 ? 0 : (h == 0 ? 0 : jsplit);
-    const int jhi = split == 1 ? p.k_pad : (h == 0 ? jsplit : p.k_pad);
+    const int jpart = (int)round_up_dev((p.k_pad + split - 1) / split, 16);
+    const int jlo = min(p.k_pad, h * jpart);
+    const int jhi = min(p.k_pad, (h + 1) * jpart);
     const bool finisher = h == 0;
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    float* part_d = reinterpret_cast<float*>(c.base + c.L.part);  // [a][slot][row]
-    int* part_i = reinterpret_cast<int*>(c.base + c.L.part + 2 * 2 * BM * 4);
+    const int np = split > 1 ? split - 1 : 1;  // partial slots per (accumulator, use slot)
+    float* part_d = reinterpret_cast<float*>(c.base + c.L.part);  // [a][slot][part][row]
+    int* part_i = reinterpret_cast<int*>(c.base + c.L.part + 2 * 2 * np * BM * 4);
     // dist = ||c||^2 - 2 x.c with x.c = acc * 2^-(xexp + cexp)
     const float negscale = P.negscale;
+    const unsigned long long s2 = pack_pair(__float_as_uint(negscale), __float_as_uint(negscale));
     const int i0 = (g < c.n_grp * split) ? (ga - ig0 % c.n_grp + c.n_grp) % c.n_grp : my_tiles;
     int old_next = -1;
     if (finisher && changed && i0 < my_tiles) {
@@ -501,79 +655,43 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
       if (!mbar_wait(c.bar(B_ACC_FULL(a)), use & 1, c.abort_flag, p.err, 2401)) break;
       tc_fence_after();
       const uint32_t taddr = c.tmem_base + lane_off + (uint32_t)(a * p.acc_cols);
-      // four independent running minima (columns j = 4m + u), merged in index order
-      float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
-      int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
-      // two 16-column loads per wait (wait::ld waits for every load of the
-      // thread, so loads are batched): 32 columns, or 16 stacked (with their
-      // c_lo half); more would spill in the 640-thread loop kernel
-      const int step = p.stacked ? 16 : 32;
-      for (int jb = jlo; jb < jhi; jb += step) {
-        uint32_t v[2][16];
-        const bool two = !p.stacked && jb + 16 < jhi;  // warp-uniform
-        // tcgen05.ld / wait::ld are .sync.aligned: the running minima below
-        // branch per lane, so the warp reconverges before the loads
-        __syncwarp();
-        tmem_ld16(taddr + (uint32_t)jb, v[0]);
-        if (p.stacked) tmem_ld16(taddr + (uint32_t)(p.k_pad + jb), v[1]);
-        else if (two) tmem_ld16(taddr + (uint32_t)(jb + 16), v[1]);
-        tmem_ld_wait16(v[0]);
-        reg_pin16(v[1]);
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (t == 1 && !two) break;
-#pragma unroll
-          for (int u4 = 0; u4 < 4; ++u4) {
-            // the bias of four columns in one 16-byte load (jb is a multiple of 16)
-            const float4 b4 = *reinterpret_cast<const float4*>(c.bias_s + jb + 16 * t + 4 * u4);
-            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const int jj = 4 * u4 + w;
-              const int j = jb + 16 * t + jj;
-              // stacked: v[0] holds acc[j], v[1] acc[k_pad + j]
-              const float dot = p.stacked ? __uint_as_float(v[0][jj]) + __uint_as_float(v[1][jj])
-                                          : __uint_as_float(v[t][jj]);
-              const float dist = fmaf(dot, negscale, bb[w]);
-              // branch-free strict '<' (a NaN distance never wins): a select
-              // per element, no divergent branch
-              bi[w] = dist < bd[w] ? j : bi[w];
-              bd[w] = fminf(dist, bd[w]);
-            }
-          }
-        }
-      }
+      float best;
+      int bl;
+      scan_row_n((jhi - jlo) >> 4, p.stacked != 0, taddr + (uint32_t)jlo, (uint32_t)p.k_pad, c.bias_s + jlo, s2,
+                 best, bl);
+      if (bl != 0x7fffffff) bl += jlo;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(c.bar(B_ACC_EMPTY(a)));
-      float best = bd[0];
-      int bl = bi[0];
-#pragma unroll
-      for (int u = 1; u < 4; ++u)
-        if (better(bd[u], bi[u], best, bl)) {
-          best = bd[u];
-          bl = bi[u];
-        }
       if (split > 1) {
-        // partial minima of the two parts meet in slot use mod 2 of accumulator a
+        // partial minima of the parts meet in slot use mod 2 of accumulator a
         const int sl = use & 1;
         const uint32_t ph = (uint32_t)(use >> 1) & 1u;
-        const int o = (a * 2 + sl) * BM + row;
+        const int o = (a * 2 + sl) * np * BM + row;
         if (!finisher) {
           if (!mbar_wait(c.bar(B_PART_EMPTY(a, sl)), ph ^ 1u, c.abort_flag, p.err, 2402)) break;
-          part_d[o] = best;
-          part_i[o] = bl;
+          part_d[o + (h - 1) * BM] = best;
+          part_i[o + (h - 1) * BM] = bl;
           mbar_arrive(c.bar(B_PART_FULL(a, sl)));
           continue;
         }
         if (!mbar_wait(c.bar(B_PART_FULL(a, sl)), ph, c.abort_flag, p.err, 2403)) break;
-        const float ob = part_d[o];
-        const int oi = part_i[o];
-        mbar_arrive(c.bar(B_PART_EMPTY(a, sl)));
-        if (better(ob, oi, best, bl)) {
-          best = ob;
-          bl = oi;
+        float ob[EPI_GROUPS - 1];
+        int oi[EPI_GROUPS - 1];
+#pragma unroll
+        for (int u = 0; u < EPI_GROUPS - 1; ++u) {
+          if (u < split - 1) {
+            ob[u] = part_d[o + u * BM];
+            oi[u] = part_i[o + u * BM];
+          }
         }
+        mbar_arrive(c.bar(B_PART_EMPTY(a, sl)));
+#pragma unroll
+        for (int u = 0; u < EPI_GROUPS - 1; ++u)
+          if (u < split - 1 && better(ob[u], oi[u], best, bl)) {
+            best = ob[u];
+            bl = oi[u];
+          }
       }
       if (bl >= p.k) bl = 0;  // only reachable when every distance is +inf or NaN
       bool ch = false;

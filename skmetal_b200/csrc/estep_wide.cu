@@ -197,6 +197,7 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
   tc::tc_fence_after();
   const uint32_t tmem_base = misc[0];
   const float negscale = -ldexpf(1.0f, 1 - __ldcg(p.sexp) - __ldcg(p.sexp + 1));
+  const unsigned long long s2 = tc::pack_pair(__float_as_uint(negscale), __float_as_uint(negscale));
 
   if (warp == PROD_X_W) {
     // ------------------------------------------------------------ X tiles
@@ -304,46 +305,16 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
         tc::tc_fence_after();
         const uint32_t taddr = tmem_base + lane_off + (uint32_t)(a * p.nbs);
         const float* bias_b = bias_s + b * p.nbs;
-        // four independent running minima (columns j = 4 t + w), merged in index order
-        float bd[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
-        int bi[4] = {0x7fffffff, 0x7fffffff, 0x7fffffff, 0x7fffffff};
-        // 64 columns per wait: four loads in flight together (wait::ld waits
-        // for every load of the thread, so loads are batched, not pipelined)
-        for (int jb = 0; jb < p.nbs; jb += 64) {
-          uint32_t v[4][16];
-          const int nv = min(4, (p.nbs - jb) >> 4);  // warp-uniform
-          // tcgen05.ld / wait::ld are .sync.aligned: the minima branch per lane
-          __syncwarp();
-          tc::tmem_ld16(taddr + (uint32_t)jb, v[0]);
-          if (nv > 1) tc::tmem_ld16(taddr + (uint32_t)(jb + 16), v[1]);
-          if (nv > 2) tc::tmem_ld16(taddr + (uint32_t)(jb + 32), v[2]);
-          if (nv > 3) tc::tmem_ld16(taddr + (uint32_t)(jb + 48), v[3]);
-          tc::tmem_ld_wait16(v[0]);
-          tc::reg_pin16(v[1]);
-          tc::reg_pin16(v[2]);
-          tc::reg_pin16(v[3]);
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (t >= nv) break;
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int j = jb + 16 * t + jj;
-              const float dist = fmaf(__uint_as_float(v[t][jj]), negscale, bias_b[j]);
-              // branch-free strict '<' (a NaN distance never wins)
-              bi[jj & 3] = dist < bd[jj & 3] ? b * p.nbs + j : bi[jj & 3];
-              bd[jj & 3] = fminf(dist, bd[jj & 3]);
-            }
-          }
-        }
+        float bb;
+        int bj;
+        tc::scan_row4_n(p.nbs >> 4, taddr, bias_b, s2, bb, bj);
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(AE(a)));
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (tc::better(bd[t], bi[t], best, bl)) {
-            best = bd[t];
-            bl = bi[t];
-          }
+        if (bj != 0x7fffffff && tc::better(bb, b * p.nbs + bj, best, bl)) {
+          best = bb;
+          bl = b * p.nbs + bj;
+        }
       }
       if (!ok) break;
       // merge the two groups' minima of this tile (index order: better())

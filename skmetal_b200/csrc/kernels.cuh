@@ -66,6 +66,12 @@ __host__ __device__ inline size_t mstep_smem_bytes(int k, int ld) {
 }
 
 
+// k-means++ seeding (kmeanspp.cu)
+size_t kmeanspp_scratch_bytes(long long n, int T);
+int kmeanspp_device(const float* X, int ld, long long n, int d, int k, const float* mean, const float* w,
+                    long long first, const double* u, int T, void* scratch, float* centers, long long* indices,
+                    cudaStream_t s);
+
 struct MStepArgs {
   FitState* st;
   const float* X;       // blocked layout (xblk_index)

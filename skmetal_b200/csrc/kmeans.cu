@@ -722,6 +722,74 @@ static int stage_xc(DevBuffers& buf, const float* X, const float* C, long long n
 
 // After the stream has been synchronised: ERR_INVALID when X or C held NaN
 // or infinity (their max |x| words, copied back into mx).
+// Exact column mean of n raw rows into mean (ld entries, float32): the
+// fixed-point column sums of run_fit's single-GPU prologue, so that a seeding
+// centres X exactly as the fit that follows does.
+static int exact_mean(const float* raw, int ld, long long n, int d, float* mean, DevBuffers& buf, cudaStream_t s) {
+  unsigned int* mx = nullptr;
+  double* scale = nullptr;
+  long long* colsum = nullptr;
+  SKM_TRY(buf.alloc_n(&mx, 1));
+  SKM_TRY(buf.alloc_n(&scale, 1));
+  SKM_TRY(buf.alloc_n(&colsum, (size_t)ld));
+  SKM_CUDA(cudaMemsetAsync(mx, 0, sizeof(unsigned int), s));
+  SKM_CUDA(cudaMemsetAsync(colsum, 0, sizeof(long long) * ld, s));
+  SKM_CUDA(cudaMemsetAsync(mean, 0, sizeof(float) * ld, s));
+  maxabs_kernel<<<blocks_for(n * ld / 4, 256, 8), 256, 0, s>>>(raw, ld, n, d, mx);
+  SKM_TRY(check_launch("maxabs_kernel"));
+  scale_kernel<<<1, 32, 0, s>>>(mx, (double)n, scale);
+  SKM_TRY(check_launch("scale_kernel"));
+  const int q = ld / 4;
+  const int threads = q <= 1024 ? q * std::max(1, 256 / q) : 1024;
+  colsum_fixed_kernel<<<sm_count() * 2, threads, sizeof(long long) * ld, s>>>(raw, ld, n, d, scale, colsum);
+  SKM_TRY(check_launch("colsum_fixed_kernel"));
+  mean_from_colsum_kernel<<<1, 256, 0, s>>>(colsum, d, scale, (double)n, mean);
+  SKM_TRY(check_launch("mean_from_colsum_kernel"));
+  return OK;
+}
+
+// k-means++ seeding of device rows (raw, stride ld): host weights (nullable)
+// and uniforms ((k - 1) x T) in, host centres (k x d, raw rows) and indices out.
+static int plusplus_rows(const float* Xd, int ld, long long n, int d, size_t k, const float* sample_weight,
+                         int64_t first_index, const double* uniforms, size_t n_local_trials, int center,
+                         float* centers_out, int64_t* indices_out, cudaStream_t s) {
+  SKM_TRY(validate(n, d, (long long)k));
+  if ((long long)k > n || n_local_trials < 1 || n_local_trials > 16 || first_index < 0 || first_index >= n ||
+      (k > 1 && uniforms == nullptr) || centers_out == nullptr || indices_out == nullptr) {
+    set_error(ERR_INVALID, "kmeans_plusplus: invalid arguments (k=%zu, n=%lld, n_local_trials=%zu, first=%lld)", k, n,
+              n_local_trials, (long long)first_index);
+    return ERR_INVALID;
+  }
+  DevBuffers buf(s);
+  float* mean = nullptr;
+  if (center) {
+    SKM_TRY(buf.alloc_n(&mean, (size_t)ld));
+    SKM_TRY(exact_mean(Xd, ld, n, d, mean, buf, s));
+  }
+  float* w = nullptr;
+  if (sample_weight) {
+    SKM_TRY(buf.alloc_n(&w, (size_t)n));
+    SKM_CUDA(cudaMemcpyAsync(w, sample_weight, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+  }
+  const int T = (int)n_local_trials;
+  double* u = nullptr;
+  if (k > 1) {
+    SKM_TRY(buf.alloc_n(&u, (k - 1) * (size_t)T));
+    SKM_CUDA(cudaMemcpyAsync(u, uniforms, sizeof(double) * (k - 1) * T, cudaMemcpyHostToDevice, s));
+  }
+  void* scratch = nullptr;
+  SKM_TRY(buf.alloc(&scratch, kmeanspp_scratch_bytes(n, T)));
+  float* cen = nullptr;
+  long long* idx = nullptr;
+  SKM_TRY(buf.alloc_n(&cen, k * (size_t)d));
+  SKM_TRY(buf.alloc_n(&idx, k));
+  SKM_TRY(kmeanspp_device(Xd, ld, n, d, (int)k, mean, w, first_index, u, T, scratch, cen, idx, s));
+  SKM_CUDA(cudaMemcpyAsync(centers_out, cen, sizeof(float) * k * d, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaMemcpyAsync(indices_out, idx, sizeof(long long) * k, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
+  return OK;
+}
+
 static int check_finite(const unsigned int* mx, const char* what) {
   if ((mx[0] & 0x7fffffffu) >= 0x7f800000u || (mx[1] & 0x7fffffffu) >= 0x7f800000u) {
     set_error(ERR_INVALID, "%s: %s contains NaN or infinity", what,
@@ -1060,6 +1128,37 @@ int skmetal_kmeans_predict_dataset(void* handle, const float* centroids, size_t 
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   return OK;
+}
+
+int skmetal_kmeans_plusplus(const float* X, size_t n, size_t d, size_t k, const float* sample_weight,
+                            int64_t first_index, const double* uniforms, size_t n_local_trials, int center,
+                            float* centers_out, int64_t* indices_out) {
+  SKM_TRY(check_injected("kmeans_plusplus"));
+  SKM_TRY(validate((long long)n, (long long)d, (long long)k));
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  DevBuffers buf(s);
+  const int ld = ld_of((int)d);
+  float* Xd = nullptr;
+  SKM_TRY(buf.alloc_n(&Xd, n * (size_t)ld));
+  SKM_TRY(upload_rows(Xd, ld, X, (long long)n, (int)d, s));
+  return plusplus_rows(Xd, ld, (long long)n, (int)d, k, sample_weight, first_index, uniforms, n_local_trials, center,
+                       centers_out, indices_out, s);
+}
+
+int skmetal_dataset_kmeans_plusplus(void* handle, size_t k, const float* sample_weight, int64_t first_index,
+                                    const double* uniforms, size_t n_local_trials, int center, float* centers_out,
+                                    int64_t* indices_out) {
+  SKM_TRY(check_injected("dataset_kmeans_plusplus"));
+  Dataset* ds = static_cast<Dataset*>(handle);
+  if (!ds) {
+    set_error(ERR_INVALID, "dataset_kmeans_plusplus: null dataset");
+    return ERR_INVALID;
+  }
+  cudaStream_t s;
+  SKM_TRY(thread_stream(&s, nullptr));
+  return plusplus_rows(ds->X, ds->ld, ds->n, ds->d, k, sample_weight, first_index, uniforms, n_local_trials, center,
+                       centers_out, indices_out, s);
 }
 
 int skmetal_debug_loop_stamps(uint64_t* out, int cap) {

@@ -4,10 +4,12 @@ Replaces ``MetalKMeans`` of the reference (``skmetal/estimators/cluster.py:18-14
 with scikit-learn's ``KMeans.fit`` semantics (``sklearn/cluster/_kmeans.py:1436-1562``)
 run on the CUDA library:
 
-* the init is honoured: an explicit array is used as given; ``"k-means++"``,
-  ``"random"`` and callables are drawn with scikit-learn's own initialisation
-  routine and random stream, so a fixed ``random_state`` yields the same
-  initial centres as scikit-learn;
+* the init is honoured: an explicit array is used as given; ``"k-means++"``
+  is seeded on the GPU (scikit-learn's greedy k-means++ on the centred rows,
+  drawing from the same random stream in the same order; the cumulative
+  sums and potentials are float64 where scikit-learn's are float32, so on
+  large inputs a candidate row can differ); ``"random"`` and callables are
+  drawn with scikit-learn's own initialisation routine and random stream;
 * ``n_init`` restarts keep scikit-learn's best-run rule (lower inertia and
   not the same clustering up to a permutation);
 * the Lloyd loop, the final E-step, the inertia, ``predict``, ``transform``,
@@ -109,8 +111,10 @@ class MetalKMeans(BaseGPUEstimator):
                               f"KMeans instead of n_init={n_init}.", RuntimeWarning, stacklevel=2)
                 n_init = 1
         random_state = check_random_state(est.random_state)
+        if isinstance(init, str) and init == "k-means++":
+            return self._fit_plusplus(X, k, n_init, random_state, t0=time.perf_counter())
 
-        # scikit-learn draws non-array inits on the centred data
+        # scikit-learn draws the other non-array inits on the centred data
         Xc = x_sq = mean = None
         if not init_is_array:
             mean = X.mean(axis=0)
@@ -131,6 +135,32 @@ class MetalKMeans(BaseGPUEstimator):
                 _bridge.kmeans_fit, X, centers_init, int(est.max_iter), float(est.tol), center=True)
             if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
                 best = (centers, labels, inertia, n_iter)
+        self._finish_fit(best, n, d, k, n_init, t0)
+        return self
+
+    def _fit_plusplus(self, X, k, n_init, random_state, t0):
+        """init="k-means++": every restart seeds on the GPU (scikit-learn's
+        greedy k-means++ on the centred rows, drawing from ``random_state`` in
+        scikit-learn's order) and fits from there; X is uploaded once."""
+        est = self._estimator
+        n, d = X.shape
+        ds = _gpu_call(_bridge.Dataset, X)
+        try:
+            best = None
+            for _ in range(n_init):
+                centers_init, _ = _gpu_call(_bridge.kmeans_plusplus, ds, k, random_state)
+                labels = np.empty(n, dtype=np.int32)
+                centers, inertia, n_iter = _gpu_call(ds.fit, centers_init, int(est.max_iter), float(est.tol),
+                                                     labels_out=labels)
+                if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
+                    best = (centers, labels, inertia, n_iter)
+        finally:
+            ds.close()
+        self._finish_fit(best, n, d, k, n_init, t0)
+        return self
+
+    def _finish_fit(self, best, n, d, k, n_init, t0):
+        est = self._estimator
         centers, labels, inertia, n_iter = best
 
         distinct = int(np.count_nonzero(np.bincount(labels, minlength=k)))
@@ -154,7 +184,6 @@ class MetalKMeans(BaseGPUEstimator):
             print(f"[skmetal] KMeans: {n}x{d} k={k} n_init={n_init} n_iter={n_iter} "
                   f"wall={time.perf_counter() - t0:.4f}s gpu_loop={st['ms_loop']:.3f}ms "
                   f"({st['ms_loop'] / max(1, st['iterations']):.4f} ms/iter)")
-        return self
 
     # ------------------------------------------------------------------ inference
     def _centers(self):

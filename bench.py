@@ -393,9 +393,13 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    last_fit = {}
+
     def step(profile):
         if fit:
-            return ds.fit(init, w.max_iter, 0.0, profile=profile, shard=shard)[2]
+            c, _, n_it = ds.fit(init, w.max_iter, 0.0, profile=profile, shard=shard)
+            last_fit["c"], last_fit["n_iter"] = c, n_it
+            return n_it
         ds.predict(init, labels)
         return 1
 
@@ -435,6 +439,18 @@ def main():
     t_dev = ms_total / 1e3
     if dist is not None:
         t_dev, wall = max_over_ranks(dist, [t_dev, wall], device="cuda")
+    ranks_agree = None
+    if dist is not None and fit:
+        # a sharded fit returns the same centres and n_iter on every rank (the
+        # sums are exact integers): compare a hash of them across ranks
+        import hashlib
+
+        h = hashlib.sha256(last_fit["c"].tobytes() + int(last_fit["n_iter"]).to_bytes(4, "little")).digest()
+        hv = torch.tensor([int.from_bytes(h[:7], "little")], dtype=torch.int64, device="cuda")
+        hmin, hmax = hv.clone(), hv.clone()
+        dist.all_reduce(hmin, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hmax, op=dist.ReduceOp.MAX)
+        ranks_agree = bool(hmin.item() == hmax.item())
     units = n_total * iters  # every rank ran the same iterations over its shard
     value = units / t_dev
     unit = UNIT_FIT if fit else UNIT_PREDICT
@@ -547,6 +563,7 @@ def main():
                 if world == 1 or not fit else "skmetal_kmeans_fit_shard (C ABI, per rank)"},
         "e2e_pinned": {"value": e2e_pinned, "unit": unit, "host_memory": "page-locked"},
         "gpu_launches": int(launches),
+        "ranks_agree": ranks_agree,
         "roofline": roofline,
         "phases": phases,
         "clocks": clk,

@@ -141,9 +141,26 @@ static int peer_region_exchange(Comm* c, unsigned char* dev, cudaStream_t s) {
   static_assert(hb == 64, "IPC handle size");
   unsigned int* word = reinterpret_cast<unsigned int*>(dev + hb * (c->nranks + 1));
   unsigned int bad = c->nranks > kMaxPeerRanks ? 1u : 0u;
+  // every rank's GPU by PCI bus id (gathered into dev), mapped to this
+  // process's device ordinals: a peer whose GPU this process cannot see (its
+  // own CUDA_VISIBLE_DEVICES, another host) has no peer access
+  constexpr size_t bid = 16;
+  char mine[bid] = {};
+  if (cudaDeviceGetPCIBusId(mine, (int)bid, c->device) != cudaSuccess) bad = 1;
+  cudaGetLastError();
+  SKM_CUDA(cudaMemcpyAsync(dev + bid * c->nranks, mine, bid, cudaMemcpyHostToDevice, s));
+  SKM_TRY(comm_allgather_bytes(c, dev + bid * c->nranks, dev, bid, s));
+  std::vector<char> ids(bid * c->nranks);
+  SKM_CUDA(cudaMemcpyAsync(ids.data(), dev, bid * c->nranks, cudaMemcpyDeviceToHost, s));
+  SKM_CUDA(cudaStreamSynchronize(s));
   for (int r = 0; r < c->nranks && !bad; ++r) {
-    int can = 0;
-    if (r != c->rank && (cudaDeviceCanAccessPeer(&can, c->device, r) != cudaSuccess || !can)) bad = 1;
+    if (r == c->rank) continue;
+    char id[bid + 1] = {};
+    memcpy(id, ids.data() + bid * r, bid);
+    int dev_r = -1, can = 0;
+    if (cudaDeviceGetByPCIBusId(&dev_r, id) != cudaSuccess || dev_r == c->device ||
+        cudaDeviceCanAccessPeer(&can, c->device, dev_r) != cudaSuccess || !can)
+      bad = 1;
   }
   cudaIpcMemHandle_t h{};
   if (!bad && cudaMalloc(&c->region, kPeerRegionBytes) != cudaSuccess) bad = 1;

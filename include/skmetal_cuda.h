@@ -127,6 +127,24 @@ int skmetal_kmeans_fit(const float* X, size_t n, size_t d, size_t k, const float
                        uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
                        int32_t* n_iter_out);
 
+/* skmetal_kmeans_fit with sample weights (KMeans.fit(X, sample_weight=...),
+ * reached through skmetal/estimators/cluster.py:20-65 and scikit-learn's
+ * weighted Lloyd, sklearn/cluster/_k_means_lloyd.pyx _update_chunk_dense and
+ * _k_means_common.pyx _relocate_empty_clusters_dense): a row adds its values
+ * times its weight (float32 products) to its cluster's sum and its weight to
+ * the cluster's weight, a cluster of weight zero is empty, and the inertia is
+ * weighted. sample_weight: n finite, non-negative host floats (not all zero),
+ * or NULL for unit weights. One GPU only. */
+int skmetal_kmeans_fit_weighted(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter,
+                                double tol, uint32_t flags, const float* sample_weight, float* centers_out,
+                                int32_t* labels_out, double* inertia_out, int32_t* n_iter_out);
+
+/* skmetal_kmeans_inertia with sample weights: sum_i w_i ||x_i - c_{labels[i]}||^2
+ * (KMeans.score(X, sample_weight=...), sklearn/cluster/_k_means_common.pyx
+ * _inertia_dense); returns -1.0f on error. */
+float skmetal_kmeans_inertia_weighted(const float* X, const float* centroids, const uint32_t* labels,
+                                      const float* sample_weight, size_t n, size_t d, size_t k);
+
 /* One E+M step of sklearn's lloyd_iter_chunked_dense
  * (sklearn/cluster/_k_means_lloyd.pyx:23-165, update_centers=True) on X as
  * given: labels_out gets the E-step labels against centers_old, centers_new
@@ -151,6 +169,11 @@ int skmetal_dataset_free(void* handle);
 int skmetal_kmeans_fit_dataset(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
                                uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
                                int32_t* n_iter_out);
+
+/* skmetal_kmeans_fit_weighted on a resident dataset. */
+int skmetal_dataset_fit_weighted(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
+                                 uint32_t flags, const float* sample_weight, float* centers_out, int32_t* labels_out,
+                                 double* inertia_out, int32_t* n_iter_out);
 
 /* Predict on a resident dataset: labels_out (host, may be NULL to keep the
  * labels on the device). */

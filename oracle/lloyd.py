@@ -121,7 +121,7 @@ class LloydStep:
 
 
 def lloyd_iter(X: np.ndarray, centers_old: np.ndarray, mode: str = "fp32",
-               relocation_order: str = "argpartition") -> LloydStep:
+               relocation_order: str = "argpartition", sample_weight: np.ndarray | None = None) -> LloydStep:
     """One E+M step of ``lloyd_iter_chunked_dense`` on already-centred X.
 
     ``relocation_order`` selects how the farthest points are paired with the
@@ -129,6 +129,13 @@ def lloyd_iter(X: np.ndarray, centers_old: np.ndarray, mode: str = "fp32",
     (``_k_means_common.pyx:186-187``), whose order among the farthest points is
     left unspecified by numpy; ``"sorted"`` pairs them by decreasing distance,
     ties to the lower row index (the order the CUDA path uses).
+
+    With ``sample_weight`` (float32, one per row) a row adds ``x * w`` (the
+    float32 product, ``_k_means_lloyd.pyx:_update_chunk_dense``) to its
+    cluster's sum and ``w`` to its weight; a cluster of weight 0 is empty, and
+    a relocated row carries its weighted values and its weight
+    (``_k_means_common.pyx:_relocate_empty_clusters_dense``). ``counts`` stays
+    the number of rows per cluster.
     """
     X = np.asarray(X, dtype=np.float32)
     centers_old = np.asarray(centers_old, dtype=np.float32)
@@ -136,12 +143,18 @@ def lloyd_iter(X: np.ndarray, centers_old: np.ndarray, mode: str = "fp32",
     labels, _ = assign(X, centers_old, mode)
     counts = np.bincount(labels, minlength=k).astype(np.int64)
     acc = np.float32 if mode == "fp32" else np.float64
+    if sample_weight is None:
+        w = np.ones(X.shape[0], dtype=np.float32)
+        Xw = X
+    else:
+        w = np.asarray(sample_weight, dtype=np.float32)
+        Xw = X * w[:, None]  # float32 products
     sums = np.zeros((k, d), dtype=np.float64)
-    np.add.at(sums, labels, X.astype(np.float64))
+    np.add.at(sums, labels, Xw.astype(np.float64))
     sums = sums.astype(acc)
-    weight = counts.astype(acc)
+    weight = np.bincount(labels, weights=w.astype(np.float64), minlength=k).astype(acc)
 
-    empty = np.where(counts == 0)[0].astype(np.int32)
+    empty = np.where(weight == 0)[0].astype(np.int32)
     far = np.zeros(0, dtype=np.int64)
     if empty.size:
         dist = ((X - centers_old[labels]) ** 2).sum(axis=1)  # float32, as the reference
@@ -154,10 +167,10 @@ def lloyd_iter(X: np.ndarray, centers_old: np.ndarray, mode: str = "fp32",
                 far = order[:m]
             for new_id, fi in zip(empty, far):
                 old_id = labels[fi]
-                sums[old_id] -= X[fi].astype(acc)
-                sums[new_id] = X[fi].astype(acc)
-                weight[new_id] = 1
-                weight[old_id] -= 1
+                sums[old_id] -= Xw[fi].astype(acc)
+                sums[new_id] = Xw[fi].astype(acc)
+                weight[new_id] = w[fi]
+                weight[old_id] -= w[fi]
         else:
             empty = np.zeros(0, dtype=np.int32)
 
@@ -174,11 +187,15 @@ def lloyd_iter(X: np.ndarray, centers_old: np.ndarray, mode: str = "fp32",
     return LloydStep(labels, centers_new, weight.astype(np.float32), shift, counts, empty, np.asarray(far))
 
 
-def inertia(X: np.ndarray, C: np.ndarray, labels: np.ndarray, mode: str = "fp64") -> float:
-    """Sum of squared direct differences to the assigned centre (``_k_means_common.pyx:94-124``)."""
+def inertia(X: np.ndarray, C: np.ndarray, labels: np.ndarray, mode: str = "fp64",
+            sample_weight: np.ndarray | None = None) -> float:
+    """Sum of (weighted) squared direct differences to the assigned centre
+    (``_k_means_common.pyx:94-124``)."""
     dt = np.float32 if mode == "fp32" else np.float64
     diff = X.astype(dt) - C.astype(dt)[labels]
-    return float(np.einsum("ij,ij->", diff, diff))
+    if sample_weight is None:
+        return float(np.einsum("ij,ij->", diff, diff))
+    return float(np.einsum("ij,ij->i", diff, diff) @ np.asarray(sample_weight, dtype=dt))
 
 
 @dataclass
@@ -193,7 +210,7 @@ class LloydResult:
 
 def kmeans_lloyd(X: np.ndarray, init: np.ndarray, max_iter: int = 300, tol: float = 1e-4,
                  mode: str = "fp32", relocation_order: str = "argpartition",
-                 keep_centers: bool = False) -> LloydResult:
+                 keep_centers: bool = False, sample_weight: np.ndarray | None = None) -> LloydResult:
     """Full ``KMeans(algorithm="lloyd", n_init=1, init=array).fit`` restated.
 
     Follows ``_kmeans.py:1487-1496`` (centring) and ``:705-758`` (loop).
@@ -206,7 +223,7 @@ def kmeans_lloyd(X: np.ndarray, init: np.ndarray, max_iter: int = 300, tol: floa
     strict = False
     i = 0
     for i in range(max_iter):
-        step = lloyd_iter(Xc, centers, mode, relocation_order)
+        step = lloyd_iter(Xc, centers, mode, relocation_order, sample_weight)
         n_changed = int(np.count_nonzero(step.labels != labels_old))
         rec = {"n_changed": n_changed, "n_empty": int(step.empty.size),
                "shift_tot": float((step.center_shift.astype(np.float64) ** 2).sum())}
@@ -226,5 +243,5 @@ def kmeans_lloyd(X: np.ndarray, init: np.ndarray, max_iter: int = 300, tol: floa
         labels_old = labels
     if not strict:
         labels, _ = assign(Xc, centers, mode)
-    inert = inertia(Xc, centers, labels, "fp64")
+    inert = inertia(Xc, centers, labels, "fp64", sample_weight)
     return LloydResult(labels, inert, (centers + mean).astype(np.float32), i + 1, strict, history)

@@ -23,6 +23,7 @@ import numpy as np
 __all__ = [
     "CUDA_AVAILABLE", "GPU_AVAILABLE", "METAL_AVAILABLE", "LIB_PATH",
     "ensure_warmed_up", "kmeans_assign", "kmeans_batch_fused", "compute_mindists", "kmeans_inertia",
+    "kmeans_inertia_weighted",
     "row_norm_sq", "pairwise_distance", "kmeans_plusplus", "kmeans_fit", "kmeans_lloyd_iter", "kmeans_transform", "Dataset", "last_fit_stats",
     "launch_count", "device_info", "device_count", "is_loaded", "set_device", "comm_unique_id", "comm_init",
     "comm_destroy", "kmeans_fit_shard", "debug_inject_failure", "debug_loop_stamps", "FIT_CENTER", "FIT_SIMT", "FIT_PROFILE",
@@ -68,6 +69,13 @@ _SIGNATURES = [
     ("skmetal_kmeans_lloyd_iter", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                            _c_size_t, _c_size_t, _c_size_t]),
     ("skmetal_kmeans_transform", _c_int, [_c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_size_t, _c_size_t]),
+    ("skmetal_kmeans_fit_weighted", _c_int, [_c_void_p, _c_size_t, _c_size_t, _c_size_t, _c_void_p, _c_i32,
+                                             _c_double, _c_u32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                             _c_void_p]),
+    ("skmetal_kmeans_inertia_weighted", _c_float, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t,
+                                                   _c_size_t, _c_size_t]),
+    ("skmetal_dataset_fit_weighted", _c_int, [_c_void_p, _c_void_p, _c_size_t, _c_i32, _c_double, _c_u32,
+                                              _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     ("skmetal_kmeans_plusplus", _c_int, [_c_void_p, _c_size_t, _c_size_t, _c_size_t, _c_void_p, ctypes.c_int64,
                                          _c_void_p, _c_size_t, _c_int, _c_void_p, _c_void_p]),
     ("skmetal_dataset_kmeans_plusplus", _c_int, [_c_void_p, _c_size_t, _c_void_p, ctypes.c_int64, _c_void_p,
@@ -295,6 +303,18 @@ def kmeans_inertia(X, centroids, assignments, n: int, d: int, k: int) -> float:
     return float(v)
 
 
+def kmeans_inertia_weighted(X, centroids, assignments, sample_weight, n: int, d: int, k: int) -> float:
+    """Weighted sum of squared distances to the assigned centres."""
+    _f32c(X, "X"), _f32c(centroids, "centroids"), _lab32(assignments), _f32c(sample_weight, "sample_weight")
+    f = _fn("skmetal_kmeans_inertia_weighted")
+    ensure_warmed_up()
+    v = f(X.ctypes.data, centroids.ctypes.data, assignments.ctypes.data, sample_weight.ctypes.data, int(n), int(d),
+          int(k))
+    if v < 0:
+        raise RuntimeError(f"skmetal_kmeans_inertia_weighted failed: {_last_error()}")
+    return float(v)
+
+
 def row_norm_sq(X) -> np.ndarray:
     X = _f32c(X, "X")
     out = np.empty(X.shape[0], dtype=np.float32)
@@ -358,7 +378,8 @@ def pairwise_distance(X: np.ndarray) -> np.ndarray:
 # ----------------------------------------------------------------------------
 
 def kmeans_fit(X, init, max_iter: int, tol: float, *, center: bool = True, tol_abs: bool = False,
-               simt: bool = False, profile: bool = False, want_labels: bool = True, bulk_sums: bool = False):
+               simt: bool = False, profile: bool = False, want_labels: bool = True, bulk_sums: bool = False,
+               sample_weight=None):
     """One Lloyd run from ``init`` (KMeans.fit semantics with n_init=1).
 
     Returns ``(centers, labels, inertia, n_iter)``; ``labels`` is None when
@@ -376,9 +397,17 @@ def kmeans_fit(X, init, max_iter: int, tol: float, *, center: bool = True, tol_a
     n_iter = _c_i32(0)
     flags = (FIT_CENTER if center else 0) | (FIT_TOL_ABS if tol_abs else 0) | (FIT_SIMT if simt else 0) \
         | (FIT_PROFILE if profile else 0) | (FIT_BULK_SUMS if bulk_sums else 0)
-    _bridge_call("skmetal_kmeans_fit", X, int(n), int(d), int(k), init, _c_i32(int(max_iter)), _c_double(tol),
-                 _c_u32(flags), centers, labels if labels is not None else None, ctypes.byref(inertia),
-                 ctypes.byref(n_iter))
+    if sample_weight is None:
+        _bridge_call("skmetal_kmeans_fit", X, int(n), int(d), int(k), init, _c_i32(int(max_iter)), _c_double(tol),
+                     _c_u32(flags), centers, labels if labels is not None else None, ctypes.byref(inertia),
+                     ctypes.byref(n_iter))
+    else:
+        w = _f32c(sample_weight, "sample_weight")
+        if w.shape != (n,):
+            raise ValueError(f"sample_weight has shape {w.shape}, expected ({n},)")
+        _bridge_call("skmetal_kmeans_fit_weighted", X, int(n), int(d), int(k), init, _c_i32(int(max_iter)),
+                     _c_double(tol), _c_u32(flags), w, centers, labels if labels is not None else None,
+                     ctypes.byref(inertia), ctypes.byref(n_iter))
     return centers, labels, float(inertia.value), int(n_iter.value)
 
 
@@ -431,7 +460,8 @@ class Dataset:
             pass
 
     def fit(self, init, max_iter: int, tol: float, *, center: bool = True, tol_abs: bool = False,
-            simt: bool = False, profile: bool = False, labels_out=None, shard: tuple | None = None):
+            simt: bool = False, profile: bool = False, labels_out=None, shard: tuple | None = None,
+            sample_weight=None):
         """Fit on the resident rows; ``shard=(row_base, n_total)`` for a distributed fit."""
         init = _f32c(init, "init")
         k = init.shape[0]
@@ -442,7 +472,16 @@ class Dataset:
             | (FIT_PROFILE if profile else 0)
         if labels_out is not None:
             _lab32(labels_out)
-        if shard is None:
+        if sample_weight is not None:
+            if shard is not None:
+                raise ValueError("sample weights are supported on one GPU only")
+            w = _f32c(sample_weight, "sample_weight")
+            if w.shape != (self.n,):
+                raise ValueError(f"sample_weight has shape {w.shape}, expected ({self.n},)")
+            _bridge_call("skmetal_dataset_fit_weighted", self._h, init, int(k), _c_i32(int(max_iter)),
+                         _c_double(tol), _c_u32(flags), w, centers, labels_out, ctypes.byref(inertia),
+                         ctypes.byref(n_iter))
+        elif shard is None:
             _bridge_call("skmetal_kmeans_fit_dataset", self._h, init, int(k), _c_i32(int(max_iter)),
                          _c_double(tol), _c_u32(flags), centers, labels_out, ctypes.byref(inertia),
                          ctypes.byref(n_iter))

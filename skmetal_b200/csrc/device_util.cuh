@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "skm.cuh"
+
 namespace skm {
 
 // ---------------------------------------------------------------------------
@@ -148,12 +150,12 @@ __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
 // (one float4) and a warp fetches a whole row (ld <= 128) in one round trip.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void quad_delta(const float4& v, int q, int d, long long* __restrict__ dn,
-                                           long long* __restrict__ dold, double scale) {
+                                           long long* __restrict__ dold, double scale, float wr) {
   const float x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int j = 4 * q + u;
-    const long long f = to_fixed(x[u], scale);
+    const long long f = to_fixed(x[u] * wr, scale);  // the float32 product, as the reference's sums take it
     if (j < d && f != 0) {
       red_add_s64(dn + j, f);
       if (dold) red_add_s64(dold + j, -f);
@@ -161,19 +163,24 @@ __device__ __forceinline__ void quad_delta(const float4& v, int q, int d, long l
   }
 }
 
-__device__ __forceinline__ void count_delta(int k, int ld, int old, int neu, long long* __restrict__ D) {
+__device__ __forceinline__ void count_delta(int k, int ld, int old, int neu, long long* __restrict__ D,
+                                            long long cw) {
   long long* cnt = D + (long long)k * ld;
-  red_add_s64(cnt + neu, 1);
-  if (old >= 0) red_add_s64(cnt + old, -1);
+  red_add_s64(cnt + neu, cw);
+  if (old >= 0) red_add_s64(cnt + old, -cw);
 }
 
-// For every lane of the calling warp whose row changed label, apply its delta.
-// Rows are taken two at a time so that both rows' loads are in flight together.
+// For every lane of the calling warp whose row changed label, apply its delta
+// (weighted fits: the row's values times its weight, and its fixed-point
+// weight instead of a count of 1). Rows are taken two at a time so that both
+// rows' loads are in flight together.
 __device__ __forceinline__ void warp_apply_changed(const float* __restrict__ X, int ld, int d, int k, long long row,
                                                    int old, int neu, bool changed, long long* __restrict__ D,
-                                                   double scale) {
+                                                   const FitState* st) {
   const int lane = threadIdx.x & 31;
   const int nq = ld >> 2;
+  const double scale = st->scale;
+  const float* w = st->w;
   unsigned int m = __ballot_sync(0xffffffffu, changed);
   while (m) {
     const int s1 = __ffs(m) - 1;
@@ -190,15 +197,16 @@ __device__ __forceinline__ void warp_apply_changed(const float* __restrict__ X, 
     long long* do1 = o1 >= 0 ? D + (long long)o1 * ld : nullptr;
     long long* dn2 = D + (long long)n2 * ld;
     long long* do2 = o2 >= 0 ? D + (long long)o2 * ld : nullptr;
+    const float w1 = w ? __ldg(w + r1) : 1.0f, w2 = w ? __ldg(w + r2) : 1.0f;
     for (int q = lane; q < nq; q += 32) {
       const float4 v1 = __ldg(x1 + (long long)q * 128);
       const float4 v2 = two ? __ldg(x2 + (long long)q * 128) : v1;
-      quad_delta(v1, q, d, dn1, do1, scale);
-      if (two) quad_delta(v2, q, d, dn2, do2, scale);
+      quad_delta(v1, q, d, dn1, do1, scale, w1);
+      if (two) quad_delta(v2, q, d, dn2, do2, scale, w2);
     }
     if (lane == 0) {
-      count_delta(k, ld, o1, n1, D);
-      if (two) count_delta(k, ld, o2, n2, D);
+      count_delta(k, ld, o1, n1, D, w ? to_fixed(w1, st->wscale) : 1);
+      if (two) count_delta(k, ld, o2, n2, D, w ? to_fixed(w2, st->wscale) : 1);
     }
   }
 }

@@ -702,7 +702,7 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
       if (changed) {
         const unsigned int m = __ballot_sync(0xffffffffu, ch);
         if (lane == 0 && m) atomicAdd(changed, (unsigned long long)__popc(m));
-        if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st->scale);
+        if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st);
       }
     }
   }

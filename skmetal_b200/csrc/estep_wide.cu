@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
         if (p.changed) {
           const unsigned int mk = __ballot_sync(0xffffffffu, ch);
           if (lane == 0 && mk) atomicAdd(p.changed, (unsigned long long)__popc(mk));
-          if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st->scale);
+          if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st);
         }
       }
     }

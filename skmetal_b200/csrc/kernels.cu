@@ -243,7 +243,8 @@ __global__ void scale_kernel(const unsigned int* __restrict__ maxabs_bits, doubl
 // Initialise the fit state. tol_mode 0: `tol` is already absolute; 1: `tol` is
 // relative and is scaled by the mean column variance sumsq / (n_total * d).
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
-                                  double n_total, int d, const unsigned int* maxabs_bits, int bulk_always) {
+                                  double n_total, int d, const unsigned int* maxabs_bits, int bulk_always,
+                                  const float* w, const unsigned int* wmax_bits) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   st->iter = 0;
   st->done = max_iter <= 0;
@@ -269,8 +270,34 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
   st->bulk_threshold = (long long)fmax(1.0, n_total / (double)kBulkDivisor);
   st->xexp = split_exp(*maxabs_bits);
   st->cexp = st->xexp;
-  st->scale = fixed_scale(*maxabs_bits, n_total);
-  st->inv_scale = 1.0 / st->scale;
+  // weighted fits: the sums hold w * x (wmax_bits[0] = max |w x|) and the
+  // cluster weights w (wmax_bits[1] = max w), each with its own scale
+  st->w = w;
+  st->scale = fixed_scale(w ? wmax_bits[0] : *maxabs_bits, n_total);
+  st->wscale = w ? fixed_scale(wmax_bits[1], n_total) : 1.0;
+  st->inv_scale = st->wscale / st->scale;
+}
+
+// max |w_r x_rj| (float32 products, as the sums take them) and max w_r over
+// the rows of the blocked copy, as float bits (non-negative values order as
+// their bits); atomicMax into out[0], out[1]
+__global__ void weight_max_kernel(const float* __restrict__ X, int ld, long long n, const float* __restrict__ w,
+                                  unsigned int* __restrict__ out) {
+  unsigned int mx = 0u, mw = 0u;
+  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)gridDim.x * blockDim.x) {
+    const float wr = w[r];
+    mw = max(mw, __float_as_uint(fabsf(wr)));
+    for (int j = 0; j < ld; ++j) mx = max(mx, __float_as_uint(fabsf(X[xblk_index(r, j, ld)] * wr)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    mw = max(mw, __shfl_xor_sync(0xffffffffu, mw, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(out, mx);
+    atomicMax(out + 1, mw);
+  }
 }
 
 // centres: C[c][j] = init[c][j] - mean[j] for j < d, 0 in the padding
@@ -347,7 +374,7 @@ __global__ void assign_simt_kernel(const float* __restrict__ X, int ld, long lon
   if (changed) {
     const unsigned int b = __ballot_sync(0xffffffffu, ch);
     if ((threadIdx.x & 31) == 0 && b) atomicAdd(changed, (unsigned long long)__popc(b));
-    if (D && !st->bulk) warp_apply_changed(X, ld, d, k, r, old, bl, ch, D, st->scale);
+    if (D && !st->bulk) warp_apply_changed(X, ld, d, k, r, old, bl, ch, D, st);
   }
 }
 
@@ -408,7 +435,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a) {
   if (done) return;
   extern __shared__ __align__(16) long long dyn_smem[];
   if (bulk && !a.bulk_external) {
-    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, reinterpret_cast<unsigned char*>(dyn_smem),
+    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st, reinterpret_cast<unsigned char*>(dyn_smem),
               mstep_smem_bytes(a.k, a.ld), &st->error);
     if (!grid_barrier(st, nb)) return;
   }
@@ -493,7 +520,7 @@ __global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long l
   const int bulk = st->bulk;
   extern __shared__ __align__(16) long long dyn_smem[];
   if (bulk)
-    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st->scale, reinterpret_cast<unsigned char*>(dyn_smem),
+    bulk_pass(a.X, a.ld, a.n, a.labels, a.k, a.D, st, reinterpret_cast<unsigned char*>(dyn_smem),
               mstep_smem_bytes(a.k, a.ld), &st->error);
   if (!grid_barrier(st, nb)) return;
   // local counts after this iteration, and how many clusters this rank has empty
@@ -578,7 +605,7 @@ __global__ void centre_prep_kernel(const float* __restrict__ C, int k, int ld, i
 // a 32-row group, walking the quads (coalesced 512-byte warp loads).
 __global__ void inertia_partial_kernel(const float* __restrict__ X, int ld, long long n, int d,
                                        const float* __restrict__ C, const int32_t* __restrict__ labels,
-                                       double* __restrict__ partial, int blocked) {
+                                       double* __restrict__ partial, int blocked, const float* __restrict__ w) {
   __shared__ double scratch[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   double acc = 0.0;
@@ -589,21 +616,27 @@ __global__ void inertia_partial_kernel(const float* __restrict__ X, int ld, long
       const long long r = it * 32 + lane;
       if (r >= n) continue;
       const float4* xp = X4 + (r >> 7) * (32LL * ld) + (r & 127);
-      const float* cr = C + (long long)labels[r] * ld;
+      const float4* cr = reinterpret_cast<const float4*>(C + (long long)labels[r] * ld);  // ld % 4 == 0
+      // four quads' loads in flight per lane; the sum stays in quad order
+      double rs = 0.0;  // the row's sum, times its weight in weighted fits
+#pragma unroll 4
       for (int q = 0; q < (ld >> 2); ++q) {
         const float4 v = __ldcs(xp + (long long)q * 128);
-        const double t0 = (double)v.x - cr[4 * q], t1 = (double)v.y - cr[4 * q + 1];
-        const double t2 = (double)v.z - cr[4 * q + 2], t3 = (double)v.w - cr[4 * q + 3];
-        acc += t0 * t0 + t1 * t1 + t2 * t2 + t3 * t3;  // padding columns are zero in X and C
+        const float4 c = __ldg(cr + q);
+        const double t0 = (double)v.x - c.x, t1 = (double)v.y - c.y;
+        const double t2 = (double)v.z - c.z, t3 = (double)v.w - c.w;
+        rs += t0 * t0 + t1 * t1 + t2 * t2 + t3 * t3;  // padding columns are zero in X and C
       }
+      acc += w ? (double)w[r] * rs : rs;
     }
   } else {
     for (long long r = (long long)blockIdx.x * nw + warp; r < n; r += (long long)gridDim.x * nw) {
       const float* xr = X + r * ld;
       const float* cr = C + (long long)labels[r] * ld;
+      const double wr = w ? (double)w[r] : 1.0;
       for (int j = lane; j < d; j += 32) {
         const double t = (double)__ldcs(xr + j) - (double)cr[j];
-        acc += t * t;
+        acc += w ? wr * (t * t) : t * t;
       }
     }
   }

@@ -23,15 +23,16 @@ __host__ __device__ inline size_t bulk_acc_bytes(int k, int ld, size_t avail) {
 // blocked X in shared memory with bulk copies, one per 2 KB column-quad block
 // at a stride of 2064 bytes (so that lanes reading consecutive quads of one
 // row hit distinct banks), two tiles in flight. Layout: 2 x [nq quad blocks |
-// 128 labels (int32)], 2 mbarriers, then the sort tables (hist 2 x k, offs
-// k + 1, cur k, rows 128; int32). Usable when each thread owns at most 2
-// (cluster, column quad) pairs and ld <= 128; the labels buffer must hold
-// round_up(n, 128) entries (-1 past n).
+// 128 labels (int32) | 128 weights (float32, copied for weighted fits)], 2
+// mbarriers, then two mask sets. Usable when each thread owns at most 2
+// (cluster, column quad) pairs and ld <= 128; the labels buffer (and the
+// weights of a weighted fit) must hold round_up(n, 128) entries (labels -1
+// past n).
 constexpr int kBulkTileRows = 128;
 constexpr int kBulkMaxPairsPerThread = 2;
 constexpr int kBulkQuadStride = 2064;  // bytes between quad blocks of a staged tile
 __host__ __device__ inline size_t bulk_tile_bytes(int ld) {
-  return (size_t)(ld / 4) * kBulkQuadStride + 4 * kBulkTileRows;  // quads, then labels
+  return (size_t)(ld / 4) * kBulkQuadStride + 8 * kBulkTileRows;  // quads, then labels, then weights
 }
 __host__ __device__ inline size_t bulk_tiles_bytes(int k, int ld) {
   return 2 * bulk_tile_bytes(ld) + 16 + 4 * 8 * (size_t)k;  // tiles, barriers, two mask sets
@@ -95,6 +96,7 @@ struct MStepArgs {
   long long* cnt_adj;   // k
   int* reloc_label;     // kMaxEmptyCap
   float* reloc_dist;    // kMaxEmptyCap
+  float* reloc_w;       // kMaxEmptyCap: weights of the relocated rows
   float* reloc_x;       // min(k, kMaxEmptyCap) x ld
   double* shift_partial;  // max(k, gridDim.x) entries
   float* shift_out;       // per-centre shift (nullable)
@@ -121,7 +123,9 @@ __global__ void colsum_fixed_kernel(const float* X, int ld, long long n, int d, 
 __global__ void mean_from_colsum_kernel(const long long* colsum, int d, const double* scale, double n_total, float* mean);
 __global__ void scale_kernel(const unsigned int* maxabs_bits, double n_total, double* out);
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
-                                  double n_total, int d, const unsigned int* maxabs_bits, int bulk_always);
+                                  double n_total, int d, const unsigned int* maxabs_bits, int bulk_always,
+                                  const float* w, const unsigned int* wmax_bits);
+__global__ void weight_max_kernel(const float* X, int ld, long long n, const float* w, unsigned int* out);
 __global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits,
                               double* partial);
 __global__ void sumsq_partial_kernel(const float* X, int ld, long long n, int d, double* partial);
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(1024, 1) mstep_kernel(MStepArgs a);
 __global__ void __launch_bounds__(1024, 1) shard_prep_kernel(MStepArgs a, long long* local_counts, int rank);
 __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* bias, CentreImage ci, FitState* st);
 __global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
-                                       const int32_t* labels, double* partial, int blocked);
+                                       const int32_t* labels, double* partial, int blocked, const float* w);
 __global__ void ordered_sum_kernel(const double* partial, int m, double* out);
 __global__ void mindist_kernel(const float* X, int ld, long long n, int d, const float* C, const int32_t* labels,
                                float* out);

@@ -61,6 +61,7 @@ struct FitParams {
   int d = 0;
   int k = 0;
   const float* init_host = nullptr;  // k x d
+  const float* w_host = nullptr;     // n sample weights (host, nullable: unit weights)
   int max_iter = 300;
   double tol = 0.0;
   bool tol_abs = false;
@@ -198,10 +199,30 @@ static int run_fit(const FitParams& p) {
   int* empty_ids = nullptr;
   long long *sel = nullptr, *cnt_adj = nullptr;
   int* reloc_label = nullptr;
-  float *reloc_dist = nullptr, *reloc_x = nullptr;
+  float *reloc_dist = nullptr, *reloc_x = nullptr, *reloc_w = nullptr;
   const int n_part = nsm * 4;
   const int reloc_rows = std::min(k, kMaxEmptyCap);
 
+  // sample weights: finite and non-negative, not all zero; single-GPU fits
+  if (p.w_host) {
+    if (comm) {
+      set_error(ERR_INVALID, "sample weights are supported on one GPU only");
+      return ERR_INVALID;
+    }
+    double wsum = 0.0;
+    for (long long i = 0; i < n; ++i) {
+      const float wi = p.w_host[i];
+      if (!(wi >= 0.0f) || !std::isfinite(wi)) {
+        set_error(ERR_INVALID, "sample_weight[%lld] = %g: weights must be finite and non-negative", i, (double)wi);
+        return ERR_INVALID;
+      }
+      wsum += wi;
+    }
+    if (!(wsum > 0.0)) {
+      set_error(ERR_INVALID, "sample weights sum to zero");
+      return ERR_INVALID;
+    }
+  }
   // X: the blocked working copy (round_up(n, 128) rows, see xblk_index)
   const long long n_pad = (n + 127) / 128 * 128;
   SKM_TRY(buf.alloc_n(&X, (size_t)n_pad * ld));
@@ -227,13 +248,20 @@ static int run_fit(const FitParams& p) {
   unsigned long long* changed = reinterpret_cast<unsigned long long*>(D + (size_t)k * ld + k);
   SKM_TRY(buf.alloc_n(&colsum, (size_t)ld));
   SKM_TRY(buf.alloc_n(&st, 1));
-  SKM_TRY(buf.alloc_n(&u32s, 2 + 512));
+  SKM_TRY(buf.alloc_n(&u32s, 2 + 512 + 2));  // [514], [515]: max |w x|, max w (weighted fits)
+  float* w_dev = nullptr;  // weighted fits: n_pad weights, 0 past n (the tiled bulk pass copies whole tiles)
+  if (p.w_host) {
+    SKM_TRY(buf.alloc_n(&w_dev, (size_t)n_pad));
+    SKM_CUDA(cudaMemsetAsync(w_dev, 0, sizeof(float) * n_pad, s));
+    SKM_CUDA(cudaMemcpyAsync(w_dev, p.w_host, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+  }
   SKM_TRY(buf.alloc_n(&dscr, 2 + n_part + std::max(nsm, k)));
   SKM_TRY(buf.alloc_n(&empty_ids, kMaxEmptyCap));
   SKM_TRY(buf.alloc_n(&sel, kMaxEmptyCap));
   SKM_TRY(buf.alloc_n(&cnt_adj, (size_t)k));
   SKM_TRY(buf.alloc_n(&reloc_label, kMaxEmptyCap));
   SKM_TRY(buf.alloc_n(&reloc_dist, kMaxEmptyCap));
+  SKM_TRY(buf.alloc_n(&reloc_w, kMaxEmptyCap));
   SKM_TRY(buf.alloc_n(&reloc_x, (size_t)reloc_rows * ld));
   double* scale_mean = dscr;
   double* sumsq = dscr + 1;
@@ -277,7 +305,7 @@ static int run_fit(const FitParams& p) {
     raw = staged;
   }
   SKM_CUDA(cudaMemcpyAsync(init_d, p.init_host, sizeof(float) * (size_t)k * d, cudaMemcpyHostToDevice, s));
-  SKM_CUDA(cudaMemsetAsync(u32s, 0, sizeof(unsigned int) * (2 + 512), s));
+  SKM_CUDA(cudaMemsetAsync(u32s, 0, sizeof(unsigned int) * (2 + 512 + 2), s));
   SKM_CUDA(cudaMemsetAsync(colsum, 0, sizeof(long long) * ld, s));
   SKM_CUDA(cudaMemsetAsync(mean, 0, sizeof(float) * ld, s));
 
@@ -322,8 +350,12 @@ static int run_fit(const FitParams& p) {
     SKM_TRY(check_launch("ordered_sum_kernel"));
     if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, sumsq, 1, s));
   }
+  if (w_dev) {
+    weight_max_kernel<<<n_part, 256, 0, s>>>(X, ld, n, w_dev, &u32s[514]);
+    SKM_TRY(check_launch("weight_max_kernel"));
+  }
   init_state_kernel<<<1, 32, 0, s>>>(st, p.max_iter, p.tol, tol_rel ? 1 : 0, tol_rel ? sumsq : nullptr,
-                                     (double)n_total, d, &u32s[1], p.bulk_sums ? 1 : 0);
+                                     (double)n_total, d, &u32s[1], p.bulk_sums ? 1 : 0, w_dev, &u32s[514]);
   SKM_TRY(check_launch("init_state_kernel"));
   SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n_pad, s));  // label -1: every row changes in iteration 1
   SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));
@@ -381,6 +413,7 @@ static int run_fit(const FitParams& p) {
   ma.reloc_label = reloc_label;
   ma.reloc_dist = reloc_dist;
   ma.reloc_x = reloc_x;
+  ma.reloc_w = reloc_w;
   ma.shift_partial = shift_partial;
   ma.cimg = cimg;
   ma.bias = bias;
@@ -615,7 +648,7 @@ static int run_fit(const FitParams& p) {
       SKM_TRY(launch_assign_simt(X, ld, n, d, Cfin, k, labels, nullptr, nullptr, nullptr, nullptr, 0, 1, s));
     }
   }
-  inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials, 1);
+  inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials, 1, w_dev);
   SKM_TRY(check_launch("inertia_partial_kernel"));
   ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, &dscr[1]);
   SKM_TRY(check_launch("ordered_sum_kernel"));
@@ -799,6 +832,38 @@ static int check_finite(const unsigned int* mx, const char* what) {
   return OK;
 }
 
+static float inertia_common(const float* X, const float* centroids, const uint32_t* labels, const float* sample_weight,
+                            size_t n, size_t d, size_t k) {
+  if (validate((long long)n, (long long)d, (long long)k)) return -1.0f;
+  cudaStream_t s;
+  if (thread_stream(&s, nullptr)) return -1.0f;
+  DevBuffers buf(s);
+  Staged g;
+  if (stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, false, labels, &g, s)) return -1.0f;
+  const int n_part = sm_count() * 4;
+  double* part = nullptr;
+  if (buf.alloc_n(&part, (size_t)n_part + 1)) return -1.0f;
+  float* w = nullptr;
+  if (sample_weight) {
+    if (buf.alloc_n(&w, n)) return -1.0f;
+    if (cudaMemcpyAsync(w, sample_weight, sizeof(float) * n, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1.0f;
+  }
+  inertia_partial_kernel<<<n_part, 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, part, 0, w);
+  if (check_launch("inertia_partial_kernel")) return -1.0f;
+  ordered_sum_kernel<<<1, 32, 0, s>>>(part, n_part, part + n_part);
+  if (check_launch("ordered_sum_kernel")) return -1.0f;
+  double v = 0;
+  unsigned int mx[2];
+  if (cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
+  if (cudaMemcpyAsync(&v, part + n_part, sizeof(double), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
+  if (cudaStreamSynchronize(s) != cudaSuccess) {
+    set_error(ERR_CUDA, "kmeans_inertia: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1.0f;
+  }
+  if (check_finite(mx, "kmeans_inertia")) return -1.0f;
+  return (float)v;
+}
+
 }  // namespace skm
 
 using namespace skm;
@@ -846,29 +911,13 @@ int skmetal_compute_mindists(const float* X, const float* centroids, const uint3
 float skmetal_kmeans_inertia(const float* X, const float* centroids, const uint32_t* labels, size_t n, size_t d,
                              size_t k) {
   if (check_injected("kmeans_inertia")) return -1.0f;
-  if (validate((long long)n, (long long)d, (long long)k)) return -1.0f;
-  cudaStream_t s;
-  if (thread_stream(&s, nullptr)) return -1.0f;
-  DevBuffers buf(s);
-  Staged g;
-  if (stage_xc(buf, X, centroids, (long long)n, (int)d, (int)k, false, labels, &g, s)) return -1.0f;
-  const int n_part = sm_count() * 4;
-  double* part = nullptr;
-  if (buf.alloc_n(&part, (size_t)n_part + 1)) return -1.0f;
-  inertia_partial_kernel<<<n_part, 256, 0, s>>>(g.X, g.ld, (long long)n, (int)d, g.C, g.labels, part, 0);
-  if (check_launch("inertia_partial_kernel")) return -1.0f;
-  ordered_sum_kernel<<<1, 32, 0, s>>>(part, n_part, part + n_part);
-  if (check_launch("ordered_sum_kernel")) return -1.0f;
-  double v = 0;
-  unsigned int mx[2];
-  if (cudaMemcpyAsync(mx, g.maxabs, sizeof(mx), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
-  if (cudaMemcpyAsync(&v, part + n_part, sizeof(double), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1.0f;
-  if (cudaStreamSynchronize(s) != cudaSuccess) {
-    set_error(ERR_CUDA, "kmeans_inertia: %s", cudaGetErrorString(cudaGetLastError()));
-    return -1.0f;
-  }
-  if (check_finite(mx, "kmeans_inertia")) return -1.0f;
-  return (float)v;
+  return inertia_common(X, centroids, labels, nullptr, n, d, k);
+}
+
+float skmetal_kmeans_inertia_weighted(const float* X, const float* centroids, const uint32_t* labels,
+                                      const float* sample_weight, size_t n, size_t d, size_t k) {
+  if (check_injected("kmeans_inertia_weighted")) return -1.0f;
+  return inertia_common(X, centroids, labels, sample_weight, n, d, k);
 }
 
 int skmetal_row_norm_sq(const float* X, float* norms, size_t n, size_t d) {
@@ -936,6 +985,13 @@ int skmetal_kmeans_batch_fused(const float* X, float* centroids, uint32_t* label
 int skmetal_kmeans_fit(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter, double tol,
                        uint32_t flags, float* centers_out, int32_t* labels_out, double* inertia_out,
                        int32_t* n_iter_out) {
+  return skmetal_kmeans_fit_weighted(X, n, d, k, init, max_iter, tol, flags, nullptr, centers_out, labels_out,
+                                     inertia_out, n_iter_out);
+}
+
+int skmetal_kmeans_fit_weighted(const float* X, size_t n, size_t d, size_t k, const float* init, int32_t max_iter,
+                                double tol, uint32_t flags, const float* sample_weight, float* centers_out,
+                                int32_t* labels_out, double* inertia_out, int32_t* n_iter_out) {
   if (flags & SKMETAL_FIT_DISTRIBUTED) {
     set_error(ERR_INVALID, "use skmetal_kmeans_fit_shard for distributed fits");
     return ERR_INVALID;
@@ -946,6 +1002,7 @@ int skmetal_kmeans_fit(const float* X, size_t n, size_t d, size_t k, const float
   p.d = (int)d;
   p.k = (int)k;
   p.init_host = init;
+  p.w_host = sample_weight;
   p.max_iter = max_iter;
   p.tol = tol;
   p.tol_abs = (flags & SKMETAL_FIT_TOL_ABS) != 0;
@@ -1047,7 +1104,8 @@ int skmetal_dataset_free(void* handle) {
 
 static int fit_dataset_common(void* handle, const float* init, size_t k, int32_t max_iter, double tol, uint32_t flags,
                               bool distributed, uint64_t row_base, uint64_t n_total, float* centers_out,
-                              int32_t* labels_out, double* inertia_out, int32_t* n_iter_out) {
+                              int32_t* labels_out, double* inertia_out, int32_t* n_iter_out,
+                              const float* sample_weight = nullptr) {
   Dataset* ds = static_cast<Dataset*>(handle);
   if (!ds) {
     set_error(ERR_INVALID, "null dataset handle");
@@ -1059,6 +1117,7 @@ static int fit_dataset_common(void* handle, const float* init, size_t k, int32_t
   p.d = ds->d;
   p.k = (int)k;
   p.init_host = init;
+  p.w_host = sample_weight;
   p.max_iter = max_iter;
   p.tol = tol;
   p.tol_abs = (flags & SKMETAL_FIT_TOL_ABS) != 0;
@@ -1081,6 +1140,13 @@ int skmetal_kmeans_fit_dataset(void* handle, const float* init, size_t k, int32_
                                int32_t* n_iter_out) {
   return fit_dataset_common(handle, init, k, max_iter, tol, flags, false, 0, 0, centers_out, labels_out, inertia_out,
                             n_iter_out);
+}
+
+int skmetal_dataset_fit_weighted(void* handle, const float* init, size_t k, int32_t max_iter, double tol,
+                                 uint32_t flags, const float* sample_weight, float* centers_out, int32_t* labels_out,
+                                 double* inertia_out, int32_t* n_iter_out) {
+  return fit_dataset_common(handle, init, k, max_iter, tol, flags, false, 0, 0, centers_out, labels_out, inertia_out,
+                            n_iter_out, sample_weight);
 }
 
 int skmetal_dataset_fit_shard(void* handle, const float* init, size_t k, int32_t max_iter, double tol,

@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(tc::THREADS, 1) lloyd_loop_kernel(LoopArgs la)
     a.C_new = C_new;
     a.host_done = nullptr;
     if (bulk) {
-      bulk_pass(p.X, ld, p.n, p.labels, k, Dp, st->scale, c.base, c.L.bars, &st->error);
+      bulk_pass(p.X, ld, p.n, p.labels, k, Dp, st, c.base, c.L.bars, &st->error);
       zero_stage_padding(p, c);
       proxy_fence_all();
       if (!loop_barrier(st, la.bar, nb * ++n_bar)) break;

@@ -101,7 +101,9 @@ static __device__ double block_ordered_sum(const double* v, int n, double* scrat
 // directly.
 static __device__ void bulk_pass_atomic(const float* __restrict__ X, int ld, long long n,
                                         const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                        double scale, long long* acc) {
+                                        const FitState* st, long long* acc) {
+  const double scale = st->scale;
+  const float* __restrict__ w = st->w;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int rsub = lane & 7, qsub = lane >> 3;
   const int nq = ld >> 2;
@@ -116,13 +118,14 @@ static __device__ void bulk_pass_atomic(const float* __restrict__ X, int ld, lon
     const long long r = b * 8 + rsub;
     const bool valid = r < n;
     const int c = valid ? labels[r] : 0;
+    const float wr = (valid && w) ? w[r] : 1.0f;
     const float4* xr = X4 + (r >> 7) * (32LL * ld) + (r & 127);  // quad q of row r at xr[128 q]
     for (int q0 = 0; q0 < nq; q0 += 4) {
       const int q = q0 + qsub;
       if (!valid || q >= nq) continue;
       const float4 v = __ldcs(xr + (long long)q * 128);
-      const long long f[4] = {to_fixed(v.x, scale), to_fixed(v.y, scale), to_fixed(v.z, scale),
-                              to_fixed(v.w, scale)};
+      const long long f[4] = {to_fixed(v.x * wr, scale), to_fixed(v.y * wr, scale), to_fixed(v.z * wr, scale),
+                              to_fixed(v.w * wr, scale)};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (f[u] == 0) continue;
@@ -134,10 +137,11 @@ static __device__ void bulk_pass_atomic(const float* __restrict__ X, int ld, lon
       }
     }
     if (valid && qsub == 0) {
+      const long long cw = w ? to_fixed(wr, st->wscale) : 1;
       if (acc)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&acc[ks + c]), 1ull);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&acc[ks + c]), static_cast<unsigned long long>(cw));
       else
-        red_add_s64(D + ks + c, 1);
+        red_add_s64(D + ks + c, cw);
     }
   }
   if (acc) {
@@ -172,8 +176,11 @@ static __device__ void bulk_pass_atomic(const float* __restrict__ X, int ld, lon
 // (error 1004 in *err; the pass then stops).
 static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long long n,
                                        const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                       double scale, unsigned char* ws, int* err) {
+                                       const FitState* st, unsigned char* ws, int* err) {
   constexpr int TR = kBulkTileRows;
+  const double scale = st->scale;
+  const float* __restrict__ w = st->w;
+  const double wscale = st->wscale;
   const int nq = ld >> 2;
   const size_t tb = bulk_tile_bytes(ld);
   unsigned char* tile_s[2] = {ws, ws + tb};
@@ -187,7 +194,7 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
   const int T = blockDim.x;
   const int pairs = k * nq;
   const long long n_tiles = (n + TR - 1) / TR;
-  const uint32_t tx = (uint32_t)nq * 2048u + 4u * TR;
+  const uint32_t tx = (uint32_t)nq * 2048u + (w ? 8u : 4u) * TR;
   long long acc[kBulkMaxPairsPerThread][4];
   long long cnt_acc[kBulkMaxPairsPerThread];
 #pragma unroll
@@ -204,9 +211,10 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
     __syncwarp();
     const char* src = reinterpret_cast<const char*>(X + t * TR * ld);
     const uint32_t dst = smem_u32(tile_s[b]);
-    for (int q = lane; q <= nq; q += 32) {
+    for (int q = lane; q <= nq + 1; q += 32) {
       if (q < nq) bulk_load(dst + (uint32_t)q * kBulkQuadStride, src + (size_t)q * 2048, 2048u, bar);
-      else bulk_load(smem_u32(lab_s[b]), labels + t * TR, 4u * TR, bar);
+      else if (q == nq) bulk_load(smem_u32(lab_s[b]), labels + t * TR, 4u * TR, bar);
+      else if (w) bulk_load(smem_u32(lab_s[b] + TR), w + t * TR, 4u * TR, bar);  // weights after the labels
     }
   };
   if (tid == 0) {
@@ -264,16 +272,19 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
       const unsigned char* qb = cb + (size_t)q * kBulkQuadStride;
       const uint4 w4 = *reinterpret_cast<const uint4*>(mk + c * 4);
       const unsigned int wv[4] = {w4.x, w4.y, w4.z, w4.w};
-      if (q == 0) cnt_acc[m] += __popc(wv[0]) + __popc(wv[1]) + __popc(wv[2]) + __popc(wv[3]);
+      const float* wt = reinterpret_cast<const float*>(lab_s[b] + TR);  // the tile's weights (weighted fits)
+      if (q == 0 && !w) cnt_acc[m] += __popc(wv[0]) + __popc(wv[1]) + __popc(wv[2]) + __popc(wv[3]);
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         for (unsigned int bits = wv[g]; bits; bits &= bits - 1) {
           const int r = g * 32 + __ffs(bits) - 1;
           const float4 v = *reinterpret_cast<const float4*>(qb + r * 16);
-          acc[m][0] += to_fixed(v.x, scale);
-          acc[m][1] += to_fixed(v.y, scale);
-          acc[m][2] += to_fixed(v.z, scale);
-          acc[m][3] += to_fixed(v.w, scale);
+          const float wr = w ? wt[r] : 1.0f;
+          acc[m][0] += to_fixed(v.x * wr, scale);
+          acc[m][1] += to_fixed(v.y * wr, scale);
+          acc[m][2] += to_fixed(v.z * wr, scale);
+          acc[m][3] += to_fixed(v.w * wr, scale);
+          if (q == 0 && w) cnt_acc[m] += to_fixed(wr, wscale);
         }
       }
     }
@@ -315,11 +326,11 @@ static __device__ void bulk_pass_tiles(const float* __restrict__ X, int ld, long
 // of every block calls it; `err` receives a code if a wait times out.
 static __device__ __forceinline__ void bulk_pass(const float* __restrict__ X, int ld, long long n,
                                                  const int32_t* __restrict__ labels, int k, long long* __restrict__ D,
-                                                 double scale, unsigned char* ws, size_t ws_bytes, int* err) {
+                                                 const FitState* st, unsigned char* ws, size_t ws_bytes, int* err) {
   if (bulk_tiles_ok(k, ld, blockDim.x, ws_bytes))
-    bulk_pass_tiles(X, ld, n, labels, k, D, scale, ws, err);
+    bulk_pass_tiles(X, ld, n, labels, k, D, st, ws, err);
   else
-    bulk_pass_atomic(X, ld, n, labels, k, D, scale,
+    bulk_pass_atomic(X, ld, n, labels, k, D, st,
                      bulk_acc_bytes(k, ld, ws_bytes) ? reinterpret_cast<long long*>(ws) : nullptr);
 }
 
@@ -436,12 +447,19 @@ static __device__ bool select_farthest(const float* __restrict__ mind, long long
 }
 
 // Averaged centre value of a non-empty cluster c (after relocation), column j.
+// A relocated row carries its weighted values and its weight (weighted fits;
+// unit weights otherwise, where a cluster that receives a row is that row).
 static __device__ __forceinline__ float centre_value(const MStepArgs& a, int c, int j, int n_reloc) {
+  const bool weighted = a.st->w != nullptr;
   for (int i = 0; i < n_reloc; ++i)
-    if (a.empty_ids[i] == c) return a.reloc_x[(long long)i * a.ld + j];  // exactly the far row
+    if (a.empty_ids[i] == c) {
+      if (!weighted) return a.reloc_x[(long long)i * a.ld + j];  // exactly the far row
+      const long long s1 = to_fixed(a.reloc_x[(long long)i * a.ld + j] * a.reloc_w[i], a.st->scale);
+      return centre_from_sum(s1, centre_factor(a.st->inv_scale, a.cnt_adj[c]));
+    }
   long long s = a.S[(long long)c * a.ld + j];
   for (int i = 0; i < n_reloc; ++i)
-    if (a.reloc_label[i] == c) s -= to_fixed(a.reloc_x[(long long)i * a.ld + j], a.st->scale);
+    if (a.reloc_label[i] == c) s -= to_fixed(a.reloc_x[(long long)i * a.ld + j] * a.reloc_w[i], a.st->scale);
   return centre_from_sum(s, centre_factor(a.st->inv_scale, a.cnt_adj[c]));
 }
 
@@ -705,6 +723,7 @@ static __device__ bool relocation_path(const MStepArgs& a, int n_empty, int bulk
         const long long r = a.sel[i];
         a.reloc_dist[rank] = di;
         a.reloc_label[rank] = a.labels[r];
+        a.reloc_w[rank] = st->w ? st->w[r] : 1.0f;
         for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = a.X[xblk_index(r, j, a.ld)];
       }
     }
@@ -743,6 +762,7 @@ static __device__ bool relocation_path(const MStepArgs& a, int n_empty, int bulk
         if (rank < n_empty) {
           a.reloc_dist[rank] = di;
           a.reloc_label[rank] = reinterpret_cast<const int*>(blk + cand_label_off(a.cand_cap))[i];
+          a.reloc_w[rank] = 1.0f;  // sharded fits have unit weights
           const float* xs = reinterpret_cast<const float*>(blk + cand_x_off(a.cand_cap)) + (long long)i * a.ld;
           for (int j = 0; j < a.ld; ++j) a.reloc_x[(long long)rank * a.ld + j] = xs[j];
         }
@@ -759,8 +779,9 @@ static __device__ bool relocation_path(const MStepArgs& a, int n_empty, int bulk
     block_sync();
     if (threadIdx.x == 0) {
       for (int i = 0; i < n_reloc; ++i) {
-        a.cnt_adj[a.reloc_label[i]] -= 1;
-        a.cnt_adj[a.empty_ids[i]] += 1;
+        const long long cw = st->w ? to_fixed(a.reloc_w[i], st->wscale) : 1;
+        a.cnt_adj[a.reloc_label[i]] -= cw;
+        a.cnt_adj[a.empty_ids[i]] += cw;
       }
       st->relocated = n_reloc;
     }

@@ -37,7 +37,7 @@ namespace {
 
 template <int D, int KM>
 struct ConstCentres {
-  float cm2[KM][D];  // -2 (c - m)
+  float cm2[D][KM];  // -2 (c - m), centre-minor: centres c and c + 1 of a column are one 8-byte pair
   float nrm[KM];     // ||c - m||^2, +inf for padding centres (c >= k)
   float m[D];        // offset: the centres' column means
   float a_max;       // max over centres of ||c - m||^2
@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(256) assign_const_kernel(const float* __restri
                                                            const float* __restrict__ C, int ldc,
                                                            int32_t* __restrict__ labels) {
   static_assert(D % 4 == 0, "rows are read as float4");
+  static_assert(KM % 2 == 0, "centres are scored in pairs");
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += stride) {
     float x[D];
@@ -71,17 +72,34 @@ __global__ void __launch_bounds__(256) assign_const_kernel(const float* __restri
       xm[j] = x[j] - P.m[j];
       l1 += fabsf(xm[j]);
     }
+    // x - m broadcast to both halves of a pair, once per row
+    unsigned long long xx[D];
+#pragma unroll
+    for (int j = 0; j < D; ++j) asm("mov.b64 %0, {%1, %1};" : "=l"(xx[j]) : "f"(xm[j]));
     float s1 = INFINITY, s2 = INFINITY;
     int i1 = 0;
 #pragma unroll
-    for (int c = 0; c < KM; ++c) {
-      float s = P.nrm[c];
+    for (int c = 0; c < KM; c += 2) {
+      // the scores of centres c and c + 1 together: one fma.rn.f32x2 per
+      // column (each half rounds exactly as fmaf, in the same order)
+      unsigned long long sp;
+      asm("mov.b64 %0, {%1, %2};" : "=l"(sp) : "f"(P.nrm[c]), "f"(P.nrm[c + 1]));
 #pragma unroll
-      for (int j = 0; j < D; ++j) s = fmaf(xm[j], P.cm2[c][j], s);
-      const bool lt = s < s1;
-      s2 = lt ? s1 : fminf(s2, s);
-      i1 = lt ? c : i1;
-      s1 = lt ? s : s1;
+      for (int j = 0; j < D; ++j) {
+        unsigned long long cp;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(cp) : "f"(P.cm2[j][c]), "f"(P.cm2[j][c + 1]));
+        asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(sp) : "l"(xx[j]), "l"(cp));
+      }
+      float sc[2];
+      asm("mov.b64 {%0, %1}, %2;" : "=f"(sc[0]), "=f"(sc[1]) : "l"(sp));
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float s = sc[u];
+        const bool lt = s < s1;
+        s2 = lt ? s1 : fminf(s2, s);
+        i1 = lt ? c + u : i1;
+        s1 = lt ? s : s1;
+      }
     }
     // |rounding error| of every score <= eps (a_max + 2 b_max ||x - m||_1)
     const float e = P.eps * (P.a_max + 2.0f * P.b_max * l1);
@@ -121,14 +139,14 @@ int launch_const(const float* X, long long n, const float* C_host, const float* 
   for (int c = 0; c < KM; ++c) {
     if (c >= k) {
       P.nrm[c] = INFINITY;
-      for (int j = 0; j < D; ++j) P.cm2[c][j] = 0.0f;
+      for (int j = 0; j < D; ++j) P.cm2[j][c] = 0.0f;
       continue;
     }
     // the kernel's offset is the float P.m; c - m is exact in float64
     double nrm = 0.0;
     for (int j = 0; j < D; ++j) {
       const double t = (double)C_host[(size_t)c * D + j] - (double)P.m[j];
-      P.cm2[c][j] = (float)(-2.0 * t);
+      P.cm2[j][c] = (float)(-2.0 * t);
       nrm += t * t;
       b_max = std::max(b_max, std::fabs(t));
     }

@@ -47,8 +47,8 @@ struct FitState {
   int32_t sel_remaining;
   int32_t sel_count;
   double tol;          // absolute tolerance on the sum of squared shifts
-  double scale;        // 2^F
-  double inv_scale;    // 2^-F
+  double scale;        // 2^F: a row's value v enters the sums as round(v * w * 2^F)
+  double inv_scale;    // 2^-F * wscale: centre = S * inv_scale / W
   double shift_tot;    // sum of squared centre shifts of the last M-step
   double inertia;
   unsigned int barrier_count;  // software grid barrier
@@ -62,6 +62,8 @@ struct FitState {
   int32_t bulk_always; // every iteration does (diagnostic flag)
   int32_t pad0;
   long long bulk_threshold;  // changed rows above which the next iteration is a bulk one
+  const float* w;      // per-row sample weights (device), null: unit weights
+  double wscale;       // 2^G: a row's weight enters the cluster weights W as round(w * 2^G); 1 unweighted
 };
 
 constexpr int kMaxEmptyCap = 4096;  // upper bound on relocations per iteration

@@ -12,6 +12,9 @@ run on the CUDA library:
   drawn with scikit-learn's own initialisation routine and random stream;
 * ``n_init`` restarts keep scikit-learn's best-run rule (lower inertia and
   not the same clustering up to a permutation);
+* ``sample_weight`` weights the sums, the cluster weights (a cluster of
+  weight zero is empty), the seeding and the inertia, as scikit-learn's
+  weighted Lloyd does (one GPU);
 * the Lloyd loop, the final E-step, the inertia, ``predict``, ``transform``,
   ``fit_predict``, ``fit_transform`` and ``score`` run on the GPU;
 * there is no CPU fallback: without a GPU, or under ``set_device("cpu")``,
@@ -75,13 +78,19 @@ class MetalKMeans(BaseGPUEstimator):
         _bridge.set_device(get_config().gpu_index)
 
     def _check_weights(self, sample_weight, n):
+        """float32 weights of the n rows (scikit-learn's _check_sample_weight
+        rules: a scalar broadcasts, shape (n,), finite), or None for unit
+        weights. The library rejects negative weights and an all-zero set."""
         if sample_weight is None:
-            return
-        w = np.asarray(sample_weight, dtype=np.float64)
+            return None
+        w = np.asarray(sample_weight, dtype=np.float32)
         if w.ndim == 0:
-            w = np.full(n, float(w))
-        if w.shape != (n,) or not np.all(w == 1.0):
-            raise NotImplementedError("skmetal_b200 KMeans supports unit sample weights only")
+            w = np.full(n, float(w), dtype=np.float32)
+        if w.shape != (n,):
+            raise ValueError(f"sample_weight.shape == {w.shape}, expected ({n},)!")
+        if not np.all(np.isfinite(w)):
+            raise ValueError("Input sample_weight contains NaN or infinity.")
+        return np.ascontiguousarray(w)
 
     # ---------------------------------------------------------------------- fit
     def fit(self, X, y=None, sample_weight=None):
@@ -93,7 +102,7 @@ class MetalKMeans(BaseGPUEstimator):
         k = int(est.n_clusters)
         if n < k:
             raise ValueError(f"n_samples={n} should be >= n_clusters={k}.")
-        self._check_weights(sample_weight, n)
+        sw = self._check_weights(sample_weight, n)
 
         init = est.init
         init_is_array = hasattr(init, "__array__") or isinstance(init, (list, tuple))
@@ -112,7 +121,7 @@ class MetalKMeans(BaseGPUEstimator):
                 n_init = 1
         random_state = check_random_state(est.random_state)
         if isinstance(init, str) and init == "k-means++":
-            return self._fit_plusplus(X, k, n_init, random_state, t0=time.perf_counter())
+            return self._fit_plusplus(X, k, n_init, random_state, sw, t0=time.perf_counter())
 
         # scikit-learn draws the other non-array inits on the centred data
         Xc = x_sq = mean = None
@@ -120,7 +129,7 @@ class MetalKMeans(BaseGPUEstimator):
             mean = X.mean(axis=0)
             Xc = X - mean
             x_sq = np.einsum("ij,ij->i", Xc, Xc)
-        ones = np.ones(n, dtype=np.float32)
+        ones = np.ones(n, dtype=np.float32) if sw is None else sw
 
         t0 = time.perf_counter()
         best = None
@@ -132,13 +141,13 @@ class MetalKMeans(BaseGPUEstimator):
                                                    random_state=random_state, sample_weight=ones)
                 centers_init = np.ascontiguousarray((centers_init + mean).astype(np.float32))
             centers, labels, inertia, n_iter = _gpu_call(
-                _bridge.kmeans_fit, X, centers_init, int(est.max_iter), float(est.tol), center=True)
+                _bridge.kmeans_fit, X, centers_init, int(est.max_iter), float(est.tol), center=True, sample_weight=sw)
             if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
                 best = (centers, labels, inertia, n_iter)
         self._finish_fit(best, n, d, k, n_init, t0)
         return self
 
-    def _fit_plusplus(self, X, k, n_init, random_state, t0):
+    def _fit_plusplus(self, X, k, n_init, random_state, sw, t0):
         """init="k-means++": every restart seeds on the GPU (scikit-learn's
         greedy k-means++ on the centred rows, drawing from ``random_state`` in
         scikit-learn's order) and fits from there; X is uploaded once."""
@@ -148,10 +157,10 @@ class MetalKMeans(BaseGPUEstimator):
         try:
             best = None
             for _ in range(n_init):
-                centers_init, _ = _gpu_call(_bridge.kmeans_plusplus, ds, k, random_state)
+                centers_init, _ = _gpu_call(_bridge.kmeans_plusplus, ds, k, random_state, sample_weight=sw)
                 labels = np.empty(n, dtype=np.int32)
                 centers, inertia, n_iter = _gpu_call(ds.fit, centers_init, int(est.max_iter), float(est.tol),
-                                                     labels_out=labels)
+                                                     labels_out=labels, sample_weight=sw)
                 if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
                     best = (centers, labels, inertia, n_iter)
         finally:
@@ -220,6 +229,8 @@ class MetalKMeans(BaseGPUEstimator):
     def score(self, X, y=None, sample_weight=None):
         C = self._centers()
         X = self._check_test(X)
-        self._check_weights(sample_weight, X.shape[0])
+        sw = self._check_weights(sample_weight, X.shape[0])
         labels = self.predict(X)
+        if sw is not None:
+            return -_gpu_call(_bridge.kmeans_inertia_weighted, X, C, labels, sw, X.shape[0], X.shape[1], C.shape[0])
         return -_gpu_call(_bridge.kmeans_inertia, X, C, labels, X.shape[0], X.shape[1], C.shape[0])

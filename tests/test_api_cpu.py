@@ -88,10 +88,16 @@ def test_fit_without_gpu_raises():
         skm.accelerate(KMeans(n_clusters=2, n_init=1)).fit(X)
 
 
-def test_only_unit_sample_weights():
+def test_sample_weight_checks():
+    """scikit-learn's _check_sample_weight rules on the host: None stays None
+    (unit weights), a scalar broadcasts, the shape must be (n,), values must
+    be finite; the library itself rejects negative and all-zero weights."""
     km = MetalKMeans(KMeans(n_clusters=2))
-    km._check_weights(None, 5)
-    km._check_weights(np.ones(5), 5)
-    km._check_weights(1.0, 5)
-    with pytest.raises(NotImplementedError):
-        km._check_weights(np.arange(5.0), 5)
+    assert km._check_weights(None, 5) is None
+    np.testing.assert_array_equal(km._check_weights(2.0, 5), np.full(5, 2.0, np.float32))
+    w = km._check_weights(np.arange(5.0), 5)
+    assert w.dtype == np.float32 and w.flags["C_CONTIGUOUS"]
+    with pytest.raises(ValueError):
+        km._check_weights(np.ones(4), 5)
+    with pytest.raises(ValueError):
+        km._check_weights(np.array([1.0, np.nan, 1.0, 1.0, 1.0]), 5)

@@ -79,3 +79,24 @@ def test_oracle_single_step_matches_reference(name):
     labels, _ = ora.assign(Xc, step.centers_new)
     check_labels(Xc, step.centers_new, labels, z[f"{name}/step1/labels"], f"{name} step labels")
     assert int(z[f"{name}/step1/n_iter"]) == 1
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_weighted_oracle_matches_sklearn(seed):
+    """The weighted restatement (sample_weight) against scikit-learn's own
+    weighted Lloyd on well-separated data, including rows of weight zero."""
+    from sklearn.cluster import KMeans
+
+    rng = np.random.default_rng(seed)
+    n, d, k = 3000, 8, 6
+    C = rng.uniform(-10, 10, (k, d))
+    X = (C[rng.integers(0, k, n)] + rng.normal(size=(n, d))).astype(np.float32)
+    w = rng.uniform(0.2, 3.0, n).astype(np.float32)
+    if seed == 2:
+        w[:500] = 0.0
+    init = X[rng.choice(n, k, replace=False)]
+    sk = KMeans(n_clusters=k, init=init, n_init=1, max_iter=50, tol=0, algorithm="lloyd").fit(X, sample_weight=w)
+    r = ora.kmeans_lloyd(X, init, 50, 0.0, sample_weight=w)
+    np.testing.assert_array_equal(sk.labels_, r.labels)
+    np.testing.assert_allclose(sk.cluster_centers_, r.centers, rtol=1e-5, atol=1e-5)
+    assert sk.inertia_ == pytest.approx(r.inertia, rel=1e-5)

@@ -181,6 +181,41 @@ def test_estep_many_tiles_per_cta(n, d, k):
     np.testing.assert_array_equal(weight.astype(np.int64), np.bincount(lab, minlength=k))
 
 
+@pytest.mark.parametrize("ratio,k", [(1e-3, 16), (1e-5, 16), (1e-3, 200)])
+def test_wide_dynamic_range_columns(ratio, k):
+    """One column spans the whole range of X (uniform noise, the same for
+    every centre) while the clusters live in columns `ratio` times smaller.
+    The tensor-core E-step scales each operand by one power of two, so the
+    small columns sit far down fp16's range. One E-step from the true centres
+    must give the float64 argmin of ||c||^2 - 2 x.c for every row whose two
+    best float64 values are further apart than 2^-20 of the magnitudes that
+    enter them (2 sum|x||c| + ||c||^2 of both centres); here every row is, by
+    a factor of about 250 at ratio 1e-5."""
+    rng = np.random.default_rng(int(round(1 / ratio)) + k)
+    n, d = 60000, 24
+    centres = rng.uniform(-10, 10, size=(k, d)) * ratio
+    centres[:, 0] = 0.0
+    lab = rng.integers(0, k, n)
+    X = centres[lab] + ratio * rng.normal(size=(n, d))
+    X[:, 0] = rng.uniform(-1, 1, size=n)
+    X = X.astype(np.float32)
+    mean, Xc, C = ora.center_data(X, centres.astype(np.float32))
+    got, _, weight, _ = _bridge.kmeans_lloyd_iter(Xc, C)
+    np.testing.assert_array_equal(weight.astype(np.int64), np.bincount(got, minlength=k))
+    Xd, Cd = Xc.astype(np.float64), C.astype(np.float64)
+    cn = (Cd ** 2).sum(axis=1)
+    E = cn[None, :] - 2.0 * (Xd @ Cd.T)
+    want = np.argmin(E, axis=1)
+    mism = np.nonzero(got != want)[0]
+    if mism.size:
+        A = np.abs(Xd[mism]) @ np.abs(Cd).T
+        a, b = got[mism], want[mism]
+        gap = np.abs(E[mism, a] - E[mism, b])
+        bound = 2.0 ** -20 * (2 * A[np.arange(mism.size), a] + 2 * A[np.arange(mism.size), b] + cn[a] + cn[b])
+        assert np.all(gap <= bound), (f"{int((gap > bound).sum())} of {n} labels differ from the float64 argmin "
+                                      f"beyond the split's precision (gap/bound {np.sort(gap / bound)[-5:]})")
+
+
 # ---------------------------------------------------------------------------
 # tensor-core vs SIMT E-step, full fits
 # ---------------------------------------------------------------------------

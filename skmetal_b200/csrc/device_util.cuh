@@ -245,6 +245,12 @@ __device__ __forceinline__ void split8(const float4& a, const float4& b, float s
 // exactly one K = 16 slice of the kind::f16 A operand in the canonical
 // no-swizzle K-major layout (8-row groups 128 bytes apart, K halves 2048 bytes
 // apart). Columns past d and rows past n are zero.
+// Half last chunk (stacked layout, ld = 4 mod 8): the last chunk has four
+// columns and is stored in 2 KB, x_hi of its four columns in K 0..3 and x_lo
+// in K 4..7 of the first K half, so a tile takes nk * 4096 - 2048 bytes; the
+// second K half, read by the MMA from the shared-memory stage, is the stage's
+// zeroed padding, and the centre image moves the matching c_hi copy to
+// K 4..7 (cimg_put4).
 
 // Scale exponent for values bounded by the float whose bits are given: with
 // max |v| < 2^E, v * 2^(14 - E) < 2^14 (fp16 reaches 65504, so centres may be
@@ -282,6 +288,7 @@ struct CentreImage {
   int nk;         // K chunks of 8 columns
   int stacked;    // layout: kCimgTwoSegment, kCimgStacked or kCimgBlocked
   int nbs;        // blocked: clusters per block
+  int half_last;  // stacked: the last chunk is a half chunk (the split copy's layout note)
 };
 
 __host__ __device__ inline size_t cimg_halves(int k_pad, int nk, int stacked) {
@@ -322,7 +329,9 @@ __device__ __forceinline__ void cimg_put4(const CentreImage& ci, int c, int q, c
   const size_t base = (size_t)chunk * N * 16;
   const size_t r = (size_t)(c >> 3) * 64 + (size_t)(c & 7) * 8 + e;
   *reinterpret_cast<uint2*>(ci.img + base + r) = hv;
-  *reinterpret_cast<uint2*>(ci.img + base + (size_t)N * 8 + r) = hv;
+  // the copy of c_hi that multiplies x_lo: K half 1, or K 4..7 of a half chunk
+  const bool half = ci.stacked == kCimgStacked && ci.half_last && chunk == ci.nk - 1;
+  *reinterpret_cast<uint2*>(ci.img + base + (half ? (size_t)4 : (size_t)N * 8) + r) = hv;
   if (ci.stacked) {
     const int cl = ci.k_pad + c;
     *reinterpret_cast<uint2*>(ci.img + base + (size_t)(cl >> 3) * 64 + (size_t)(cl & 7) * 8 + e) = lv;
@@ -350,7 +359,8 @@ __device__ __forceinline__ void cimg_put(const CentreImage& ci, int c, int j, fl
   const size_t base = (size_t)chunk * N * 16;
   const size_t r = (size_t)(c >> 3) * 64 + (size_t)(c & 7) * 8 + e;
   ci.img[base + r] = hb;
-  ci.img[base + (size_t)N * 8 + r] = hb;
+  const bool half = ci.stacked == kCimgStacked && ci.half_last && chunk == ci.nk - 1;
+  ci.img[base + (half ? (size_t)4 : (size_t)N * 8) + r] = hb;
   if (ci.stacked) {
     const int cl = ci.k_pad + c;
     ci.img[base + (size_t)(cl >> 3) * 64 + (size_t)(cl & 7) * 8 + e] = lb;

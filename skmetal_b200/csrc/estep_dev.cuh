@@ -42,7 +42,7 @@ struct Params {
   int acc_cols;   // TMEM columns of one accumulator
   int tmem_cols;
   uint32_t stage_bytes;  // >= tile_bytes (an even number of chunks when not stacked)
-  uint32_t tile_bytes;   // nk * 4096: one tile of the split copy
+  uint32_t tile_bytes;   // one tile of the split copy: nk * 4096, less 2048 with a half last chunk
   uint32_t img_bytes;
   const unsigned char* Xs;  // split working copy
   const uint16_t* img;      // centre image
@@ -74,6 +74,16 @@ static __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* ab
       }
     }
   }
+}
+
+// Bounded wait of a whole warp (every lane waits) with one outcome for all
+// lanes, so that the warp stays converged for the .sync.aligned TMEM loads,
+// votes and per-warp arrivals that follow, even if the wait ends at its time
+// limit on some lanes only.
+static __device__ __forceinline__ bool warp_wait_all(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                                     int code) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, code);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // K-major no-swizzle shared-memory matrix descriptor: core matrices of 8 rows
@@ -490,8 +500,11 @@ __device__ __forceinline__ void cta_setup(const Params& p, unsigned char* smem_r
     for (int a = 0; a < 2; ++a)
       for (int sl = 0; sl < 2; ++sl) {
         // every thread of the partner groups (unused without a split)
-        mbar_init(c.bar(B_PART_FULL(a, sl)), BM * (epi_split(p.nacc) > 1 ? epi_split(p.nacc) - 1 : 1));
-        mbar_init(c.bar(B_PART_EMPTY(a, sl)), BM);  // every thread of the finishing group
+        // one arrival per warp (after __syncwarp, which orders the warp's
+        // shared-memory accesses before its lane 0's arrival): the partner
+        // groups' warps, and the finishing group's four
+        mbar_init(c.bar(B_PART_FULL(a, sl)), 4 * (epi_split(p.nacc) > 1 ? epi_split(p.nacc) - 1 : 1));
+        mbar_init(c.bar(B_PART_EMPTY(a, sl)), 4);
       }
     mbar_init(c.bar(B_C_FULL), 1);
     mbar_init(c.bar(B_DONE(0)), 1);
@@ -652,7 +665,7 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
         const long long g1 = grow + (long long)c.n_grp * gridDim.x * BM;
         old_next = g1 < p.n ? p.labels[g1] : -1;
       }
-      if (!mbar_wait(c.bar(B_ACC_FULL(a)), use & 1, c.abort_flag, p.err, 2401)) break;
+      if (!warp_wait_all(c.bar(B_ACC_FULL(a)), use & 1, c.abort_flag, p.err, 2401)) break;
       tc_fence_after();
       const uint32_t taddr = c.tmem_base + lane_off + (uint32_t)(a * p.acc_cols);
       float best;
@@ -669,13 +682,14 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
         const uint32_t ph = (uint32_t)(use >> 1) & 1u;
         const int o = (a * 2 + sl) * np * BM + row;
         if (!finisher) {
-          if (!mbar_wait(c.bar(B_PART_EMPTY(a, sl)), ph ^ 1u, c.abort_flag, p.err, 2402)) break;
+          if (!warp_wait_all(c.bar(B_PART_EMPTY(a, sl)), ph ^ 1u, c.abort_flag, p.err, 2402)) break;
           part_d[o + (h - 1) * BM] = best;
           part_i[o + (h - 1) * BM] = bl;
-          mbar_arrive(c.bar(B_PART_FULL(a, sl)));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(c.bar(B_PART_FULL(a, sl)));
           continue;
         }
-        if (!mbar_wait(c.bar(B_PART_FULL(a, sl)), ph, c.abort_flag, p.err, 2403)) break;
+        if (!warp_wait_all(c.bar(B_PART_FULL(a, sl)), ph, c.abort_flag, p.err, 2403)) break;
         float ob[EPI_GROUPS - 1];
         int oi[EPI_GROUPS - 1];
 #pragma unroll
@@ -685,7 +699,8 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
             oi[u] = part_i[o + u * BM];
           }
         }
-        mbar_arrive(c.bar(B_PART_EMPTY(a, sl)));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.bar(B_PART_EMPTY(a, sl)));
 #pragma unroll
         for (int u = 0; u < EPI_GROUPS - 1; ++u)
           if (u < split - 1 && better(ob[u], oi[u], best, bl)) {
@@ -744,7 +759,7 @@ inline Params make_params(const TcPlan& plan) {
   p.tmem_cols = plan.tmem_cols;
   p.stage_bytes = plan.stage_bytes;
   p.img_bytes = plan.img_bytes;
-  p.tile_bytes = (uint32_t)(plan.k_steps * CHUNK_BYTES);
+  p.tile_bytes = tc_tile_bytes(plan);
   p.Xs = plan.Xs;
   p.X = plan.X;
   p.ld = plan.ld;

@@ -83,7 +83,8 @@ __global__ void __launch_bounds__(THREADS, 1) estep_tc_kernel(Params p) {
 // at the same row position of the chunk's two halves; consecutive threads take
 // consecutive rows, so reads and writes are coalesced 512-byte runs per warp.
 __global__ void split_x_kernel(const float* __restrict__ X, int ld, int nk, long long n_tiles,
-                               const int* __restrict__ sexp, uint4* __restrict__ Xs) {
+                               const int* __restrict__ sexp, uint4* __restrict__ Xs, uint32_t tile_bytes,
+                               int half_last) {
   const float s = ldexpf(1.0f, sexp[0]);
   const int nq = ld >> 2;
   const long long total = n_tiles * nk * BM;
@@ -99,9 +100,13 @@ __global__ void split_x_kernel(const float* __restrict__ X, int ld, int nk, long
     const float4 b = (2 * c + 1 < nq) ? xt[(long long)(2 * c + 1) * 128 + row] : make_float4(0.f, 0.f, 0.f, 0.f);
     uint4 hi, lo;
     split8(a, b, s, &hi, &lo);
-    uint4* dst = Xs + tc * (CHUNK_BYTES / 16);
-    dst[row] = hi;
-    dst[BM + row] = lo;
+    uint4* dst = Xs + (t * tile_bytes + (size_t)c * CHUNK_BYTES) / 16;
+    if (half_last && c == nk - 1) {  // x_hi of the four columns, then their x_lo
+      dst[row] = make_uint4(hi.x, hi.y, lo.x, lo.y);
+    } else {
+      dst[row] = hi;
+      dst[BM + row] = lo;
+    }
   }
 }
 
@@ -275,6 +280,7 @@ int tc_probe(int* mode_out, uint32_t* raw_out) {
 
 int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   plan->supported = false;
+  plan->half_last = 0;
   if (getenv("SKMETAL_DISABLE_TC")) return OK;
   if (d > tc::MAX_NK * tc::KC || n < 1) return OK;
   if ((reinterpret_cast<uintptr_t>(X) & 15) || ((ld * 4) & 15)) return OK;
@@ -308,6 +314,7 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
       const tc::Smem L = tc::smem_layout(stage_bytes, img_bytes, plan->k_pad, st, nacc);
       if ((int)L.total <= avail) {
         plan->stacked = stacked;
+        plan->half_last = stacked && (ld % tc::KC) == 4;
         plan->stages = st;
         plan->stage_bytes = stage_bytes;
         plan->img_bytes = img_bytes;
@@ -334,8 +341,12 @@ int tc_plan(const float* X, int ld, long long n, int d, int k, TcPlan* plan) {
   return OK;
 }
 
+uint32_t tc_tile_bytes(const TcPlan& plan) {
+  return (uint32_t)(plan.k_steps * tc::CHUNK_BYTES) - (plan.half_last ? (uint32_t)tc::CHUNK_BYTES / 2 : 0u);
+}
+
 size_t tc_split_bytes(const TcPlan& plan) {
-  return (size_t)((plan.n + tc::BM - 1) / tc::BM) * plan.k_steps * tc::CHUNK_BYTES;
+  return (size_t)((plan.n + tc::BM - 1) / tc::BM) * tc_tile_bytes(plan);
 }
 
 int tc_split_x(TcPlan* plan, void* Xs, const int* sexp, cudaStream_t s) {
@@ -343,14 +354,14 @@ int tc_split_x(TcPlan* plan, void* Xs, const int* sexp, cudaStream_t s) {
   const long long work = n_tiles * plan->k_steps * tc::BM;
   const int blocks = (int)std::max(1LL, std::min((work + 255) / 256, (long long)sm_count() * 8));
   tc::split_x_kernel<<<blocks, 256, 0, s>>>(plan->X, plan->ld, plan->k_steps, n_tiles, sexp,
-                                            reinterpret_cast<uint4*>(Xs));
+                                            reinterpret_cast<uint4*>(Xs), tc_tile_bytes(*plan), plan->half_last);
   SKM_TRY(check_launch("split_x_kernel"));
   plan->Xs = static_cast<const unsigned char*>(Xs);
   return OK;
 }
 
 CentreImage tc_centre_image(const TcPlan& plan, uint16_t* img) {
-  return CentreImage{img, plan.k_pad, plan.k_steps, plan.stacked, plan.nbs};
+  return CentreImage{img, plan.k_pad, plan.k_steps, plan.stacked, plan.nbs, plan.half_last};
 }
 
 int tc_estep(const TcPlan& plan, const uint16_t* img, const int* sexp, const float* bias, int32_t* labels,

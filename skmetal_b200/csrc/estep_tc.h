@@ -23,6 +23,7 @@ struct TcPlan {
   int k_pad = 0;     // clusters padded to the MMA N granularity (16)
   int k_steps = 0;   // K = ld in chunks of 8 columns
   int stacked = 0;   // centre image layout (CentreImage)
+  int half_last = 0; // stacked, ld = 4 mod 8: the last chunk is a half chunk (2 KB)
   int stages = 0;    // X stages in shared memory
   int nacc = 0;      // accumulators in tensor memory
   int acc_cols = 0;  // tensor-memory columns per accumulator
@@ -62,6 +63,8 @@ int tc_plan_wide(const float* X, int ld, long long n, int d, int k, int optin, T
 // builds it from the fp32 blocked copy with the scale 2^sexp[0] (device int);
 // the plan then reads its tiles from Xs.
 size_t tc_split_bytes(const TcPlan& plan);
+// Bytes of one 128-row tile of the split copy.
+uint32_t tc_tile_bytes(const TcPlan& plan);
 int tc_split_x(TcPlan* plan, void* Xs, const int* sexp, cudaStream_t s);
 
 // Geometry of the centre image the plan's kernel reads (img: cimg_halves(...)

@@ -24,14 +24,16 @@
 //     block whose sequence number has parity a, keeping a running argmin per
 //     row; at the end of a tile group 1 hands its partial minimum to group 0
 //     through shared memory (two mbarriers per tile parity), which merges the
-//     two in index order, writes the label, counts the change and adds the
-//     row's fixed-point deltas.
+//     two in index order, writes the label, counts the change and queues a
+//     changed row in the deferred-delta ring (delta_ring.cuh), whose
+//     fixed-point deltas warp 3 adds; the previous labels are loaded one
+//     tile ahead.
 // The n x k distance matrix never leaves the SM, and X is read from HBM once
 // per launch.
 //
 // Warp roles (384 threads): 0 X producer, 1 TMEM owner and MMA issuer (the
 // whole warp runs the issuing loop on warp-uniform values, one elected lane
-// issues each MMA), 2 centre-unit producer, 3 idle, 4-7 epilogue group 0,
+// issues each MMA), 2 centre-unit producer, 3 delta drainer, 4-7 epilogue group 0,
 // 8-11 epilogue group 1.
 //
 // Every wait is bounded (2 s); on a timeout the CTA records an error code,
@@ -48,6 +50,7 @@
 #include <cstring>
 #include <vector>
 
+#include "delta_ring.cuh"
 #include "device_util.cuh"
 #include "driver.h"
 #include "estep_dev.cuh"
@@ -65,7 +68,8 @@ constexpr int MAX_XST = 4;    // X stages
 constexpr int MAX_RING = 8;   // centre-unit stages
 constexpr int MAX_NBS = 256;  // clusters per block (one UMMA N)
 constexpr int MAX_K = 4096;
-constexpr int PROD_X_W = 0, MMA_W = 1, PROD_C_W = 2, EPI_W0 = 4;
+static_assert(MAX_K <= DQ_MAX_LABEL, "ring entries hold every label");
+constexpr int PROD_X_W = 0, MMA_W = 1, PROD_C_W = 2, IDLE_W = 3, EPI_W0 = 4;
 static_assert((EPI_W0 + 8) * 32 == THREADS, "two epilogue groups of four warps end the block");
 
 struct Params {
@@ -100,7 +104,7 @@ constexpr int B_DONE = 2 * MAX_XST + 2 * MAX_RING + 8;
 constexpr int NUM_BARS = B_DONE + 1;
 
 struct Layout {
-  uint32_t ring, bias, part, bars, misc, total;
+  uint32_t ring, bias, part, bars, misc, dq, total;
 };
 
 __host__ __device__ inline Layout layout(uint32_t stage_bytes, int xst, uint32_t unit_bytes, int ring, int k_pad) {
@@ -116,6 +120,8 @@ __host__ __device__ inline Layout layout(uint32_t stage_bytes, int xst, uint32_t
   off += NUM_BARS * 8;
   L.misc = off;  // [0] tensor-memory base, [1] abort flag
   off += 16;
+  L.dq = off;  // deferred-delta ring (delta_ring.cuh)
+  off += dq_bytes();
   L.total = off + 1024;  // slack for aligning the base to 1024
   return L;
 }
@@ -172,8 +178,10 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar(AF(a)), 1);
       mbar_init(bar(AE(a)), 4);      // the four warps of the accumulator's epilogue group
-      mbar_init(bar(PF(a)), BM);     // every thread of group 1
-      mbar_init(bar(PE(a)), BM);     // every thread of group 0
+      // one arrival per warp, after __syncwarp (which orders the warp's
+      // shared-memory accesses before its lane 0's arrival)
+      mbar_init(bar(PF(a)), 4);      // the four warps of group 1
+      mbar_init(bar(PE(a)), 4);      // the four warps of group 0
     }
     mbar_init(bar(B_DONE), 1);
     misc[1] = 0;
@@ -185,6 +193,8 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   for (int j = threadIdx.x; j < p.k_pad; j += blockDim.x) bias_s[j] = j < p.k ? __ldcg(p.bias + j) : INFINITY;
+  const DeltaRing ring = dq_ring(base + L.dq);
+  dq_init(ring);
   // the extra chunk of an odd nk (the x_hi / x_lo K half of the last pair)
   // is zero in every stage; the bulk copies write only tile_bytes
   if (p.tile_bytes < p.stage_bytes)
@@ -290,9 +300,21 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
     const int q = warp & 3;  // TMEM lane quarter of this warp
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const bool finisher = g == 0;
+    // the finisher loads each tile's previous labels one tile ahead
+    int old_next = -1;
+    if (finisher && p.changed && my_tiles > 0) {
+      const long long g0 = (long long)blockIdx.x * BM + row;
+      old_next = g0 < p.n ? p.labels[g0] : -1;
+    }
     bool ok = true;
     for (int i = 0; ok && i < my_tiles; ++i) {
       const long long grow = (long long)((int)blockIdx.x + i * (int)gridDim.x) * BM + row;
+      const int old = old_next;
+      if (finisher && p.changed && i + 1 < my_tiles) {
+        const long long g1 = grow + (long long)gridDim.x * BM;
+        old_next = g1 < p.n ? p.labels[g1] : -1;
+      }
       float best = INFINITY;
       int bl = 0x7fffffff;
       for (int b = 0; b < p.nblk; ++b) {
@@ -324,33 +346,36 @@ __global__ void __launch_bounds__(THREADS, 1) estep_wide_kernel(Params p) {
         if (!warp_wait(bar(PE(par)), use ^ 1u, abort_flag, p.err, 2608)) break;
         part_d[par * BM + row] = best;
         part_i[par * BM + row] = bl;
-        mbar_arrive(bar(PF(par)));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(PF(par)));
       } else {
         if (!warp_wait(bar(PF(par)), use, abort_flag, p.err, 2609)) break;
         const float ob = part_d[par * BM + row];
         const int oi = part_i[par * BM + row];
-        mbar_arrive(bar(PE(par)));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(PE(par)));
         if (tc::better(ob, oi, best, bl)) {
           best = ob;
           bl = oi;
         }
         if (bl >= p.k) bl = 0;  // only reachable when every distance is +inf or NaN
         bool ch = false;
-        int old = -1;
         if (grow < p.n) {
-          if (p.changed) {
-            old = p.labels[grow];
-            ch = old != bl;
-          }
+          ch = p.changed && old != bl;
           p.labels[grow] = bl;
         }
         if (p.changed) {
           const unsigned int mk = __ballot_sync(0xffffffffu, ch);
           if (lane == 0 && mk) atomicAdd(p.changed, (unsigned long long)__popc(mk));
-          if (deltas) warp_apply_changed(p.X, p.ld, p.d, p.k, grow, old, bl, ch, deltas, p.st);
+          // the deltas are applied by warp IDLE_W (delta_ring.cuh)
+          if (deltas) dq_push(ring, abort_flag, p.err, grow, old, bl, ch);
         }
       }
     }
+    if (finisher && p.changed && deltas) dq_close(ring);
+  } else if (warp == IDLE_W && p.changed && deltas) {
+    // ---------------------------------------------------- delta drainer
+    dq_drain(ring, 4u, abort_flag, p.err, p.X, p.ld, p.d, p.k, p.st, deltas);
   }
   // the single-lane roles leave warps 0-2 diverged: reconverge before the
   // block barrier

@@ -456,7 +456,7 @@ def main():
     unit = UNIT_FIT if fit else UNIT_PREDICT
 
     # ---- end to end through the public API, pageable host X (and pinned)
-    e2e, e2e_pinned = None, None
+    e2e, e2e_pinned, e2e_calls, e2e_pinned_calls = None, None, None, None
     h2d = int(Xs.nbytes + init.nbytes)
     d2h = int(Xs.shape[0] * 4 + (init.nbytes + 12 if fit else 0))
     if not args.no_e2e:
@@ -485,20 +485,21 @@ def main():
         def e2e_time(X, steps):
             e2e_call(X)  # untimed warm-up of the host-buffer path
             barrier()
-            t_sum, it_sum = 0.0, 0
+            t_sum, it_sum, calls = 0.0, 0, []
             for _ in range(steps):
                 t_i, n_i = e2e_call(X)
                 t_sum += t_i
                 it_sum += n_i
+                calls.append(round(t_i * 1e3, 3))
             if dist is not None:
                 (t_sum,) = max_over_ranks(dist, [t_sum], device="cuda")
-            return n_total * it_sum / t_sum
+            return n_total * it_sum / t_sum, calls
 
-        e2e_steps = max(1, min(args.steps, 3))
-        e2e = e2e_time(Xs, e2e_steps)
+        e2e_steps = max(1, min(args.steps, 5))
+        e2e, e2e_calls = e2e_time(Xs, e2e_steps)
         Xp = torch.empty(Xs.shape, dtype=torch.float32, pin_memory=True).numpy()
         Xp[...] = Xs
-        e2e_pinned = e2e_time(Xp, e2e_steps)
+        e2e_pinned, e2e_pinned_calls = e2e_time(Xp, e2e_steps)
         del Xp
 
     hbm, bf16, bf16_sus, src = _peaks()
@@ -560,8 +561,9 @@ def main():
         "e2e": {"value": e2e, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "host_memory": "pageable numpy (as a user passes it)",
                 "path": ("skmetal_b200.accelerate(KMeans).fit" if fit else "skmetal_b200.accelerate(KMeans).predict")
-                if world == 1 or not fit else "skmetal_kmeans_fit_shard (C ABI, per rank)"},
-        "e2e_pinned": {"value": e2e_pinned, "unit": unit, "host_memory": "page-locked"},
+                if world == 1 or not fit else "skmetal_kmeans_fit_shard (C ABI, per rank)",
+                "calls_ms": e2e_calls},
+        "e2e_pinned": {"value": e2e_pinned, "unit": unit, "host_memory": "page-locked", "calls_ms": e2e_pinned_calls},
         "gpu_launches": int(launches),
         "ranks_agree": ranks_agree,
         "roofline": roofline,

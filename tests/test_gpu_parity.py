@@ -169,11 +169,14 @@ def test_fit_single_empty_cluster_matches_oracle():
     assert inertia == pytest.approx(res.inertia, rel=INERTIA_RTOL)
 
 
-@pytest.mark.parametrize("n,d,k", [(300_000, 36, 24), (200_000, 100, 50), (150_000, 64, 256)])
+@pytest.mark.parametrize("n,d,k", [(300_000, 36, 24), (200_000, 100, 50), (150_000, 64, 256), (120_000, 40, 200),
+                                   (100_000, 24, 137)])
 def test_estep_many_tiles_per_cta(n, d, k):
     """Sizes at which every CTA of the persistent tensor-core E-step runs many
     tiles, so its shared-memory stages, accumulators and both MMA issuers wrap
-    around many times: one Lloyd step against the oracle's E-step."""
+    around many times: one Lloyd step against the oracle's E-step. With
+    k = 200 and k = 137 the four epilogue groups that share each tile scan
+    unequal column ranges (64, 64, 64, 16 and 48, 48, 48, none)."""
     X, init = gaussian_mixture(n, d, k, seed=n + d + k)
     lab, cnew, weight, shift = _bridge.kmeans_lloyd_iter(X, init)
     want, _ = ora.assign(X, init, "fp32")

@@ -244,7 +244,7 @@ __global__ void scale_kernel(const unsigned int* __restrict__ maxabs_bits, doubl
 // relative and is scaled by the mean column variance sumsq / (n_total * d).
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
                                   double n_total, int d, const unsigned int* maxabs_bits, int bulk_always,
-                                  const float* w, const unsigned int* wmax_bits) {
+                                  const float* w, const unsigned int* wmax_bits, int bulk_divisor) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   st->iter = 0;
   st->done = max_iter <= 0;
@@ -267,7 +267,7 @@ __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int to
   st->maxabs_bits = *maxabs_bits;
   st->bulk = 1;  // the first iteration starts from labels -1: every row changes
   st->bulk_always = bulk_always;
-  st->bulk_threshold = (long long)fmax(1.0, n_total / (double)kBulkDivisor);
+  st->bulk_threshold = (long long)fmax(1.0, n_total / (double)bulk_divisor);
   st->xexp = split_exp(*maxabs_bits);
   st->cexp = st->xexp;
   // weighted fits: the sums hold w * x (wmax_bits[0] = max |w x|) and the

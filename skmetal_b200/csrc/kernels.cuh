@@ -58,8 +58,13 @@ __host__ __device__ inline size_t cand_x_off(int cap) { return 16 + (size_t)cap 
 
 // Above n / 10 changed rows in an iteration, per-row deltas (about 2 d
 // contended reductions per row) cost more than rebuilding the sums from all
-// rows, so the next iteration is a bulk one.
+// rows, so the next iteration is a bulk one. When the bulk pass itself adds
+// every element to global memory (the k x ld sums fit neither the tiled pass
+// nor a shared accumulator), a delta costs two global reductions per element
+// of a changed row against one per element of every row, so deltas stay
+// cheaper up to n / 4 changed rows.
 constexpr int kBulkDivisor = 10;
+constexpr int kBulkDivisorGlobal = 4;
 
 // Dynamic shared memory of mstep_kernel for k clusters of ld columns.
 __host__ __device__ inline size_t mstep_smem_bytes(int k, int ld) {
@@ -124,7 +129,15 @@ __global__ void mean_from_colsum_kernel(const long long* colsum, int d, const do
 __global__ void scale_kernel(const unsigned int* maxabs_bits, double n_total, double* out);
 __global__ void init_state_kernel(FitState* st, int max_iter, double tol, int tol_mode, const double* sumsq,
                                   double n_total, int d, const unsigned int* maxabs_bits, int bulk_always,
-                                  const float* w, const unsigned int* wmax_bits);
+                                  const float* w, const unsigned int* wmax_bits, int bulk_divisor);
+
+// kBulkDivisorGlobal when the bulk pass of k clusters of ld columns (in the
+// M-step kernel's shared memory) adds straight to global memory, else
+// kBulkDivisor.
+inline int bulk_divisor(int k, int ld) {
+  return (bulk_tiles_ok(k, ld, 1024, kBulkSmemBytes) || bulk_acc_bytes(k, ld, kBulkSmemBytes)) ? kBulkDivisor
+                                                                                              : kBulkDivisorGlobal;
+}
 __global__ void weight_max_kernel(const float* X, int ld, long long n, const float* w, unsigned int* out);
 __global__ void center_kernel(float* X, int ld, long long n, int d, const float* mean, unsigned int* maxabs_bits,
                               double* partial);

@@ -355,7 +355,8 @@ static int run_fit(const FitParams& p) {
     SKM_TRY(check_launch("weight_max_kernel"));
   }
   init_state_kernel<<<1, 32, 0, s>>>(st, p.max_iter, p.tol, tol_rel ? 1 : 0, tol_rel ? sumsq : nullptr,
-                                     (double)n_total, d, &u32s[1], p.bulk_sums ? 1 : 0, w_dev, &u32s[514]);
+                                     (double)n_total, d, &u32s[1], p.bulk_sums ? 1 : 0, w_dev, &u32s[514],
+                                     bulk_divisor(k, ld));
   SKM_TRY(check_launch("init_state_kernel"));
   SKM_CUDA(cudaMemsetAsync(labels, 0xff, sizeof(int32_t) * n_pad, s));  // label -1: every row changes in iteration 1
   SKM_CUDA(cudaMemsetAsync(S, 0, sizeof(long long) * ((size_t)k * ld + k), s));

@@ -369,11 +369,15 @@ def test_fit_rejects_bad_input():
         _bridge.kmeans_fit(Xn, Xn[:2].copy(), 5, 0.0)
 
 
-@pytest.mark.parametrize("simt", [False, True])
-def test_incremental_sums_equal_bulk_sums(simt):
+@pytest.mark.parametrize("simt,name,n", [(False, "c1", 20000), (True, "c1", 20000), (False, "c4", 60000),
+                                          (False, "c3", 40000)])
+def test_incremental_sums_equal_bulk_sums(simt, name, n):
     """Fixed-point sums are exact: updating them with the rows that changed
-    label must give bit-identical fits to recomputing them every iteration."""
-    X, init = make_workload(scaled("c1", 20000))
+    label must give bit-identical fits to recomputing them every iteration.
+    c4 (k = 256) takes the persistent loop's atomic bulk pass and the
+    epilogue's deltas; c3 (k = 1024) the wide E-step, whose deltas go through
+    the deferred-delta ring, and the M-step kernel's global bulk sums."""
+    X, init = make_workload(scaled(name, n))
     a = _bridge.kmeans_fit(X, init, 30, 0.0, simt=simt)
     b = _bridge.kmeans_fit(X, init, 30, 0.0, simt=simt, bulk_sums=True)
     np.testing.assert_array_equal(a[0], b[0])

@@ -111,6 +111,12 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
   return pol;
 }
 
+// Prefetch of `bytes` (a multiple of 16) at a 16-byte-aligned global address
+// into L2; no shared memory, no completion to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_load_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
                                                uint64_t pol) {
   asm volatile(

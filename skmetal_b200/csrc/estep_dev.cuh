@@ -28,6 +28,7 @@ constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
 constexpr int THREADS = 640;
 constexpr int MAX_STAGES = 4;
 constexpr int MAX_ACC = 4;
+constexpr int L2_AHEAD = 4;  // tiles of the next pass prefetched into L2 beyond the stages
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
 
 struct Params {
@@ -590,6 +591,12 @@ __device__ __forceinline__ void estep_pass(const Params& p, Cta& c, const Pass& 
         bulk_load_hint(c.sbase + (uint32_t)s * p.stage_bytes, src, p.tile_bytes, c.bar(B_FULL(s)), pol);
         c.issued = ig + 1;
       }
+      // the next pass's tiles after those copied into the stages go to L2
+      // now, so HBM keeps streaming while the caller's work between passes
+      // runs and the next pass's first MMAs wait for their centre image
+      if (P.pre_next > 0 && !*c.abort_flag)
+        for (int i = P.pre_next; i < min(my_tiles, P.pre_next + L2_AHEAD); ++i)
+          bulk_prefetch_l2(p.Xs + (size_t)((int)blockIdx.x + i * (int)gridDim.x) * p.tile_bytes, p.tile_bytes);
       if (P.wait_image) {  // the image copy lands before the pass ends
         volatile int no_abort = 0;
         mbar_wait(c.bar(B_C_FULL), P.img_par, &no_abort, p.err, 2102);

@@ -216,6 +216,13 @@ int skmetal_debug_loop_stamps(uint64_t* out, int cap);
 int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,
                            int32_t* estep_launches, double* estep_ms_sum, uint64_t* launches, int32_t* iterations);
 
+/* The number of distinct labels in the final assignment of the calling
+ * thread's last full one-GPU fit (skmetal_kmeans_fit*, skmetal_dataset_fit*),
+ * counted on the device; -1 when it was not counted (sharded fits, single
+ * Lloyd steps, k > 4096, or before any fit). scikit-learn warns when it is
+ * below n_clusters (sklearn/cluster/_kmeans.py:1545-1552). */
+int skmetal_last_fit_distinct(void);
+
 /* ---- multi-GPU (one process per GPU) -------------------------------------- */
 
 /* 128-byte NCCL unique id, produced on one rank and broadcast by the caller. */

@@ -89,6 +89,7 @@ _SIGNATURES = [
     ("skmetal_last_fit_stats", _c_int, [ctypes.POINTER(_c_double)] * 4 + [ctypes.POINTER(_c_i32),
                                         ctypes.POINTER(_c_double), ctypes.POINTER(_c_u64),
                                         ctypes.POINTER(_c_i32)]),
+    ("skmetal_last_fit_distinct", _c_int, []),
     ("skmetal_comm_unique_id", _c_int, [_c_void_p]),
     ("skmetal_comm_init", _c_int, [_c_void_p, _c_int, _c_int]),
     ("skmetal_comm_destroy", _c_int, []),
@@ -507,6 +508,12 @@ def last_fit_stats() -> dict:
     return {"ms_total": v[0].value, "ms_prep": v[1].value, "ms_loop": v[2].value, "ms_final": v[3].value,
             "estep_launches": el.value, "estep_ms_sum": ems.value, "launches": int(la.value),
             "iterations": it.value}
+
+
+def last_fit_distinct() -> int:
+    """Distinct labels in the final assignment of this thread's last one-GPU
+    fit, counted on the device; -1 when the fit did not count them."""
+    return int(_fn("skmetal_last_fit_distinct")())
 
 
 def launch_count() -> int:

@@ -646,6 +646,23 @@ __global__ void inertia_partial_kernel(const float* __restrict__ X, int ld, long
 
 // out = sum of partial[0..m) in a fixed order (one warp: strided lane sums,
 // then a fixed butterfly)
+// The labels present among n: a shared-memory bitmap per block (k bits), ORed
+// into the global one word by word at the end (the distinct-cluster count of
+// scikit-learn's fit, _kmeans.py:1545-1552, without a host pass over n labels).
+__global__ void label_bitmap_kernel(const int32_t* __restrict__ labels, long long n, int k, unsigned int* bitmap) {
+  __shared__ unsigned int sb[kLabelBitmapMaxK / 32];
+  const int words = (k + 31) >> 5;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) sb[i] = 0;
+  __syncthreads();
+  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < n; r += (long long)gridDim.x * blockDim.x) {
+    const int c = labels[r];
+    if ((unsigned)c < (unsigned)k) atomicOr(&sb[c >> 5], 1u << (c & 31));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < words; i += blockDim.x)
+    if (sb[i]) atomicOr(&bitmap[i], sb[i]);
+}
+
 __global__ void ordered_sum_kernel(const double* __restrict__ partial, int m, double* __restrict__ out) {
   if (blockIdx.x != 0 || threadIdx.x >= 32) return;
   double t = 0.0;

@@ -169,6 +169,9 @@ __global__ void centre_prep_kernel(const float* C, int k, int ld, int d, float* 
 __global__ void inertia_partial_kernel(const float* X, int ld, long long n, int d, const float* C,
                                        const int32_t* labels, double* partial, int blocked, const float* w);
 __global__ void ordered_sum_kernel(const double* partial, int m, double* out);
+// Bit c of bitmap (k <= kLabelBitmapMaxK) is set when some label equals c.
+constexpr int kLabelBitmapMaxK = 4096;
+__global__ void label_bitmap_kernel(const int32_t* labels, long long n, int k, unsigned int* bitmap);
 __global__ void mindist_kernel(const float* X, int ld, long long n, int d, const float* C, const int32_t* labels,
                                float* out);
 __global__ void transform_kernel(const float* X, int ld, long long n, int d, const float* C, int k, float* D);

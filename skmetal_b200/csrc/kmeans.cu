@@ -41,6 +41,7 @@ struct FitStats {
   double estep_ms_sum = 0;
   unsigned long long launches = 0;
   int iterations = 0;
+  int distinct = -1;  // labels present in the final assignment (-1: not counted)
 };
 static thread_local FitStats t_stats;
 // globaltimer stamps of the last profiled persistent-loop fit (lloyd_loop_kernel)
@@ -651,6 +652,17 @@ static int run_fit(const FitParams& p) {
   }
   inertia_partial_kernel<<<n_part, 256, 0, s>>>(X, ld, n, d, Cfin, labels, partials, 1, w_dev);
   SKM_TRY(check_launch("inertia_partial_kernel"));
+  // the clusters the final labels use (one GPU; sharded fits leave the count out)
+  unsigned int* bitmap = nullptr;
+  std::vector<unsigned int> bitmap_h;
+  if (!comm && k <= kLabelBitmapMaxK) {
+    const int words = (k + 31) / 32;
+    SKM_TRY(buf.alloc_n(&bitmap, (size_t)words));
+    SKM_CUDA(cudaMemsetAsync(bitmap, 0, sizeof(unsigned int) * words, s));
+    label_bitmap_kernel<<<blocks_for(n, 256, 4), 256, 0, s>>>(labels, n, k, bitmap);
+    SKM_TRY(check_launch("label_bitmap_kernel"));
+    bitmap_h.resize(words);
+  }
   ordered_sum_kernel<<<1, 32, 0, s>>>(partials, n_part, &dscr[1]);
   SKM_TRY(check_launch("ordered_sum_kernel"));
   if (comm) SKM_TRY(comm_allreduce_sum_f64(comm, &dscr[1], 1, s));
@@ -667,6 +679,9 @@ static int run_fit(const FitParams& p) {
     SKM_CUDA(cudaMemcpyAsync(p.labels_out, labels, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
   if (p.labels_out_u32)
     SKM_CUDA(cudaMemcpyAsync(p.labels_out_u32, labels, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, s));
+  if (bitmap)
+    SKM_CUDA(cudaMemcpyAsync(bitmap_h.data(), bitmap, sizeof(unsigned int) * bitmap_h.size(), cudaMemcpyDeviceToHost,
+                             s));
   SKM_CUDA(cudaStreamSynchronize(s));
   if (p.inertia_out) *p.inertia_out = inertia;
   if (p.n_iter_out) *p.n_iter_out = iters;
@@ -703,6 +718,10 @@ static int run_fit(const FitParams& p) {
   }
   fs.launches = g_launches.load() - launches0;
   fs.iterations = iters;
+  if (bitmap) {
+    fs.distinct = 0;
+    for (unsigned int wd : bitmap_h) fs.distinct += __builtin_popcount(wd);
+  }
   t_stats = fs;
   return OK;
 }
@@ -1233,6 +1252,8 @@ int skmetal_debug_loop_stamps(uint64_t* out, int cap) {
   for (int i = 0; i < n; ++i) out[i] = t_loop_stamps[i];
   return (int)t_loop_stamps.size();
 }
+
+int skmetal_last_fit_distinct(void) { return t_stats.distinct; }
 
 int skmetal_last_fit_stats(double* ms_total, double* ms_prep, double* ms_loop, double* ms_final,
                            int32_t* estep_launches, double* estep_ms_sum, uint64_t* launches, int32_t* iterations) {

@@ -143,7 +143,7 @@ class MetalKMeans(BaseGPUEstimator):
             centers, labels, inertia, n_iter = _gpu_call(
                 _bridge.kmeans_fit, X, centers_init, int(est.max_iter), float(est.tol), center=True, sample_weight=sw)
             if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
-                best = (centers, labels, inertia, n_iter)
+                best = (centers, labels, inertia, n_iter, _bridge.last_fit_distinct())
         self._finish_fit(best, n, d, k, n_init, t0)
         return self
 
@@ -162,7 +162,7 @@ class MetalKMeans(BaseGPUEstimator):
                 centers, inertia, n_iter = _gpu_call(ds.fit, centers_init, int(est.max_iter), float(est.tol),
                                                      labels_out=labels, sample_weight=sw)
                 if best is None or (inertia < best[2] and not _same_clustering(labels, best[1], k)):
-                    best = (centers, labels, inertia, n_iter)
+                    best = (centers, labels, inertia, n_iter, _bridge.last_fit_distinct())
         finally:
             ds.close()
         self._finish_fit(best, n, d, k, n_init, t0)
@@ -170,9 +170,9 @@ class MetalKMeans(BaseGPUEstimator):
 
     def _finish_fit(self, best, n, d, k, n_init, t0):
         est = self._estimator
-        centers, labels, inertia, n_iter = best
-
-        distinct = int(np.count_nonzero(np.bincount(labels, minlength=k)))
+        centers, labels, inertia, n_iter, distinct = best
+        if distinct < 0:  # not counted by the library
+            distinct = int(np.count_nonzero(np.bincount(labels, minlength=k)))
         if distinct < k:
             warnings.warn(f"Number of distinct clusters ({distinct}) found smaller than "
                           f"n_clusters ({k}). Possibly due to duplicate points in X.", ConvergenceWarning,

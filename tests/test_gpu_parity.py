@@ -344,6 +344,31 @@ def test_fit_odd_shapes(n, d, k):
         assert inertia == pytest.approx(ref.inertia, rel=INERTIA_RTOL)
 
 
+def test_last_fit_distinct_counts_final_labels():
+    """The library counts the distinct final labels on the device (for
+    scikit-learn's fewer-distinct-clusters warning): equal to the host count on
+    a regular fit, below k when X has fewer distinct rows than k, and the
+    estimator warns as scikit-learn does."""
+    import warnings
+
+    from sklearn.cluster import KMeans
+    from sklearn.exceptions import ConvergenceWarning
+
+    import skmetal_b200 as skmetal
+
+    X, init = make_workload(scaled("c1", 20000))
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(X, init, 20, 0.0)
+    assert _bridge.last_fit_distinct() == len(np.unique(lab))
+    Xd = np.repeat(X[:3], 200, axis=0)  # three distinct rows, eight clusters
+    init_d = np.ascontiguousarray(Xd[::75][:8])
+    c, lab, inertia, n_iter = _bridge.kmeans_fit(Xd, init_d, 10, 0.0)
+    assert _bridge.last_fit_distinct() == len(np.unique(lab)) <= 3
+    with warnings.catch_warnings(record=True) as rec:
+        warnings.simplefilter("always")
+        skmetal.accelerate(KMeans(8, init=init_d, n_init=1, max_iter=10, tol=0)).fit(Xd)
+    assert any(issubclass(r.category, ConvergenceWarning) for r in rec)
+
+
 def test_fit_all_rows_identical():
     X = np.ones((500, 6), dtype=np.float32) * 3.5
     init = np.ascontiguousarray(X[:4])

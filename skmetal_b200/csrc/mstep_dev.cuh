@@ -76,14 +76,6 @@ static __device__ double block_sum_f64(double v, double* scratch /* >= 32 */) {
   return r;
 }
 
-// Sum of v[0, n) in a fixed order for a given block size: thread t adds v[t],
-// v[t + blockDim.x], ... in index order, then the fixed block tree; result
-// valid in thread 0. All threads of the block must call it.
-static __device__ double block_ordered_sum(const double* v, int n, double* scratch) {
-  double t = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) t += v[i];
-  return block_sum_f64(t, scratch);
-}
 // ---------------------------------------------------------------------------
 // bulk fixed-point sums from the labels into the delta buffer D (zero on entry)
 // ---------------------------------------------------------------------------

@@ -28,7 +28,7 @@ constexpr int MAX_KPAD = 256;             // k <= 256 (one UMMA N)
 constexpr int THREADS = 640;
 constexpr int MAX_STAGES = 4;
 constexpr int MAX_ACC = 4;
-constexpr int L2_AHEAD = 4;  // tiles of the next pass prefetched into L2 beyond the stages
+constexpr int L2_AHEAD = 8;  // tiles of the next pass prefetched into L2 beyond the stages
 constexpr unsigned long long TIMEOUT_NS = 2000000000ull;  // 2 s per wait
 
 struct Params {
